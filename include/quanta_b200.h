@@ -1,0 +1,158 @@
+/* quanta_b200.h -- C ABI of the B200 (sm_100a) engine for Quanta.cpp's quantized-transformer hot path.
+ *
+ * Plain C: pointers, sizes and int status codes; no C++ or CUDA types cross this boundary (streams are void*).
+ * Every entry point returns QNT_OK (0) or a negative QNT_ERR_*; qnt_last_error() gives the message of the
+ * calling thread's last failure.  Exceptions never cross the ABI.
+ *
+ * Each declaration names the reference interface it replaces (paths inside the Quanta.cpp tree).
+ */
+#ifndef QUANTA_B200_H
+#define QUANTA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QNT_OK 0
+#define QNT_ERR_INVALID (-1)     /* bad argument / shape */
+#define QNT_ERR_CUDA (-2)        /* CUDA runtime error */
+#define QNT_ERR_IO (-3)          /* file open / parse error */
+#define QNT_ERR_UNSUPPORTED (-4) /* valid for the reference, not implemented on the device */
+#define QNT_ERR_RANGE (-5)       /* position / context overflow (reference: std::out_of_range) */
+#define QNT_ERR_DEVICE (-6)      /* a kernel reported an error bit (bad token id, bounded wait timed out...) */
+
+/* dtypes of engine/src/model_file.h:16 */
+#define QNT_F32 0
+#define QNT_F16 1
+#define QNT_Q8_0 2
+#define QNT_Q4_0 3
+
+const char* qnt_last_error(void);
+int qnt_version(void);          /* 100 * major + minor */
+int qnt_device_count(void);
+int qnt_set_device(int device); /* cudaSetDevice for the calling thread */
+
+/* ---------------------------------------------------------------- ops level (engine/src/ops.h) */
+
+typedef struct qnt_dtensor qnt_dtensor;
+
+/* Uploads a quantized weight matrix given in the .qnt layout (quants, then fp16 scales: engine/src/model_file.h:25-38,
+ * scripts/export.py:10-13) to device memory.  Replaces passing `const Tensor& W` (engine/src/ops.h:57,68). */
+int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_dtensor** out);
+int qnt_tensor_free(qnt_dtensor* t);
+int qnt_tensor_shape(const qnt_dtensor* t, int* dtype, int* rows, int* cols);
+
+/* quantize_q8 (engine/src/ops.h:52, ops_ref.cpp:69-83) on device memory: x [n_tok][n] -> q [n_tok][n],
+ * d [n_tok][n/32].  stream: a cudaStream_t or NULL. */
+int qnt_quantize_q8(const float* x, int n_tok, int n, int8_t* q, float* d, void* stream);
+
+/* MatvecQFn (engine/src/ops.h:57): out[r] = sum_b float(sum_i qW*qx) * dW * dx for r in [r0, r1); device pointers.
+ * Bit-identical to matvec_q_ref (engine/src/ops_ref.cpp:85-120) built without FMA contraction. */
+int qnt_matvec(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, int r1, float* out, void* stream);
+
+/* MatmulQFn (engine/src/ops.h:68): n activations (q [n][cols], d [n][cols/32]), out[t * ldo + r]; device pointers.
+ * Per (row, token) bit-identical to qnt_matvec.  impl: 0 auto, 1 CUDA cores, 2 tensor cores (tcgen05). */
+int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo,
+               int impl, void* stream);
+
+/* Synchronous host-pointer forms of the three calls above: the drop-in for the reference's function pointers
+ * (a MatvecQFn / MatmulQFn shim passes QuantVec::q / QuantVec::d and the caller's output buffer). */
+int qnt_quantize_q8_host(const float* x, int n, int8_t* q, float* d);
+int qnt_matvec_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, int r1, float* out);
+int qnt_matmul_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo,
+                    int impl);
+
+/* ---------------------------------------------------------------- model level (engine/src/model.h) */
+
+typedef struct qnt_model qnt_model;
+
+/* HeadQuery (engine/src/model.h:20-29). */
+typedef struct qnt_head_query {
+    int top_k;        /* 0 = full head */
+    int n_valid;      /* ids >= n_valid are padding (0 = whole vocab) */
+    const int* must;  /* ids whose logits must also be exact (e.g. penalized history) */
+    int n_must;
+} qnt_head_query;
+
+/* HParams (engine/src/model_file.h:40-45). */
+typedef struct qnt_hparams {
+    int vocab_size, dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, max_seq;
+    float rope_theta, norm_eps;
+    int tied_embeddings, qkv_bias;
+    uint32_t flags;
+    int n_tokens;  /* tokenizer vocabulary (Tokenizer::n_tokens, engine/src/tokenizer.h:24) */
+    int ctx_len;   /* KV cache positions of this model handle */
+    int has_shortlist;
+} qnt_hparams;
+
+/* Model::load (engine/src/model.h:35): mmaps the .qnt, uploads every tensor once to HBM in the device layout and
+ * allocates one sequence's f16 KV cache for ctx_len positions (<= 0: the file's max_seq).  flags: reserved, 0. */
+int qnt_model_open(const char* path, int ctx_len, int flags, qnt_model** out);
+void qnt_model_close(qnt_model* m);
+int qnt_model_hparams(const qnt_model* m, qnt_hparams* out);
+
+/* Model::forward (engine/src/model.h:39): one token at pos (positions fed in order), then the head for hq (NULL or
+ * top_k <= 0: full head).  logits: host buffer of vocab_size floats or NULL.  QNT_ERR_RANGE if pos >= ctx_len. */
+int qnt_model_forward(qnt_model* m, int token, int pos, const qnt_head_query* hq, float* logits);
+
+/* Model::forward_batch (engine/src/model.h:44): n tokens at pos0..pos0+n-1 in 32-token chunks; logits of the last. */
+int qnt_model_forward_batch(qnt_model* m, const int* tokens, int n, int pos0, const qnt_head_query* hq, float* logits);
+
+/* Model::head (engine/src/model.h:47) for the last token; coarse / upper (may be NULL) receive the shortlist pass's
+ * 4-bit scores and upper bounds (Model::head_coarse / head_upper, model.h:50-51). */
+int qnt_model_head(qnt_model* m, const qnt_head_query* hq, float* logits, float* coarse, float* upper);
+
+/* Model::last_head_rows / has_shortlist_head / kv_cache_bytes (engine/src/model.h:48-49,58). */
+int qnt_model_last_head_rows(const qnt_model* m);
+int qnt_model_has_shortlist(const qnt_model* m);
+size_t qnt_model_kv_cache_bytes(const qnt_model* m);
+size_t qnt_model_weight_bytes(const qnt_model* m);
+
+/* ---------------------------------------------------------------- session + sampling (engine/src/session.h, sampler.h) */
+
+/* SamplerParams (engine/src/sampler.h:9-18). */
+typedef struct qnt_sampler_params {
+    float temperature; /* <= 0: greedy */
+    int top_k;         /* device sampler: 1..32 when temperature > 0 */
+    float top_p, min_p;
+    float repeat_penalty;
+    int repeat_window; /* 0 = whole history */
+    uint64_t seed;     /* 0 = fixed default seed (the reference uses the clock) */
+} qnt_sampler_params;
+
+typedef struct qnt_gen_stats {
+    double prefill_ms, decode_ms;  /* device time (CUDA events) */
+    long long head_rows, head_calls;
+    int kernels_per_step;
+} qnt_gen_stats;
+
+#define QNT_GEN_SHORTLIST 1     /* Session::set_sampler: use the Exact Shortlist Head when the file has one */
+#define QNT_GEN_BATCH_PREFILL 2 /* Session::set_batch_prefill(true) */
+
+/* Session::feed + Session::generate (engine/src/session.cpp:13-52) with Sampler::sample (sampler.cpp:22-85) on the
+ * device: prefill the prompt, then n_gen steps of sample -> append -> forward without host round trips.
+ * Writes the sampled ids to out_ids and returns how many (or < 0). */
+int qnt_generate(qnt_model* m, const int* prompt, int n_prompt, const qnt_sampler_params* sp, int flags, int n_gen,
+                 int* out_ids, qnt_gen_stats* stats);
+
+/* The same loop in pieces, for callers that drive decoding step by step (and for timing exactly K steps):
+ * qnt_session_begin = Session::feed of the prompt (engine/src/session.cpp:13-31) with the sampler configured;
+ * qnt_session_step  = n iterations of Session::generate's loop body (session.cpp:45-53), queued on the model's stream
+ *                     (returns without waiting; at most ctx_len - 1 positions in total);
+ * qnt_session_read  = waits for the queued steps and copies the sampled ids (returns how many). */
+int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_sampler_params* sp, int flags);
+int qnt_session_step(qnt_model* m, int n);
+int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* stats);
+
+/* The cudaStream_t (as void*) every call on this model is queued on: lets a caller record CUDA events around
+ * qnt_session_step for device timing. */
+void* qnt_model_stream(const qnt_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QUANTA_B200_H */

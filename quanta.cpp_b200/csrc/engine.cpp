@@ -1,0 +1,711 @@
+#include "engine.h"
+
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <stdexcept>
+
+namespace qb {
+
+namespace {
+
+size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+}  // namespace
+
+Engine::~Engine() {
+    if (st_) cudaStreamSynchronize(st_);
+    for (auto& g : graphs_) cudaGraphExecDestroy(g.second);
+    for (void* p : allocs_) cudaFree(p);
+    if (st_) cudaStreamDestroy(st_);
+}
+
+bool Engine::fail(const std::string& m) {
+    err_ = m;
+    return false;
+}
+
+int Engine::cuda_fail(cudaError_t e, const char* what) {
+    err_ = std::string(what) + ": " + cudaGetErrorString(e);
+    return -2;
+}
+
+void* Engine::dalloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, align_up(std::max<size_t>(bytes, 1), 256)) != cudaSuccess) throw std::runtime_error("cudaMalloc failed");
+    allocs_.push_back(p);
+    return p;
+}
+
+int Engine::n_valid_default() const {
+    return std::min(file_.tokenizer().n_tokens > 0 ? file_.tokenizer().n_tokens : hp_.vocab_size, hp_.vocab_size);
+}
+
+// Quantized matrix: quants then fp16 scales, each in its own 256-byte aligned device array.
+DMat Engine::upload_matrix(const HostTensor& t) {
+    if (t.dtype != DT_Q8_0 && t.dtype != DT_Q4_0)
+        throw std::runtime_error("weight matrices must be q8_0 or q4_0 on the device");
+    DMat m;
+    m.dtype = t.dtype;
+    m.rows = t.rows;
+    m.cols = t.cols;
+    const size_t qb = t.quant_bytes(), sb = size_t(t.rows) * (t.cols / QK) * 2;
+    void* q = dalloc(qb);
+    void* d = dalloc(sb);
+    if (cudaMemcpy(q, t.data, qb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d, t.data + qb, sb, cudaMemcpyHostToDevice) != cudaSuccess)
+        throw std::runtime_error("upload failed");
+    m.q = static_cast<const uint8_t*>(q);
+    m.d = static_cast<const __half*>(d);
+    weight_bytes_ += qb + sb;
+    return m;
+}
+
+// Fused matrices.  mode 0: q|k|v, rows pair-interleaved per head (row i and i + head_dim/2 adjacent);
+// mode 1: gate|up interleaved per 32 rows (64j..64j+31 gate block j, 64j+32..64j+63 up block j).
+DMat Engine::upload_fused(const std::vector<const HostTensor*>& parts, int mode) {
+    const int dtype = parts[0]->dtype, cols = parts[0]->cols;
+    int rows = 0;
+    for (const HostTensor* p : parts) {
+        if (p->dtype != dtype || p->cols != cols) throw std::runtime_error("fused matrices need one dtype and width");
+        if (p->dtype != DT_Q8_0 && p->dtype != DT_Q4_0) throw std::runtime_error("weight matrices must be q8_0 or q4_0");
+        rows += p->rows;
+    }
+    const int rb = row_bytes_host(dtype, cols), nb = cols / QK;
+    std::vector<std::pair<const HostTensor*, int>> order;  // (source, source row) per fused row
+    order.reserve(size_t(rows));
+    if (mode == 0) {
+        const int hd = hp_.head_dim, half = hd / 2;
+        for (const HostTensor* p : parts)
+            for (int u = 0; u < p->rows / hd; ++u)
+                for (int i = 0; i < half; ++i) {
+                    order.emplace_back(p, u * hd + i);
+                    order.emplace_back(p, u * hd + i + half);
+                }
+    } else {
+        const HostTensor *g = parts[0], *up = parts[1];
+        for (int j = 0; j < g->rows / QK; ++j) {
+            for (int i = 0; i < QK; ++i) order.emplace_back(g, j * QK + i);
+            for (int i = 0; i < QK; ++i) order.emplace_back(up, j * QK + i);
+        }
+    }
+    std::vector<uint8_t> hq(size_t(rows) * rb);
+    std::vector<uint16_t> hd(size_t(rows) * nb);
+    for (int r = 0; r < rows; ++r) {
+        const HostTensor* src = order[size_t(r)].first;
+        const int sr = order[size_t(r)].second;
+        std::memcpy(hq.data() + size_t(r) * rb, src->data + size_t(sr) * rb, size_t(rb));
+        std::memcpy(hd.data() + size_t(r) * nb, src->scales() + size_t(sr) * nb, size_t(nb) * 2);
+    }
+    DMat m;
+    m.dtype = dtype;
+    m.rows = rows;
+    m.cols = cols;
+    void* q = dalloc(hq.size());
+    void* d = dalloc(hd.size() * 2);
+    cudaMemcpy(q, hq.data(), hq.size(), cudaMemcpyHostToDevice);
+    cudaMemcpy(d, hd.data(), hd.size() * 2, cudaMemcpyHostToDevice);
+    m.q = static_cast<const uint8_t*>(q);
+    m.d = static_cast<const __half*>(d);
+    weight_bytes_ += hq.size() + hd.size() * 2;
+    return m;
+}
+
+bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
+    auto bad = [&](const std::string& m) {
+        err_ = m;
+        if (err) *err = m;
+        return false;
+    };
+    std::string e;
+    if (!file_.open(path, &e)) return bad(e);
+    hp_ = file_.hparams();
+    if (hp_.n_heads * hp_.head_dim != hp_.dim || hp_.n_kv_heads <= 0 || hp_.n_heads % hp_.n_kv_heads != 0)
+        return bad("unsupported head configuration");
+    if (hp_.head_dim != 64) return bad("the device attention kernel needs head_dim == 64");
+    if (hp_.n_heads / hp_.n_kv_heads > 8) return bad("the device attention kernel needs <= 8 query heads per kv head");
+    if (hp_.dim % QK || hp_.ffn_dim % QK || hp_.dim > 8192 || hp_.ffn_dim > 16384) return bad("unsupported dims");
+    if (hp_.flags & 1u) return bad("FLAG_HADAMARD_DOWN files are not supported on the device yet");
+    ctx_ = (ctx_len > 0 && ctx_len < hp_.max_seq) ? ctx_len : hp_.max_seq;
+    if (cudaGetDevice(&device_) != cudaSuccess) return bad("no CUDA device");
+    cudaDeviceProp prop;
+    cudaGetDeviceProperties(&prop, device_);
+    if (prop.major < 10) return bad("this build needs an sm_100 (Blackwell) GPU");
+    n_sm_ = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) return bad("stream create failed");
+    try {
+        const HostTensor& emb = file_.get("model.embed_tokens.weight");
+        embed_ = upload_matrix(emb);
+        lm_head_ = hp_.tied_embeddings ? embed_ : upload_matrix(file_.get("lm_head.weight"));
+        const HostTensor& fn = file_.get("model.norm.weight");
+        auto upload_f32 = [&](const HostTensor& t) {
+            if (t.dtype != DT_F32) throw std::runtime_error("norms and biases must be f32");
+            void* p = dalloc(size_t(t.cols) * t.rows * 4);
+            cudaMemcpy(p, t.data, size_t(t.cols) * t.rows * 4, cudaMemcpyHostToDevice);
+            weight_bytes_ += size_t(t.cols) * t.rows * 4;
+            return static_cast<const float*>(p);
+        };
+        final_norm_ = upload_f32(fn);
+        const int kv_dim = hp_.n_kv_heads * hp_.head_dim;
+        const size_t kv_elems = size_t(hp_.n_layers) * ctx_ * kv_dim;
+        kcache_ = static_cast<__half*>(dalloc(kv_elems * 2));
+        vcache_ = static_cast<__half*>(dalloc(kv_elems * 2));
+        cudaMemset(kcache_, 0, kv_elems * 2);
+        cudaMemset(vcache_, 0, kv_elems * 2);
+        kv_bytes_ = kv_elems * 4;
+
+        // RoPE tables with the reference's own expressions (engine/src/ops_ref.cpp:204-206).
+        const int half = hp_.head_dim / 2;
+        std::vector<float> cs(size_t(ctx_) * half), sn(size_t(ctx_) * half);
+        for (int i = 0; i < half; ++i) {
+            const float freq = std::pow(hp_.rope_theta, -2.0f * i / hp_.head_dim);
+            for (int pos = 0; pos < ctx_; ++pos) {
+                const float angle = pos * freq;
+                cs[size_t(pos) * half + i] = std::cos(angle);
+                sn[size_t(pos) * half + i] = std::sin(angle);
+            }
+        }
+        rope_cos_ = static_cast<float*>(dalloc(cs.size() * 4));
+        rope_sin_ = static_cast<float*>(dalloc(sn.size() * 4));
+        cudaMemcpy(rope_cos_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(rope_sin_, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+
+        max_chunks_ = (ctx_ + 63) / 64;
+        part_ml_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * 2 * 4));
+        part_o_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * hp_.head_dim * 4));
+        counters_ = static_cast<unsigned*>(dalloc(size_t(kChunk) * hp_.n_kv_heads * 4));
+        cudaMemset(counters_, 0, size_t(kChunk) * hp_.n_kv_heads * 4);
+
+        layers_.resize(size_t(hp_.n_layers));
+        const size_t before_layers = weight_bytes_;
+        for (int l = 0; l < hp_.n_layers; ++l) {
+            const std::string p = "model.layers." + std::to_string(l) + ".";
+            Layer& L = layers_[size_t(l)];
+            L.attn_norm = upload_f32(file_.get(p + "input_layernorm.weight"));
+            L.ffn_norm = upload_f32(file_.get(p + "post_attention_layernorm.weight"));
+            const HostTensor &wq = file_.get(p + "self_attn.q_proj.weight"), &wk = file_.get(p + "self_attn.k_proj.weight"),
+                             &wv = file_.get(p + "self_attn.v_proj.weight");
+            L.qkv = upload_fused({&wq, &wk, &wv}, 0);
+            L.o = upload_matrix(file_.get(p + "self_attn.o_proj.weight"));
+            L.gu = upload_fused({&file_.get(p + "mlp.gate_proj.weight"), &file_.get(p + "mlp.up_proj.weight")}, 1);
+            L.down = upload_matrix(file_.get(p + "mlp.down_proj.weight"));
+            // fused bias in the q|k|v pair-interleaved order
+            std::vector<float> b(size_t(L.qkv.rows), 0.f);
+            if (hp_.qkv_bias) {
+                const HostTensor* bs[3] = {&file_.get(p + "self_attn.q_proj.bias"), &file_.get(p + "self_attn.k_proj.bias"),
+                                           &file_.get(p + "self_attn.v_proj.bias")};
+                int fr = 0;
+                for (const HostTensor* t : bs) {
+                    if (t->dtype != DT_F32) throw std::runtime_error("qkv biases must be f32");
+                    const float* v = reinterpret_cast<const float*>(t->data);
+                    for (int u = 0; u < t->cols / hp_.head_dim; ++u)
+                        for (int i = 0; i < half; ++i) {
+                            b[size_t(fr++)] = v[u * hp_.head_dim + i];
+                            b[size_t(fr++)] = v[u * hp_.head_dim + i + half];
+                        }
+                }
+            }
+            float* db = static_cast<float*>(dalloc(b.size() * 4));
+            cudaMemcpy(db, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
+            weight_bytes_ += b.size() * 4;
+            L.bqkv = db;
+            QkvArgs& qa = L.qa;
+            qa.W = L.qkv;
+            qa.bias = db;
+            qa.rope_cos = rope_cos_;
+            qa.rope_sin = rope_sin_;
+            qa.kcache = kcache_ + size_t(l) * ctx_ * kv_dim;
+            qa.vcache = vcache_ + size_t(l) * ctx_ * kv_dim;
+            qa.n_heads = hp_.n_heads;
+            qa.n_kv = hp_.n_kv_heads;
+            qa.head_dim = hp_.head_dim;
+            qa.kv_dim = kv_dim;
+            AttnArgs& aa = L.aa;
+            aa.kcache = qa.kcache;
+            aa.vcache = qa.vcache;
+            aa.n_heads = hp_.n_heads;
+            aa.n_kv = hp_.n_kv_heads;
+            aa.head_dim = hp_.head_dim;
+            aa.kv_dim = kv_dim;
+            aa.scale = 1.0f / std::sqrt(float(hp_.head_dim));
+            aa.max_chunks = max_chunks_;
+            aa.part_ml = part_ml_;
+            aa.part_o = part_o_;
+            aa.counters = counters_;
+            L.p_qkv = plan_rows(L.qkv.dtype, L.qkv.rows, L.qkv.cols, n_sm_, 2);
+            L.p_o = plan_rows(L.o.dtype, L.o.rows, L.o.cols, n_sm_, 2);
+            L.p_gu = plan_rows(L.gu.dtype, L.gu.rows, L.gu.cols, n_sm_, 64);
+            L.p_down = plan_rows(L.down.dtype, L.down.rows, L.down.cols, n_sm_, 2);
+        }
+        layer_bytes_ = weight_bytes_ - before_layers + size_t(hp_.dim) * 4;
+
+        // Exact Shortlist Head tensors (validated like engine/src/model.cpp:47-58).
+        const HostTensor* q4 = file_.find("quanta.head_q4");
+        const HostTensor* he = file_.find("quanta.head_err");
+        if (q4 || he) {
+            const bool ok = q4 && he && q4->dtype == DT_Q4_0 && he->dtype == DT_F16 && lm_head_.dtype == DT_Q8_0 &&
+                            q4->rows == lm_head_.rows && q4->cols == lm_head_.cols && he->rows == lm_head_.rows &&
+                            he->cols == lm_head_.cols / QK;
+            if (!ok) return bad("bad shortlist head tensors");
+            head_q4_dm_ = upload_matrix(*q4);
+            head_q4_ = head_q4_dm_.q;
+            void* pe = dalloc(he->quant_bytes());
+            cudaMemcpy(pe, he->data, he->quant_bytes(), cudaMemcpyHostToDevice);
+            weight_bytes_ += he->quant_bytes();
+            head_err_ = static_cast<const __half*>(pe);
+        }
+
+        // activations
+        const int wmax = std::max(hp_.dim, hp_.ffn_dim);
+        const int rmax = std::max({layers_[0].qkv.rows, 2 * hp_.ffn_dim, hp_.dim});
+        X_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
+        Q_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
+        ATT_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
+        R_ = static_cast<float*>(dalloc(size_t(kChunk) * rmax * 4));
+        XQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * wmax));
+        DX_ = static_cast<float*>(dalloc(size_t(kChunk) * (wmax / QK) * 4));
+        HQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * hp_.ffn_dim));
+        HD_ = static_cast<float*>(dalloc(size_t(kChunk) * (hp_.ffn_dim / QK) * 4));
+        tokens_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
+        pos_ = static_cast<int*>(dalloc(16));
+
+        const int V = hp_.vocab_size, nbd = hp_.dim / QK;
+        hin_.xq = static_cast<int8_t*>(dalloc(size_t(hp_.dim)));
+        hin_.dx = static_cast<float*>(dalloc(size_t(nbd) * 4));
+        hin_.xsum = static_cast<int*>(dalloc(size_t(nbd) * 4));
+        hin_.xnorm = static_cast<float*>(dalloc(size_t(nbd) * 4));
+        plan_head8_ = plan_head(lm_head_.dtype, V, hp_.dim);
+        logits_ = static_cast<float*>(dalloc(size_t(V) * 4));
+        coarse_ = static_cast<float*>(dalloc(size_t(V) * 4));
+        upper_ = static_cast<float*>(dalloc(size_t(V) * 4));
+        mark_ = static_cast<unsigned char*>(dalloc(size_t(V)));
+        cudaMemset(mark_, 0, size_t(V));
+        hs_ = static_cast<HeadState*>(dalloc(sizeof(HeadState)));
+        cudaMemset(hs_, 0, sizeof(HeadState));
+        must_ = static_cast<int*>(dalloc(size_t(ctx_ + 64) * 4));
+        n_must_ = static_cast<int*>(dalloc(16));
+        coarse_ctas_ = 4 * n_sm_;
+        cand_ctas_ = 2 * n_sm_;
+        if (head_q4_) plan_head4_ = plan_head(DT_Q4_0, V, hp_.dim);
+        seed_buf_ = dalloc(size_t(coarse_ctas_) * 32 * 8);
+
+        ss_ = static_cast<SamplerState*>(dalloc(sizeof(SamplerState)));
+        cudaMemset(ss_, 0, sizeof(SamplerState));
+        hist_ = static_cast<int*>(dalloc(size_t(ctx_ + 1) * 4));
+        flag_ = static_cast<unsigned*>(dalloc(size_t(V) * 4));
+        cudaMemset(flag_, 0, size_t(V) * 4);
+        sample_parts_ = 2 * n_sm_;
+        part_buf_ = dalloc(size_t(sample_parts_) * 32 * 8);
+        status_ = static_cast<unsigned*>(dalloc(16));
+        cudaMemset(status_, 0, 16);
+        host_tmp_.resize(size_t(V));
+    } catch (const std::exception& ex) {
+        return bad(ex.what());
+    }
+    cudaError_t ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) return bad(std::string("device error after load: ") + cudaGetErrorString(ce));
+    return true;
+}
+
+size_t Engine::head_bytes_full() const {
+    return size_t(lm_head_.rows) * (row_bytes_host(lm_head_.dtype, lm_head_.cols) + lm_head_.cols / QK * 2);
+}
+
+unsigned Engine::read_status() {
+    unsigned s = 0;
+    cudaMemcpy(&s, status_, 4, cudaMemcpyDeviceToHost);
+    if (s) cudaMemset(status_, 0, 4);
+    return s;
+}
+
+int Engine::sync_check() {
+    cudaError_t e = cudaStreamSynchronize(st_);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel");
+    unsigned s = read_status();
+    if (s) {
+        err_ = "device status error bits 0x" + std::to_string(s);
+        return -6;
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------- launch sequences
+
+#define QB_TRY(expr)                                                     \
+    do {                                                                 \
+        cudaError_t e_ = (expr);                                         \
+        ++kernel_count_;                                                 \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #expr);              \
+    } while (0)
+
+int Engine::launch_layers_decode(const int* pos_dev) {
+    for (const Layer& L : layers_) {
+        QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
+        QB_TRY(launch_attn(L.aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
+        QB_TRY(launch_resid_dec(L.o, L.p_o, ATT_, nullptr, nullptr, X_, st_, pdl_));
+        QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, st_, pdl_));
+        QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_));
+    }
+    return 0;
+}
+
+int Engine::launch_matmul(const DMat& W, const int8_t* xq, const float* dx, int n, float* out) {
+    QB_TRY(launch_matmul_simt(W, xq, dx, n, 0, W.rows, out, W.rows, st_));
+    return 0;
+}
+
+int Engine::launch_chunk(int n, const int* pos_dev) {
+    const int dim = hp_.dim;
+    for (const Layer& L : layers_) {
+        QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
+        if (int r = launch_matmul(L.qkv, XQ_, DX_, n, R_)) return r;
+        QB_TRY(launch_qkv_epilogue(L.qa, R_, n, pos_dev, Q_, st_, pdl_));
+        QB_TRY(launch_attn(L.aa, Q_, pos_dev, n, ATT_, st_, pdl_));
+        QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, st_, pdl_));
+        if (int r = launch_matmul(L.o, XQ_, DX_, n, R_)) return r;
+        QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
+        QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
+        if (int r = launch_matmul(L.gu, XQ_, DX_, n, R_)) return r;
+        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, st_, pdl_));
+        if (int r = launch_matmul(L.down, HQ_, HD_, n, R_)) return r;
+        QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
+    }
+    return 0;
+}
+
+int Engine::launch_head(const HeadQueryC& hq, bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev,
+                        int n_must_host, int window) {
+    (void)hq;
+    if (!shortlist) {
+        QB_TRY(launch_head_full(lm_head_, plan_head8_, hin_, logits_, st_, pdl_));
+        return 0;
+    }
+    ShortlistArgs a;
+    a.W8 = lm_head_;
+    a.W4 = head_q4_dm_;
+    a.err = head_err_;
+    a.plan4 = plan_head4_;
+    a.coarse_ctas = coarse_ctas_;
+    a.cand_ctas = cand_ctas_;
+    a.k = k;
+    a.n_valid = n_valid;
+    a.must = must;
+    a.n_must_dev = n_must_dev;
+    a.n_must_host = n_must_host;
+    a.window = window;
+    a.mark = mark_;
+    a.coarse = coarse_;
+    a.upper = upper_;
+    a.logits = logits_;
+    a.seed_buf = seed_buf_;
+    a.hs = hs_;
+    QB_TRY(launch_shortlist(a, hin_, st_, pdl_));
+    kernel_count_ += 3;
+    return 0;
+}
+
+int Engine::run_graph(const std::string& key, const std::function<int()>& body) {
+    if (!use_graphs_) return body();
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+        cudaGraph_t g;
+        if (cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return cuda_fail(cudaGetLastError(), "capture");
+        const int r = body();
+        cudaError_t e = cudaStreamEndCapture(st_, &g);
+        if (r) return r;
+        if (e != cudaSuccess) return cuda_fail(e, "end capture");
+        cudaGraphExec_t ex;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+        it = graphs_.emplace(key, ex).first;
+    }
+    cudaError_t e = cudaGraphLaunch(it->second, st_);
+    if (e != cudaSuccess) return cuda_fail(e, "graph launch");
+    return 0;
+}
+
+// ---------------------------------------------------------------- public API
+
+namespace {
+struct HeadMode {
+    bool shortlist;
+    int k;
+    int n_valid;
+};
+}  // namespace
+
+static HeadMode head_mode(const HeadQueryC* hq, bool has_sl, int V) {
+    HeadMode m{false, 0, V};
+    if (hq && hq->top_k > 0 && has_sl) {
+        m.shortlist = true;
+        m.k = hq->top_k;
+        m.n_valid = (hq->n_valid > 0 && hq->n_valid < V) ? hq->n_valid : V;
+    }
+    return m;
+}
+
+int Engine::forward(int token, int pos, const HeadQueryC* hq, float* out) {
+    if (pos < 0 || pos >= ctx_) {
+        err_ = "position exceeds context length";
+        return -5;
+    }
+    const int V = hp_.vocab_size;
+    const HeadMode hm = head_mode(hq, has_shortlist(), V);
+    if (hm.shortlist && hm.k + 8 > 32) {
+        err_ = "shortlist head supports top_k <= 24";
+        return -4;
+    }
+    SamplerState st{};
+    st.token = token;
+    st.pos = pos;
+    cudaMemcpyAsync(&ss_->pos, &st.pos, 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(&ss_->token, &st.token, 4, cudaMemcpyHostToDevice, st_);
+    const int n_must = hm.shortlist ? hq->n_must : 0;
+    if (n_must > ctx_ + 64) {
+        err_ = "too many must ids";
+        return -1;
+    }
+    if (n_must > 0) cudaMemcpyAsync(must_, hq->must, size_t(n_must) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(n_must_, &n_must, 4, cudaMemcpyHostToDevice, st_);
+    const std::string key = hm.shortlist ? "fwd|sl|" + std::to_string(hm.k) + "|" + std::to_string(hm.n_valid) : "fwd|full";
+    const int r = run_graph(key, [&]() -> int {
+        QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
+        if (int rr = launch_layers_decode(&ss_->pos)) return rr;
+        QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, hm.shortlist ? 0 : V, st_, pdl_));
+        return launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0);
+    });
+    if (r) return r;
+    if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
+    if (int rr = sync_check()) return rr;
+    if (hm.shortlist) {
+        HeadState h;
+        cudaMemcpy(&h, hs_, sizeof h, cudaMemcpyDeviceToHost);
+        last_head_rows_ = h.rows;
+    } else {
+        last_head_rows_ = V;
+    }
+    return 0;
+}
+
+int Engine::forward_batch(const int* tokens, int n, int pos0, const HeadQueryC* hq, float* out) {
+    if (n <= 0) {
+        err_ = "forward_batch needs at least one token";
+        return -1;
+    }
+    if (pos0 < 0 || pos0 + n > ctx_) {
+        err_ = "position exceeds context length";
+        return -5;
+    }
+    const int V = hp_.vocab_size;
+    const HeadMode hm = head_mode(hq, has_shortlist(), V);
+    if (hm.shortlist && hm.k + 8 > 32) {
+        err_ = "shortlist head supports top_k <= 24";
+        return -4;
+    }
+    int last = 0;
+    for (int i = 0; i < n; i += kChunk) {
+        const int m = std::min(kChunk, n - i);
+        const int p = pos0 + i;
+        cudaMemcpyAsync(tokens_, tokens + i, size_t(m) * 4, cudaMemcpyHostToDevice, st_);
+        cudaMemcpyAsync(pos_, &p, 4, cudaMemcpyHostToDevice, st_);
+        QB_TRY(launch_embed(embed_, tokens_, m, X_, status_, st_, false));
+        if (int r = launch_chunk(m, pos_)) return r;
+        last = m - 1;
+    }
+    const int n_must = hm.shortlist ? hq->n_must : 0;
+    if (n_must > 0) cudaMemcpyAsync(must_, hq->must, size_t(n_must) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(n_must_, &n_must, 4, cudaMemcpyHostToDevice, st_);
+    QB_TRY(launch_head_input(X_ + size_t(last) * hp_.dim, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, hm.shortlist ? 0 : V, st_, pdl_));
+    if (int r = launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0)) return r;
+    if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
+    if (int rr = sync_check()) return rr;
+    if (hm.shortlist) {
+        HeadState h;
+        cudaMemcpy(&h, hs_, sizeof h, cudaMemcpyDeviceToHost);
+        last_head_rows_ = h.rows;
+    } else {
+        last_head_rows_ = V;
+    }
+    return 0;
+}
+
+int Engine::head(const HeadQueryC* hq, float* out, float* coarse, float* upper) {
+    const int V = hp_.vocab_size;
+    const HeadMode hm = head_mode(hq, has_shortlist(), V);
+    if (hm.shortlist && hm.k + 8 > 32) {
+        err_ = "shortlist head supports top_k <= 24";
+        return -4;
+    }
+    const int n_must = hm.shortlist ? hq->n_must : 0;
+    if (n_must > 0) cudaMemcpyAsync(must_, hq->must, size_t(n_must) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(n_must_, &n_must, 4, cudaMemcpyHostToDevice, st_);
+    if (int r = launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0)) return r;
+    if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
+    if (hm.shortlist && coarse) cudaMemcpyAsync(coarse, coarse_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
+    if (hm.shortlist && upper) cudaMemcpyAsync(upper, upper_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
+    if (int rr = sync_check()) return rr;
+    if (hm.shortlist) {
+        HeadState h;
+        cudaMemcpy(&h, hs_, sizeof h, cudaMemcpyDeviceToHost);
+        last_head_rows_ = h.rows;
+    } else {
+        last_head_rows_ = V;
+    }
+    return 0;
+}
+
+int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill) {
+    if (n_prompt <= 0 || n_prompt + 1 >= ctx_) {
+        err_ = "prompt does not fit in the context";
+        return -5;
+    }
+    const bool greedy = sp.temperature <= 0.f;
+    const int K = greedy ? 1 : sp.top_k;
+    if (K < 1 || K > 32) {
+        err_ = "device sampler supports 1 <= top_k <= 32";
+        return -4;
+    }
+    const int nv = n_valid_default();
+    const bool sl = use_shortlist && has_shortlist();
+    if (sl && K + 8 > 32) {
+        err_ = "shortlist head supports top_k <= 24";
+        return -4;
+    }
+    const bool penal = sp.repeat_penalty != 1.0f;
+    sess_ = Sess{};
+    sess_.active = false;
+    sess_.sp = sp;
+    sess_.sl = sl;
+    sess_.K = K;
+    sess_.nv = nv;
+    sess_.penal = penal;
+    sess_.n_prompt = n_prompt;
+    // session state: history = prompt, rng = seed | 1 (engine/src/sampler.cpp:15-20)
+    SamplerState st{};
+    st.rng = (sp.seed ? sp.seed : 0x9E3779B97F4A7C15ULL) | 1ULL;
+    st.n_hist = n_prompt;
+    st.pos = n_prompt - 1;
+    cudaMemcpyAsync(hist_, prompt, size_t(n_prompt) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemsetAsync(hs_, 0, sizeof(HeadState), st_);
+    // prefill (Session::feed): head query k with must = history (when penalized)
+    HeadQueryC hq;
+    std::vector<int> must;
+    if (sl) {
+        hq.top_k = K;
+        hq.n_valid = nv;
+        if (penal) {
+            const int from = (sp.repeat_window > 0 && n_prompt > sp.repeat_window) ? n_prompt - sp.repeat_window : 0;
+            must.assign(prompt + from, prompt + n_prompt);
+        }
+        hq.must = must.data();
+        hq.n_must = int(must.size());
+    }
+    if (batch_prefill) {
+        if (int r = forward_batch(prompt, n_prompt, 0, sl ? &hq : nullptr, nullptr)) return r;
+    } else {
+        for (int i = 0; i < n_prompt; ++i) {
+            if (sl && penal) {
+                const int from = (sp.repeat_window > 0 && i + 1 > sp.repeat_window) ? i + 1 - sp.repeat_window : 0;
+                hq.must = prompt + from;
+                hq.n_must = i + 1 - from;
+            }
+            if (int r = forward(prompt[i], i, sl ? &hq : nullptr, nullptr)) return r;
+        }
+    }
+    cudaMemcpyAsync(ss_, &st, sizeof st, cudaMemcpyHostToDevice, st_);  // forward() used token/pos
+    if (int rr = sync_check()) return rr;
+    sess_.active = true;
+    sess_.steps = 0;
+    return 0;
+}
+
+int Engine::session_step(int n) {
+    if (!sess_.active) {
+        err_ = "no active session";
+        return -1;
+    }
+    const int room = ctx_ - 1 - (sess_.n_prompt + sess_.steps);
+    n = std::min(n, room);
+    if (n <= 0) return 0;
+    const SamplerParamsC& sp = sess_.sp;
+    SamplerLaunch sl_args;
+    sl_args.logits = logits_;
+    sl_args.n_valid = sess_.nv;
+    sl_args.K = sess_.K;
+    sl_args.parts = sample_parts_;
+    sl_args.part_buf = part_buf_;
+    sl_args.args = SamplerArgs{sp.temperature, sp.top_p, sp.min_p, sp.repeat_penalty, 1};
+    sl_args.state = ss_;
+    sl_args.hist = hist_;
+    sl_args.n_hist_dev = &ss_->n_hist;
+    sl_args.hist_cap = ctx_;
+    sl_args.window = sp.repeat_window;
+    sl_args.flag = flag_;
+    const bool sl = sess_.sl, penal = sess_.penal;
+    const int K = sess_.K, nv = sess_.nv, V = hp_.vocab_size;
+    const std::string key = "gen|" + std::to_string(sl) + "|" + std::to_string(K) + "|" + std::to_string(penal) + "|" +
+                            std::to_string(sp.repeat_window) + "|" + std::to_string(sp.temperature) + "|" +
+                            std::to_string(sp.top_p) + "|" + std::to_string(sp.min_p) + "|" + std::to_string(sp.repeat_penalty);
+    for (int s = 0; s < n; ++s) {
+        const int r = run_graph(key, [&]() -> int {
+            const int c0 = kernel_count_;
+            QB_TRY(launch_sampler(sl_args, st_, pdl_));
+            kernel_count_ += penal ? 2 : 1;
+            QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
+            if (int rr = launch_layers_decode(&ss_->pos)) return rr;
+            QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, sl ? 0 : V, st_, pdl_));
+            // must ids = the penalized history window (session.cpp:63-79); none without a penalty
+            const int rr = launch_head(HeadQueryC{}, sl, K, nv, penal ? hist_ : nullptr, penal ? &ss_->n_hist : nullptr, 0,
+                                       penal ? sp.repeat_window : 0);
+            kernels_per_step_ = kernel_count_ - c0;
+            return rr;
+        });
+        if (r) return r;
+    }
+    sess_.steps += n;
+    return n;
+}
+
+int Engine::session_read(int* out_ids, int max_ids, GenStats* stats) {
+    if (int rr = sync_check()) return rr;
+    const int n = std::min(sess_.steps, max_ids);
+    if (n > 0) cudaMemcpy(out_ids, hist_ + sess_.n_prompt, size_t(n) * 4, cudaMemcpyDeviceToHost);
+    if (stats) {
+        HeadState h;
+        cudaMemcpy(&h, hs_, sizeof h, cudaMemcpyDeviceToHost);
+        // every head call of the session (session.cpp:54-61): k_head_input accumulates the previous head's rows
+        stats->head_rows = h.rows_total + h.rows;
+        stats->head_calls = h.calls;
+    }
+    return n;
+}
+
+int Engine::generate(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill,
+                     int n_gen, int* out_ids, GenStats* stats) {
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&e2);
+    cudaEventRecord(e0, st_);
+    int r = session_begin(prompt, n_prompt, sp, use_shortlist, batch_prefill);
+    cudaEventRecord(e1, st_);
+    if (r == 0) r = session_step(n_gen);
+    cudaEventRecord(e2, st_);
+    if (r >= 0) r = session_read(out_ids, n_gen, stats);
+    float ms_pre = 0, ms_dec = 0;
+    if (r >= 0) {
+        cudaEventElapsedTime(&ms_pre, e0, e1);
+        cudaEventElapsedTime(&ms_dec, e1, e2);
+        if (stats) {
+            stats->prefill_ms = ms_pre;
+            stats->decode_ms = ms_dec;
+        }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    return r;
+}
+
+}  // namespace qb

@@ -1,0 +1,177 @@
+// Model engine: the device-side replacement of quanta::Model + Session (engine/src/model.h:31-102,
+// engine/src/session.h:13-80).  One Engine owns one model in HBM, one sequence's f16 KV cache and the buffers of a
+// 32-token prefill chunk; forward / forward_batch / head keep the reference's contracts.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "head_kernels.h"
+#include "layer_kernels.h"
+#include "qnt_file.h"
+
+namespace qb {
+
+struct HeadQueryC {
+    int top_k = 0;
+    int n_valid = 0;
+    const int* must = nullptr;
+    int n_must = 0;
+};
+
+struct SamplerParamsC {
+    float temperature = 0.7f;
+    int top_k = 20;
+    float top_p = 0.8f;
+    float min_p = 0.0f;
+    float repeat_penalty = 1.1f;
+    int repeat_window = 0;
+    unsigned long long seed = 0;
+};
+
+struct GenStats {
+    double prefill_ms = 0, decode_ms = 0;
+    long long head_rows = 0, head_calls = 0;
+};
+
+enum MatmulImpl { MM_AUTO = 0, MM_SIMT = 1, MM_TC = 2 };
+
+class Engine {
+public:
+    Engine() = default;
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    bool load(const std::string& path, int ctx_len, std::string* err);
+
+    // Model::forward (model.h:39): token at `pos`, logits of the head query (copied to `out` if not null).
+    int forward(int token, int pos, const HeadQueryC* hq, float* out);
+    // Model::forward_batch (model.h:44): n tokens at pos0.., 32-token chunks, logits of the last one.
+    int forward_batch(const int* tokens, int n, int pos0, const HeadQueryC* hq, float* out);
+    // Model::head (model.h:47): head of the last token again.  coarse/upper get the shortlist pass's scores.
+    int head(const HeadQueryC* hq, float* out, float* coarse, float* upper);
+    int last_head_rows() const { return last_head_rows_; }
+    bool has_shortlist() const { return head_q4_ != nullptr; }
+
+    // Session::feed + Session::generate (session.cpp:13-52) with sampling on the device: the prompt is prefilled,
+    // then each step samples from the current logits, appends the id to the history and runs the next forward.
+    // Returns the number of generated ids (no stop tokens), or < 0 on error.
+    int generate(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill, int n_gen,
+                 int* out_ids, GenStats* stats);
+
+    // The same loop in pieces: prefill the prompt, run n decode steps (sample -> append -> forward, one CUDA graph
+    // replay each), read the sampled ids.  generate() = begin + step(n_gen) + read.
+    int session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill);
+    int session_step(int n);
+    int session_read(int* out_ids, int max_ids, GenStats* stats);
+
+    const HParams& hparams() const { return hp_; }
+    int ctx_len() const { return ctx_; }
+    int n_valid_default() const;
+    size_t weight_bytes() const { return weight_bytes_; }
+    size_t kv_cache_bytes() const { return kv_bytes_; }
+    const std::string& error() const { return err_; }
+    void set_matmul_impl(int impl) { mm_impl_ = impl; }
+    void set_use_graphs(bool on) { use_graphs_ = on; }
+    void set_use_pdl(bool on) { pdl_ = on; }
+    unsigned read_status();  // device error bits (and clears them)
+    cudaStream_t stream() const { return st_; }
+    // Per-token algorithmic bytes of one decode step's weights (layers + final norm), head excluded.
+    size_t layer_weight_bytes() const { return layer_bytes_; }
+    size_t head_bytes_full() const;
+    // Counters of the last generate() (kernels per decode step, captured in the step graph).
+    int kernels_per_step() const { return kernels_per_step_; }
+
+    const float* logits_dev() const { return logits_; }
+
+private:
+    struct Layer {
+        DMat qkv, o, gu, down;
+        const float *attn_norm, *ffn_norm, *bqkv;
+        QkvArgs qa;
+        AttnArgs aa;
+        SlicePlan p_qkv, p_o, p_gu, p_down;
+    };
+
+    bool fail(const std::string& m);
+    int cuda_fail(cudaError_t e, const char* what);
+    void* dalloc(size_t bytes);
+    DMat upload_matrix(const HostTensor& t);
+    DMat upload_fused(const std::vector<const HostTensor*>& parts, int mode);
+    int launch_layers_decode(const int* pos_dev);
+    int launch_chunk(int n, const int* pos_dev);
+    int launch_head(const HeadQueryC& hq, bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev,
+                    int n_must_host, int window);
+    int launch_matmul(const DMat& W, const int8_t* xq, const float* dx, int n, float* out);
+    int run_graph(const std::string& key, const std::function<int()>& body);
+    int sync_check();
+
+    QntFile file_;
+    HParams hp_;
+    int ctx_ = 0, max_chunks_ = 0;
+    std::string err_;
+    cudaStream_t st_ = nullptr;
+    bool pdl_ = true, use_graphs_ = true;
+    int mm_impl_ = MM_AUTO;
+    int device_ = 0, n_sm_ = 148;
+
+    std::vector<void*> allocs_;
+    size_t weight_bytes_ = 0, kv_bytes_ = 0, layer_bytes_ = 0;
+
+    DMat embed_{}, lm_head_{};
+    const float* final_norm_ = nullptr;
+    DMat head_q4_dm_{};
+    const void* head_q4_ = nullptr;
+    const __half* head_err_ = nullptr;
+    std::vector<Layer> layers_;
+    float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
+    __half *kcache_ = nullptr, *vcache_ = nullptr;
+
+    // activations (chunk of up to kChunk tokens)
+    static constexpr int kChunk = 32;
+    float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
+    int8_t *XQ_ = nullptr, *HQ_ = nullptr;
+    float *part_ml_ = nullptr, *part_o_ = nullptr;
+    unsigned* counters_ = nullptr;
+    int* tokens_ = nullptr;
+    int* pos_ = nullptr;  // chunk start position (device)
+
+    // head
+    HeadIn hin_{};
+    HeadPlan plan_head8_{}, plan_head4_{};
+    float *logits_ = nullptr, *coarse_ = nullptr, *upper_ = nullptr;
+    unsigned char* mark_ = nullptr;
+    void* seed_buf_ = nullptr;
+    HeadState* hs_ = nullptr;
+    int* must_ = nullptr;
+    int* n_must_ = nullptr;
+    int coarse_ctas_ = 0, cand_ctas_ = 0;
+
+    // sampler / session state
+    SamplerState* ss_ = nullptr;
+    int* hist_ = nullptr;
+    unsigned* flag_ = nullptr;
+    void* part_buf_ = nullptr;
+    int sample_parts_ = 0;
+    unsigned* status_ = nullptr;
+
+    struct Sess {
+        bool active = false, sl = false, penal = false;
+        int K = 1, nv = 0, n_prompt = 0, steps = 0;
+        SamplerParamsC sp;
+    } sess_;
+    int last_head_rows_ = 0;
+    int kernels_per_step_ = 0;
+    int kernel_count_ = 0;  // launches issued since the last reset (counted by the launch helpers)
+    std::map<std::string, cudaGraphExec_t> graphs_;
+    std::vector<float> host_tmp_;
+};
+
+}  // namespace qb

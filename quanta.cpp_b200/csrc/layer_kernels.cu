@@ -1,0 +1,467 @@
+// Per-layer kernels of the Qwen2 forward (engine/src/model.cpp:165-228 decode, :363-433 prefill chunk).
+//
+// Decode (one token) runs five kernels per layer, each fusing its neighbours:
+//   k_qkv_dec     rmsnorm + quantize (prologue) -> fused q|k|v integer matvec -> bias + RoPE -> q, f16 K/V store
+//   k_attn        GQA attention over the f16 KV cache, split over 64-position chunks, last CTA combines
+//   k_o_dec       quantize(attn) -> o_proj matvec -> residual add
+//   k_gateup_dec  rmsnorm + quantize -> gate|up matvec (rows interleaved per 32-block) -> SwiGLU -> quantize
+//   k_down_dec    down_proj matvec -> residual add
+// Every kernel first triggers its dependents and loads its weight slice, then waits for the previous kernel
+// (programmatic dependent launch), so weight traffic overlaps the launch gap and the previous kernel's tail.
+//
+// Prefill runs the matmul (tensor-core or CUDA-core) on whole chunks and the same elementwise helpers as the
+// decode kernels' epilogues, so batched and token-by-token give the same bits.
+#include "kernels.cuh"
+#include "layer_kernels.h"
+
+namespace qb {
+
+// ---------------------------------------------------------------- embedding (engine/src/ops_ref.cpp:162-192 get_row)
+
+__global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float* __restrict__ X, unsigned* status) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x;
+    if (t >= n_tok) return;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= E.rows) {
+        if (threadIdx.x == 0) set_error(status, ERR_BAD_TOKEN);
+        tok = 0;
+    }
+    const int dim = E.cols;
+    const int8_t* q = reinterpret_cast<const int8_t*>(E.q) + size_t(tok) * dim;
+    const __half* d = E.d + size_t(tok) * (dim / QK);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        X[size_t(t) * dim + i] = fmul(float(q[i]), __half2float(d[i / QK]));
+}
+
+// ---------------------------------------------------------------- shared epilogues
+
+// Fused q|k|v rows are stored pair-interleaved per head: fused row 2i / 2i+1 of head unit u is original row i / i+half,
+// units ordered q heads, k heads, v heads.  Applies bias, RoPE to q/k units and stores q (f32) and K/V (f16).
+__device__ __forceinline__ void qkv_pair_out(const QkvArgs& a, int fused_row, float va, float vb, int pos, float* Qt) {
+    const int hd = a.head_dim, half = hd / 2;
+    const int u = fused_row / hd, i = (fused_row - u * hd) >> 1;
+    va = fadd(va, a.bias[fused_row]);
+    vb = fadd(vb, a.bias[fused_row + 1]);
+    if (u < a.n_heads + a.n_kv) {
+        const float c = a.rope_cos[size_t(pos) * half + i], s = a.rope_sin[size_t(pos) * half + i];
+        rope_pair(va, vb, c, s);
+    }
+    if (u < a.n_heads) {
+        Qt[u * hd + i] = va;
+        Qt[u * hd + i + half] = vb;
+    } else {
+        const bool is_k = u < a.n_heads + a.n_kv;
+        const int kvh = is_k ? u - a.n_heads : u - a.n_heads - a.n_kv;
+        __half* C = (is_k ? a.kcache : a.vcache) + size_t(pos) * a.kv_dim + kvh * hd;
+        C[i] = __float2half_rn(va);
+        C[i + half] = __float2half_rn(vb);
+    }
+}
+
+// ---------------------------------------------------------------- decode kernels
+
+struct SliceSmem {
+    int8_t* sx;
+    float* sdx;
+    int* ssum;
+    float* sterm;
+    float* sval;  // row results
+    float* sred;
+};
+
+__device__ __forceinline__ SliceSmem carve(unsigned char* smem, int cols, int rows, int tstride) {
+    SliceSmem s;
+    const int nb = cols / QK;
+    s.sx = reinterpret_cast<int8_t*>(smem);
+    s.sdx = reinterpret_cast<float*>(smem + cols);
+    s.ssum = reinterpret_cast<int*>(s.sdx + nb);
+    s.sred = reinterpret_cast<float*>(s.ssum + nb);
+    s.sval = s.sred + 32;
+    s.sterm = s.sval + ((rows + 3) & ~3);
+    return s;
+}
+
+size_t slice_smem_bytes(int cols, int rows) {
+    const int nb = cols / QK;
+    return size_t(cols) + size_t(nb) * 8 + 32 * 4 + size_t((rows + 3) & ~3) * 4 + size_t(rows) * (nb | 1) * 4;
+}
+
+__device__ __forceinline__ RowSlice make_slice(const DMat& W, int dt, int row0, int nrows, unsigned magic) {
+    RowSlice S;
+    const int rb = row_bytes(dt, W.cols);
+    S.wq = W.q + size_t(row0) * rb;
+    S.wd = W.d + size_t(row0) * (W.cols / QK);
+    S.nrows = nrows;
+    S.nb = W.cols / QK;
+    S.cpr = rb / 16;
+    S.cpr_magic = magic;
+    S.tstride = term_stride(S.nb);
+    return S;
+}
+
+template <int DT, int U>
+__global__ void __launch_bounds__(kThreads) k_qkv_dec(QkvArgs a, const float* __restrict__ X, const float* __restrict__ norm_w,
+                                                      float eps, const int* __restrict__ pos_dev, float* __restrict__ Q,
+                                                      int rows_per_cta, unsigned magic) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    pdl_launch_dependents();
+    const int dim = a.W.cols;
+    const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, a.W.rows - row0);
+    SliceSmem s = carve(smem, dim, rows_per_cta, term_stride(dim / QK));
+    RowSlice S = make_slice(a.W, DT, row0, nrows, magic);
+    int pos = 0;
+    slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
+        pdl_wait();
+        pos = *pos_dev;
+        norm_quant(X, norm_w, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+    });
+    __syncthreads();
+    for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
+    __syncthreads();
+    for (int p = threadIdx.x; p < nrows / 2; p += blockDim.x)
+        qkv_pair_out(a, row0 + 2 * p, s.sval[2 * p], s.sval[2 * p + 1], pos, Q);
+}
+
+// out rows -> X[row] += value (residual).  mode 0: input is f32 attn output to quantize; mode 1: pre-quantized.
+template <int DT, int U, int MODE>
+__global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __restrict__ xin, const int8_t* __restrict__ qin,
+                                                        const float* __restrict__ din, float* __restrict__ X,
+                                                        int rows_per_cta, unsigned magic) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    pdl_launch_dependents();
+    const int cols = W.cols;
+    const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
+    SliceSmem s = carve(smem, cols, rows_per_cta, term_stride(cols / QK));
+    RowSlice S = make_slice(W, DT, row0, nrows, magic);
+    slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
+        pdl_wait();
+        if (MODE == 0) quant_only(xin, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
+        else load_quant(qin, din, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
+    });
+    __syncthreads();
+    for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+        const float v = row_sum(s.sterm + r * S.tstride, S.nb);
+        X[row0 + r] = fadd(X[row0 + r], v);
+    }
+}
+
+// gate|up rows interleaved per 32-block: fused row 64j + i = gate row 32j + i, 64j + 32 + i = up row 32j + i.
+// Each CTA owns whole ffn blocks, so it finishes SwiGLU and the block's int8 quantization itself.
+template <int DT, int U>
+__global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __restrict__ X, const float* __restrict__ norm_w,
+                                                         float eps, int8_t* __restrict__ HQ, float* __restrict__ HD,
+                                                         int blocks_per_cta, unsigned magic) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    pdl_launch_dependents();
+    const int dim = W.cols;
+    const int rows_per_cta = blocks_per_cta * 64;
+    const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
+    SliceSmem s = carve(smem, dim, rows_per_cta, term_stride(dim / QK));
+    RowSlice S = make_slice(W, DT, row0, nrows, magic);
+    slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
+        pdl_wait();
+        norm_quant(X, norm_w, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+    });
+    __syncthreads();
+    for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int jb = warp; jb < nrows / 64; jb += kWarps) {
+        const float h = swiglu1(s.sval[jb * 64 + lane], s.sval[jb * 64 + 32 + lane]);
+        float d;
+        const int8_t q = quantize_lane(h, &d);
+        const int j = row0 / 64 + jb;
+        HQ[j * QK + lane] = q;
+        if (lane == 0) HD[j] = d;
+    }
+}
+
+// ---------------------------------------------------------------- batched (prefill) elementwise kernels
+
+// One CTA per token: rmsnorm + quantize (norm_w != null) or quantize only.
+__global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __restrict__ X, const float* __restrict__ norm_w,
+                                                              int dim, float eps, int8_t* __restrict__ XQ,
+                                                              float* __restrict__ DX) {
+    __shared__ float sred[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x;
+    if (norm_w) norm_quant(X + size_t(t) * dim, norm_w, dim, eps, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr, sred);
+    else quant_only(X + size_t(t) * dim, dim, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr);
+}
+
+// R [n][fused rows] raw q|k|v -> bias + RoPE + store, token t at position pos0 + t.
+__global__ void k_qkv_epilogue(QkvArgs a, const float* __restrict__ R, int n_tok, const int* __restrict__ pos_dev,
+                               float* __restrict__ Q) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.y;
+    const int pairs = a.W.rows / 2;
+    const int pos = *pos_dev + t;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x)
+        qkv_pair_out(a, 2 * p, R[size_t(t) * a.W.rows + 2 * p], R[size_t(t) * a.W.rows + 2 * p + 1], pos,
+                     Q + size_t(t) * a.n_heads * a.head_dim);
+}
+
+__global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, long long n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        X[i] = fadd(X[i], R[i]);
+}
+
+// R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
+__global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
+                               float* __restrict__ HD) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
+    const int nbk = ffn / QK;
+    if (w >= (long long)n_tok * nbk) return;
+    const int t = int(w / nbk), j = int(w - (long long)t * nbk), lane = threadIdx.x & 31;
+    const float* r = R + size_t(t) * 2 * ffn + size_t(j) * 64;
+    const float h = swiglu1(r[lane], r[32 + lane]);
+    float d;
+    const int8_t q = quantize_lane(h, &d);
+    HQ[size_t(t) * ffn + j * QK + lane] = q;
+    if (lane == 0) HD[size_t(t) * nbk + j] = d;
+}
+
+// ---------------------------------------------------------------- attention (engine/src/model.cpp:115-137)
+
+// grid (n_kv, max_chunks, n_tok).  Query token t sits at position pos0 + t and attends to [0, pos].  Each CTA scores
+// one 64-position chunk for the `group` query heads sharing kv head g: exact sequential q.k per score, a chunk-local
+// softmax (max m, sum l) and unnormalized output o; the last CTA to finish a (token, kv head) merges the chunks in
+// chunk order.  Decode and prefill launch this same kernel, so a token's output has the same bits either way.
+constexpr int kAttnChunk = 64, kAttnHd = 64, kAttnGmax = 8;
+
+__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
+                                                   int n_tok, float* __restrict__ out) {
+    __shared__ float sq[kAttnGmax][kAttnHd];
+    __shared__ float sk[kAttnChunk][kAttnHd + 1];
+    __shared__ float sv[kAttnChunk][kAttnHd];
+    __shared__ float ss[kAttnGmax][kAttnChunk];
+    __shared__ int s_last;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int g = blockIdx.x, c = blockIdx.y, t = blockIdx.z;
+    const int pos = *pos_dev + t;
+    const int nch = pos / kAttnChunk + 1;
+    if (c >= nch) return;
+    const int group = a.n_heads / a.n_kv, hd = kAttnHd;
+    const int tb = c * kAttnChunk, len = min(kAttnChunk, pos + 1 - tb);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* q = Q + size_t(t) * a.n_heads * hd + size_t(g) * group * hd;
+    for (int i = tid; i < group * hd; i += blockDim.x) sq[i / hd][i % hd] = q[i];
+    const __half* K = a.kcache + size_t(tb) * a.kv_dim + g * hd;
+    const __half* V = a.vcache + size_t(tb) * a.kv_dim + g * hd;
+    for (int i = tid; i < len * hd / 2; i += blockDim.x) {
+        const int r = (2 * i) / hd, col = (2 * i) % hd;
+        const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(K + size_t(r) * a.kv_dim + col));
+        const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(V + size_t(r) * a.kv_dim + col));
+        sk[r][col] = kf.x;
+        sk[r][col + 1] = kf.y;
+        sv[r][col] = vf.x;
+        sv[r][col + 1] = vf.y;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < group * len; idx += blockDim.x) {
+        const int h = idx / len, tt = idx - h * len;
+        float s = 0.f;
+#pragma unroll 16
+        for (int i = 0; i < hd; ++i) s = fadd(s, fmul(sq[h][i], sk[tt][i]));
+        ss[h][tt] = fmul(s, a.scale);
+    }
+    __syncthreads();
+    float* pml = a.part_ml + (size_t(t) * a.n_heads) * a.max_chunks * 2;
+    float* po = a.part_o + (size_t(t) * a.n_heads) * a.max_chunks * hd;
+    for (int h = warp; h < group; h += kWarps) {
+        const int head = g * group + h;
+        float m = -INFINITY;
+        for (int tt = lane; tt < len; tt += 32) m = fmaxf(m, ss[h][tt]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int tt = lane; tt < len; tt += 32) {
+            const float e = expf(fsub(ss[h][tt], m));
+            ss[h][tt] = e;
+            l = fadd(l, e);
+        }
+        l = warp_sum(l);
+        __syncwarp();
+        float o0 = 0.f, o1 = 0.f;
+        for (int tt = 0; tt < len; ++tt) {
+            const float e = ss[h][tt];
+            o0 = fadd(o0, fmul(e, sv[tt][lane]));
+            o1 = fadd(o1, fmul(e, sv[tt][lane + 32]));
+        }
+        if (nch == 1) {
+            out[size_t(t) * a.n_heads * hd + head * hd + lane] = fdiv(o0, l);
+            out[size_t(t) * a.n_heads * hd + head * hd + lane + 32] = fdiv(o1, l);
+        } else {
+            if (lane == 0) {
+                pml[(size_t(head) * a.max_chunks + c) * 2] = m;
+                pml[(size_t(head) * a.max_chunks + c) * 2 + 1] = l;
+            }
+            po[(size_t(head) * a.max_chunks + c) * hd + lane] = o0;
+            po[(size_t(head) * a.max_chunks + c) * hd + lane + 32] = o1;
+        }
+    }
+    if (nch == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned* ctr = a.counters + size_t(t) * a.n_kv + g;
+        const unsigned prev = atomicAdd(ctr, 1u);
+        s_last = prev == unsigned(nch - 1);
+        if (s_last) *ctr = 0u;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int h = warp; h < group; h += kWarps) {
+        const int head = g * group + h;
+        const float* ml = pml + size_t(head) * a.max_chunks * 2;
+        float M = -INFINITY;
+        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(ml + 2 * cc));
+        float L = 0.f, O0 = 0.f, O1 = 0.f;
+        for (int cc = 0; cc < nch; ++cc) {
+            const float w = expf(fsub(__ldcg(ml + 2 * cc), M));
+            L = fadd(L, fmul(w, __ldcg(ml + 2 * cc + 1)));
+            const float* oc = po + (size_t(head) * a.max_chunks + cc) * hd;
+            O0 = fadd(O0, fmul(w, __ldcg(oc + lane)));
+            O1 = fadd(O1, fmul(w, __ldcg(oc + lane + 32)));
+        }
+        out[size_t(t) * a.n_heads * hd + head * hd + lane] = fdiv(O0, L);
+        out[size_t(t) * a.n_heads * hd + head * hd + lane + 32] = fdiv(O1, L);
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+namespace {
+
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int pick_u(int chunks) {
+    const int per = (chunks + kThreads - 1) / kThreads;
+    return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 16;
+}
+
+}  // namespace
+
+SlicePlan plan_rows(int dtype, int rows, int cols, int target_ctas, int row_multiple) {
+    SlicePlan p;
+    const int cpr = row_bytes_host(dtype, cols) / 16;
+    int rpc = (rows + target_ctas - 1) / target_ctas;
+    rpc = (rpc + row_multiple - 1) / row_multiple * row_multiple;
+    while (rpc > row_multiple && rpc * cpr > kThreads * 16) rpc -= row_multiple;
+    p.rows_per_cta = rpc;
+    p.grid = (rows + rpc - 1) / rpc;
+    p.u = pick_u(rpc * cpr);
+    p.magic = div_magic(unsigned(cpr));
+    p.smem = slice_smem_bytes(cols, rpc);
+    return p;
+}
+
+#define QB_DISPATCH_U(U, ...)                   \
+    switch (U) {                                \
+        case 1: { constexpr int UU = 1; __VA_ARGS__; break; }  \
+        case 2: { constexpr int UU = 2; __VA_ARGS__; break; }  \
+        case 4: { constexpr int UU = 4; __VA_ARGS__; break; }  \
+        case 8: { constexpr int UU = 8; __VA_ARGS__; break; }  \
+        default: { constexpr int UU = 16; __VA_ARGS__; break; } \
+    }
+
+cudaError_t launch_embed(const DMat& E, const int* tokens, int n_tok, float* X, unsigned* status, cudaStream_t st, bool pdl) {
+    return launch_pdl(k_embed, dim3(n_tok), dim3(kThreads), 0, st, pdl, E, tokens, n_tok, X, status);
+}
+
+cudaError_t launch_qkv_dec(const QkvArgs& a, const SlicePlan& p, const float* X, const float* norm_w, float eps,
+                           const int* pos_dev, float* Q, cudaStream_t st, bool pdl) {
+    cudaError_t e = cudaErrorInvalidValue;
+    if (a.W.dtype == DT_Q8_0) {
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_qkv_dec<DT_Q8_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, a, X, norm_w,
+                                          eps, pos_dev, Q, p.rows_per_cta, p.magic));
+    } else if (a.W.dtype == DT_Q4_0) {
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_qkv_dec<DT_Q4_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, a, X, norm_w,
+                                          eps, pos_dev, Q, p.rows_per_cta, p.magic));
+    }
+    return e;
+}
+
+cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin, const int8_t* qin, const float* din,
+                             float* X, cudaStream_t st, bool pdl) {
+    cudaError_t e = cudaErrorInvalidValue;
+    const bool pre = qin != nullptr;
+    if (W.dtype == DT_Q8_0) {
+        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+    } else if (W.dtype == DT_Q4_0) {
+        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+    }
+    return e;
+}
+
+cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
+                              int8_t* HQ, float* HD, cudaStream_t st, bool pdl) {
+    cudaError_t e = cudaErrorInvalidValue;
+    const int bpc = p.rows_per_cta / 64;
+    if (W.dtype == DT_Q8_0) {
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q8_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
+                                          eps, HQ, HD, bpc, p.magic));
+    } else if (W.dtype == DT_Q4_0) {
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q4_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
+                                          eps, HQ, HD, bpc, p.magic));
+    }
+    return e;
+}
+
+cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl) {
+    if (a.head_dim != kAttnHd || a.n_heads / a.n_kv > kAttnGmax) return cudaErrorInvalidValue;
+    return launch_pdl(k_attn, dim3(a.n_kv, a.max_chunks, n_tok), dim3(kThreads), 0, st, pdl, a, Q, pos_dev, n_tok, out);
+}
+
+cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
+                                   cudaStream_t st, bool pdl) {
+    return launch_pdl(k_norm_quant_rows, dim3(n_tok), dim3(kThreads), 0, st, pdl, X, norm_w, dim, eps, XQ, DX);
+}
+
+cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
+                                bool pdl) {
+    const int pairs = a.W.rows / 2;
+    return launch_pdl(k_qkv_epilogue, dim3((pairs + kThreads - 1) / kThreads, n_tok), dim3(kThreads), 0, st, pdl, a, R, n_tok,
+                      pos_dev, Q);
+}
+
+cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl) {
+    const int grid = int(std::min<long long>((n + kThreads - 1) / kThreads, 1184));
+    return launch_pdl(k_residual, dim3(grid), dim3(kThreads), 0, st, pdl, X, R, n);
+}
+
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, cudaStream_t st, bool pdl) {
+    const long long warps = (long long)n_tok * (ffn / QK);
+    return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD);
+}
+
+}  // namespace qb

@@ -1,0 +1,55 @@
+// Launchers for the per-layer kernels (layer_kernels.cu).
+#pragma once
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace qb {
+
+struct QkvArgs {
+    DMat W;                  // fused q|k|v, pair-interleaved rows
+    const float* bias;       // fused, same row order
+    const float* rope_cos;   // [ctx][head_dim/2]
+    const float* rope_sin;
+    __half* kcache;          // this layer's [ctx][kv_dim]
+    __half* vcache;
+    int n_heads, n_kv, head_dim, kv_dim;
+};
+
+struct AttnArgs {
+    const __half* kcache;    // this layer's [ctx][kv_dim]
+    const __half* vcache;
+    int n_heads, n_kv, head_dim, kv_dim;
+    float scale;             // 1/sqrt(head_dim)
+    int max_chunks;          // ceil(ctx / 64)
+    float* part_ml;          // scratch [n_tok][n_heads][max_chunks][2]
+    float* part_o;           // scratch [n_tok][n_heads][max_chunks][head_dim]
+    unsigned* counters;      // [n_tok][n_kv], zero between launches
+};
+
+struct SlicePlan {
+    int rows_per_cta = 0, grid = 0, u = 0;
+    unsigned magic = 0;
+    size_t smem = 0;
+};
+
+SlicePlan plan_rows(int dtype, int rows, int cols, int target_ctas, int row_multiple);
+
+cudaError_t launch_embed(const DMat& E, const int* tokens, int n_tok, float* X, unsigned* status, cudaStream_t st, bool pdl);
+cudaError_t launch_qkv_dec(const QkvArgs& a, const SlicePlan& p, const float* X, const float* norm_w, float eps,
+                           const int* pos_dev, float* Q, cudaStream_t st, bool pdl);
+cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin, const int8_t* qin, const float* din,
+                             float* X, cudaStream_t st, bool pdl);
+cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
+                              int8_t* HQ, float* HD, cudaStream_t st, bool pdl);
+cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl);
+cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
+                                   cudaStream_t st, bool pdl);
+cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
+                                bool pdl);
+cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl);
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, cudaStream_t st, bool pdl);
+
+}  // namespace qb

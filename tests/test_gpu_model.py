@@ -1,0 +1,118 @@
+"""Model-level parity on the GPU against the reference engine on the same synthetic .qnt files.
+
+Bars: logits within 1e-3 relative (max |diff| / max |ref logit|, as checks.cpp:97-102 scales
+errors), greedy ids identical, batched prefill equal to token-by-token (on the device: bit-identical), shortlist
+head exact rows bit-identical to the full head and its bound never violated (check_head, checks.cpp:178-239).
+"""
+import numpy as np
+import pytest
+
+import ref as R
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def rel_err(got, want):
+    return float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+
+
+@pytest.fixture(scope="module")
+def tiny(qb, models):
+    out = {}
+    for name in ("tiny_q8", "tiny_q4sl"):
+        out[name] = (qb.Model(models(name)), R.RefModel(models(name), threads=4))
+    yield out
+    for m, r in out.values():
+        m.close()
+        r.close()
+
+
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+def test_forward_logits_match_reference(tiny, name):
+    m, r = tiny[name]
+    rng = np.random.default_rng(5)
+    ids = rng.integers(0, m.vocab, 70)
+    worst = 0.0
+    for p, t in enumerate(ids):
+        got = m.forward(t, p)
+        want = r.forward(t, p)
+        worst = max(worst, rel_err(got, want))
+        assert worst < TOL, (p, worst)
+
+
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+def test_batched_prefill_equals_token_by_token(tiny, name):
+    """check_batch (checks.cpp:148-176) on the device: maxdiff must be 0, incl. a second turn at pos0 > 0."""
+    m, r = tiny[name]
+    rng = np.random.default_rng(6)
+    ids = rng.integers(0, m.vocab, 140)
+    for pos0, n in [(0, 1), (0, 31), (0, 32), (0, 33), (0, 100), (40, 45), (0, 140)]:
+        for p in range(pos0 + n):
+            lg = m.forward(ids[p], p)
+        want = lg
+        if pos0 > 0:
+            m.forward_batch(ids[:pos0], 0)
+        got = m.forward_batch(ids[pos0:pos0 + n], pos0)
+        assert np.array_equal(got, want), (pos0, n, np.abs(got - want).max())
+        ref_lg = r.forward_batch(ids[:pos0 + n], 0)
+        assert rel_err(got, ref_lg) < TOL
+
+
+@pytest.mark.parametrize("k", [1, 20])
+def test_shortlist_head_exact(tiny, k):
+    """check_head: bound holds for every row; exact rows bit-identical to the full head; top-k and must included."""
+    m, r = tiny["tiny_q4sl"]
+    assert m.has_shortlist
+    rng = np.random.default_rng(7)
+    ids = rng.integers(0, m.vocab, 30)
+    nv = m.hp.n_tokens
+    for p, t in enumerate(ids):
+        full = m.forward(t, p)
+        must = ids[max(0, p - 63):p + 1]
+        sl, coarse, upper = m.head(dict(top_k=k, n_valid=nv, must=must), want_bounds=True)
+        bound = upper - coarse
+        assert np.all(np.abs(full - coarse) <= bound)
+        exact = sl != -np.inf
+        assert np.array_equal(sl[exact], full[exact])
+        top = np.argsort(-full[:nv], kind="stable")[:k]
+        assert np.all(exact[top]) and np.all(exact[must[must < nv]])
+        assert m.last_head_rows == int(exact.sum())
+        # the reference's shortlist on the same token agrees on the chosen token and its coarse scores' bound
+        rfull = r.forward(t, p)
+        rsl, rco, rup, rows = r.head(top_k=k, n_valid=nv, must=must, want_bounds=True)
+        assert int(np.argmax(sl[:nv])) == int(np.argmax(full[:nv]))
+        assert rel_err(coarse, rco) < TOL
+
+
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+def test_greedy_ids_match_reference(tiny, name):
+    m, r = tiny[name]
+    rng = np.random.default_rng(8)
+    prompt = rng.integers(0, m.hp.n_tokens, 40)
+    sp = __import__("quanta_b200").SamplerParams(temperature=0.0, repeat_penalty=1.0)
+    got, st = m.generate(prompt, sp, 64, shortlist=True, batch_prefill=True)
+    want, _ = r.generate(prompt, 64, temperature=0.0, repeat_penalty=1.0, batch_prefill=True, shortlist=True)
+    assert len(got) == 64
+    assert np.array_equal(got, want)
+
+
+def test_sampled_shortlist_equals_full_head(tiny, qb):
+    """bench's `decode output identical (full vs shortlist)` (checks.cpp:371-373) with Qwen defaults, seed 1234."""
+    m, _ = tiny["tiny_q4sl"]
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, m.hp.n_tokens, 50)
+    sp = qb.SamplerParams(seed=1234)
+    a, sa = m.generate(prompt, sp, 48, shortlist=True)
+    b, sb = m.generate(prompt, sp, 48, shortlist=False)
+    assert np.array_equal(a, b)
+    assert sa["head_rows"] < sb["head_rows"]
+
+
+def test_bad_position_and_token(tiny):
+    m, _ = tiny["tiny_q8"]
+    with pytest.raises(Exception):
+        m.forward(1, m.hp.ctx_len)
+    with pytest.raises(Exception):
+        m.forward(m.vocab + 5, 0)
+    m.forward(1, 0)  # the handle stays usable
