@@ -147,6 +147,11 @@ int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_s
 int qnt_session_step(qnt_model* m, int n);
 int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* stats);
 
+/* Diagnostics (no reference counterpart): copies an internal buffer of the last forward as floats -- 0 roped q,
+ * 1 attention output, 2 residual x (of the last layer, before the final norm), 3 quantized SwiGLU output, 4 its block
+ * scales, 5 the head's quantized input.  Returns the element count. */
+int qnt_model_debug_buffer(qnt_model* m, int what, float* out);
+
 /* The cudaStream_t (as void*) every call on this model is queued on: lets a caller record CUDA events around
  * qnt_session_step for device timing. */
 void* qnt_model_stream(const qnt_model* m);

@@ -148,13 +148,19 @@ static void rope(float* v, int n_heads, int hd, int pos, float theta) {
     }
 }
 
+/* exp as the reference evaluates it (std::exp on float = expf).  orc_set_exp_double(1) switches to the double exp
+ * rounded once to float, to measure how much the libm's last-bit choices matter. */
+static int g_exp_double = 0;
+void orc_set_exp_double(int on) { g_exp_double = on; }
+static float ref_expf(float x) { return g_exp_double ? (float)exp((double)x) : expf(x); }
+
 /* softmax (engine/src/ops_ref.cpp:216-226). */
 static void softmax(float* x, int n) {
     float mx = x[0];
     for (int i = 1; i < n; ++i) mx = x[i] > mx ? x[i] : mx;
     float sum = 0.f;
     for (int i = 0; i < n; ++i) {
-        x[i] = expf(x[i] - mx);
+        x[i] = ref_expf(x[i] - mx);
         sum += x[i];
     }
     const float inv = 1.0f / sum;
@@ -189,6 +195,8 @@ typedef struct {
     uint16_t *kc, *vc;
     uint8_t* must_mark;
     int last_head_rows;
+    /* snapshots of the last layer of the last forward (debugging aid for the device path) */
+    float *dbg_q, *dbg_att, *dbg_x;
 } OModel;
 
 static size_t quant_bytes(const OTensor* t) {
@@ -365,6 +373,9 @@ OModel* orc_model_open(const char* path, int ctx, char* err, int errlen) {
     m->kc = calloc((size_t)m->n_layers * m->ctx * kvd, 2);
     m->vc = calloc((size_t)m->n_layers * m->ctx * kvd, 2);
     m->must_mark = calloc((size_t)V, 1);
+    m->dbg_q = calloc((size_t)qd, 4);
+    m->dbg_att = calloc((size_t)m->dim, 4);
+    m->dbg_x = calloc((size_t)m->dim, 4);
     return m;
 }
 
@@ -380,10 +391,27 @@ void orc_model_close(OModel* m) {
     free(m->kc);
     free(m->vc);
     free(m->must_mark);
+    free(m->dbg_q);
+    free(m->dbg_att);
+    free(m->dbg_x);
     free(m);
 }
 
 int orc_vocab(const OModel* m) { return m->vocab; }
+
+/* Copies a snapshot of the last forward: 0 q (roped, last layer), 1 attention output (last layer), 2 residual x before
+ * the final norm, 3 quantized swiglu of the last layer (as float), 4 its block scales, 5 the head's quantized input. */
+int orc_debug(const OModel* m, int what, float* out) {
+    switch (what) {
+        case 0: memcpy(out, m->dbg_q, sizeof(float) * (size_t)(m->n_heads * m->hd)); return m->n_heads * m->hd;
+        case 1: memcpy(out, m->dbg_att, sizeof(float) * (size_t)m->dim); return m->dim;
+        case 2: memcpy(out, m->dbg_x, sizeof(float) * (size_t)m->dim); return m->dim;
+        case 3: for (int i = 0; i < m->ffn; ++i) out[i] = m->hq[i]; return m->ffn;
+        case 4: memcpy(out, m->hd_, sizeof(float) * (size_t)(m->ffn / QK)); return m->ffn / QK;
+        case 5: for (int i = 0; i < m->dim; ++i) out[i] = m->xq[i]; return m->dim;
+    }
+    return 0;
+}
 int orc_n_tokens(const OModel* m) { return m->n_tokens; }
 int orc_last_head_rows(const OModel* m) { return m->last_head_rows; }
 
@@ -458,6 +486,8 @@ int orc_forward(OModel* m, int token, int pos, int top_k, int n_valid, const int
             vc[(size_t)pos * kvd + i] = f32_to_f16(m->v[i]);
         }
         attend(m, kc, vc, pos);
+        memcpy(m->dbg_q, m->q, sizeof(float) * (size_t)(m->n_heads * hd));
+        memcpy(m->dbg_att, m->xb, sizeof(float) * (size_t)dim);
         orc_quantize_q8(m->xb, dim, m->xq, m->xd);
         linear(m, m->xb2, L[4], m->xq, m->xd);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
@@ -467,12 +497,13 @@ int orc_forward(OModel* m, int token, int pos, int top_k, int n_valid, const int
         linear(m, m->hb2, L[10], m->xq, m->xd);
         for (int i = 0; i < m->ffn; ++i) { /* swiglu, engine/src/ops_ref.cpp:243-248 */
             const float g = m->hb[i];
-            m->hb[i] = g / (1.0f + expf(-g)) * m->hb2[i];
+            m->hb[i] = g / (1.0f + ref_expf(-g)) * m->hb2[i];
         }
         orc_quantize_q8(m->hb, m->ffn, m->hq, m->hd_);
         linear(m, m->xb2, L[11], m->hq, m->hd_);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
     }
+    memcpy(m->dbg_x, m->x, sizeof(float) * (size_t)dim);
     rmsnorm(m->x, m->x, (const float*)m->final_norm->data, dim, m->eps);
     orc_quantize_q8(m->x, dim, m->xq, m->xd);
     head(m, top_k, n_valid, must, n_must);

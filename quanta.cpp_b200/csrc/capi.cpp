@@ -322,6 +322,11 @@ int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* sta
     return r;
 }
 
+int qnt_model_debug_buffer(qnt_model* m, int what, float* out) {
+    if (!m || !out) return set_err(QNT_ERR_INVALID, "null argument");
+    return m->eng.debug_buffer(what, out);
+}
+
 void* qnt_model_stream(const qnt_model* m) { return m ? static_cast<void*>(m->eng.stream()) : nullptr; }
 
 }  // extern "C"

@@ -1,6 +1,7 @@
 #include "engine.h"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <stdexcept>
@@ -133,6 +134,9 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     if (prop.major < 10) return bad("this build needs an sm_100 (Blackwell) GPU");
     n_sm_ = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) return bad("stream create failed");
+    // Launch-mode switches for diagnosis (defaults: programmatic dependent launch on, CUDA graphs on).
+    if (const char* v = std::getenv("QNT_PDL")) pdl_ = std::atoi(v) != 0;
+    if (const char* v = std::getenv("QNT_GRAPHS")) use_graphs_ = std::atoi(v) != 0;
     try {
         const HostTensor& emb = file_.get("model.embed_tokens.weight");
         embed_ = upload_matrix(emb);
@@ -170,9 +174,17 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         cudaMemcpy(rope_cos_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(rope_sin_, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
 
+        // The host libm's expf exceptions, so device exps return the reference's bits (exp_table.cpp).
+        {
+            const std::vector<uint64_t>& slots = expf_exception_slots(&exp_note_);
+            void* p = dalloc(slots.size() * 8);
+            cudaMemcpy(p, slots.data(), slots.size() * 8, cudaMemcpyHostToDevice);
+            exptab_.slots = static_cast<const unsigned long long*>(p);
+            exptab_.mask = unsigned(slots.size() - 1);
+        }
         max_chunks_ = (ctx_ + 63) / 64;
         part_ml_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * 2 * 4));
-        part_o_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * hp_.head_dim * 4));
+        scores_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * 64 * 4));
         counters_ = static_cast<unsigned*>(dalloc(size_t(kChunk) * hp_.n_kv_heads * 4));
         cudaMemset(counters_, 0, size_t(kChunk) * hp_.n_kv_heads * 4);
 
@@ -230,8 +242,9 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
             aa.scale = 1.0f / std::sqrt(float(hp_.head_dim));
             aa.max_chunks = max_chunks_;
             aa.part_ml = part_ml_;
-            aa.part_o = part_o_;
+            aa.scores = scores_;
             aa.counters = counters_;
+            aa.exptab = exptab_;
             L.p_qkv = plan_rows(L.qkv.dtype, L.qkv.rows, L.qkv.cols, n_sm_, 2);
             L.p_o = plan_rows(L.o.dtype, L.o.rows, L.o.cols, n_sm_, 2);
             L.p_gu = plan_rows(L.gu.dtype, L.gu.rows, L.gu.cols, n_sm_, 64);
@@ -274,7 +287,8 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         hin_.dx = static_cast<float*>(dalloc(size_t(nbd) * 4));
         hin_.xsum = static_cast<int*>(dalloc(size_t(nbd) * 4));
         hin_.xnorm = static_cast<float*>(dalloc(size_t(nbd) * 4));
-        plan_head8_ = plan_head(lm_head_.dtype, V, hp_.dim);
+        n_lists_ = n_sm_;
+        plan_full_ = plan_stream(lm_head_.dtype, V, hp_.dim, n_lists_, false, false);
         logits_ = static_cast<float*>(dalloc(size_t(V) * 4));
         coarse_ = static_cast<float*>(dalloc(size_t(V) * 4));
         upper_ = static_cast<float*>(dalloc(size_t(V) * 4));
@@ -284,18 +298,16 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         cudaMemset(hs_, 0, sizeof(HeadState));
         must_ = static_cast<int*>(dalloc(size_t(ctx_ + 64) * 4));
         n_must_ = static_cast<int*>(dalloc(16));
-        coarse_ctas_ = 4 * n_sm_;
-        cand_ctas_ = 2 * n_sm_;
-        if (head_q4_) plan_head4_ = plan_head(DT_Q4_0, V, hp_.dim);
-        seed_buf_ = dalloc(size_t(coarse_ctas_) * 32 * 8);
+        if (head_q4_) {
+            plan_coarse_ = plan_stream(DT_Q4_0, V, hp_.dim, n_lists_, true, false);
+            plan_gather_ = plan_stream(DT_Q8_0, V, hp_.dim, n_lists_, false, true);
+        }
+        seed_buf_ = dalloc(size_t(n_lists_) * 32 * sizeof(Cand));
 
         ss_ = static_cast<SamplerState*>(dalloc(sizeof(SamplerState)));
         cudaMemset(ss_, 0, sizeof(SamplerState));
         hist_ = static_cast<int*>(dalloc(size_t(ctx_ + 1) * 4));
-        flag_ = static_cast<unsigned*>(dalloc(size_t(V) * 4));
-        cudaMemset(flag_, 0, size_t(V) * 4);
-        sample_parts_ = 2 * n_sm_;
-        part_buf_ = dalloc(size_t(sample_parts_) * 32 * 8);
+        part_buf_ = dalloc(size_t(n_lists_) * 32 * sizeof(Cand));
         status_ = static_cast<unsigned*>(dalloc(16));
         cudaMemset(status_, 0, 16);
         host_tmp_.resize(size_t(V));
@@ -309,6 +321,29 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
 
 size_t Engine::head_bytes_full() const {
     return size_t(lm_head_.rows) * (row_bytes_host(lm_head_.dtype, lm_head_.cols) + lm_head_.cols / QK * 2);
+}
+
+int Engine::debug_buffer(int what, float* out) {
+    cudaStreamSynchronize(st_);
+    const int dim = hp_.dim, ffn = hp_.ffn_dim;
+    std::vector<int8_t> q;
+    switch (what) {
+        case 0: cudaMemcpy(out, Q_, size_t(dim) * 4, cudaMemcpyDeviceToHost); return dim;
+        case 1: cudaMemcpy(out, ATT_, size_t(dim) * 4, cudaMemcpyDeviceToHost); return dim;
+        case 2: cudaMemcpy(out, X_, size_t(dim) * 4, cudaMemcpyDeviceToHost); return dim;
+        case 3:
+            q.resize(size_t(ffn));
+            cudaMemcpy(q.data(), HQ_, size_t(ffn), cudaMemcpyDeviceToHost);
+            for (int i = 0; i < ffn; ++i) out[i] = q[size_t(i)];
+            return ffn;
+        case 4: cudaMemcpy(out, HD_, size_t(ffn / QK) * 4, cudaMemcpyDeviceToHost); return ffn / QK;
+        case 5:
+            q.resize(size_t(dim));
+            cudaMemcpy(q.data(), hin_.xq, size_t(dim), cudaMemcpyDeviceToHost);
+            for (int i = 0; i < dim; ++i) out[i] = q[size_t(i)];
+            return dim;
+    }
+    return 0;
 }
 
 unsigned Engine::read_status() {
@@ -343,7 +378,7 @@ int Engine::launch_layers_decode(const int* pos_dev) {
         QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
         QB_TRY(launch_attn(L.aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
         QB_TRY(launch_resid_dec(L.o, L.p_o, ATT_, nullptr, nullptr, X_, st_, pdl_));
-        QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, st_, pdl_));
+        QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_));
         QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_));
     }
     return 0;
@@ -366,27 +401,36 @@ int Engine::launch_chunk(int n, const int* pos_dev) {
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
         QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
         if (int r = launch_matmul(L.gu, XQ_, DX_, n, R_)) return r;
-        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, st_, pdl_));
+        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, exptab_, st_, pdl_));
         if (int r = launch_matmul(L.down, HQ_, HD_, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
     }
     return 0;
 }
 
-int Engine::launch_head(const HeadQueryC& hq, bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev,
-                        int n_must_host, int window) {
-    (void)hq;
+int Engine::launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host,
+                        int window, int n_list, bool penal, float penalty) {
     if (!shortlist) {
-        QB_TRY(launch_head_full(lm_head_, plan_head8_, hin_, logits_, st_, pdl_));
+        if (penal) QB_TRY(launch_mark(must, n_must_dev, n_must_host, window, n_valid, mark_, st_, pdl_));
+        HeadFullArgs a;
+        a.W = lm_head_;
+        a.plan = plan_full_;
+        a.n_valid = n_valid;
+        a.n_list = n_list;
+        a.penal = penal ? 1 : 0;
+        a.penalty = penalty;
+        a.mark = mark_;
+        a.logits = logits_;
+        a.lists = part_buf_;
+        QB_TRY(launch_head_full(a, hin_, st_, pdl_));
         return 0;
     }
     ShortlistArgs a;
     a.W8 = lm_head_;
     a.W4 = head_q4_dm_;
     a.err = head_err_;
-    a.plan4 = plan_head4_;
-    a.coarse_ctas = coarse_ctas_;
-    a.cand_ctas = cand_ctas_;
+    a.plan4 = plan_coarse_;
+    a.plan8g = plan_gather_;
     a.k = k;
     a.n_valid = n_valid;
     a.must = must;
@@ -399,8 +443,13 @@ int Engine::launch_head(const HeadQueryC& hq, bool shortlist, int k, int n_valid
     a.logits = logits_;
     a.seed_buf = seed_buf_;
     a.hs = hs_;
-    QB_TRY(launch_shortlist(a, hin_, st_, pdl_));
-    kernel_count_ += 3;
+    a.n_list = n_list;
+    a.penal = penal ? 1 : 0;
+    a.penalty = penalty;
+    a.lists = part_buf_;
+    int extra = 0;
+    QB_TRY(launch_shortlist(a, hin_, st_, pdl_, &extra));
+    kernel_count_ += extra - 1;
     return 0;
 }
 
@@ -473,7 +522,7 @@ int Engine::forward(int token, int pos, const HeadQueryC* hq, float* out) {
         QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
         if (int rr = launch_layers_decode(&ss_->pos)) return rr;
         QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, hm.shortlist ? 0 : V, st_, pdl_));
-        return launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0);
+        return launch_head(hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0, 0, false, 1.f);
     });
     if (r) return r;
     if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
@@ -517,7 +566,7 @@ int Engine::forward_batch(const int* tokens, int n, int pos0, const HeadQueryC* 
     if (n_must > 0) cudaMemcpyAsync(must_, hq->must, size_t(n_must) * 4, cudaMemcpyHostToDevice, st_);
     cudaMemcpyAsync(n_must_, &n_must, 4, cudaMemcpyHostToDevice, st_);
     QB_TRY(launch_head_input(X_ + size_t(last) * hp_.dim, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, hm.shortlist ? 0 : V, st_, pdl_));
-    if (int r = launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0)) return r;
+    if (int r = launch_head(hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0, 0, false, 1.f)) return r;
     if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
     if (int rr = sync_check()) return rr;
     if (hm.shortlist) {
@@ -540,7 +589,7 @@ int Engine::head(const HeadQueryC* hq, float* out, float* coarse, float* upper) 
     const int n_must = hm.shortlist ? hq->n_must : 0;
     if (n_must > 0) cudaMemcpyAsync(must_, hq->must, size_t(n_must) * 4, cudaMemcpyHostToDevice, st_);
     cudaMemcpyAsync(n_must_, &n_must, 4, cudaMemcpyHostToDevice, st_);
-    if (int r = launch_head(HeadQueryC{}, hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0)) return r;
+    if (int r = launch_head(hm.shortlist, hm.k, hm.n_valid, must_, n_must_, 0, 0, 0, false, 1.f)) return r;
     if (out) cudaMemcpyAsync(out, logits_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
     if (hm.shortlist && coarse) cudaMemcpyAsync(coarse, coarse_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
     if (hm.shortlist && upper) cudaMemcpyAsync(upper, upper_, size_t(V) * 4, cudaMemcpyDeviceToHost, st_);
@@ -614,6 +663,9 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
         }
     }
     cudaMemcpyAsync(ss_, &st, sizeof st, cudaMemcpyHostToDevice, st_);  // forward() used token/pos
+    // sampler stage-1 lists of the prompt's logits (the decode steps get theirs from the fused head)
+    if (penal) QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, false));
+    QB_TRY(launch_topk_partial(logits_, nv, K, penal ? 1 : 0, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, false));
     if (int rr = sync_check()) return rr;
     sess_.active = true;
     sess_.steps = 0;
@@ -629,19 +681,7 @@ int Engine::session_step(int n) {
     n = std::min(n, room);
     if (n <= 0) return 0;
     const SamplerParamsC& sp = sess_.sp;
-    SamplerLaunch sl_args;
-    sl_args.logits = logits_;
-    sl_args.n_valid = sess_.nv;
-    sl_args.K = sess_.K;
-    sl_args.parts = sample_parts_;
-    sl_args.part_buf = part_buf_;
-    sl_args.args = SamplerArgs{sp.temperature, sp.top_p, sp.min_p, sp.repeat_penalty, 1};
-    sl_args.state = ss_;
-    sl_args.hist = hist_;
-    sl_args.n_hist_dev = &ss_->n_hist;
-    sl_args.hist_cap = ctx_;
-    sl_args.window = sp.repeat_window;
-    sl_args.flag = flag_;
+    const SamplerArgs sa{sp.temperature, sp.top_p, sp.min_p, sp.repeat_penalty, 1, exptab_};
     const bool sl = sess_.sl, penal = sess_.penal;
     const int K = sess_.K, nv = sess_.nv, V = hp_.vocab_size;
     const std::string key = "gen|" + std::to_string(sl) + "|" + std::to_string(K) + "|" + std::to_string(penal) + "|" +
@@ -650,14 +690,13 @@ int Engine::session_step(int n) {
     for (int s = 0; s < n; ++s) {
         const int r = run_graph(key, [&]() -> int {
             const int c0 = kernel_count_;
-            QB_TRY(launch_sampler(sl_args, st_, pdl_));
-            kernel_count_ += penal ? 2 : 1;
+            QB_TRY(launch_sample_final(part_buf_, n_lists_, K, sa, ss_, hist_, ctx_, st_, pdl_));
             QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
             if (int rr = launch_layers_decode(&ss_->pos)) return rr;
             QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, sl ? 0 : V, st_, pdl_));
             // must ids = the penalized history window (session.cpp:63-79); none without a penalty
-            const int rr = launch_head(HeadQueryC{}, sl, K, nv, penal ? hist_ : nullptr, penal ? &ss_->n_hist : nullptr, 0,
-                                       penal ? sp.repeat_window : 0);
+            const int rr = launch_head(sl, K, nv, penal ? hist_ : nullptr, penal ? &ss_->n_hist : nullptr, 0,
+                                       penal ? sp.repeat_window : 0, K, penal, sp.repeat_penalty);
             kernels_per_step_ = kernel_count_ - c0;
             return rr;
         });

@@ -90,6 +90,9 @@ public:
     int kernels_per_step() const { return kernels_per_step_; }
 
     const float* logits_dev() const { return logits_; }
+    // Copies an internal buffer of the last forward (token 0 of the chunk): 0 q, 1 attention output, 2 residual x,
+    // 3 quantized swiglu (as float), 4 its block scales, 5 the head's quantized input.  Returns the element count.
+    int debug_buffer(int what, float* out);
 
 private:
     struct Layer {
@@ -107,8 +110,10 @@ private:
     DMat upload_fused(const std::vector<const HostTensor*>& parts, int mode);
     int launch_layers_decode(const int* pos_dev);
     int launch_chunk(int n, const int* pos_dev);
-    int launch_head(const HeadQueryC& hq, bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev,
-                    int n_must_host, int window);
+    // Head pass: full or shortlist; n_list > 0 also produces the sampler's stage-1 lists (with the penalty of the
+    // marked must ids when penal).
+    int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
+                    int n_list, bool penal, float penalty);
     int launch_matmul(const DMat& W, const int8_t* xq, const float* dx, int n, float* out);
     int run_graph(const std::string& key, const std::function<int()>& body);
     int sync_check();
@@ -138,28 +143,26 @@ private:
     static constexpr int kChunk = 32;
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;
-    float *part_ml_ = nullptr, *part_o_ = nullptr;
+    float *part_ml_ = nullptr, *scores_ = nullptr;
     unsigned* counters_ = nullptr;
     int* tokens_ = nullptr;
     int* pos_ = nullptr;  // chunk start position (device)
 
     // head
     HeadIn hin_{};
-    HeadPlan plan_head8_{}, plan_head4_{};
+    StreamPlan plan_full_{}, plan_coarse_{}, plan_gather_{};
     float *logits_ = nullptr, *coarse_ = nullptr, *upper_ = nullptr;
     unsigned char* mark_ = nullptr;
     void* seed_buf_ = nullptr;
     HeadState* hs_ = nullptr;
     int* must_ = nullptr;
     int* n_must_ = nullptr;
-    int coarse_ctas_ = 0, cand_ctas_ = 0;
+    int n_lists_ = 0;  // sampler stage-1 lists (one per persistent head CTA)
 
     // sampler / session state
     SamplerState* ss_ = nullptr;
     int* hist_ = nullptr;
-    unsigned* flag_ = nullptr;
     void* part_buf_ = nullptr;
-    int sample_parts_ = 0;
     unsigned* status_ = nullptr;
 
     struct Sess {
@@ -167,6 +170,8 @@ private:
         int K = 1, nv = 0, n_prompt = 0, steps = 0;
         SamplerParamsC sp;
     } sess_;
+    ExpTab exptab_{};
+    std::string exp_note_;
     int last_head_rows_ = 0;
     int kernels_per_step_ = 0;
     int kernel_count_ = 0;  // launches issued since the last reset (counted by the launch helpers)

@@ -1,18 +1,24 @@
 // Output head and sampling on the device.
 //
 // Full head (engine/src/model.cpp:230-238): the Q8 lm_head matvec over every vocab row.
-// Exact Shortlist Head (engine/src/model.cpp:240-334), three kernels with the same semantics:
-//   k_sl_coarse  4-bit score c_r of every row (same integer matvec on quanta.head_q4), the Cauchy-Schwarz bound
-//                B_r = (sum_b err[r,b] * |x_b|) * 1.001 + 1e-5, upper_r = c_r + B_r, logits = -inf, and each CTA's
-//                best k+8 coarse scores among valid non-`must` rows;
-//   k_sl_seeds   merges those into the global k+8 seeds, rescores them exactly (Q8 rows) and takes tau = the k-th
-//                best exact seed;
-//   k_sl_cands   rescores exactly every valid row with upper >= tau that is not a seed or a must id, plus the must
-//                ids, and clears the marks.
+// Exact Shortlist Head (engine/src/model.cpp:240-334):
+//   k_sl_mark     mark[id] = 1 for the must ids (model.cpp:252-253)
+//   k_head_stream coarse mode: the 4-bit score c_r of every row (same integer matvec on quanta.head_q4), the bound
+//                 B_r = (sum_b err[r,b] * |x_b|) * 1.001 + 1e-5, upper_r = c_r + B_r, logits = -inf, and each
+//                 CTA's best k+8 coarse scores among valid non-must rows (model.cpp:259-284)
+//   k_sl_seeds    the global k+8 seeds, their exact Q8 logits, tau = the k-th best exact seed (model.cpp:293-313)
+//   k_sl_cands    exact logits of every valid row with upper >= tau that is neither seed nor must, plus the must
+//                 rows (model.cpp:315-332); clears the marks
 // Exact rows use the same block-sequential arithmetic as the full head, so their logits are bit-identical to it.
 //
-// Sampler (engine/src/sampler.cpp:22-85): repetition penalty on the history's unique ids, then greedy argmax
-// (first max) or top-k (ties to the lower id) -> temperature softmax -> min-p -> top-p -> xorshift64* draw.
+// The big passes (full head: 145 MB of Q8 rows; coarse: 77 MB of Q4 rows + 8.5 MB of bounds) stream their rows
+// through a shared-memory ring filled by cp.async (16-byte async copies, several tiles in flight per SM), one
+// persistent CTA per SM.
+//
+// Sampler (engine/src/sampler.cpp:22-85).  Stage 1 -- each CTA's best K candidates after the repetition penalty
+// (the unique history ids, marked in `mark`) -- is fused into whichever head kernel finishes the exact logits; stage 2
+// (k_sample_final) merges the lists and draws: greedy = first max, else top-k (ties to the lower id) -> softmax(T) ->
+// min-p -> top-p -> xorshift64*.
 #include <climits>
 
 #include "head_kernels.h"
@@ -20,12 +26,27 @@
 
 namespace qb {
 
-// ---------------------------------------------------------------- warp top-K lists (K <= 32)
+constexpr int kHeadThreads = 512;
+constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kStages = 4;
 
-struct Cand {
-    float v;
-    int id;
-};
+// ---------------------------------------------------------------- cp.async
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------- warp top-K lists (K <= 32)
 
 __device__ __forceinline__ bool better(float av, int aid, float bv, int bid) {
     return av > bv || (av == bv && aid < bid);
@@ -39,7 +60,7 @@ struct WarpTopK {
         v = -INFINITY;
         id = INT_MAX;
     }
-    // Offer one candidate per lane (valid lanes only); K <= 32.
+    // Offer one candidate per lane (valid lanes only); K <= 32.  Whole warp.
     __device__ void offer(float cv, int cid, bool valid, int K) {
         const int lane = threadIdx.x & 31;
         float tv = __shfl_sync(0xffffffffu, v, K - 1);
@@ -68,9 +89,10 @@ struct WarpTopK {
     }
 };
 
-// Merges the CTA's per-warp lists into warp 0's list (written to slist[0..K)).
-__device__ void cta_merge_lists(WarpTopK& L, int K, Cand* slist /* [kWarps][32] */) {
+// Merges the CTA's per-warp lists into warp 0's list, written to slist[0..32) (slist: nwarps * 32 entries).
+__device__ void cta_merge_lists(WarpTopK& L, int K, Cand* slist) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
     slist[warp * 32 + lane] = Cand{L.v, L.id};
     __syncthreads();
     if (warp == 0) {
@@ -83,19 +105,40 @@ __device__ void cta_merge_lists(WarpTopK& L, int K, Cand* slist /* [kWarps][32] 
     __syncthreads();
 }
 
+// Merges n candidates from global memory into the CTA's best K (slist[0..K)).
+__device__ void cta_merge_global(const Cand* __restrict__ src, int n, int K, Cand* slist) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    WarpTopK L;
+    L.init();
+    for (int base = warp * 32; base < n; base += blockDim.x) {
+        const int i = base + lane;
+        Cand c{-INFINITY, INT_MAX};
+        if (i < n) {
+            c.v = __ldcg(&src[i].v);
+            c.id = __ldcg(&src[i].id);
+        }
+        L.offer(c.v, c.id, i < n && c.id != INT_MAX, K);
+    }
+    cta_merge_lists(L, K, slist);
+}
+
+__device__ __forceinline__ float penalize(float l, float penalty) { return l > 0.f ? fdiv(l, penalty) : fmul(l, penalty); }
+
 // ---------------------------------------------------------------- head input
 
 // rmsnorm(x, final_norm) + quantize (engine/src/model.cpp:225-226), plus the per-block |x_b| = d_b * sqrt(sum q^2)
 // the shortlist bound needs (model.cpp:247-251; the int8 squares sum exactly in float).
 __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict__ X, const float* __restrict__ norm_w, int dim,
                                                          float eps, HeadIn hin, HeadState* hs, int full_rows) {
-    __shared__ float sred[32];
-    __shared__ int8_t sx[8192];
-    __shared__ float sdx[256];
-    __shared__ int ssum[256];
+    __shared__ float sred[32 + 2048];
+    __shared__ __align__(16) int8_t sx[2048];
+    __shared__ float sdx[64];
+    __shared__ int ssum[64];
     pdl_launch_dependents();
+    NormW nw;
+    load_norm_w(norm_w, dim, nw);
     pdl_wait();
-    norm_quant(X, norm_w, dim, eps, sx, sdx, ssum, sred);
+    norm_quant(X, nw, dim, eps, sx, sdx, ssum, sred);
     if (threadIdx.x == 0 && hs) {
         hs->rows_total += hs->calls ? hs->rows : 0;
         hs->calls += 1;
@@ -116,63 +159,154 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
     }
 }
 
-// ---------------------------------------------------------------- full head
+// Activation of the head in shared memory.
+struct HeadAct {
+    int8_t* sx;
+    float* sdx;
+    int* ssum;
+    float* sxn;
+};
 
-template <int DT, int U>
-__global__ void __launch_bounds__(kThreads) k_head_rows(DMat W, HeadIn hin, int rows_per_cta, unsigned magic,
-                                                        float* __restrict__ logits) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    pdl_launch_dependents();
-    const int cols = W.cols, nb = cols / QK;
-    int8_t* sx = reinterpret_cast<int8_t*>(smem);
-    float* sdx = reinterpret_cast<float*>(smem + cols);
-    int* ssum = reinterpret_cast<int*>(sdx + nb);
-    float* sterm = reinterpret_cast<float*>(ssum + nb);
-    const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
-    if (nrows <= 0) return;
-    RowSlice S;
-    const int rb = row_bytes(DT, cols);
-    S.wq = W.q + size_t(row0) * rb;
-    S.wd = W.d + size_t(row0) * nb;
-    S.nrows = nrows;
-    S.nb = nb;
-    S.cpr = rb / 16;
-    S.cpr_magic = magic;
-    S.tstride = term_stride(nb);
-    slice_terms<DT, U>(S, sx, sdx, ssum, sterm, [&] {
-        pdl_wait();
-        for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
-            reinterpret_cast<int4*>(sx)[i] = reinterpret_cast<const int4*>(hin.xq)[i];
-        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-            sdx[b] = hin.dx[b];
-            ssum[b] = hin.xsum[b];
-        }
-        __syncthreads();
-    });
+// Every read of data another kernel wrote goes through L2 (__ldcg): a kernel started early by programmatic dependent
+// launch may find stale lines of it in its SM's L1.
+__device__ __forceinline__ void load_head_act(const HeadIn& hin, int cols, const HeadAct& a) {
+    for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
+        reinterpret_cast<int4*>(a.sx)[i] = __ldcg(reinterpret_cast<const int4*>(hin.xq) + i);
+    for (int b = threadIdx.x; b < cols / QK; b += blockDim.x) {
+        a.sdx[b] = __ldcg(hin.dx + b);
+        a.ssum[b] = __ldcg(hin.xsum + b);
+        if (a.sxn) a.sxn[b] = __ldcg(hin.xnorm + b);
+    }
     __syncthreads();
-    for (int r = threadIdx.x; r < nrows; r += blockDim.x) logits[row0 + r] = row_sum(sterm + r * S.tstride, nb);
 }
 
-// Exact Q8 logit of one row computed by one warp, same terms and order as k_head_rows.  wterm: nb floats per warp.
-__device__ __forceinline__ float warp_exact_row(const DMat& W, int row, const int8_t* sx, const float* sdx, float* wterm) {
-    const int lane = threadIdx.x & 31, cols = W.cols, nb = cols / QK, cpr = cols / 16;
-    const uint4* src = reinterpret_cast<const uint4*>(W.q + size_t(row) * cols);
-    for (int c0 = 0; c0 < cpr; c0 += 32) {
-        const int c = c0 + lane;
-        int s = 0;
-        __half dw = __float2half(0.f);
-        if (c < cpr) {
-            s = chunk_dot<DT_Q8_0>(ld_stream(src + c), sx, c);
-            dw = W.d[size_t(row) * nb + (c >> 1)];
+// Block terms of nrows rows whose quants / scales sit contiguously in shared memory (row stride rb / nb halves).
+template <int DT>
+__device__ __forceinline__ void smem_terms(const uint8_t* sq, const __half* sd, int nrows, int cpr, unsigned cpr_magic, int nb,
+                                           int tstride, const HeadAct& a, float* sterm) {
+    const int total = nrows * cpr;
+    for (int base = 0; base < total; base += blockDim.x) {
+        const int f = base + threadIdx.x;
+        const bool ok = f < total;
+        const unsigned r = fast_div(unsigned(ok ? f : 0), cpr_magic);
+        const int c = (ok ? f : 0) - int(r) * cpr;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (ok) w = reinterpret_cast<const uint4*>(sq)[f];
+        if (DT == DT_Q8_0) {
+            int s = ok ? chunk_dot<DT>(w, a.sx, c) : 0;
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            if (ok && !(c & 1)) {
+                const int b = c >> 1;
+                sterm[int(r) * tstride + b] = block_term(s, __half2float(sd[int(r) * nb + b]), a.sdx[b]);
+            }
+        } else if (ok) {
+            const int s = chunk_dot<DT>(w, a.sx, c) - 8 * a.ssum[c];
+            sterm[int(r) * tstride + c] = block_term(s, __half2float(sd[int(r) * nb + c]), a.sdx[c]);
         }
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        if (c < cpr && !(c & 1)) wterm[c >> 1] = block_term(s, __half2float(dw), sdx[c >> 1]);
     }
-    __syncwarp();
-    float acc = 0.f;
-    if (lane == 0) acc = row_sum(wterm, nb);
-    __syncwarp();
-    return __shfl_sync(0xffffffffu, acc, 0);
+}
+
+// ---------------------------------------------------------------- streaming pass over all rows (full / coarse)
+
+// mode 0 (full head): logits = exact rows of W (Q8_0 or Q4_0); with n_list > 0 each CTA also writes its best n_list
+//   rows among [0, n_valid) after the repetition penalty of marked rows, and clears those marks.
+// mode 1 (coarse): W = quanta.head_q4; coarse / upper / logits = -inf, and each CTA's best n_list coarse scores among
+//   valid unmarked rows (the seeds).
+template <int DT, int MODE>
+__global__ void __launch_bounds__(kHeadThreads, 1) k_head_stream(DMat W, const __half* __restrict__ err, HeadIn hin,
+                                                                 StreamPlan sp, int n_valid, int n_list, int penal,
+                                                                 float penalty, unsigned char* __restrict__ mark,
+                                                                 float* __restrict__ logits, float* __restrict__ coarse,
+                                                                 float* __restrict__ upper, Cand* __restrict__ lists) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ Cand slist[kHeadWarps * 32];
+    pdl_launch_dependents();
+    const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16;
+    const int TR = sp.tile_rows, tstride = nb | 1;
+    HeadAct act;
+    act.sx = reinterpret_cast<int8_t*>(smem);
+    act.sdx = reinterpret_cast<float*>(smem + sp.act_bytes - nb * 12);
+    act.ssum = reinterpret_cast<int*>(act.sdx + nb);
+    act.sxn = reinterpret_cast<float*>(act.ssum + nb);
+    float* sterm = reinterpret_cast<float*>(smem + sp.act_bytes);
+    unsigned char* ring = smem + sp.ring_off;
+    const int ta = int((long long)blockIdx.x * sp.n_tiles / gridDim.x);
+    const int tb = int((long long)(blockIdx.x + 1) * sp.n_tiles / gridDim.x);
+
+    auto issue = [&](int t) {
+        if (t < tb) {
+            unsigned char* st = ring + size_t((t - ta) % kStages) * sp.stage_bytes;
+            const int row0 = t * TR, nrows = min(TR, W.rows - row0);
+            const uint8_t* qsrc = W.q + size_t(row0) * rb;
+            for (int c = threadIdx.x; c < nrows * cpr; c += blockDim.x) cp_async16(st + c * 16, qsrc + size_t(c) * 16);
+            const uint8_t* dsrc = reinterpret_cast<const uint8_t*>(W.d) + size_t(row0) * nb * 2;
+            const int dch = (nrows * nb * 2 + 15) / 16;  // may read up to 15 bytes of the allocation's tail padding
+            for (int c = threadIdx.x; c < dch; c += blockDim.x) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
+            if (MODE == 1) {
+                const uint8_t* esrc = reinterpret_cast<const uint8_t*>(err) + size_t(row0) * nb * 2;
+                for (int c = threadIdx.x; c < dch; c += blockDim.x) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
+            }
+        }
+        cp_commit();
+    };
+
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) issue(ta + s);
+    pdl_wait();
+    load_head_act(hin, cols, act);
+
+    WarpTopK L;
+    L.init();
+    for (int t = ta; t < tb; ++t) {
+        issue(t + kStages - 1);
+        cp_wait<kStages - 1>();
+        __syncthreads();
+        const unsigned char* st = ring + size_t((t - ta) % kStages) * sp.stage_bytes;
+        const int row0 = t * TR, nrows = min(TR, W.rows - row0);
+        smem_terms<DT>(st, reinterpret_cast<const __half*>(st + sp.d_off), nrows, cpr, sp.cpr_magic, nb, tstride, act, sterm);
+        __syncthreads();
+        for (int base = 0; base < TR; base += blockDim.x) {  // TR <= blockDim: one pass
+            const int r = base + threadIdx.x;
+            float cv = -INFINITY;
+            int row = INT_MAX;
+            bool ok = false;
+            if (r < nrows) {
+                row = row0 + r;
+                const float v = row_sum(sterm + r * tstride, nb);
+                if (MODE == 0) {
+                    logits[row] = v;
+                    cv = v;
+                    if (n_list > 0) {
+                        ok = row < n_valid;
+                        if (penal) {
+                            const unsigned char mk = __ldcg(mark + row);
+                            if (mk) {
+                                cv = penalize(v, penalty);
+                                mark[row] = 0;
+                            }
+                        }
+                    }
+                } else {
+                    const __half* e = reinterpret_cast<const __half*>(st + sp.e_off) + size_t(r) * nb;
+                    float bound = 0.f;
+                    for (int b = 0; b < nb; ++b) bound = fadd(bound, fmul(__half2float(e[b]), act.sxn[b]));
+                    bound = fadd(fmul(bound, 1.001f), 1e-5f);
+                    coarse[row] = v;
+                    upper[row] = fadd(v, bound);
+                    logits[row] = -INFINITY;
+                    cv = v;
+                    ok = row < n_valid && __ldcg(mark + row) == 0;
+                }
+            }
+            if (n_list > 0) L.offer(cv, row, ok, n_list);
+        }
+        __syncthreads();  // this stage is refilled by the next iteration's issue()
+    }
+    cp_wait<0>();
+    if (n_list > 0) {
+        cta_merge_lists(L, n_list, slist);
+        if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
+    }
 }
 
 // ---------------------------------------------------------------- shortlist head
@@ -182,211 +316,203 @@ __global__ void k_sl_mark(const int* __restrict__ must, const int* __restrict__ 
                           int n_valid, unsigned char* __restrict__ mark) {
     pdl_launch_dependents();
     pdl_wait();
-    int n = n_must_dev ? *n_must_dev : n_must_host;
+    int n = n_must_dev ? __ldcg(n_must_dev) : n_must_host;
     int from = 0;
     if (window > 0 && n > window) from = n - window;
     for (int i = from + blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const int id = must[i];
+        const int id = __ldcg(must + i);
         if (id >= 0 && id < n_valid) mark[id] = 1;
     }
 }
 
-template <int U>
-__global__ void __launch_bounds__(kThreads) k_sl_coarse(DMat W4, const __half* __restrict__ err, HeadIn hin, int rows_per_tile,
-                                                        unsigned magic, int n_valid, int n_seed,
-                                                        const unsigned char* __restrict__ mark, float* __restrict__ coarse,
-                                                        float* __restrict__ upper, float* __restrict__ logits,
-                                                        Cand* __restrict__ seed_buf) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ Cand slist[kWarps * 32];
-    pdl_launch_dependents();
-    const int cols = W4.cols, nb = cols / QK;
-    int8_t* sx = reinterpret_cast<int8_t*>(smem);
-    float* sdx = reinterpret_cast<float*>(smem + cols);
-    int* ssum = reinterpret_cast<int*>(sdx + nb);
-    float* sxn = reinterpret_cast<float*>(ssum + nb);
-    float* sterm = sxn + nb;
-    WarpTopK L;
-    L.init();
-    const int n_tiles = (W4.rows + rows_per_tile - 1) / rows_per_tile;
-    bool first = true;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int row0 = tile * rows_per_tile, nrows = min(rows_per_tile, W4.rows - row0);
-        RowSlice S;
-        const int rb = cols / 2;
-        S.wq = W4.q + size_t(row0) * rb;
-        S.wd = W4.d + size_t(row0) * nb;
-        S.nrows = nrows;
-        S.nb = nb;
-        S.cpr = rb / 16;
-        S.cpr_magic = magic;
-        S.tstride = term_stride(nb);
-        __syncthreads();  // previous tile's terms consumed
-        slice_terms<DT_Q4_0, U>(S, sx, sdx, ssum, sterm, [&] {
-            if (!first) return;
-            pdl_wait();
-            for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
-                reinterpret_cast<int4*>(sx)[i] = reinterpret_cast<const int4*>(hin.xq)[i];
-            for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-                sdx[b] = hin.dx[b];
-                ssum[b] = hin.xsum[b];
-                sxn[b] = hin.xnorm[b];
-            }
-            __syncthreads();
-        });
-        first = false;
-        __syncthreads();
-        for (int base = 0; base < nrows; base += blockDim.x) {
-            const int r = base + threadIdx.x;
-            float cv = -INFINITY;
-            int row = INT_MAX;
-            bool ok = false;
-            if (r < nrows) {
-                row = row0 + r;
-                cv = row_sum(sterm + r * S.tstride, nb);
-                const __half* e = err + size_t(row) * nb;
-                float bound = 0.f;
-                for (int b = 0; b < nb; ++b) bound = fadd(bound, fmul(__half2float(e[b]), sxn[b]));
-                bound = fadd(fmul(bound, 1.001f), 1e-5f);
-                coarse[row] = cv;
-                upper[row] = fadd(cv, bound);
-                logits[row] = -INFINITY;
-                ok = row < n_valid && mark[row] == 0;
-            }
-            L.offer(cv, row, ok, n_seed);
-        }
+// Exact Q8 logit of one row by one warp, same terms and order as the streamed full head.  wterm: nb floats.
+__device__ __forceinline__ float warp_exact_row(const DMat& W, int row, const int8_t* sx, const float* sdx, float* wterm) {
+    const int lane = threadIdx.x & 31, cols = W.cols, nb = cols / QK, cpr = cols / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(W.q + size_t(row) * cols);
+    uint4 w[8];
+    __half dw[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {  // all of this lane's loads in flight together (cols <= 4096)
+        const int c = k * 32 + lane;
+        w[k] = c < cpr ? ld_stream(src + c) : make_uint4(0, 0, 0, 0);
+        dw[k] = c < cpr ? W.d[size_t(row) * nb + (c >> 1)] : __float2half(0.f);
     }
-    if (first) pdl_wait();
-    cta_merge_lists(L, n_seed, slist);
-    if (threadIdx.x < n_seed) seed_buf[size_t(blockIdx.x) * n_seed + threadIdx.x] = slist[threadIdx.x];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int c = k * 32 + lane;
+        if (k * 32 >= cpr) break;
+        int s = c < cpr ? chunk_dot<DT_Q8_0>(w[k], sx, c) : 0;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (c < cpr && !(c & 1)) wterm[c >> 1] = block_term(s, __half2float(dw[k]), sdx[c >> 1]);
+    }
+    __syncwarp();
+    float acc = 0.f;
+    if (lane == 0) acc = row_sum(wterm, nb);
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, acc, 0);
 }
 
-// One CTA: global seeds, their exact logits, tau.
-__global__ void __launch_bounds__(kThreads) k_sl_seeds(DMat W8, HeadIn hin, const Cand* __restrict__ seed_buf, int n_lists,
-                                                       int n_seed, int k, unsigned char* __restrict__ mark,
-                                                       float* __restrict__ logits, HeadState* __restrict__ hs) {
-    __shared__ Cand slist[kWarps * 32];
-    __shared__ __align__(16) int8_t sx[8192];
-    __shared__ float sdx[256];
-    __shared__ float wterm[kWarps][256];
-    __shared__ Cand seeds[32];
+// One CTA: global seeds (the n_seed best coarse scores), their exact logits, tau.
+__global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, const Cand* __restrict__ seed_lists,
+                                                           int n_lists, int n_seed, int k, unsigned char* __restrict__ mark,
+                                                           float* __restrict__ logits, HeadState* __restrict__ hs) {
+    __shared__ Cand slist[kHeadWarps * 32];
+    __shared__ __align__(16) int8_t sx[4096];
+    __shared__ float sdx[128];
+    __shared__ float wterm[kHeadWarps][128];
     __shared__ float exact[32];
+    __shared__ int s_ns;
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cols = W8.cols, nb = cols / QK;
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
-        reinterpret_cast<int4*>(sx)[i] = reinterpret_cast<const int4*>(hin.xq)[i];
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) sdx[b] = hin.dx[b];
-    WarpTopK L;
-    L.init();
-    const int total = n_lists * n_seed;
-    for (int base = warp * 32; base < total; base += blockDim.x) {
-        const int i = base + lane;
-        Cand c{-INFINITY, INT_MAX};
-        if (i < total) c = seed_buf[i];
-        L.offer(c.v, c.id, i < total && c.id != INT_MAX, n_seed);
+        reinterpret_cast<int4*>(sx)[i] = __ldcg(reinterpret_cast<const int4*>(hin.xq) + i);
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) sdx[b] = __ldcg(hin.dx + b);
+    cta_merge_global(seed_lists, n_lists * n_seed, n_seed, slist);
+    if (threadIdx.x == 0) {
+        int n = 0;
+        while (n < n_seed && slist[n].id != INT_MAX) ++n;
+        s_ns = n;
     }
-    cta_merge_lists(L, n_seed, slist);
-    if (threadIdx.x < 32) seeds[threadIdx.x] = slist[threadIdx.x];
     __syncthreads();
-    int ns = 0;
-    while (ns < n_seed && seeds[ns].id != INT_MAX) ++ns;
-    for (int s = warp; s < ns; s += kWarps) {
-        const float v = warp_exact_row(W8, seeds[s].id, sx, sdx, wterm[warp]);
+    const int ns = s_ns;
+    for (int s = warp; s < ns; s += kHeadWarps) {
+        const int id = slist[s].id;
+        const float v = warp_exact_row(W8, id, sx, sdx, wterm[warp]);
         if (lane == 0) {
             exact[s] = v;
-            logits[seeds[s].id] = v;
-            mark[seeds[s].id] = 2;
+            logits[id] = v;
+            mark[id] = 2;
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // tau = k-th largest exact seed logit (model.cpp:308-313); insertion sort of <= 32 values, descending
-        for (int i = 1; i < ns; ++i) {
-            const float v = exact[i];
-            int j = i - 1;
-            while (j >= 0 && exact[j] < v) {
-                exact[j + 1] = exact[j];
-                --j;
-            }
-            exact[j + 1] = v;
+    // tau = the k-th largest exact seed logit (model.cpp:308-313): the seed whose rank (ties by position) is k-1.
+    if (threadIdx.x < 32) {
+        const int i = threadIdx.x;
+        bool is_kth = false;
+        if (i < ns && ns >= k) {
+            int rank = 0;
+            for (int j = 0; j < ns; ++j) rank += exact[j] > exact[i] || (exact[j] == exact[i] && j < i);
+            is_kth = rank == k - 1;
         }
-        const float tau = ns >= k ? exact[k - 1] : -INFINITY;
-        hs->tau = tau;
-        hs->rows = ns;
+        const unsigned m = __ballot_sync(0xffffffffu, is_kth);
+        if (i == 0) {
+            hs->tau = m ? exact[__ffs(m) - 1] : -INFINITY;
+            hs->rows = ns;
+        }
     }
 }
 
-// Candidate scan + exact rescoring of candidates and must ids; clears marks.  One warp per 32 rows at a time.
-__global__ void __launch_bounds__(kThreads) k_sl_cands(DMat W8, HeadIn hin, int n_valid, unsigned char* __restrict__ mark,
-                                                       const float* __restrict__ upper, float* __restrict__ logits,
-                                                       HeadState* __restrict__ hs) {
-    __shared__ __align__(16) int8_t sx[8192];
-    __shared__ float sdx[256];
-    __shared__ float wterm[kWarps][256];
-    __shared__ int scount;
+// Candidate scan over this CTA's contiguous rows, exact logits of the wanted rows (gathered through the cp.async ring),
+// optional sampler stage 1, mark clearing.
+__global__ void __launch_bounds__(kHeadThreads, 1) k_sl_cands(DMat W8, HeadIn hin, StreamPlan sp, int n_valid, int n_list,
+                                                              int penal, float penalty, unsigned char* __restrict__ mark,
+                                                              const float* __restrict__ upper, float* __restrict__ logits,
+                                                              HeadState* __restrict__ hs, Cand* __restrict__ lists) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ Cand slist[kHeadWarps * 32];
+    __shared__ int s_count;
     pdl_launch_dependents();
+    const int cols = W8.cols, nb = cols / QK, cpr = cols / 16, TR = sp.tile_rows, tstride = nb | 1;
+    HeadAct act;
+    act.sx = reinterpret_cast<int8_t*>(smem);
+    act.sdx = reinterpret_cast<float*>(smem + sp.act_bytes - nb * 12);
+    act.ssum = reinterpret_cast<int*>(act.sdx + nb);
+    act.sxn = nullptr;
+    float* sterm = reinterpret_cast<float*>(smem + sp.act_bytes);
+    int* list = reinterpret_cast<int*>(smem + sp.list_off);
+    unsigned char* ring = smem + sp.ring_off;
+    const int V = W8.rows;
+    const int r0 = int((long long)blockIdx.x * V / gridDim.x), r1 = int((long long)(blockIdx.x + 1) * V / gridDim.x);
+    if (threadIdx.x == 0) s_count = 0;
     pdl_wait();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cols = W8.cols, nb = cols / QK;
-    for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
-        reinterpret_cast<int4*>(sx)[i] = reinterpret_cast<const int4*>(hin.xq)[i];
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) sdx[b] = hin.dx[b];
-    if (threadIdx.x == 0) scount = 0;
-    __syncthreads();
-    const float tau = hs->tau;
-    int mine = 0;
-    const int nwarps_total = gridDim.x * kWarps;
-    for (int base = (blockIdx.x * kWarps + warp) * 32; base < W8.rows; base += nwarps_total * 32) {
-        const int r = base + lane;
+    load_head_act(hin, cols, act);
+    const float tau = __ldcg(&hs->tau);
+    const int lane = threadIdx.x & 31;
+    // scan + compaction (order inside the list does not affect any value)
+    for (int base = r0; base < r1; base += blockDim.x) {
+        const int r = base + threadIdx.x;
         bool want = false;
-        if (r < W8.rows) {
-            const unsigned char mk = mark[r];
-            if (r < n_valid) want = mk == 1 || (mk == 0 && upper[r] >= tau);
+        if (r < r1 && r < n_valid) {
+            const unsigned char mk = __ldcg(mark + r);
+            want = mk == 1 || (mk == 0 && __ldcg(upper + r) >= tau);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, want);
+        int off = 0;
+        if (lane == 0 && m) off = atomicAdd(&s_count, __popc(m));
+        off = __shfl_sync(0xffffffffu, off, 0);
+        if (want) list[off + __popc(m & ((1u << lane) - 1))] = r;
+    }
+    __syncthreads();
+    const int n = s_count;
+    const int n_tiles = (n + TR - 1) / TR;
+    auto issue = [&](int t) {
+        if (t < n_tiles) {
+            unsigned char* st = ring + size_t(t % kStages) * sp.stage_bytes;
+            const int nrows = min(TR, n - t * TR);
+            for (int c = threadIdx.x; c < nrows * cpr; c += blockDim.x) {
+                const int rr = c / cpr, cc = c - rr * cpr;
+                cp_async16(st + c * 16, W8.q + size_t(list[t * TR + rr]) * cols + size_t(cc) * 16);
+            }
+            const int half_pairs = nb / 2;  // fp16 scales copied 4 bytes at a time (rows are not 16-byte aligned)
+            for (int c = threadIdx.x; c < nrows * half_pairs; c += blockDim.x) {
+                const int rr = c / half_pairs, cc = c - rr * half_pairs;
+                cp_async4(st + sp.d_off + (rr * nb + 2 * cc) * 2,
+                          reinterpret_cast<const uint8_t*>(W8.d) + (size_t(list[t * TR + rr]) * nb + 2 * cc) * 2);
+            }
+        }
+        cp_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) issue(s);
+    for (int t = 0; t < n_tiles; ++t) {
+        issue(t + kStages - 1);
+        cp_wait<kStages - 1>();
+        __syncthreads();
+        const unsigned char* st = ring + size_t(t % kStages) * sp.stage_bytes;
+        const int nrows = min(TR, n - t * TR);
+        smem_terms<DT_Q8_0>(st, reinterpret_cast<const __half*>(st + sp.d_off), nrows, cpr, sp.cpr_magic, nb, tstride, act,
+                            sterm);
+        __syncthreads();
+        if (int(threadIdx.x) < nrows) logits[list[t * TR + threadIdx.x]] = row_sum(sterm + threadIdx.x * tstride, nb);
+        __syncthreads();
+    }
+    cp_wait<0>();
+    __syncthreads();
+    // sampler stage 1 over every exact row of the range (seeds, must rows, candidates), marks cleared
+    WarpTopK L;
+    L.init();
+    for (int base = r0; base < r1; base += blockDim.x) {
+        const int r = base + threadIdx.x;
+        bool ok = false;
+        float cv = -INFINITY;
+        if (r < r1) {
+            const unsigned char mk = __ldcg(mark + r);
+            if (r < n_valid && n_list > 0) {
+                ok = mk != 0 || __ldcg(upper + r) >= tau;
+                if (ok) {
+                    const float l = __ldcg(logits + r);
+                    cv = (penal && mk == 1) ? penalize(l, penalty) : l;
+                }
+            }
             if (mk) mark[r] = 0;
         }
-        unsigned m = __ballot_sync(0xffffffffu, want);
-        mine += __popc(m);
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const int row = base + src;
-            const float v = warp_exact_row(W8, row, sx, sdx, wterm[warp]);
-            if (lane == 0) logits[row] = v;
-        }
+        if (n_list > 0) L.offer(cv, ok ? r : INT_MAX, ok, n_list);
     }
-    if (lane == 0) atomicAdd(&scount, mine);
-    __syncthreads();
-    if (threadIdx.x == 0 && scount) atomicAdd(&hs->rows, scount);
+    if (n_list > 0) {
+        cta_merge_lists(L, n_list, slist);
+        if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
+    }
+    if (threadIdx.x == 0 && n) atomicAdd(&hs->rows, n);
 }
 
 // ---------------------------------------------------------------- sampler
 
-// Repetition penalty on the unique ids of history[from..n) (sampler.cpp:23-33); one CTA.  flag: V bytes, all zero.
-__global__ void k_penalty(float* __restrict__ logits, int n_valid, const int* __restrict__ hist,
-                          const int* __restrict__ n_hist_dev, int window, float penalty, unsigned* __restrict__ flag) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int n = *n_hist_dev;
-    const int from = (window > 0 && n > window) ? n - window : 0;
-    for (int i = from + threadIdx.x; i < n; i += blockDim.x) {
-        const int id = hist[i];
-        if (id < 0 || id >= n_valid) continue;
-        if (atomicExch(&flag[id], 1u) == 0u) {
-            const float l = logits[id];
-            logits[id] = l > 0.f ? fdiv(l, penalty) : fmul(l, penalty);
-        }
-    }
-    __syncthreads();
-    for (int i = from + threadIdx.x; i < n; i += blockDim.x) {
-        const int id = hist[i];
-        if (id >= 0 && id < n_valid) flag[id] = 0u;
-    }
-}
-
-// Stage 1: each CTA's best K of logits[0, n_valid).
-__global__ void __launch_bounds__(kThreads) k_topk_partial(const float* __restrict__ logits, int n_valid, int K,
+// Sampler stage 1 straight from a logits array (used once after a prefill): penalty on the unique marked ids, each
+// CTA's best K of [0, n_valid); clears the marks it used.
+__global__ void __launch_bounds__(kThreads) k_topk_partial(const float* __restrict__ logits, int n_valid, int K, int penal,
+                                                           float penalty, unsigned char* __restrict__ mark,
                                                            Cand* __restrict__ out) {
     __shared__ Cand slist[kWarps * 32];
     pdl_launch_dependents();
@@ -394,12 +520,19 @@ __global__ void __launch_bounds__(kThreads) k_topk_partial(const float* __restri
     WarpTopK L;
     L.init();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int per = (n_valid + gridDim.x - 1) / gridDim.x;
-    const int r0 = blockIdx.x * per, r1 = min(n_valid, r0 + per);
+    const int r0 = int((long long)blockIdx.x * n_valid / gridDim.x), r1 = int((long long)(blockIdx.x + 1) * n_valid / gridDim.x);
     for (int base = r0 + warp * 32; base < r1; base += blockDim.x) {
         const int r = base + lane;
         const bool ok = r < r1;
-        L.offer(ok ? logits[r] : -INFINITY, ok ? r : INT_MAX, ok, K);
+        float v = -INFINITY;
+        if (ok) {
+            v = __ldcg(logits + r);
+            if (penal && __ldcg(mark + r)) {
+                v = penalize(v, penalty);
+                mark[r] = 0;
+            }
+        }
+        L.offer(v, ok ? r : INT_MAX, ok, K);
     }
     cta_merge_lists(L, K, slist);
     if (threadIdx.x < K) out[size_t(blockIdx.x) * K + threadIdx.x] = slist[threadIdx.x];
@@ -412,25 +545,15 @@ __device__ __forceinline__ uint64_t xorshift64s(uint64_t& s) {
     return s * 0x2545F4914F6CDD1DULL;
 }
 
-// Stage 2 (one CTA): merge, then greedy pick or softmax/min-p/top-p draw; appends the token to the history and
-// advances the position.  Writes the chosen id to *token_out.
-__global__ void __launch_bounds__(kThreads) k_sample_final(const Cand* __restrict__ parts, int n_lists, int K, SamplerArgs sa,
-                                                           SamplerState* __restrict__ ss, int* __restrict__ hist,
-                                                           int hist_cap) {
-    __shared__ Cand slist[kWarps * 32];
+// Stage 2 (one CTA): merge, then greedy pick or softmax/min-p/top-p draw (sampler.cpp:35-84); appends the token to the
+// history and advances the position.
+__global__ void __launch_bounds__(kHeadThreads) k_sample_final(const Cand* __restrict__ parts, int n_lists, int K, SamplerArgs sa,
+                                                               SamplerState* __restrict__ ss, int* __restrict__ hist,
+                                                               int hist_cap) {
+    __shared__ Cand slist[kHeadWarps * 32];
     pdl_launch_dependents();
     pdl_wait();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    WarpTopK L;
-    L.init();
-    const int total = n_lists * K;
-    for (int base = warp * 32; base < total; base += blockDim.x) {
-        const int i = base + lane;
-        Cand c{-INFINITY, INT_MAX};
-        if (i < total) c = parts[i];
-        L.offer(c.v, c.id, i < total && c.id != INT_MAX, K);
-    }
-    cta_merge_lists(L, K, slist);
+    cta_merge_global(parts, n_lists * K, K, slist);
     if (threadIdx.x != 0) return;
     int n = 0;
     while (n < K && slist[n].id != INT_MAX) ++n;
@@ -440,7 +563,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_final(const Cand* __restric
         const float mx = slist[0].v;
         float sum = 0.f;
         for (int i = 0; i < n; ++i) {
-            p[i] = expf(fdiv(fsub(slist[i].v, mx), sa.temperature));
+            p[i] = exp_ref(fdiv(fsub(slist[i].v, mx), sa.temperature), sa.exptab);
             sum = fadd(sum, p[i]);
         }
         for (int i = 0; i < n; ++i) p[i] = fdiv(p[i], sum);
@@ -461,7 +584,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_final(const Cand* __restric
         }
         float total_p = 0.f;
         for (int i = 0; i < keep; ++i) total_p = fadd(total_p, p[i]);
-        uint64_t st = ss->rng;
+        uint64_t st = __ldcg(&ss->rng);
         const float u = fmul(float(xorshift64s(st) >> 40), 1.0f / 16777216.0f);
         ss->rng = st;
         float r = fmul(u, total_p);
@@ -476,7 +599,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_final(const Cand* __restric
     }
     ss->token = pick;
     if (sa.append) {
-        const int nh = ss->n_hist;
+        const int nh = __ldcg(&ss->n_hist);
         if (nh < hist_cap) {
             hist[nh] = pick;
             ss->n_hist = nh + 1;
@@ -509,68 +632,87 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+size_t align16(size_t n) { return (n + 15) & ~size_t(15); }
+
 }  // namespace
 
-HeadPlan plan_head(int dtype, int rows, int cols) {
-    HeadPlan p;
-    const int cpr = row_bytes_host(dtype, cols) / 16;
-    // ~1024 chunks (16 KB of weights) per CTA, U = 4
-    int rpc = std::max(2, (kThreads * 4) / cpr) & ~1;
-    p.rows_per_cta = rpc;
-    p.grid = (rows + rpc - 1) / rpc;
-    p.u = 4;
-    p.magic = div_magic(unsigned(cpr));
-    const int nb = cols / QK;
-    p.smem = size_t(cols) + size_t(nb) * 12 + size_t(rpc) * (nb | 1) * 4;
+StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather) {
+    StreamPlan p;
+    const int rb = row_bytes_host(dtype, cols), cpr = rb / 16, nb = cols / QK;
+    int tr = (kHeadThreads * 4) / cpr;  // ~4 chunks per thread per tile
+    tr = std::max(8, std::min(tr, kHeadThreads) / 8 * 8);
+    p.tile_rows = tr;
+    p.n_tiles = (rows + tr - 1) / tr;
+    p.cpr_magic = div_magic(unsigned(cpr));
+    p.d_off = int(align16(size_t(tr) * rb));
+    p.e_off = int(p.d_off + align16(size_t(tr) * nb * 2 + 16));
+    p.stage_bytes = int(coarse ? p.e_off + align16(size_t(tr) * nb * 2 + 16) : p.e_off);
+    p.act_bytes = int(align16(size_t(cols) + size_t(nb) * 12));
+    const size_t term_bytes = align16(size_t(tr) * (nb | 1) * 4);
+    p.list_off = int(p.act_bytes + term_bytes);
+    const size_t list_bytes = gather ? align16(size_t((rows + grid - 1) / grid + 64) * 4) : 0;
+    p.ring_off = int((p.list_off + list_bytes + 127) / 128 * 128);
+    p.smem = size_t(p.ring_off) + size_t(kStages) * p.stage_bytes;
+    p.grid = grid;
     return p;
 }
 
 cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, float eps, const HeadIn& hin, HeadState* hs,
                               int full_rows, cudaStream_t st, bool pdl) {
-    if (dim > 8192) return cudaErrorInvalidValue;
+    if (dim > 2048) return cudaErrorInvalidValue;
     return launch_pdl(k_head_input, dim3(1), dim3(kThreads), 0, st, pdl, X, norm_w, dim, eps, hin, hs, full_rows);
 }
 
-cudaError_t launch_head_full(const DMat& W, const HeadPlan& p, const HeadIn& hin, float* logits, cudaStream_t st, bool pdl) {
-    if (W.dtype == DT_Q8_0)
-        return launch_pdl(k_head_rows<DT_Q8_0, 4>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, hin, p.rows_per_cta, p.magic,
-                          logits);
-    if (W.dtype == DT_Q4_0)
-        return launch_pdl(k_head_rows<DT_Q4_0, 4>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, hin, p.rows_per_cta, p.magic,
-                          logits);
+cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl) {
+    if (a.n_list > 32) return cudaErrorInvalidValue;
+    if (a.W.dtype == DT_Q8_0)
+        return launch_pdl(k_head_stream<DT_Q8_0, 0>, dim3(a.plan.grid), dim3(kHeadThreads), a.plan.smem, st, pdl, a.W,
+                          (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
+                          (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
+    if (a.W.dtype == DT_Q4_0)
+        return launch_pdl(k_head_stream<DT_Q4_0, 0>, dim3(a.plan.grid), dim3(kHeadThreads), a.plan.smem, st, pdl, a.W,
+                          (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
+                          (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl) {
+cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl, int* kernels) {
     const int n_seed = a.k + 8;
-    if (a.k < 1 || n_seed > 32 || a.W8.cols > 8192) return cudaErrorInvalidValue;
+    if (a.k < 1 || n_seed > 32 || a.W8.cols > 4096 || a.n_list > 32) return cudaErrorInvalidValue;
     cudaError_t e = launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, a.must, a.n_must_dev, a.n_must_host, a.window,
                                a.n_valid, a.mark);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_sl_coarse<4>, dim3(a.coarse_ctas), dim3(kThreads), a.plan4.smem, st, pdl, a.W4, a.err, hin,
-                   a.plan4.rows_per_cta, a.plan4.magic, a.n_valid, n_seed, (const unsigned char*)a.mark, a.coarse, a.upper,
-                   a.logits, reinterpret_cast<Cand*>(a.seed_buf));
+    e = launch_pdl(k_head_stream<DT_Q4_0, 1>, dim3(a.plan4.grid), dim3(kHeadThreads), a.plan4.smem, st, pdl, a.W4, a.err, hin,
+                   a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark, a.logits, a.coarse, a.upper,
+                   reinterpret_cast<Cand*>(a.seed_buf));
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_sl_seeds, dim3(1), dim3(kThreads), 0, st, pdl, a.W8, hin, (const Cand*)reinterpret_cast<Cand*>(a.seed_buf),
-                   a.coarse_ctas, n_seed, a.k, a.mark, a.logits, a.hs);
+    e = launch_pdl(k_sl_seeds, dim3(1), dim3(kHeadThreads), 0, st, pdl, a.W8, hin, (const Cand*)a.seed_buf, a.plan4.grid,
+                   n_seed, a.k, a.mark, a.logits, a.hs);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_sl_cands, dim3(a.cand_ctas), dim3(kThreads), 0, st, pdl, a.W8, hin, a.n_valid, a.mark,
-                      (const float*)a.upper, a.logits, a.hs);
+    e = launch_pdl(k_sl_cands, dim3(a.plan8g.grid), dim3(kHeadThreads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
+                   a.n_list, a.penal, a.penalty, a.mark, (const float*)a.upper, a.logits, a.hs,
+                   reinterpret_cast<Cand*>(a.lists));
+    if (kernels) *kernels += 4;
+    return e;
 }
 
-cudaError_t launch_sampler(const SamplerLaunch& s, cudaStream_t st, bool pdl) {
-    if (s.K < 1 || s.K > 32) return cudaErrorInvalidValue;
-    cudaError_t e;
-    if (s.args.repeat_penalty != 1.0f) {
-        e = launch_pdl(k_penalty, dim3(1), dim3(1024), 0, st, pdl, s.logits, s.n_valid, (const int*)s.hist,
-                       (const int*)s.n_hist_dev, s.window, s.args.repeat_penalty, s.flag);
-        if (e != cudaSuccess) return e;
-    }
-    e = launch_pdl(k_topk_partial, dim3(s.parts), dim3(kThreads), 0, st, pdl, (const float*)s.logits, s.n_valid, s.K,
-                   reinterpret_cast<Cand*>(s.part_buf));
-    if (e != cudaSuccess) return e;
-    return launch_pdl(k_sample_final, dim3(1), dim3(kThreads), 0, st, pdl, (const Cand*)reinterpret_cast<Cand*>(s.part_buf),
-                      s.parts, s.K, s.args, s.state, s.hist, s.hist_cap);
+cudaError_t launch_mark(const int* must, const int* n_must_dev, int n_must_host, int window, int n_valid, unsigned char* mark,
+                        cudaStream_t st, bool pdl) {
+    return launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, must, n_must_dev, n_must_host, window, n_valid, mark);
+}
+
+cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int penal, float penalty, unsigned char* mark,
+                                void* lists, int n_lists, cudaStream_t st, bool pdl) {
+    if (K < 1 || K > 32) return cudaErrorInvalidValue;
+    return launch_pdl(k_topk_partial, dim3(n_lists), dim3(kThreads), 0, st, pdl, logits, n_valid, K, penal, penalty, mark,
+                      reinterpret_cast<Cand*>(lists));
+}
+
+cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
+                                int hist_cap, cudaStream_t st, bool pdl) {
+    if (K < 1 || K > 32) return cudaErrorInvalidValue;
+    return launch_pdl(k_sample_final, dim3(1), dim3(kHeadThreads), 0, st, pdl, reinterpret_cast<const Cand*>(lists), n_lists,
+                      K, sa, ss, hist, hist_cap);
 }
 
 }  // namespace qb

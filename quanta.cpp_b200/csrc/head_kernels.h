@@ -4,9 +4,15 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "exp_table.h"
 #include "ops.h"
 
 namespace qb {
+
+struct Cand {
+    float v;
+    int id;
+};
 
 // Quantized final hidden state the head reads (written by k_head_input).
 struct HeadIn {
@@ -24,20 +30,37 @@ struct HeadState {
     int pad;
 };
 
-struct HeadPlan {
-    int rows_per_cta = 0, grid = 0, u = 0;
-    unsigned magic = 0;
+// Tiling of a streamed head pass (rows in tiles of tile_rows, tiles split over `grid` persistent CTAs, each tile staged
+// in a shared-memory ring slot of stage_bytes: quants at 0, scales at d_off, bounds at e_off).
+struct StreamPlan {
+    int tile_rows = 0, n_tiles = 0;
+    unsigned cpr_magic = 0;
+    int d_off = 0, e_off = 0, stage_bytes = 0;
+    int act_bytes = 0, list_off = 0, ring_off = 0;
     size_t smem = 0;
+    int grid = 0;
 };
-HeadPlan plan_head(int dtype, int rows, int cols);
+// coarse: stage the bounds too; gather: room for the CTA's compacted row list.
+StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather);
+
+struct HeadFullArgs {
+    DMat W;
+    StreamPlan plan;
+    int n_valid;
+    int n_list;         // sampler stage-1 list length per CTA (0: logits only)
+    int penal;          // apply the repetition penalty to marked rows (and clear the marks)
+    float penalty;
+    unsigned char* mark;
+    float* logits;
+    void* lists;        // plan.grid * n_list candidates
+};
 
 struct ShortlistArgs {
     DMat W8;                // lm_head (Q8_0)
     DMat W4;                // quanta.head_q4
     const __half* err;      // quanta.head_err [V][dim/32]
-    HeadPlan plan4;         // tiles of W4
-    int coarse_ctas;        // persistent CTAs of the coarse pass (lists merged by the seed kernel)
-    int cand_ctas;
+    StreamPlan plan4;       // streamed coarse pass over W4
+    StreamPlan plan8g;      // candidate gather over W8
     int k, n_valid;
     const int* must;        // must ids (device)
     const int* n_must_dev;  // device count (or null: n_must_host)
@@ -47,13 +70,18 @@ struct ShortlistArgs {
     float* coarse;          // [V]
     float* upper;           // [V]
     float* logits;          // [V]
-    void* seed_buf;         // coarse_ctas * (k + 8) candidates
+    void* seed_buf;         // plan4.grid * (k + 8) candidates
     HeadState* hs;
+    int n_list;             // sampler stage-1 list length (0: none)
+    int penal;
+    float penalty;
+    void* lists;            // plan8g.grid * n_list candidates
 };
 
 struct SamplerArgs {
     float temperature, top_p, min_p, repeat_penalty;
     int append;  // 1: append the pick to the history and advance the position
+    ExpTab exptab;
 };
 
 struct SamplerState {
@@ -64,26 +92,17 @@ struct SamplerState {
     int pad;
 };
 
-struct SamplerLaunch {
-    float* logits;
-    int n_valid;
-    int K;             // 1 = greedy
-    int parts;         // stage-1 CTAs
-    void* part_buf;    // parts * K candidates
-    SamplerArgs args;
-    SamplerState* state;
-    int* hist;
-    const int* n_hist_dev;
-    int hist_cap;
-    int window;
-    unsigned* flag;    // [V] zero between calls
-};
-
 // full_rows: rows the coming head pass reads when it is the full head (V), 0 for the shortlist (which counts itself).
 cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, float eps, const HeadIn& hin, HeadState* hs,
                               int full_rows, cudaStream_t st, bool pdl);
-cudaError_t launch_head_full(const DMat& W, const HeadPlan& p, const HeadIn& hin, float* logits, cudaStream_t st, bool pdl);
-cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl);
-cudaError_t launch_sampler(const SamplerLaunch& s, cudaStream_t st, bool pdl);
+cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl);
+// Launches 4 kernels (mark, coarse, seeds, candidates); adds 4 to *kernels.
+cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl, int* kernels);
+cudaError_t launch_mark(const int* must, const int* n_must_dev, int n_must_host, int window, int n_valid, unsigned char* mark,
+                        cudaStream_t st, bool pdl);
+cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int penal, float penalty, unsigned char* mark,
+                                void* lists, int n_lists, cudaStream_t st, bool pdl);
+cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
+                                int hist_cap, cudaStream_t st, bool pdl);
 
 }  // namespace qb

@@ -3,6 +3,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exp_table.h"
 
 namespace qb {
 
@@ -139,50 +140,89 @@ __device__ __forceinline__ float row_sum(const float* t, int nb) {
 }
 
 // ---- activation prologues (one token; every thread of the CTA participates)
+//
+// Element i of an activation belongs to thread i % blockDim in "round" i / blockDim; with blockDim a multiple of 32
+// warp w of round k holds exactly block w + k * nwarps, so each block is quantized by one warp.  All of a thread's
+// loads are issued before any dependent math (a decode step is a chain of these prologues).
+constexpr int kMaxRounds = 8;  // vectors up to kMaxRounds * blockDim elements take the register path
+
+// Norm weights in registers (constant: loaded before the programmatic-launch wait).
+struct NormW {
+    float w[kMaxRounds];
+};
+__device__ __forceinline__ void load_norm_w(const float* __restrict__ w, int dim, NormW& nw) {
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k) {
+        const int i = threadIdx.x + k * blockDim.x;
+        nw.w[k] = i < dim ? w[i] : 0.f;
+    }
+}
+
+// quantize one round's element (whole warp participates when the round is valid for the warp).
+__device__ __forceinline__ void quant_round(float v, int i, int8_t* sx, float* sdx, int* ssum) {
+    const int lane = threadIdx.x & 31;
+    float d;
+    const int8_t q = quantize_lane(v, &d);
+    sx[i] = q;
+    if (ssum) {
+        const int s = warp_sum_i(int(q));
+        if (lane == 0) ssum[i / QK] = s;
+    }
+    if (lane == 0) sdx[i / QK] = d;
+}
+
+// Sum of squares in element order, ((x0*x0 + x1*x1) + x2*x2) + ..., the reference's sequential loop
+// (engine/src/ops_ref.cpp:195-196): the squares are formed in parallel into sq[], one thread runs the add chain.
+// Any other order changes the last bits of the scale, and those flip int8 activations and f16 cache entries
+// downstream, so this order is kept although the chain costs ~4 cycles per element.
+__device__ __forceinline__ float sumsq_in_order(const float* sq, int n) {
+    float s = 0.f;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = sq[i + k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = fadd(s, v[k]);
+    }
+    for (; i < n; ++i) s = fadd(s, sq[i]);
+    return s;
+}
 
 // rmsnorm (engine/src/ops_ref.cpp:194-199) then quantize_q8 (:69-83) of x[dim] into sx / sdx (and block sums).
-// The sum of squares uses a fixed tree order (per-thread strided partials, warp butterfly, then warps in order),
-// so every kernel that normalizes the same vector gets the same bits.
-__device__ __forceinline__ void norm_quant(const float* __restrict__ x, const float* __restrict__ w, int dim, float eps,
-                                           int8_t* sx, float* sdx, int* ssum, float* sred) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    float ss = 0.f;
-    for (int i = tid; i < dim; i += blockDim.x) ss = fadd(ss, fmul(x[i], x[i]));
-    ss = warp_sum(ss);
-    if (lane == 0) sred[warp] = ss;
+// sred: scratch of >= dim + 32 floats.  Bit-identical to the reference.  dim <= kMaxRounds * blockDim.
+__device__ __forceinline__ void norm_quant(const float* __restrict__ x, const NormW& nw, int dim, float eps, int8_t* sx,
+                                           float* sdx, int* ssum, float* sred) {
+    const int tid = threadIdx.x, warp = tid >> 5, T = blockDim.x;
+    float xv[kMaxRounds];
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < dim ? __ldcg(x + tid + k * T) : 0.f;
+    float* sq = sred + 32;
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k)
+        if (tid + k * T < dim) sq[tid + k * T] = fmul(xv[k], xv[k]);
     __syncthreads();
-    float tot = 0.f;
-    for (int k = 0; k < nw; ++k) tot = fadd(tot, sred[k]);
+    if (tid == 0) sred[0] = sumsq_in_order(sq, dim);
+    __syncthreads();
+    const float tot = sred[0];
     const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(tot, float(dim)), eps)));
-    for (int b = warp; b < dim / QK; b += nw) {
-        const int i = b * QK + lane;
-        const float v = fmul(fmul(x[i], scale), w[i]);
-        float d;
-        const int8_t q = quantize_lane(v, &d);
-        sx[i] = q;
-        if (ssum) {
-            const int s = warp_sum_i(int(q));
-            if (lane == 0) ssum[b] = s;
-        }
-        if (lane == 0) sdx[b] = d;
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k) {
+        const int i = tid + k * T;
+        if (k * T + warp * 32 < dim) quant_round(fmul(fmul(xv[k], scale), nw.w[k]), i, sx, sdx, ssum);
     }
     __syncthreads();
 }
 
-// quantize_q8 of x[n] (no norm) into sx / sdx (and block sums).
+// quantize_q8 of x[n] (no norm) into sx / sdx (and block sums); n <= kMaxRounds * blockDim.
 __device__ __forceinline__ void quant_only(const float* __restrict__ x, int n, int8_t* sx, float* sdx, int* ssum) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int b = warp; b < n / QK; b += nw) {
-        const int i = b * QK + lane;
-        float d;
-        const int8_t q = quantize_lane(x[i], &d);
-        sx[i] = q;
-        if (ssum) {
-            const int s = warp_sum_i(int(q));
-            if (lane == 0) ssum[b] = s;
-        }
-        if (lane == 0) sdx[b] = d;
-    }
+    const int tid = threadIdx.x, warp = tid >> 5, T = blockDim.x;
+    float xv[kMaxRounds];
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < n ? __ldcg(x + tid + k * T) : 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k)
+        if (k * T + warp * 32 < n) quant_round(xv[k], tid + k * T, sx, sdx, ssum);
     __syncthreads();
 }
 
@@ -191,8 +231,27 @@ __device__ __forceinline__ void load_quant(const int8_t* __restrict__ q, const f
                                            float* sdx, int* ssum) {
     const int4* src = reinterpret_cast<const int4*>(q);
     int4* dst = reinterpret_cast<int4*>(sx);
-    for (int i = threadIdx.x; i < n / 16; i += blockDim.x) dst[i] = src[i];
-    for (int b = threadIdx.x; b < n / QK; b += blockDim.x) sdx[b] = d[b];
+    const int T = blockDim.x;
+    int4 v[4];
+    float dv[2];
+    for (int base = 0; base < n / 16; base += 4 * T) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = base + threadIdx.x + k * T;
+            if (i < n / 16) v[k] = __ldcg(src + i);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = base + threadIdx.x + k * T;
+            if (i < n / 16) dst[i] = v[k];
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) dv[k] = threadIdx.x + k * T < n / QK ? __ldcg(d + threadIdx.x + k * T) : 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+        if (threadIdx.x + k * T < n / QK) sdx[threadIdx.x + k * T] = dv[k];
+    for (int b = threadIdx.x + 2 * T; b < n / QK; b += T) sdx[b] = __ldcg(d + b);
     __syncthreads();
     if (ssum) {
         block_sums_i8(sx, n, ssum);
@@ -210,7 +269,9 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) 
     b = nb;
 }
 
-// silu(g) * u (engine/src/ops_ref.cpp:243-248).
-__device__ __forceinline__ float swiglu1(float g, float u) { return fmul(fdiv(g, fadd(1.0f, expf(-g))), u); }
+// silu(g) * u (engine/src/ops_ref.cpp:243-248), e^-g with the host libm's bits (exp_table.h).
+__device__ __forceinline__ float swiglu1(float g, float u, const ExpTab& tab) {
+    return fmul(fdiv(g, fadd(1.0f, exp_ref(-g, tab))), u);
+}
 
 }  // namespace qb

@@ -8,6 +8,9 @@
 //   k_down_dec    down_proj matvec -> residual add
 // Every kernel first triggers its dependents and loads its weight slice, then waits for the previous kernel
 // (programmatic dependent launch), so weight traffic overlaps the launch gap and the previous kernel's tail.
+// A kernel launched early this way may run on an SM whose L1 still holds lines that earlier kernels of the chain
+// have since rewritten (L1 is not coherent, and the wait does not invalidate it), so every read of data produced by
+// another kernel goes through L2 (__ldcg / ld.global.cg); only constant weights use L1 or the non-coherent path.
 //
 // Prefill runs the matmul (tensor-core or CUDA-core) on whole chunks and the same elementwise helpers as the
 // decode kernels' epilogues, so batched and token-by-token give the same bits.
@@ -23,7 +26,7 @@ __global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float
     pdl_wait();
     const int t = blockIdx.x;
     if (t >= n_tok) return;
-    int tok = tokens[t];
+    int tok = __ldcg(tokens + t);
     if (tok < 0 || tok >= E.rows) {
         if (threadIdx.x == 0) set_error(status, ERR_BAD_TOKEN);
         tok = 0;
@@ -39,15 +42,32 @@ __global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float
 
 // Fused q|k|v rows are stored pair-interleaved per head: fused row 2i / 2i+1 of head unit u is original row i / i+half,
 // units ordered q heads, k heads, v heads.  Applies bias, RoPE to q/k units and stores q (f32) and K/V (f16).
-__device__ __forceinline__ void qkv_pair_out(const QkvArgs& a, int fused_row, float va, float vb, int pos, float* Qt) {
+struct PairIn {
+    float ba, bb;  // bias of the two rows
+    float c, s;    // RoPE cos / sin at (pos, i)
+};
+
+__device__ __forceinline__ void pair_bias(const QkvArgs& a, int fused_row, PairIn& p) {
+    p.ba = a.bias[fused_row];
+    p.bb = a.bias[fused_row + 1];
+}
+__device__ __forceinline__ void pair_rope(const QkvArgs& a, int fused_row, int pos, PairIn& p) {
+    const int hd = a.head_dim, half = hd / 2, u = fused_row / hd, i = (fused_row - u * hd) >> 1;
+    p.c = 1.f;
+    p.s = 0.f;
+    if (u < a.n_heads + a.n_kv) {
+        p.c = a.rope_cos[size_t(pos) * half + i];
+        p.s = a.rope_sin[size_t(pos) * half + i];
+    }
+}
+
+__device__ __forceinline__ void qkv_pair_store(const QkvArgs& a, int fused_row, float va, float vb, int pos, const PairIn& p,
+                                               float* Qt) {
     const int hd = a.head_dim, half = hd / 2;
     const int u = fused_row / hd, i = (fused_row - u * hd) >> 1;
-    va = fadd(va, a.bias[fused_row]);
-    vb = fadd(vb, a.bias[fused_row + 1]);
-    if (u < a.n_heads + a.n_kv) {
-        const float c = a.rope_cos[size_t(pos) * half + i], s = a.rope_sin[size_t(pos) * half + i];
-        rope_pair(va, vb, c, s);
-    }
+    va = fadd(va, p.ba);
+    vb = fadd(vb, p.bb);
+    if (u < a.n_heads + a.n_kv) rope_pair(va, vb, p.c, p.s);
     if (u < a.n_heads) {
         Qt[u * hd + i] = va;
         Qt[u * hd + i + half] = vb;
@@ -58,6 +78,13 @@ __device__ __forceinline__ void qkv_pair_out(const QkvArgs& a, int fused_row, fl
         C[i] = __float2half_rn(va);
         C[i + half] = __float2half_rn(vb);
     }
+}
+
+__device__ __forceinline__ void qkv_pair_out(const QkvArgs& a, int fused_row, float va, float vb, int pos, float* Qt) {
+    PairIn p;
+    pair_bias(a, fused_row, p);
+    pair_rope(a, fused_row, pos, p);
+    qkv_pair_store(a, fused_row, va, vb, pos, p, Qt);
 }
 
 // ---------------------------------------------------------------- decode kernels
@@ -77,15 +104,15 @@ __device__ __forceinline__ SliceSmem carve(unsigned char* smem, int cols, int ro
     s.sx = reinterpret_cast<int8_t*>(smem);
     s.sdx = reinterpret_cast<float*>(smem + cols);
     s.ssum = reinterpret_cast<int*>(s.sdx + nb);
-    s.sred = reinterpret_cast<float*>(s.ssum + nb);
-    s.sval = s.sred + 32;
+    s.sred = reinterpret_cast<float*>(s.ssum + nb);  // 32 + cols floats (norm_quant's squares)
+    s.sval = s.sred + 32 + cols;
     s.sterm = s.sval + ((rows + 3) & ~3);
     return s;
 }
 
 size_t slice_smem_bytes(int cols, int rows) {
     const int nb = cols / QK;
-    return size_t(cols) + size_t(nb) * 8 + 32 * 4 + size_t((rows + 3) & ~3) * 4 + size_t(rows) * (nb | 1) * 4;
+    return size_t(cols) + size_t(nb) * 8 + size_t(32 + cols) * 4 + size_t((rows + 3) & ~3) * 4 + size_t(rows) * (nb | 1) * 4;
 }
 
 __device__ __forceinline__ RowSlice make_slice(const DMat& W, int dt, int row0, int nrows, unsigned magic) {
@@ -111,17 +138,23 @@ __global__ void __launch_bounds__(kThreads) k_qkv_dec(QkvArgs a, const float* __
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, a.W.rows - row0);
     SliceSmem s = carve(smem, dim, rows_per_cta, term_stride(dim / QK));
     RowSlice S = make_slice(a.W, DT, row0, nrows, magic);
+    NormW nw;
+    load_norm_w(norm_w, dim, nw);
+    const bool has_pair = int(threadIdx.x) < nrows / 2;  // one pair per thread (rows_per_cta <= 2 * blockDim)
+    const int pr = row0 + 2 * threadIdx.x;
+    PairIn pin{0.f, 0.f, 1.f, 0.f};
+    if (has_pair) pair_bias(a, pr, pin);
     int pos = 0;
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
-        pos = *pos_dev;
-        norm_quant(X, norm_w, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+        pos = __ldcg(pos_dev);
+        if (has_pair) pair_rope(a, pr, pos, pin);
+        norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
     });
     __syncthreads();
     for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
     __syncthreads();
-    for (int p = threadIdx.x; p < nrows / 2; p += blockDim.x)
-        qkv_pair_out(a, row0 + 2 * p, s.sval[2 * p], s.sval[2 * p + 1], pos, Q);
+    if (has_pair) qkv_pair_store(a, pr, s.sval[2 * threadIdx.x], s.sval[2 * threadIdx.x + 1], pos, pin, Q);
 }
 
 // out rows -> X[row] += value (residual).  mode 0: input is f32 attn output to quantize; mode 1: pre-quantized.
@@ -135,16 +168,15 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
     SliceSmem s = carve(smem, cols, rows_per_cta, term_stride(cols / QK));
     RowSlice S = make_slice(W, DT, row0, nrows, magic);
+    float xres = 0.f;  // this thread's residual row (rows_per_cta <= blockDim)
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
+        if (int(threadIdx.x) < nrows) xres = __ldcg(X + row0 + threadIdx.x);
         if (MODE == 0) quant_only(xin, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
         else load_quant(qin, din, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
     });
     __syncthreads();
-    for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
-        const float v = row_sum(s.sterm + r * S.tstride, S.nb);
-        X[row0 + r] = fadd(X[row0 + r], v);
-    }
+    if (int(threadIdx.x) < nrows) X[row0 + threadIdx.x] = fadd(xres, row_sum(s.sterm + threadIdx.x * S.tstride, S.nb));
 }
 
 // gate|up rows interleaved per 32-block: fused row 64j + i = gate row 32j + i, 64j + 32 + i = up row 32j + i.
@@ -152,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
 template <int DT, int U>
 __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __restrict__ X, const float* __restrict__ norm_w,
                                                          float eps, int8_t* __restrict__ HQ, float* __restrict__ HD,
-                                                         int blocks_per_cta, unsigned magic) {
+                                                         int blocks_per_cta, unsigned magic, ExpTab tab) {
     extern __shared__ __align__(16) unsigned char smem[];
     pdl_launch_dependents();
     const int dim = W.cols;
@@ -160,16 +192,18 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
     SliceSmem s = carve(smem, dim, rows_per_cta, term_stride(dim / QK));
     RowSlice S = make_slice(W, DT, row0, nrows, magic);
+    NormW nw;
+    load_norm_w(norm_w, dim, nw);
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
-        norm_quant(X, norm_w, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+        norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
     });
     __syncthreads();
     for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int jb = warp; jb < nrows / 64; jb += kWarps) {
-        const float h = swiglu1(s.sval[jb * 64 + lane], s.sval[jb * 64 + 32 + lane]);
+        const float h = swiglu1(s.sval[jb * 64 + lane], s.sval[jb * 64 + 32 + lane], tab);
         float d;
         const int8_t q = quantize_lane(h, &d);
         const int j = row0 / 64 + jb;
@@ -184,11 +218,13 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
 __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __restrict__ X, const float* __restrict__ norm_w,
                                                               int dim, float eps, int8_t* __restrict__ XQ,
                                                               float* __restrict__ DX) {
-    __shared__ float sred[32];
+    __shared__ float sred[32 + 2048];
     pdl_launch_dependents();
+    NormW nw;
+    if (norm_w) load_norm_w(norm_w, dim, nw);
     pdl_wait();
     const int t = blockIdx.x;
-    if (norm_w) norm_quant(X + size_t(t) * dim, norm_w, dim, eps, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr, sred);
+    if (norm_w) norm_quant(X + size_t(t) * dim, nw, dim, eps, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr, sred);
     else quant_only(X + size_t(t) * dim, dim, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr);
 }
 
@@ -199,9 +235,9 @@ __global__ void k_qkv_epilogue(QkvArgs a, const float* __restrict__ R, int n_tok
     pdl_wait();
     const int t = blockIdx.y;
     const int pairs = a.W.rows / 2;
-    const int pos = *pos_dev + t;
+    const int pos = __ldcg(pos_dev) + t;
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x)
-        qkv_pair_out(a, 2 * p, R[size_t(t) * a.W.rows + 2 * p], R[size_t(t) * a.W.rows + 2 * p + 1], pos,
+        qkv_pair_out(a, 2 * p, __ldcg(R + size_t(t) * a.W.rows + 2 * p), __ldcg(R + size_t(t) * a.W.rows + 2 * p + 1), pos,
                      Q + size_t(t) * a.n_heads * a.head_dim);
 }
 
@@ -209,12 +245,12 @@ __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, l
     pdl_launch_dependents();
     pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        X[i] = fadd(X[i], R[i]);
+        X[i] = fadd(__ldcg(X + i), __ldcg(R + i));
 }
 
 // R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
 __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
-                               float* __restrict__ HD) {
+                               float* __restrict__ HD, ExpTab tab) {
     pdl_launch_dependents();
     pdl_wait();
     const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
@@ -222,7 +258,7 @@ __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, 
     if (w >= (long long)n_tok * nbk) return;
     const int t = int(w / nbk), j = int(w - (long long)t * nbk), lane = threadIdx.x & 31;
     const float* r = R + size_t(t) * 2 * ffn + size_t(j) * 64;
-    const float h = swiglu1(r[lane], r[32 + lane]);
+    const float h = swiglu1(__ldcg(r + lane), __ldcg(r + 32 + lane), tab);
     float d;
     const int8_t q = quantize_lane(h, &d);
     HQ[size_t(t) * ffn + j * QK + lane] = q;
@@ -231,110 +267,159 @@ __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, 
 
 // ---------------------------------------------------------------- attention (engine/src/model.cpp:115-137)
 
-// grid (n_kv, max_chunks, n_tok).  Query token t sits at position pos0 + t and attends to [0, pos].  Each CTA scores
-// one 64-position chunk for the `group` query heads sharing kv head g: exact sequential q.k per score, a chunk-local
-// softmax (max m, sum l) and unnormalized output o; the last CTA to finish a (token, kv head) merges the chunks in
-// chunk order.  Decode and prefill launch this same kernel, so a token's output has the same bits either way.
-constexpr int kAttnChunk = 64, kAttnHd = 64, kAttnGmax = 8;
+// grid (n_kv, max_chunks, n_tok).  Query token t sits at position pos = pos0 + t and attends to [0, pos], exactly as the
+// reference evaluates it, so the result is bit-identical:
+//   score  s_j = (sum_i q_i * k_ji in dimension order) * scale        -- per 64-position chunk, in parallel CTAs
+//   max    m = max_j s_j                                                (exact in any order)
+//   weight e_j = exp(s_j - m); sum = e_0 + e_1 + ... in position order; a_j = e_j * (1 / sum)
+//   output o_i = a_0 v_0i + a_1 v_1i + ... in position order
+// The chunk CTAs write their scores and chunk maxima; the last CTA of a (token, kv head) runs the ordered sums for the
+// `group` query heads sharing that kv head, staging weights and V rows through shared memory.
+constexpr int kAttnChunk = 64, kAttnHd = 64, kAttnGmax = 8, kAttnBlk = 128;
 
 __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
                                                    int n_tok, float* __restrict__ out) {
     __shared__ float sq[kAttnGmax][kAttnHd];
-    __shared__ float sk[kAttnChunk][kAttnHd + 1];
-    __shared__ float sv[kAttnChunk][kAttnHd];
-    __shared__ float ss[kAttnGmax][kAttnChunk];
+    __shared__ float sA[kAttnGmax][kAttnBlk];        // weights of one position block
+    __shared__ float sbuf[kAttnBlk * kAttnHd];       // K chunk (scores) / V block (outputs)
+    __shared__ float ssum[kAttnGmax], sinv[kAttnGmax], smx[kAttnGmax];
     __shared__ int s_last;
     pdl_launch_dependents();
     pdl_wait();
     const int g = blockIdx.x, c = blockIdx.y, t = blockIdx.z;
-    const int pos = *pos_dev + t;
+    const int pos = __ldcg(pos_dev) + t;
     const int nch = pos / kAttnChunk + 1;
     if (c >= nch) return;
-    const int group = a.n_heads / a.n_kv, hd = kAttnHd;
+    const int group = a.n_heads / a.n_kv, hd = kAttnHd, ctx = a.max_chunks * kAttnChunk;
     const int tb = c * kAttnChunk, len = min(kAttnChunk, pos + 1 - tb);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* q = Q + size_t(t) * a.n_heads * hd + size_t(g) * group * hd;
-    for (int i = tid; i < group * hd; i += blockDim.x) sq[i / hd][i % hd] = q[i];
+    for (int i = tid; i < group * hd; i += blockDim.x) sq[i / hd][i % hd] = __ldcg(q + i);
+    float* sk = sbuf;  // [kAttnChunk][hd + 1]
     const __half* K = a.kcache + size_t(tb) * a.kv_dim + g * hd;
-    const __half* V = a.vcache + size_t(tb) * a.kv_dim + g * hd;
     for (int i = tid; i < len * hd / 2; i += blockDim.x) {
         const int r = (2 * i) / hd, col = (2 * i) % hd;
-        const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(K + size_t(r) * a.kv_dim + col));
-        const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(V + size_t(r) * a.kv_dim + col));
-        sk[r][col] = kf.x;
-        sk[r][col + 1] = kf.y;
-        sv[r][col] = vf.x;
-        sv[r][col + 1] = vf.y;
+        const float2 kf = __half22float2(__ldcg(reinterpret_cast<const __half2*>(K + size_t(r) * a.kv_dim + col)));
+        sk[r * (hd + 1) + col] = kf.x;
+        sk[r * (hd + 1) + col + 1] = kf.y;
     }
     __syncthreads();
+    float* S = a.scores + (size_t(t) * a.n_heads + size_t(g) * group) * ctx;  // this group's score rows
     for (int idx = tid; idx < group * len; idx += blockDim.x) {
-        const int h = idx / len, tt = idx - h * len;
+        const int h = idx / len, j = idx - h * len;
         float s = 0.f;
 #pragma unroll 16
-        for (int i = 0; i < hd; ++i) s = fadd(s, fmul(sq[h][i], sk[tt][i]));
-        ss[h][tt] = fmul(s, a.scale);
+        for (int i = 0; i < hd; ++i) s = fadd(s, fmul(sq[h][i], sk[j * (hd + 1) + i]));
+        const float sc = fmul(s, a.scale);
+        S[size_t(h) * ctx + tb + j] = sc;
+        sA[h][j] = sc;
     }
     __syncthreads();
-    float* pml = a.part_ml + (size_t(t) * a.n_heads) * a.max_chunks * 2;
-    float* po = a.part_o + (size_t(t) * a.n_heads) * a.max_chunks * hd;
+    float* M = a.part_ml + (size_t(t) * a.n_heads + size_t(g) * group) * a.max_chunks;
     for (int h = warp; h < group; h += kWarps) {
-        const int head = g * group + h;
         float m = -INFINITY;
-        for (int tt = lane; tt < len; tt += 32) m = fmaxf(m, ss[h][tt]);
+        for (int j = lane; j < len; j += 32) m = fmaxf(m, sA[h][j]);
         m = warp_max(m);
-        float l = 0.f;
-        for (int tt = lane; tt < len; tt += 32) {
-            const float e = expf(fsub(ss[h][tt], m));
-            ss[h][tt] = e;
-            l = fadd(l, e);
-        }
-        l = warp_sum(l);
-        __syncwarp();
-        float o0 = 0.f, o1 = 0.f;
-        for (int tt = 0; tt < len; ++tt) {
-            const float e = ss[h][tt];
-            o0 = fadd(o0, fmul(e, sv[tt][lane]));
-            o1 = fadd(o1, fmul(e, sv[tt][lane + 32]));
-        }
-        if (nch == 1) {
-            out[size_t(t) * a.n_heads * hd + head * hd + lane] = fdiv(o0, l);
-            out[size_t(t) * a.n_heads * hd + head * hd + lane + 32] = fdiv(o1, l);
-        } else {
-            if (lane == 0) {
-                pml[(size_t(head) * a.max_chunks + c) * 2] = m;
-                pml[(size_t(head) * a.max_chunks + c) * 2 + 1] = l;
-            }
-            po[(size_t(head) * a.max_chunks + c) * hd + lane] = o0;
-            po[(size_t(head) * a.max_chunks + c) * hd + lane + 32] = o1;
-        }
+        if (lane == 0) M[size_t(h) * a.max_chunks + c] = m;
     }
-    if (nch == 1) return;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        unsigned* ctr = a.counters + size_t(t) * a.n_kv + g;
-        const unsigned prev = atomicAdd(ctr, 1u);
-        s_last = prev == unsigned(nch - 1);
-        if (s_last) *ctr = 0u;  // ready for the next launch
+    if (nch > 1) {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            unsigned* ctr = a.counters + size_t(t) * a.n_kv + g;
+            const unsigned prev = atomicAdd(ctr, 1u);
+            s_last = prev == unsigned(nch - 1);
+            if (s_last) *ctr = 0u;  // ready for the next launch
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+    } else {
+        __syncthreads();
     }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+    // ---- ordered softmax and outputs (one CTA per token and kv head)
     for (int h = warp; h < group; h += kWarps) {
-        const int head = g * group + h;
-        const float* ml = pml + size_t(head) * a.max_chunks * 2;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(ml + 2 * cc));
-        float L = 0.f, O0 = 0.f, O1 = 0.f;
-        for (int cc = 0; cc < nch; ++cc) {
-            const float w = expf(fsub(__ldcg(ml + 2 * cc), M));
-            L = fadd(L, fmul(w, __ldcg(ml + 2 * cc + 1)));
-            const float* oc = po + (size_t(head) * a.max_chunks + cc) * hd;
-            O0 = fadd(O0, fmul(w, __ldcg(oc + lane)));
-            O1 = fadd(O1, fmul(w, __ldcg(oc + lane + 32)));
+        float m = -INFINITY;
+        for (int cc = lane; cc < nch; cc += 32) m = fmaxf(m, __ldcg(M + size_t(h) * a.max_chunks + cc));
+        m = warp_max(m);
+        if (lane == 0) {
+            smx[h] = m;
+            ssum[h] = 0.f;
         }
-        out[size_t(t) * a.n_heads * hd + head * hd + lane] = fdiv(O0, L);
-        out[size_t(t) * a.n_heads * hd + head * hd + lane + 32] = fdiv(O1, L);
+    }
+    __syncthreads();
+    // e_j = exp(s_j - m) into S (and the block buffer); sum in position order by one lane per head
+    for (int b0 = 0; b0 <= pos; b0 += kAttnBlk) {
+        const int bl = min(kAttnBlk, pos + 1 - b0);
+        for (int idx = tid; idx < group * bl; idx += blockDim.x) {
+            const int h = idx / bl, j = idx - h * bl;
+            const float e = exp_ref(fsub(__ldcg(S + size_t(h) * ctx + b0 + j), smx[h]), a.exptab);
+            sA[h][j] = e;
+            S[size_t(h) * ctx + b0 + j] = e;
+        }
+        __syncthreads();
+        if (tid < group) {
+            float s = ssum[tid];
+            const float* e = sA[tid];
+            int j = 0;
+            for (; j + 8 <= bl; j += 8) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = e[j + k];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) s = fadd(s, v[k]);
+            }
+            for (; j < bl; ++j) s = fadd(s, e[j]);
+            ssum[tid] = s;
+        }
+        __syncthreads();
+    }
+    if (tid < group) sinv[tid] = fdiv(1.0f, ssum[tid]);
+    // outputs: lane owns dims (lane, lane + 32) of head `warp`; V rows staged per block
+    float o0 = 0.f, o1 = 0.f;
+    const __half* V = a.vcache + g * hd;
+    for (int b0 = 0; b0 <= pos; b0 += kAttnBlk) {
+        const int bl = min(kAttnBlk, pos + 1 - b0);
+        __syncthreads();
+        for (int i = tid; i < bl * hd / 2; i += blockDim.x) {
+            const int r = (2 * i) / hd, col = (2 * i) % hd;
+            const float2 vf =
+                __half22float2(__ldcg(reinterpret_cast<const __half2*>(V + size_t(b0 + r) * a.kv_dim + col)));
+            sbuf[r * hd + col] = vf.x;
+            sbuf[r * hd + col + 1] = vf.y;
+        }
+        for (int idx = tid; idx < group * bl; idx += blockDim.x) {
+            const int h = idx / bl, j = idx - h * bl;
+            sA[h][j] = fmul(__ldcg(S + size_t(h) * ctx + b0 + j), sinv[h]);
+        }
+        __syncthreads();
+        if (warp < group) {
+            const float* aw = sA[warp];
+            int j = 0;
+            for (; j + 4 <= bl; j += 4) {
+                float av[4], v0[4], v1[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    av[k] = aw[j + k];
+                    v0[k] = sbuf[(j + k) * hd + lane];
+                    v1[k] = sbuf[(j + k) * hd + lane + 32];
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    o0 = fadd(o0, fmul(av[k], v0[k]));
+                    o1 = fadd(o1, fmul(av[k], v1[k]));
+                }
+            }
+            for (; j < bl; ++j) {
+                o0 = fadd(o0, fmul(aw[j], sbuf[j * hd + lane]));
+                o1 = fadd(o1, fmul(aw[j], sbuf[j * hd + lane + 32]));
+            }
+        }
+    }
+    if (warp < group) {
+        float* o = out + size_t(t) * a.n_heads * hd + size_t(g * group + warp) * hd;
+        o[lane] = o0;
+        o[lane + 32] = o1;
     }
 }
 
@@ -424,15 +509,15 @@ cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin
 }
 
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
-                              int8_t* HQ, float* HD, cudaStream_t st, bool pdl) {
+                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl) {
     cudaError_t e = cudaErrorInvalidValue;
     const int bpc = p.rows_per_cta / 64;
     if (W.dtype == DT_Q8_0) {
         QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q8_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
-                                          eps, HQ, HD, bpc, p.magic));
+                                          eps, HQ, HD, bpc, p.magic, tab));
     } else if (W.dtype == DT_Q4_0) {
         QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q4_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
-                                          eps, HQ, HD, bpc, p.magic));
+                                          eps, HQ, HD, bpc, p.magic, tab));
     }
     return e;
 }
@@ -459,9 +544,11 @@ cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t 
     return launch_pdl(k_residual, dim3(grid), dim3(kThreads), 0, st, pdl, X, R, n);
 }
 
-cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, cudaStream_t st, bool pdl) {
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st,
+                                bool pdl) {
     const long long warps = (long long)n_tok * (ffn / QK);
-    return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD);
+    return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD,
+                      tab);
 }
 
 }  // namespace qb

@@ -4,6 +4,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "exp_table.h"
 #include "ops.h"
 
 namespace qb {
@@ -24,9 +25,10 @@ struct AttnArgs {
     int n_heads, n_kv, head_dim, kv_dim;
     float scale;             // 1/sqrt(head_dim)
     int max_chunks;          // ceil(ctx / 64)
-    float* part_ml;          // scratch [n_tok][n_heads][max_chunks][2]
-    float* part_o;           // scratch [n_tok][n_heads][max_chunks][head_dim]
+    float* part_ml;          // scratch [n_tok][n_heads][max_chunks]: chunk maxima
+    float* scores;           // scratch [n_tok][n_heads][max_chunks * 64]: scores, then exp weights
     unsigned* counters;      // [n_tok][n_kv], zero between launches
+    ExpTab exptab;           // host libm expf exceptions (exp_table.h)
 };
 
 struct SlicePlan {
@@ -43,13 +45,14 @@ cudaError_t launch_qkv_dec(const QkvArgs& a, const SlicePlan& p, const float* X,
 cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin, const int8_t* qin, const float* din,
                              float* X, cudaStream_t st, bool pdl);
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
-                              int8_t* HQ, float* HD, cudaStream_t st, bool pdl);
+                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl);
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
                                    cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
                                 bool pdl);
 cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl);
-cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, cudaStream_t st, bool pdl);
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st,
+                                bool pdl);
 
 }  // namespace qb
