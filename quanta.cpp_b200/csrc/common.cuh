@@ -84,6 +84,28 @@ __device__ __forceinline__ int8_t quantize_lane(float x, float* d_out) {
     return (int8_t)lroundf(fmul(x, inv));
 }
 
+// Launches `kernel`, optionally as a programmatic dependent of the previous launch on the stream (the kernel then
+// calls griddepcontrol.launch_dependents / .wait); raises the dynamic shared memory limit when it needs more than 48 KB.
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace qb
 
 #define QB_CUDA_OK(expr)                                                         \

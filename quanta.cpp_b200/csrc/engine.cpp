@@ -183,10 +183,6 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
             exptab_.mask = unsigned(slots.size() - 1);
         }
         max_chunks_ = (ctx_ + 63) / 64;
-        part_ml_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * 2 * 4));
-        scores_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.n_heads * max_chunks_ * 64 * 4));
-        counters_ = static_cast<unsigned*>(dalloc(size_t(kChunk) * hp_.n_kv_heads * 4));
-        cudaMemset(counters_, 0, size_t(kChunk) * hp_.n_kv_heads * 4);
 
         layers_.resize(size_t(hp_.n_layers));
         const size_t before_layers = weight_bytes_;
@@ -241,9 +237,6 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
             aa.kv_dim = kv_dim;
             aa.scale = 1.0f / std::sqrt(float(hp_.head_dim));
             aa.max_chunks = max_chunks_;
-            aa.part_ml = part_ml_;
-            aa.scores = scores_;
-            aa.counters = counters_;
             aa.exptab = exptab_;
             L.p_qkv = plan_rows(L.qkv.dtype, L.qkv.rows, L.qkv.cols, n_sm_, 2);
             L.p_o = plan_rows(L.o.dtype, L.o.rows, L.o.cols, n_sm_, 2);

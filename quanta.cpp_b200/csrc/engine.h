@@ -143,8 +143,6 @@ private:
     static constexpr int kChunk = 32;
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;
-    float *part_ml_ = nullptr, *scores_ = nullptr;
-    unsigned* counters_ = nullptr;
     int* tokens_ = nullptr;
     int* pos_ = nullptr;  // chunk start position (device)
 

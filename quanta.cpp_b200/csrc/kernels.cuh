@@ -14,6 +14,22 @@ constexpr int kWarps = kThreads / 32;
 __device__ __forceinline__ unsigned fast_div(unsigned n, unsigned m) { return __umulhi(n, m); }
 inline unsigned div_magic(unsigned d) { return unsigned((0x100000000ULL + d - 1) / d); }
 
+// cp.async: 16-byte (L2 only) and 4-byte asynchronous copies global -> shared, grouped and awaited per thread
+// (cp.async.wait_group, then a CTA barrier, before other threads read the data).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Streaming 16-byte load that does not allocate in L1 (weights are read once per step).
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
     uint4 v;

@@ -2,7 +2,7 @@
 //
 // Decode (one token) runs five kernels per layer, each fusing its neighbours:
 //   k_qkv_dec     rmsnorm + quantize (prologue) -> fused q|k|v integer matvec -> bias + RoPE -> q, f16 K/V store
-//   k_attn        GQA attention over the f16 KV cache, split over 64-position chunks, last CTA combines
+//   k_attn        GQA attention over the f16 KV cache (attention.cu)
 //   k_o_dec       quantize(attn) -> o_proj matvec -> residual add
 //   k_gateup_dec  rmsnorm + quantize -> gate|up matvec (rows interleaved per 32-block) -> SwiGLU -> quantize
 //   k_down_dec    down_proj matvec -> residual add
@@ -265,187 +265,9 @@ __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, 
     if (lane == 0) HD[size_t(t) * nbk + j] = d;
 }
 
-// ---------------------------------------------------------------- attention (engine/src/model.cpp:115-137)
-
-// grid (n_kv, max_chunks, n_tok).  Query token t sits at position pos = pos0 + t and attends to [0, pos], exactly as the
-// reference evaluates it, so the result is bit-identical:
-//   score  s_j = (sum_i q_i * k_ji in dimension order) * scale        -- per 64-position chunk, in parallel CTAs
-//   max    m = max_j s_j                                                (exact in any order)
-//   weight e_j = exp(s_j - m); sum = e_0 + e_1 + ... in position order; a_j = e_j * (1 / sum)
-//   output o_i = a_0 v_0i + a_1 v_1i + ... in position order
-// The chunk CTAs write their scores and chunk maxima; the last CTA of a (token, kv head) runs the ordered sums for the
-// `group` query heads sharing that kv head, staging weights and V rows through shared memory.
-constexpr int kAttnChunk = 64, kAttnHd = 64, kAttnGmax = 8, kAttnBlk = 128;
-
-__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
-                                                   int n_tok, float* __restrict__ out) {
-    __shared__ float sq[kAttnGmax][kAttnHd];
-    __shared__ float sA[kAttnGmax][kAttnBlk];        // weights of one position block
-    __shared__ float sbuf[kAttnBlk * kAttnHd];       // K chunk (scores) / V block (outputs)
-    __shared__ float ssum[kAttnGmax], sinv[kAttnGmax], smx[kAttnGmax];
-    __shared__ int s_last;
-    pdl_launch_dependents();
-    pdl_wait();
-    const int g = blockIdx.x, c = blockIdx.y, t = blockIdx.z;
-    const int pos = __ldcg(pos_dev) + t;
-    const int nch = pos / kAttnChunk + 1;
-    if (c >= nch) return;
-    const int group = a.n_heads / a.n_kv, hd = kAttnHd, ctx = a.max_chunks * kAttnChunk;
-    const int tb = c * kAttnChunk, len = min(kAttnChunk, pos + 1 - tb);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* q = Q + size_t(t) * a.n_heads * hd + size_t(g) * group * hd;
-    for (int i = tid; i < group * hd; i += blockDim.x) sq[i / hd][i % hd] = __ldcg(q + i);
-    float* sk = sbuf;  // [kAttnChunk][hd + 1]
-    const __half* K = a.kcache + size_t(tb) * a.kv_dim + g * hd;
-    for (int i = tid; i < len * hd / 2; i += blockDim.x) {
-        const int r = (2 * i) / hd, col = (2 * i) % hd;
-        const float2 kf = __half22float2(__ldcg(reinterpret_cast<const __half2*>(K + size_t(r) * a.kv_dim + col)));
-        sk[r * (hd + 1) + col] = kf.x;
-        sk[r * (hd + 1) + col + 1] = kf.y;
-    }
-    __syncthreads();
-    float* S = a.scores + (size_t(t) * a.n_heads + size_t(g) * group) * ctx;  // this group's score rows
-    for (int idx = tid; idx < group * len; idx += blockDim.x) {
-        const int h = idx / len, j = idx - h * len;
-        float s = 0.f;
-#pragma unroll 16
-        for (int i = 0; i < hd; ++i) s = fadd(s, fmul(sq[h][i], sk[j * (hd + 1) + i]));
-        const float sc = fmul(s, a.scale);
-        S[size_t(h) * ctx + tb + j] = sc;
-        sA[h][j] = sc;
-    }
-    __syncthreads();
-    float* M = a.part_ml + (size_t(t) * a.n_heads + size_t(g) * group) * a.max_chunks;
-    for (int h = warp; h < group; h += kWarps) {
-        float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sA[h][j]);
-        m = warp_max(m);
-        if (lane == 0) M[size_t(h) * a.max_chunks + c] = m;
-    }
-    if (nch > 1) {
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            unsigned* ctr = a.counters + size_t(t) * a.n_kv + g;
-            const unsigned prev = atomicAdd(ctr, 1u);
-            s_last = prev == unsigned(nch - 1);
-            if (s_last) *ctr = 0u;  // ready for the next launch
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-    } else {
-        __syncthreads();
-    }
-    // ---- ordered softmax and outputs (one CTA per token and kv head)
-    for (int h = warp; h < group; h += kWarps) {
-        float m = -INFINITY;
-        for (int cc = lane; cc < nch; cc += 32) m = fmaxf(m, __ldcg(M + size_t(h) * a.max_chunks + cc));
-        m = warp_max(m);
-        if (lane == 0) {
-            smx[h] = m;
-            ssum[h] = 0.f;
-        }
-    }
-    __syncthreads();
-    // e_j = exp(s_j - m) into S (and the block buffer); sum in position order by one lane per head
-    for (int b0 = 0; b0 <= pos; b0 += kAttnBlk) {
-        const int bl = min(kAttnBlk, pos + 1 - b0);
-        for (int idx = tid; idx < group * bl; idx += blockDim.x) {
-            const int h = idx / bl, j = idx - h * bl;
-            const float e = exp_ref(fsub(__ldcg(S + size_t(h) * ctx + b0 + j), smx[h]), a.exptab);
-            sA[h][j] = e;
-            S[size_t(h) * ctx + b0 + j] = e;
-        }
-        __syncthreads();
-        if (tid < group) {
-            float s = ssum[tid];
-            const float* e = sA[tid];
-            int j = 0;
-            for (; j + 8 <= bl; j += 8) {
-                float v[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = e[j + k];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) s = fadd(s, v[k]);
-            }
-            for (; j < bl; ++j) s = fadd(s, e[j]);
-            ssum[tid] = s;
-        }
-        __syncthreads();
-    }
-    if (tid < group) sinv[tid] = fdiv(1.0f, ssum[tid]);
-    // outputs: lane owns dims (lane, lane + 32) of head `warp`; V rows staged per block
-    float o0 = 0.f, o1 = 0.f;
-    const __half* V = a.vcache + g * hd;
-    for (int b0 = 0; b0 <= pos; b0 += kAttnBlk) {
-        const int bl = min(kAttnBlk, pos + 1 - b0);
-        __syncthreads();
-        for (int i = tid; i < bl * hd / 2; i += blockDim.x) {
-            const int r = (2 * i) / hd, col = (2 * i) % hd;
-            const float2 vf =
-                __half22float2(__ldcg(reinterpret_cast<const __half2*>(V + size_t(b0 + r) * a.kv_dim + col)));
-            sbuf[r * hd + col] = vf.x;
-            sbuf[r * hd + col + 1] = vf.y;
-        }
-        for (int idx = tid; idx < group * bl; idx += blockDim.x) {
-            const int h = idx / bl, j = idx - h * bl;
-            sA[h][j] = fmul(__ldcg(S + size_t(h) * ctx + b0 + j), sinv[h]);
-        }
-        __syncthreads();
-        if (warp < group) {
-            const float* aw = sA[warp];
-            int j = 0;
-            for (; j + 4 <= bl; j += 4) {
-                float av[4], v0[4], v1[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    av[k] = aw[j + k];
-                    v0[k] = sbuf[(j + k) * hd + lane];
-                    v1[k] = sbuf[(j + k) * hd + lane + 32];
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    o0 = fadd(o0, fmul(av[k], v0[k]));
-                    o1 = fadd(o1, fmul(av[k], v1[k]));
-                }
-            }
-            for (; j < bl; ++j) {
-                o0 = fadd(o0, fmul(aw[j], sbuf[j * hd + lane]));
-                o1 = fadd(o1, fmul(aw[j], sbuf[j * hd + lane + 32]));
-            }
-        }
-    }
-    if (warp < group) {
-        float* o = out + size_t(t) * a.n_heads * hd + size_t(g * group + warp) * hd;
-        o[lane] = o0;
-        o[lane + 32] = o1;
-    }
-}
-
 // ---------------------------------------------------------------- launchers
 
 namespace {
-
-template <class... KArgs, class... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
-                       Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-    }
-    return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
 
 int pick_u(int chunks) {
     const int per = (chunks + kThreads - 1) / kThreads;
@@ -457,8 +279,9 @@ int pick_u(int chunks) {
 SlicePlan plan_rows(int dtype, int rows, int cols, int target_ctas, int row_multiple) {
     SlicePlan p;
     const int cpr = row_bytes_host(dtype, cols) / 16;
-    int rpc = (rows + target_ctas - 1) / target_ctas;
-    rpc = (rpc + row_multiple - 1) / row_multiple * row_multiple;
+    // rows per CTA: the multiple of row_multiple nearest to rows / target_ctas (at least one multiple)
+    int rpc = int((double(rows) / target_ctas) / row_multiple + 0.5) * row_multiple;
+    if (rpc < row_multiple) rpc = row_multiple;
     while (rpc > row_multiple && rpc * cpr > kThreads * 16) rpc -= row_multiple;
     p.rows_per_cta = rpc;
     p.grid = (rows + rpc - 1) / rpc;
@@ -520,11 +343,6 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
                                           eps, HQ, HD, bpc, p.magic, tab));
     }
     return e;
-}
-
-cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl) {
-    if (a.head_dim != kAttnHd || a.n_heads / a.n_kv > kAttnGmax) return cudaErrorInvalidValue;
-    return launch_pdl(k_attn, dim3(a.n_kv, a.max_chunks, n_tok), dim3(kThreads), 0, st, pdl, a, Q, pos_dev, n_tok, out);
 }
 
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,

@@ -24,10 +24,7 @@ struct AttnArgs {
     const __half* vcache;
     int n_heads, n_kv, head_dim, kv_dim;
     float scale;             // 1/sqrt(head_dim)
-    int max_chunks;          // ceil(ctx / 64)
-    float* part_ml;          // scratch [n_tok][n_heads][max_chunks]: chunk maxima
-    float* scores;           // scratch [n_tok][n_heads][max_chunks * 64]: scores, then exp weights
-    unsigned* counters;      // [n_tok][n_kv], zero between launches
+    int max_chunks;          // ceil(ctx / 64): the KV cache holds max_chunks * 64 >= ctx positions of room
     ExpTab exptab;           // host libm expf exceptions (exp_table.h)
 };
 

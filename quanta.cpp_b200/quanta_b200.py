@@ -167,9 +167,9 @@ class DeviceTensor:
         self.h = h
 
     def close(self):
-        if getattr(self, "h", None):
-            lib().qnt_tensor_free(self.h)
-            self.h = None
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.qnt_tensor_free(self.h)
+        self.h = None
 
     __del__ = close
 
@@ -214,9 +214,9 @@ class Model:
         self._logits = np.zeros(self.vocab, np.float32)
 
     def close(self):
-        if getattr(self, "h", None):
-            lib().qnt_model_close(self.h)
-            self.h = None
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.qnt_model_close(self.h)
+        self.h = None
 
     __del__ = close
 

@@ -46,6 +46,7 @@ def models(qb):
         specs = {
             "tiny_q8": dict(shape=qb.TINY, mlp_q4=False, shortlist=True, seed=7),
             "tiny_q4sl": dict(shape=qb.TINY, mlp_q4=True, shortlist=True, seed=11),
+            "tiny_long": dict(shape=dict(qb.TINY, max_seq=2048), mlp_q4=True, shortlist=True, seed=13),
             "q8_0": dict(shape=qb.QWEN05B, mlp_q4=False, shortlist=False, seed=1234),
             "q4mix_sl": dict(shape=qb.QWEN05B, mlp_q4=True, shortlist=True, seed=1234),
         }

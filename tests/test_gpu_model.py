@@ -59,6 +59,29 @@ def test_batched_prefill_equals_token_by_token(tiny, name):
         assert rel_err(got, ref_lg) < TOL
 
 
+def test_long_prompt_batched_windows(qb, models):
+    """Prompts past 512 positions: the batched attention streams its scores in windows (the single-token path keeps
+    them resident), and both must give the same bits; the reference bounds the logits."""
+    m = qb.Model(models("tiny_long"), ctx_len=2048)
+    r = R.RefModel(models("tiny_long"), ctx=2048, threads=4)
+    try:
+        ids = np.random.default_rng(8).integers(0, m.vocab, 1200)
+        by_token = {}
+        for p in range(1200):
+            lg = m.forward(ids[p], p)
+            if p in (599, 1199):
+                by_token[p] = lg
+        got = m.forward_batch(ids[:1200], 0)
+        assert np.array_equal(got, by_token[1199])
+        m.forward_batch(ids[:600], 0)
+        got2 = m.forward_batch(ids[600:1200], 600)
+        assert np.array_equal(got2, by_token[1199])
+        assert rel_err(got, r.forward_batch(ids[:1200], 0)) < TOL
+    finally:
+        m.close()
+        r.close()
+
+
 @pytest.mark.parametrize("k", [1, 20])
 def test_shortlist_head_exact(tiny, k):
     """check_head: bound holds for every row; exact rows bit-identical to the full head; top-k and must included."""
