@@ -147,6 +147,22 @@ int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_s
 int qnt_session_step(qnt_model* m, int n);
 int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* stats);
 
+/* Sampler (engine/src/sampler.h:20-38): Sampler::sample (sampler.cpp:22-85) on logits that are already in device
+ * memory -- repetition penalty -> greedy argmax (first max) or top-k -> softmax(T) -> min-p -> top-p -> xorshift64*
+ * draw, with the reference's float operations, so the same logits, history and seed give the same ids.
+ *   qnt_sampler_create  = Sampler(const SamplerParams&): the xorshift state starts at (seed ? seed : fixed) | 1, on the
+ *                         current device; top_k must be 1..32 when temperature > 0 (QNT_ERR_UNSUPPORTED otherwise).
+ *   qnt_sampler_sample  = Sampler::sample(float* logits, int n_valid, const std::vector<int>& history): `logits` is a
+ *                         DEVICE array of at least n_valid floats and is edited in place like the reference's (the
+ *                         penalised ids); `history` is a host array of n_history ids.  Work is queued on `stream`
+ *                         (a cudaStream_t, NULL = legacy default); the call waits for it and writes the id to *token.
+ *   qnt_sampler_free    = ~Sampler. */
+typedef struct qnt_sampler qnt_sampler;
+int qnt_sampler_create(const qnt_sampler_params* sp, qnt_sampler** out);
+int qnt_sampler_sample(qnt_sampler* s, float* logits, int n_valid, const int* history, int n_history, int* token,
+                       void* stream);
+void qnt_sampler_free(qnt_sampler* s);
+
 /* Diagnostics (no reference counterpart): copies an internal buffer of the last forward as floats -- 0 roped q,
  * 1 attention output, 2 residual x (of the last layer, before the final norm), 3 quantized SwiGLU output, 4 its block
  * scales, 5 the head's quantized input.  Returns the element count. */

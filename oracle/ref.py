@@ -285,7 +285,9 @@ class Sampler:
     def sample(self, logits: np.ndarray, n_valid: int, history) -> int:
         lg = np.ascontiguousarray(logits, np.float32).copy()
         h = np.ascontiguousarray(history, np.int32)
-        return ref().ref_sample(self.h, _p(lg), n_valid, _p(h), h.size)
+        tok = ref().ref_sample(self.h, _p(lg), n_valid, _p(h), h.size)
+        self.last_logits = lg  # the reference edits its logits in place (the penalised ids)
+        return tok
 
     def __del__(self):
         if getattr(self, "h", None):

@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "../../include/quanta_b200.h"
+#include "capi_util.h"
 #include "engine.h"
 #include "ops.h"
 
@@ -20,7 +21,7 @@ struct qnt_model {
     qb::Engine eng;
 };
 
-namespace {
+namespace qnt_capi {
 
 thread_local std::string g_err;
 
@@ -30,6 +31,12 @@ int set_err(int code, const std::string& m) {
 }
 
 int cuda_err(cudaError_t e, const char* what) { return set_err(QNT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)); }
+
+}  // namespace qnt_capi
+
+namespace {
+
+using namespace qnt_capi;
 
 int engine_code(qb::Engine& e, int r) {
     if (r >= 0) return r;
@@ -51,7 +58,7 @@ bool shape_ok(int dtype, int rows, int cols) {
 
 extern "C" {
 
-const char* qnt_last_error(void) { return g_err.c_str(); }
+const char* qnt_last_error(void) { return qnt_capi::g_err.c_str(); }
 int qnt_version(void) { return 100; }
 
 int qnt_device_count(void) {

@@ -493,11 +493,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_sl_cands(DMat W8, HeadIn hi
 
 // ---------------------------------------------------------------- sampler
 
-// Sampler stage 1 straight from a logits array (used once after a prefill): penalty on the unique marked ids, each
-// CTA's best K of [0, n_valid); clears the marks it used.
-__global__ void __launch_bounds__(kThreads) k_topk_partial(const float* __restrict__ logits, int n_valid, int K, int penal,
+// Sampler stage 1 straight from a logits array (after a prefill, and the standalone sampler): penalty on the unique
+// marked ids (written back to wb[id] when wb is set, as Sampler::sample edits its logits in place), each CTA's best K
+// of [0, n_valid); clears the marks it used.
+__global__ void __launch_bounds__(kThreads) k_topk_partial(const float* logits, int n_valid, int K, int penal,
                                                            float penalty, unsigned char* __restrict__ mark,
-                                                           Cand* __restrict__ out) {
+                                                           Cand* __restrict__ out, float* wb) {
     __shared__ Cand slist[kWarps * 32];
     pdl_launch_dependents();
     pdl_wait();
@@ -514,6 +515,7 @@ __global__ void __launch_bounds__(kThreads) k_topk_partial(const float* __restri
             if (penal && __ldcg(mark + r)) {
                 v = penalize(v, penalty);
                 mark[r] = 0;
+                if (wb) wb[r] = v;
             }
         }
         L.offer(v, ok ? r : INT_MAX, ok, K);
@@ -666,10 +668,10 @@ cudaError_t launch_mark(const int* must, const int* n_must_dev, int n_must_host,
 }
 
 cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int penal, float penalty, unsigned char* mark,
-                                void* lists, int n_lists, cudaStream_t st, bool pdl) {
+                                void* lists, int n_lists, cudaStream_t st, bool pdl, float* write_back) {
     if (K < 1 || K > 32) return cudaErrorInvalidValue;
     return launch_pdl(k_topk_partial, dim3(n_lists), dim3(kThreads), 0, st, pdl, logits, n_valid, K, penal, penalty, mark,
-                      reinterpret_cast<Cand*>(lists));
+                      reinterpret_cast<Cand*>(lists), write_back);
 }
 
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,

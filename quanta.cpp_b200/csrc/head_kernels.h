@@ -100,8 +100,9 @@ cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStrea
 cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl, int* kernels);
 cudaError_t launch_mark(const int* must, const int* n_must_dev, int n_must_host, int window, int n_valid, unsigned char* mark,
                         cudaStream_t st, bool pdl);
+// write_back: where the penalised logits go (the logits array itself for an in-place edit), or null.
 cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int penal, float penalty, unsigned char* mark,
-                                void* lists, int n_lists, cudaStream_t st, bool pdl);
+                                void* lists, int n_lists, cudaStream_t st, bool pdl, float* write_back = nullptr);
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
                                 int hist_cap, cudaStream_t st, bool pdl);
 

@@ -115,6 +115,10 @@ def lib() -> C.CDLL:
         L.qnt_session_read.argtypes = [P, P, I, C.POINTER(GenStatsC)]
         L.qnt_model_stream.argtypes = [P]
         L.qnt_model_stream.restype = P
+        L.qnt_sampler_create.argtypes = [C.POINTER(SamplerParamsC), C.POINTER(P)]
+        L.qnt_sampler_sample.argtypes = [P, P, I, P, I, C.POINTER(I), P]
+        L.qnt_sampler_free.argtypes = [P]
+        L.qnt_sampler_free.restype = None
         _lib = L
     return _lib
 
@@ -190,6 +194,37 @@ class DeviceTensor:
                                      self.rows, impl))
         return out
 
+
+
+class Sampler:
+    """Sampler (engine/src/sampler.h:20-38) on the device: sample(logits, n_valid, history) -> id, as
+    Sampler::sample (sampler.cpp:22-85).  `logits` is a float32 CUDA tensor (torch) on the current device and is edited
+    in place like the reference's array; `history` is a sequence of ids."""
+
+    def __init__(self, sp: SamplerParams):
+        spc = SamplerParamsC(sp.temperature, sp.top_k, sp.top_p, sp.min_p, sp.repeat_penalty, sp.repeat_window, sp.seed)
+        h = C.c_void_p()
+        _check(lib().qnt_sampler_create(C.byref(spc), C.byref(h)))
+        self.h = h
+        self.params = sp
+
+    def sample(self, logits, n_valid: int | None = None, history=(), stream=None) -> int:
+        if not (getattr(logits, "is_cuda", False) and str(logits.dtype) == "torch.float32" and logits.is_contiguous()):
+            raise TypeError("logits must be a contiguous float32 CUDA tensor")
+        n_valid = logits.numel() if n_valid is None else n_valid
+        hist = np.ascontiguousarray(np.asarray(history, np.int32).ravel())
+        tok = C.c_int(-1)
+        st = None if stream is None else C.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+        _check(lib().qnt_sampler_sample(self.h, C.c_void_p(logits.data_ptr()), n_valid, _ptr(hist) if hist.size else None,
+                                        hist.size, C.byref(tok), st))
+        return tok.value
+
+    def close(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.qnt_sampler_free(self.h)
+        self.h = None
+
+    __del__ = close
 
 # ---------------------------------------------------------------- model level
 
