@@ -163,6 +163,24 @@ int qnt_sampler_sample(qnt_sampler* s, float* logits, int n_valid, const int* hi
                        void* stream);
 void qnt_sampler_free(qnt_sampler* s);
 
+/* No counterpart in the reference: qnt_sampler_sample without a sampler object and without allocating memory, for
+ * callers that cannot allocate -- a serving process whose device memory is reserved up front by its own pool (weights
+ * and KV pages), where a cudaMalloc fails or fragments that pool, and a token loop that must not stall other streams,
+ * as cudaMalloc / cudaFree can synchronise the device.  Same kernels and results as qnt_sampler_sample.
+ *   *rng_state: the xorshift64* state, in/out; start it at (seed ? seed : any nonzero) | 1 as Sampler's constructor
+ *               does (sampler.cpp:10-13); each call advances it exactly like the sampler object's.
+ *   Limits: n_valid <= 262144, n_history <= 32768, 1 <= top_k <= 32 when temperature > 0; larger sizes return
+ *           QNT_ERR_INVALID with the limit in qnt_last_error().
+ *   Scratch: one static device array of 459,008 bytes per device (sampler state, candidate lists, history copy and
+ *            penalty marks) plus a static 4 MiB copy of the host exp table.  The marks must be all zero when a call
+ *            starts: they start zeroed and every completed call clears the ones it set.  Calls whose GPU work overlaps
+ *            (other host threads, or other streams) share that scratch and race: serialise them.
+ *   The first call on each device does the set-up, with that device current: cudaGetSymbolAddress of the scratch and
+ *            of the table, and a synchronous copy of the exp table into it.  Make that first call before any stream
+ *            capture.  The call waits for its stream and writes the id to *token. */
+int qnt_sampler_sample_noalloc(const qnt_sampler_params* sp, uint64_t* rng_state, float* logits, int n_valid,
+                               const int* history, int n_history, int* token, void* stream);
+
 /* Diagnostics (no reference counterpart): copies an internal buffer of the last forward as floats -- 0 roped q,
  * 1 attention output, 2 residual x (of the last layer, before the final norm), 3 quantized SwiGLU output, 4 its block
  * scales, 5 the head's quantized input.  Returns the element count. */

@@ -119,6 +119,8 @@ def lib() -> C.CDLL:
         L.qnt_sampler_sample.argtypes = [P, P, I, P, I, C.POINTER(I), P]
         L.qnt_sampler_free.argtypes = [P]
         L.qnt_sampler_free.restype = None
+        L.qnt_sampler_sample_noalloc.argtypes = [C.POINTER(SamplerParamsC), C.POINTER(C.c_uint64), P, I, P, I,
+                                                 C.POINTER(I), P]
         _lib = L
     return _lib
 
@@ -225,6 +227,22 @@ class Sampler:
         self.h = None
 
     __del__ = close
+
+
+def sample_noalloc(sp: SamplerParams, rng_state: int, logits, n_valid: int | None = None, history=(), stream=None):
+    """qnt_sampler_sample_noalloc: the Sampler without an object and without allocating (static device scratch).
+    rng_state is the xorshift64* state ((seed or any nonzero) | 1 to start); returns (id, next rng_state)."""
+    if not (getattr(logits, "is_cuda", False) and str(logits.dtype) == "torch.float32" and logits.is_contiguous()):
+        raise TypeError("logits must be a contiguous float32 CUDA tensor")
+    n_valid = logits.numel() if n_valid is None else n_valid
+    spc = SamplerParamsC(sp.temperature, sp.top_k, sp.top_p, sp.min_p, sp.repeat_penalty, sp.repeat_window, sp.seed)
+    hist = np.ascontiguousarray(np.asarray(history, np.int32).ravel())
+    state = C.c_uint64(rng_state)
+    tok = C.c_int(-1)
+    st = None if stream is None else C.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+    _check(lib().qnt_sampler_sample_noalloc(C.byref(spc), C.byref(state), C.c_void_p(logits.data_ptr()), n_valid,
+                                            _ptr(hist) if hist.size else None, hist.size, C.byref(tok), st))
+    return tok.value, state.value
 
 # ---------------------------------------------------------------- model level
 
