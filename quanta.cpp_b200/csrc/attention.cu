@@ -12,9 +12,9 @@
 //      distributed shared memory.
 //   2. cluster barrier; every CTA reads the CS maxima, exponentiates its own scores and stores the weights straight
 //      into the leader's weight row (distributed shared memory).
-//   3. cluster barrier; the other CTAs exit.  The leader sums the row in position order on one thread, normalises it,
-//      and two warps chain the outputs (one lane per dimension) over V rows that stream through a cp.async ring the
-//      leader filled from its first instruction on.
+//   3. cluster barrier; the other CTAs exit.  The leader sums the row in position order on one thread and normalises
+//      it.  Six warps stream V rows through a cp.async ring (the first blocks requested inside the second barrier, so
+//      they land during the sum); two warps, one lane per dimension, chain o_d += a_j * v_jd in position order.
 // Decode launches CS = min(8, chunks); multi-token (prefill) launches use CS = 1, one CTA per (head, token), which
 // keeps the SMs busy with many tokens at once.  The cluster barriers are hardware barriers (no spin loops).
 #include <cooperative_groups.h>
@@ -32,25 +32,32 @@ constexpr int kPosChunk = 64;       // KV positions per chunk (the unit of max_c
 constexpr int kHd = 64;             // supported head_dim
 constexpr int kTile = 128;          // positions scored per K tile (one thread each)
 constexpr int kVBlk = 64;           // V rows per ring slot
-constexpr int kRing = 4;            // V ring slots
-constexpr int kOutThreads = 64;     // output threads of the leader (one per dimension)
+constexpr int kOutThreads = 64;     // chain threads of the leader (one per dimension, warps 0-1)
 constexpr int kMaxCluster = 8;      // portable cluster size limit
 constexpr int kKfStride = kHd + 1;  // f32 K tile row stride (conflict-free column walks)
+constexpr int kSlotBytes = kVBlk * kHd * 2;  // one f16 V block
 
-// Dynamic shared memory layout (byte offsets): the same for every CTA of a launch.
-constexpr int kOffQ = 0;                                       // f32 [kHd] query
-constexpr int kOffMax = kOffQ + kHd * 4;                       // f32 [kMaxCluster] local maxima (leader's copy used)
-constexpr int kOffKf = kOffMax + 256;                          // f32 [kTile][kKfStride] K tile
-constexpr int kOffRing = kOffKf + kTile * kKfStride * 4;       // f16 [kRing][kVBlk][kHd] V ring (leader)
-constexpr int kOffLs = kOffRing + kRing * kVBlk * kHd * 2;     // f32 [lsmax] own scores, then f32 [ctx] weights
-static_assert(kOffKf % 16 == 0 && kOffRing % 16 == 0 && kOffLs % 16 == 0, "16-byte aligned regions");
+// Dynamic shared memory layout (byte offsets), the same for every CTA of a launch.  The K tile (scores) and the V
+// ring (outputs) share one region: the ring is first written after the first cluster barrier.
+constexpr int kOffQ = 0;                        // f32 [kHd] query
+constexpr int kOffMax = kOffQ + kHd * 4;        // f32 [kMaxCluster] local maxima (the leader's copy is used)
+constexpr int kOffRegion = kOffMax + 256;       // f32 [kTile][kKfStride] K tile | f16 [R][kVBlk][kHd] V ring
+constexpr int kKfBytes = kTile * kKfStride * 4;
+static_assert(kOffRegion % 16 == 0 && kKfBytes % 16 == 0, "16-byte aligned regions");
 static_assert(kThreads == 256 && kTile * 8 % kThreads == 0, "K tile loader");
 
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
+__host__ __device__ constexpr int region_bytes(int ring) { return ring * kSlotBytes > kKfBytes ? ring * kSlotBytes : kKfBytes; }
 __host__ __device__ inline int ls_len(int ctx, int cs) { return ((ctx + cs - 1) / cs + 3) & ~3; }
-inline size_t attn_smem_bytes(int ctx, int cs) { return size_t(kOffLs) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4; }
+// then f32 [ls_len] own scores, f32 [ctx] weights
+__host__ __device__ inline int off_ls(int ring) { return kOffRegion + region_bytes(ring); }
+inline size_t attn_smem_bytes(int ctx, int cs, int ring) {
+    return size_t(off_ls(ring)) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4;
+}
 
-__device__ __forceinline__ void bar_out() { asm volatile("bar.sync 1, %0;" ::"n"(kOutThreads) : "memory"); }
-
+template <int R>
 __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
                                                    int n_tok, float* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -61,9 +68,9 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     const int ctx = a.max_chunks * kPosChunk;
     float* sq = reinterpret_cast<float*>(smem + kOffQ);
     float* smx = reinterpret_cast<float*>(smem + kOffMax);
-    float* kf = reinterpret_cast<float*>(smem + kOffKf);
-    __half* ring = reinterpret_cast<__half*>(smem + kOffRing);
-    float* LS = reinterpret_cast<float*>(smem + kOffLs);
+    float* kf = reinterpret_cast<float*>(smem + kOffRegion);
+    __half* ring = reinterpret_cast<__half*>(smem + kOffRegion);
+    float* LS = reinterpret_cast<float*>(smem + off_ls(R));
     float* E = LS + ls_len(ctx, CS);
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
@@ -72,20 +79,18 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = __ldcg(pos_dev) + t + 1;
     const int P = (n + CS - 1) / CS, p0 = min(n, r * P), p1 = min(n, p0 + P);
-    const bool leader = r == 0, out_thread = tid < kOutThreads;
+    const bool leader = r == 0, producer = tid >= kOutThreads;
     const int nblk = (n + kVBlk - 1) / kVBlk;
     const __half* V = a.vcache + g * kHd;
-    auto issue_v = [&](int b) {  // V rows [64 b, min(64 b + 64, n)) into slot b % kRing; an empty group past the end
+    auto issue_v = [&](int b) {  // V rows [64 b, min(64 b + 64, n)) into slot b % R (producer threads); empty past the end
         if (b < nblk) {
             const int r0 = b * kVBlk, rows = min(kVBlk, n - r0);
-            __half* dst = ring + (b % kRing) * kVBlk * kHd;
-            for (int i = tid; i < rows * 8; i += kOutThreads)
+            __half* dst = ring + (b % R) * kVBlk * kHd;
+            for (int i = tid - kOutThreads; i < rows * 8; i += kThreads - kOutThreads)
                 cp_async16(dst + (i >> 3) * kHd + (i & 7) * 8, V + size_t(r0 + (i >> 3)) * a.kv_dim + (i & 7) * 8);
         }
         cp_commit();
     };
-    if (leader && out_thread)
-        for (int b = 0; b < kRing - 1; ++b) issue_v(b);
     if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
 
     // ---- 1. scores of [p0, p1), one position per thread
@@ -147,60 +152,71 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
         const float m = s_m;
         for (int j = tid; j < p1 - p0; j += kThreads) lead_E[p0 + j] = exp_ref(fsub(LS[j], m), a.exptab);
     }
-    cluster.sync();
+    // Split cluster barrier: the leader's producer warps request the first V blocks between arrive and wait (the
+    // K tile space is free: every thread passed the barrier after its last score).
+    cluster_arrive();
+    if (leader && producer)
+        for (int b = 0; b < R - 1; ++b) issue_v(b);
+    cluster_wait();
     if (!leader) return;
 
     // ---- 3. leader: ordered sum, normalise, output chains
-    if (tid == 0) {
-        float sum = 0.f;
-        int j = 0;
-        for (; j + 8 <= n; j += 8) {
-            const float4 v0 = *reinterpret_cast<const float4*>(E + j);
-            const float4 v1 = *reinterpret_cast<const float4*>(E + j + 4);
-            sum = fadd(sum, v0.x);
-            sum = fadd(sum, v0.y);
-            sum = fadd(sum, v0.z);
-            sum = fadd(sum, v0.w);
-            sum = fadd(sum, v1.x);
-            sum = fadd(sum, v1.y);
-            sum = fadd(sum, v1.z);
-            sum = fadd(sum, v1.w);
-        }
-        for (; j < n; ++j) sum = fadd(sum, E[j]);
-        s_inv = fdiv(1.0f, sum);
-    }
+    if (tid == 0) s_inv = fdiv(1.0f, ordered_sum(E, n));
     __syncthreads();
     {
         const float iv = s_inv;
         for (int j = tid; j < n; j += kThreads) E[j] = fmul(E[j], iv);
     }
-    __syncthreads();
-    if (!out_thread) return;
+    // V blocks stream through the ring: the producer warps (2-7) only copy; the chain threads (warps 0-1, one lane per
+    // dimension) form a_j * v_jd (the reference's separately rounded multiply) and add it in position order, the next
+    // 16 rows' loads ahead of the current 16 rows' adds.  One barrier per block publishes the landed block and frees
+    // the slot the previous block used.
     float o = 0.f;
-    for (int b = 0; b < nblk; ++b) {
-        issue_v(b + kRing - 1);
-        cp_wait<kRing - 1>();
-        bar_out();
-        const int rows = min(kVBlk, n - b * kVBlk);
-        const float* e = E + b * kVBlk;
-        const __half* v = ring + (b % kRing) * kVBlk * kHd + tid;
-        int j = 0;
-        for (; j + 8 <= rows; j += 8) {
-            float av[8], vv[8];
+    for (int it = 0; it < nblk; ++it) {
+        if (producer) cp_wait<R - 2>();  // V block `it` has landed (for this thread's copies)
+        __syncthreads();
+        if (producer) {
+            issue_v(it + R - 1);  // into the slot block it-1 used, which the chain threads have finished with
+        } else {
+            const int r0 = it * kVBlk, rows = min(kVBlk, n - r0);
+            const __half* v = ring + (it % R) * kVBlk * kHd + tid;
+            const float* e = E + r0;
+            if (rows == kVBlk) {
+                float ac[16], an[16];
+                __half vc[16], vn[16];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                av[k] = e[j + k];
-                vv[k] = __half2float(v[(j + k) * kHd]);
+                for (int k = 0; k < 16; ++k) {
+                    ac[k] = e[k];
+                    vc[k] = v[k * kHd];
+                }
+#pragma unroll
+                for (int g16 = 0; g16 < kVBlk / 16; ++g16) {
+                    if (g16 + 1 < kVBlk / 16) {
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            an[k] = e[(g16 + 1) * 16 + k];
+                            vn[k] = v[((g16 + 1) * 16 + k) * kHd];
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) o = fadd(o, fmul(ac[k], __half2float(vc[k])));
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        ac[k] = an[k];
+                        vc[k] = vn[k];
+                    }
+                }
+            } else {
+                for (int j = 0; j < rows; ++j) o = fadd(o, fmul(e[j], __half2float(v[j * kHd])));
             }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) o = fadd(o, fmul(av[k], vv[k]));
         }
-        for (; j < rows; ++j) o = fadd(o, fmul(e[j], __half2float(v[j * kHd])));
-        bar_out();  // slot b % kRing is free again
     }
-    cp_wait<0>();
-    out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
+    if (producer) cp_wait<0>();
+    else out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
 }
+
+constexpr int kRingDecode = 8;  // V blocks in flight behind a decode token's softmax
+constexpr int kRingBatch = 3;   // multi-token launches: smaller footprint, more CTAs per SM
 
 }  // namespace
 
@@ -208,10 +224,14 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
     if (a.head_dim != kHd || group < 1 || group * a.n_kv != a.n_heads || a.max_chunks < 1) return cudaErrorInvalidValue;
     const int ctx = a.max_chunks * kPosChunk;
-    const int cs = n_tok == 1 ? std::min(kMaxCluster, a.max_chunks) : 1;
-    const size_t smem = attn_smem_bytes(ctx, cs);
+    // Decode: a cluster per head and a deep V ring; multi-token launches: one CTA per (head, token), a short ring.
+    const bool decode = n_tok == 1;
+    const int cs = decode ? std::min(kMaxCluster, a.max_chunks) : 1;
+    const int ring = decode ? kRingDecode : kRingBatch;
+    auto kern = decode ? k_attn<kRingDecode> : k_attn<kRingBatch>;
+    const size_t smem = attn_smem_bytes(ctx, cs, ring);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(cs * a.n_heads), unsigned(n_tok));
@@ -227,7 +247,7 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, k_attn, a, Q, pos_dev, n_tok, out);
+    return cudaLaunchKernelEx(&cfg, kern, a, Q, pos_dev, n_tok, out);
 }
 
 }  // namespace qb

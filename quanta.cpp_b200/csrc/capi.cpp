@@ -6,7 +6,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/quanta_b200.h"
+#include "quanta_b200.h"
 #include "capi_util.h"
 #include "engine.h"
 #include "ops.h"

@@ -114,7 +114,7 @@ __device__ __forceinline__ float penalize(float l, float penalty) { return l > 0
 // the shortlist bound needs (model.cpp:247-251; the int8 squares sum exactly in float).
 __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict__ X, const float* __restrict__ norm_w, int dim,
                                                          float eps, HeadIn hin, HeadState* hs, int full_rows) {
-    __shared__ float sred[32 + 2048];
+    __shared__ __align__(16) float sred[32 + 2048];
     __shared__ __align__(16) int8_t sx[2048];
     __shared__ float sdx[64];
     __shared__ int ssum[64];

@@ -191,17 +191,36 @@ __device__ __forceinline__ void quant_round(float v, int i, int8_t* sx, float* s
 // (engine/src/ops_ref.cpp:195-196): the squares are formed in parallel into sq[], one thread runs the add chain.
 // Any other order changes the last bits of the scale, and those flip int8 activations and f16 cache entries
 // downstream, so this order is kept although the chain costs ~4 cycles per element.
-__device__ __forceinline__ float sumsq_in_order(const float* sq, int n) {
-    float s = 0.f;
+// s = ((s0 + v_0) + v_1) + ... + v_{n-1}: the reference's sequential float sum, on one thread.  The chain of adds is
+// the latency floor, so the loads run one 16-value group ahead of the adds (v 16-byte aligned for the vector path).
+__device__ __forceinline__ float ordered_sum(const float* v, int n, float s = 0.f) {
     int i = 0;
-    for (; i + 8 <= n; i += 8) {
-        float v[8];
+    if (n >= 16 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+        const float4* v4 = reinterpret_cast<const float4*>(v);
+        float4 cur[4], nxt[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = sq[i + k];
+        for (int k = 0; k < 4; ++k) cur[k] = v4[k];
+        for (i = 16; i + 16 <= n; i += 16) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s = fadd(s, v[k]);
+            for (int k = 0; k < 4; ++k) nxt[k] = v4[i / 4 + k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                s = fadd(s, cur[k].x);
+                s = fadd(s, cur[k].y);
+                s = fadd(s, cur[k].z);
+                s = fadd(s, cur[k].w);
+                cur[k] = nxt[k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            s = fadd(s, cur[k].x);
+            s = fadd(s, cur[k].y);
+            s = fadd(s, cur[k].z);
+            s = fadd(s, cur[k].w);
+        }
     }
-    for (; i < n; ++i) s = fadd(s, sq[i]);
+    for (; i < n; ++i) s = fadd(s, v[i]);
     return s;
 }
 
@@ -218,7 +237,7 @@ __device__ __forceinline__ void norm_quant(const float* __restrict__ x, const No
     for (int k = 0; k < kMaxRounds; ++k)
         if (tid + k * T < dim) sq[tid + k * T] = fmul(xv[k], xv[k]);
     __syncthreads();
-    if (tid == 0) sred[0] = sumsq_in_order(sq, dim);
+    if (tid == 0) sred[0] = ordered_sum(sq, dim);
     __syncthreads();
     const float tot = sred[0];
     const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(tot, float(dim)), eps)));

@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
 __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __restrict__ X, const float* __restrict__ norm_w,
                                                               int dim, float eps, int8_t* __restrict__ XQ,
                                                               float* __restrict__ DX) {
-    __shared__ float sred[32 + 2048];
+    __shared__ __align__(16) float sred[32 + 2048];
     pdl_launch_dependents();
     NormW nw;
     if (norm_w) load_norm_w(norm_w, dim, nw);

@@ -10,7 +10,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/quanta_b200.h"
+#include "quanta_b200.h"
 #include "capi_util.h"
 #include "head_kernels.h"
 

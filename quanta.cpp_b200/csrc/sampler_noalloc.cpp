@@ -7,7 +7,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "../../include/quanta_b200.h"
+#include "quanta_b200.h"
 #include "capi_util.h"
 #include "head_kernels.h"
 
