@@ -27,83 +27,141 @@
 namespace qb {
 
 constexpr int kHeadThreads = 512;
+// Rows per streamed tile = threads per CTA of the row-per-thread head passes.
+__host__ __device__ constexpr int head_tile_rows(int dtype) { return dtype == DT_Q4_0 ? 128 : 64; }
 constexpr int kHeadWarps = kHeadThreads / 32;
 constexpr int kStages = 4;
 
-// ---------------------------------------------------------------- warp top-K lists (K <= 32)
+// ---------------------------------------------------------------- candidate lists (K <= 32), kept with bitonic networks
 
 __device__ __forceinline__ bool better(float av, int aid, float bv, int bid) {
     return av > bv || (av == bv && aid < bid);
 }
 
-// Sorted list, lane i holds the i-th best (lanes >= K hold sentinels).
-struct WarpTopK {
+// ---- merging sorted candidate lists (K <= 32, best first, sentinels {-inf, INT_MAX} past the valid entries)
+
+// Sorts a bitonic warp-wide sequence (one candidate per lane) best-first: five half-cleaner stages over shuffles.
+__device__ __forceinline__ void warp_bitonic_to_sorted(float& v, int& id) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const float pv = __shfl_xor_sync(0xffffffffu, v, s);
+        const int pid = __shfl_xor_sync(0xffffffffu, id, s);
+        const bool keep_better = (lane & s) == 0;
+        if (keep_better == better(pv, pid, v, id)) {
+            v = pv;
+            id = pid;
+        }
+    }
+}
+
+// (v, id) and (bv, bid) are warp-wide lists sorted best-first; leaves the best 32 of their union in (v, id), sorted.
+// The lane-wise better of A and reversed B is bitonic and holds the top 32 of A u B.
+__device__ __forceinline__ void warp_merge_top(float& v, int& id, float bv, int bid) {
+    const int lane = threadIdx.x & 31;
+    const float rv = __shfl_sync(0xffffffffu, bv, 31 - lane);
+    const int rid = __shfl_sync(0xffffffffu, bid, 31 - lane);
+    if (better(rv, rid, v, id)) {
+        v = rv;
+        id = rid;
+    }
+    warp_bitonic_to_sorted(v, id);
+}
+
+// Sorts one candidate per lane best-first (bitonic sorting network over shuffles).
+__device__ __forceinline__ void warp_bitonic_sort(float& v, int& id) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float pv = __shfl_xor_sync(0xffffffffu, v, j);
+            const int pid = __shfl_xor_sync(0xffffffffu, id, j);
+            const bool keep_better = ((lane & j) == 0) == ((lane & k) == 0);  // k-blocks alternate best-first / worst-first
+            if (keep_better == better(pv, pid, v, id)) {
+                v = pv;
+                id = pid;
+            }
+        }
+    }
+}
+
+// A warp's running list: lane i holds the i-th best candidate so far (sentinels {-inf, INT_MAX} past the filled part).
+struct WarpTop32 {
     float v;
     int id;
     __device__ void init() {
         v = -INFINITY;
         id = INT_MAX;
     }
-    // Offer one candidate per lane (valid lanes only); K <= 32.  Whole warp.
+    // One candidate per lane (valid lanes only).  Candidates that do not beat the current K-th best cannot enter the
+    // final best K; the others are sorted and merged in (the list keeps the best 32, a superset of the best K).
     __device__ void offer(float cv, int cid, bool valid, int K) {
-        const int lane = threadIdx.x & 31;
-        float tv = __shfl_sync(0xffffffffu, v, K - 1);
-        int tid = __shfl_sync(0xffffffffu, id, K - 1);
-        unsigned m = __ballot_sync(0xffffffffu, valid && better(cv, cid, tv, tid));
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const float xv = __shfl_sync(0xffffffffu, cv, src);
-            const int xid = __shfl_sync(0xffffffffu, cid, src);
-            if (!better(xv, xid, tv, tid)) continue;  // threshold moved up meanwhile
-            const unsigned ahead = __ballot_sync(0xffffffffu, lane < K && better(v, id, xv, xid));
-            const int p = __popc(ahead);
-            const float uv = __shfl_up_sync(0xffffffffu, v, 1);
-            const int uid = __shfl_up_sync(0xffffffffu, id, 1);
-            if (lane > p && lane < K) {
-                v = uv;
-                id = uid;
-            } else if (lane == p) {
-                v = xv;
-                id = xid;
-            }
-            tv = __shfl_sync(0xffffffffu, v, K - 1);
-            tid = __shfl_sync(0xffffffffu, id, K - 1);
+        const float tv = __shfl_sync(0xffffffffu, v, K - 1);
+        const int tid = __shfl_sync(0xffffffffu, id, K - 1);
+        const bool beat = valid && better(cv, cid, tv, tid);
+        if (__any_sync(0xffffffffu, beat)) {
+            float nv = beat ? cv : -INFINITY;
+            int nid = beat ? cid : INT_MAX;
+            warp_bitonic_sort(nv, nid);
+            warp_merge_top(v, id, nv, nid);
         }
     }
 };
 
-// Merges the CTA's per-warp lists into warp 0's list, written to slist[0..32) (slist: nwarps * 32 entries).
-__device__ void cta_merge_lists(WarpTopK& L, int K, Cand* slist) {
+// Merges the CTA's warp lists into slist[0..32), best first, sentinels past K.  slist: (blockDim / 32) * 32 entries,
+// blockDim / 32 a power of two.
+__device__ void cta_merge_lists(WarpTop32& L, int K, Cand* slist) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     __syncthreads();
     slist[warp * 32 + lane] = Cand{L.v, L.id};
     __syncthreads();
-    if (warp == 0) {
-        for (int w = 1; w < nw; ++w) {
-            const Cand c = slist[w * 32 + lane];
-            L.offer(c.v, c.id, lane < K && c.id != INT_MAX, K);
+    for (int half = nw / 2; half >= 1; half >>= 1) {
+        if (warp < half) {
+            const Cand c = slist[(warp + half) * 32 + lane];
+            warp_merge_top(L.v, L.id, c.v, c.id);
+            slist[warp * 32 + lane] = Cand{L.v, L.id};
         }
-        slist[lane] = Cand{L.v, L.id};
+        __syncthreads();
     }
+    if (warp == 0 && lane >= K) slist[lane] = Cand{-INFINITY, INT_MAX};
     __syncthreads();
 }
 
-// Merges n candidates from global memory into the CTA's best K (slist[0..K)).
-__device__ void cta_merge_global(const Cand* __restrict__ src, int n, int K, Cand* slist) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    WarpTopK L;
-    L.init();
-    for (int base = warp * 32; base < n; base += blockDim.x) {
-        const int i = base + lane;
-        Cand c{-INFINITY, INT_MAX};
-        if (i < n) {
-            c.v = __ldcg(&src[i].v);
-            c.id = __ldcg(&src[i].id);
+// Best K of n_lists sorted lists of K candidates each (global memory, written by other kernels) into slist[0..32),
+// best first.  Each warp merges its share of the lists in registers, then a tree over the warps' results.
+// slist: (blockDim / 32) * 32 entries; blockDim / 32 a power of two.
+__device__ void cta_merge_sorted(const Cand* __restrict__ src, int n_lists, int K, Cand* slist) {
+    constexpr int kBatch = 8;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float v = -INFINITY;
+    int id = INT_MAX;
+    for (int l0 = warp; l0 < n_lists; l0 += kBatch * nw) {
+        float bv[kBatch];
+        int bid[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {  // loads first: one list per batch slot
+            const int l = l0 + u * nw;
+            const bool ok = l < n_lists && lane < K;
+            bv[u] = ok ? __ldcg(&src[size_t(l) * K + lane].v) : -INFINITY;
+            bid[u] = ok ? __ldcg(&src[size_t(l) * K + lane].id) : INT_MAX;
         }
-        L.offer(c.v, c.id, i < n && c.id != INT_MAX, K);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (l0 + u * nw < n_lists) warp_merge_top(v, id, bv[u], bid[u]);
     }
-    cta_merge_lists(L, K, slist);
+    slist[warp * 32 + lane] = Cand{v, id};
+    __syncthreads();
+    for (int half = nw / 2; half >= 1; half >>= 1) {
+        if (warp < half) {
+            const Cand c = slist[(warp + half) * 32 + lane];
+            warp_merge_top(v, id, c.v, c.id);
+            slist[warp * 32 + lane] = Cand{v, id};
+        }
+        __syncthreads();
+    }
+    if (lane >= K && warp == 0) slist[lane] = Cand{-INFINITY, INT_MAX};  // keep exactly the best K
+    __syncthreads();
 }
 
 __device__ __forceinline__ float penalize(float l, float penalty) { return l > 0.f ? fdiv(l, penalty) : fmul(l, penalty); }
@@ -143,13 +201,23 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
     }
 }
 
-// Activation of the head in shared memory.
+// Activation of the head in shared memory: sx [cols] int8, then sdx, ssum, sxn [cols/32] (sxn: coarse pass only).
 struct HeadAct {
     int8_t* sx;
     float* sdx;
     int* ssum;
     float* sxn;
 };
+
+__device__ __forceinline__ HeadAct carve_act(unsigned char* smem, int cols, bool with_norm) {
+    const int nb = cols / QK;
+    HeadAct a;
+    a.sx = reinterpret_cast<int8_t*>(smem);
+    a.sdx = reinterpret_cast<float*>(smem + cols);
+    a.ssum = reinterpret_cast<int*>(a.sdx + nb);
+    a.sxn = with_norm ? reinterpret_cast<float*>(a.ssum + nb) : nullptr;
+    return a;
+}
 
 // Every read of data another kernel wrote goes through L2 (__ldcg): a kernel started early by programmatic dependent
 // launch may find stale lines of it in its SM's L1.
@@ -164,126 +232,140 @@ __device__ __forceinline__ void load_head_act(const HeadIn& hin, int cols, const
     __syncthreads();
 }
 
-// Block terms of nrows rows whose quants / scales sit contiguously in shared memory (row stride rb / nb halves).
+// One row's exact logit from its quants (16-byte granules, wq) and fp16 block scales (four per 8-byte load, wd) in
+// shared memory: acc = acc + (float(s_b) * dw_b) * dx_b in block order, as matvec_q_ref.  nb % 4 == 0.
 template <int DT>
-__device__ __forceinline__ void smem_terms(const uint8_t* sq, const __half* sd, int nrows, int cpr, unsigned cpr_magic, int nb,
-                                           int tstride, const HeadAct& a, float* sterm) {
-    const int total = nrows * cpr;
-    for (int base = 0; base < total; base += blockDim.x) {
-        const int f = base + threadIdx.x;
-        const bool ok = f < total;
-        const unsigned r = fast_div(unsigned(ok ? f : 0), cpr_magic);
-        const int c = (ok ? f : 0) - int(r) * cpr;
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (ok) w = reinterpret_cast<const uint4*>(sq)[f];
-        if (DT == DT_Q8_0) {
-            int s = ok ? chunk_dot<DT>(w, a.sx, c) : 0;
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            if (ok && !(c & 1)) {
-                const int b = c >> 1;
-                sterm[int(r) * tstride + b] = block_term(s, __half2float(sd[int(r) * nb + b]), a.sdx[b]);
-            }
-        } else if (ok) {
-            const int s = chunk_dot<DT>(w, a.sx, c) - 8 * a.ssum[c];
-            sterm[int(r) * tstride + c] = block_term(s, __half2float(sd[int(r) * nb + c]), a.sdx[c]);
+__device__ __forceinline__ float smem_row_value(const uint4* wq, const uint2* wd, const HeadAct& a, int nb) {
+    float acc = 0.f;
+#pragma unroll 2
+    for (int b4 = 0; b4 < nb; b4 += 4) {
+        const uint2 d4 = wd[b4 >> 2];
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&d4.x));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&d4.y));
+        const float dw[4] = {f01.x, f01.y, f23.x, f23.y};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int b = b4 + k;
+            int s;
+            if (DT == DT_Q4_0)
+                s = chunk_dot<DT>(wq[b], a.sx, b) - 8 * a.ssum[b];
+            else
+                s = chunk_dot<DT>(wq[2 * b], a.sx, 2 * b) + chunk_dot<DT>(wq[2 * b + 1], a.sx, 2 * b + 1);
+            acc = fadd(acc, block_term(s, dw[k], a.sdx[b]));
         }
     }
+    return acc;
+}
+
+// The shortlist bound B = (sum_b err_b * |x_b| in block order) * 1.001 + 1e-5 (engine/src/model.cpp:271-277).
+__device__ __forceinline__ float smem_row_bound(const uint2* we, const float* sxn, int nb) {
+    float bound = 0.f;
+#pragma unroll 2
+    for (int b4 = 0; b4 < nb; b4 += 4) {
+        const uint2 e4 = we[b4 >> 2];
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&e4.x));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&e4.y));
+        const float e[4] = {f01.x, f01.y, f23.x, f23.y};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) bound = fadd(bound, fmul(e[k], sxn[b4 + k]));
+    }
+    return fadd(fmul(bound, 1.001f), 1e-5f);
+}
+
+__device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n groups are pending (n in 0..3)
+    if (n <= 0) cp_wait<0>();
+    else if (n == 1) cp_wait<1>();
+    else if (n == 2) cp_wait<2>();
+    else cp_wait<3>();
 }
 
 // ---------------------------------------------------------------- streaming pass over all rows (full / coarse)
 
+// One persistent CTA per SM streams its contiguous tiles of head_tile_rows rows through a cp.async ring; one thread
+// owns one row of a tile and chains its blocks in order straight from shared memory (row stride padded by 16 bytes so
+// the 16-byte loads of a warp hit distinct banks).
 // mode 0 (full head): logits = exact rows of W (Q8_0 or Q4_0); with n_list > 0 each CTA also writes its best n_list
 //   rows among [0, n_valid) after the repetition penalty of marked rows, and clears those marks.
 // mode 1 (coarse): W = quanta.head_q4; coarse / upper / logits = -inf, and each CTA's best n_list coarse scores among
 //   valid unmarked rows (the seeds).
 template <int DT, int MODE>
-__global__ void __launch_bounds__(kHeadThreads, 1) k_head_stream(DMat W, const __half* __restrict__ err, HeadIn hin,
-                                                                 StreamPlan sp, int n_valid, int n_list, int penal,
-                                                                 float penalty, unsigned char* __restrict__ mark,
-                                                                 float* __restrict__ logits, float* __restrict__ coarse,
-                                                                 float* __restrict__ upper, Cand* __restrict__ lists) {
+__global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
+                                                                     StreamPlan sp, int n_valid, int n_list, int penal,
+                                                                     float penalty, unsigned char* __restrict__ mark,
+                                                                     float* __restrict__ logits, float* __restrict__ coarse,
+                                                                     float* __restrict__ upper, Cand* __restrict__ lists) {
+    constexpr int TR = head_tile_rows(DT);
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ Cand slist[kHeadWarps * 32];
+    __shared__ Cand slist[TR];
     pdl_launch_dependents();
-    const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16;
-    const int TR = sp.tile_rows, tstride = nb | 1;
-    HeadAct act;
-    act.sx = reinterpret_cast<int8_t*>(smem);
-    act.sdx = reinterpret_cast<float*>(smem + sp.act_bytes - nb * 12);
-    act.ssum = reinterpret_cast<int*>(act.sdx + nb);
-    act.sxn = reinterpret_cast<float*>(act.ssum + nb);
-    float* sterm = reinterpret_cast<float*>(smem + sp.act_bytes);
+    const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16, S = sp.stages;
+    const HeadAct act = carve_act(smem, cols, MODE == 1);
     unsigned char* ring = smem + sp.ring_off;
     const int ta = int((long long)blockIdx.x * sp.n_tiles / gridDim.x);
     const int tb = int((long long)(blockIdx.x + 1) * sp.n_tiles / gridDim.x);
 
     auto issue = [&](int t) {
         if (t < tb) {
-            unsigned char* st = ring + size_t((t - ta) % kStages) * sp.stage_bytes;
+            unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
             const int row0 = t * TR, nrows = min(TR, W.rows - row0);
             const uint8_t* qsrc = W.q + size_t(row0) * rb;
-            for (int c = threadIdx.x; c < nrows * cpr; c += blockDim.x) cp_async16(st + c * 16, qsrc + size_t(c) * 16);
+            for (int c = threadIdx.x; c < nrows * cpr; c += TR) {
+                const int rr = int(fast_div(unsigned(c), sp.cpr_magic));
+                cp_async16(st + rr * sp.qstride + (c - rr * cpr) * 16, qsrc + size_t(c) * 16);
+            }
             const uint8_t* dsrc = reinterpret_cast<const uint8_t*>(W.d) + size_t(row0) * nb * 2;
             const int dch = (nrows * nb * 2 + 15) / 16;  // may read up to 15 bytes of the allocation's tail padding
-            for (int c = threadIdx.x; c < dch; c += blockDim.x) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
+            for (int c = threadIdx.x; c < dch; c += TR) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
             if (MODE == 1) {
                 const uint8_t* esrc = reinterpret_cast<const uint8_t*>(err) + size_t(row0) * nb * 2;
-                for (int c = threadIdx.x; c < dch; c += blockDim.x) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
+                for (int c = threadIdx.x; c < dch; c += TR) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
             }
         }
         cp_commit();
     };
 
-#pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) issue(ta + s);
+    for (int s = 0; s < S - 1; ++s) issue(ta + s);
     pdl_wait();
     load_head_act(hin, cols, act);
 
-    WarpTopK L;
+    WarpTop32 L;
     L.init();
+    const int r = threadIdx.x;
     for (int t = ta; t < tb; ++t) {
-        issue(t + kStages - 1);
-        cp_wait<kStages - 1>();
+        issue(t + S - 1);
+        cp_wait_upto(S - 1);
         __syncthreads();
-        const unsigned char* st = ring + size_t((t - ta) % kStages) * sp.stage_bytes;
+        const unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
         const int row0 = t * TR, nrows = min(TR, W.rows - row0);
-        smem_terms<DT>(st, reinterpret_cast<const __half*>(st + sp.d_off), nrows, cpr, sp.cpr_magic, nb, tstride, act, sterm);
-        __syncthreads();
-        for (int base = 0; base < TR; base += blockDim.x) {  // TR <= blockDim: one pass
-            const int r = base + threadIdx.x;
-            float cv = -INFINITY;
-            int row = INT_MAX;
-            bool ok = false;
-            if (r < nrows) {
-                row = row0 + r;
-                const float v = row_sum(sterm + r * tstride, nb);
-                if (MODE == 0) {
-                    logits[row] = v;
-                    cv = v;
-                    if (n_list > 0) {
-                        ok = row < n_valid;
-                        if (penal) {
-                            const unsigned char mk = __ldcg(mark + row);
-                            if (mk) {
-                                cv = penalize(v, penalty);
-                                mark[row] = 0;
-                            }
+        float cv = -INFINITY;
+        int row = INT_MAX;
+        bool ok = false;
+        if (r < nrows) {
+            row = row0 + r;
+            const float v = smem_row_value<DT>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
+                                               reinterpret_cast<const uint2*>(st + sp.d_off + r * nb * 2), act, nb);
+            cv = v;
+            if (MODE == 0) {
+                logits[row] = v;
+                if (n_list > 0) {
+                    ok = row < n_valid;
+                    if (penal) {
+                        const unsigned char mk = __ldcg(mark + row);
+                        if (mk) {
+                            cv = penalize(v, penalty);
+                            mark[row] = 0;
                         }
                     }
-                } else {
-                    const __half* e = reinterpret_cast<const __half*>(st + sp.e_off) + size_t(r) * nb;
-                    float bound = 0.f;
-                    for (int b = 0; b < nb; ++b) bound = fadd(bound, fmul(__half2float(e[b]), act.sxn[b]));
-                    bound = fadd(fmul(bound, 1.001f), 1e-5f);
-                    coarse[row] = v;
-                    upper[row] = fadd(v, bound);
-                    logits[row] = -INFINITY;
-                    cv = v;
-                    ok = row < n_valid && __ldcg(mark + row) == 0;
                 }
+            } else {
+                const float bound = smem_row_bound(reinterpret_cast<const uint2*>(st + sp.e_off + r * nb * 2), act.sxn, nb);
+                coarse[row] = v;
+                upper[row] = fadd(v, bound);
+                logits[row] = -INFINITY;
+                ok = row < n_valid && __ldcg(mark + row) == 0;
             }
-            if (n_list > 0) L.offer(cv, row, ok, n_list);
         }
+        if (n_list > 0) L.offer(cv, row, ok, n_list);
         __syncthreads();  // this stage is refilled by the next iteration's issue()
     }
     cp_wait<0>();
@@ -353,7 +435,7 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
         reinterpret_cast<int4*>(sx)[i] = __ldcg(reinterpret_cast<const int4*>(hin.xq) + i);
     for (int b = threadIdx.x; b < nb; b += blockDim.x) sdx[b] = __ldcg(hin.dx + b);
-    cta_merge_global(seed_lists, n_lists * n_seed, n_seed, slist);
+    cta_merge_sorted(seed_lists, n_lists, n_seed, slist);
     if (threadIdx.x == 0) {
         int n = 0;
         while (n < n_seed && slist[n].id != INT_MAX) ++n;
@@ -388,23 +470,21 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     }
 }
 
-// Candidate scan over this CTA's contiguous rows, exact logits of the wanted rows (gathered through the cp.async ring),
-// optional sampler stage 1, mark clearing.
-__global__ void __launch_bounds__(kHeadThreads, 1) k_sl_cands(DMat W8, HeadIn hin, StreamPlan sp, int n_valid, int n_list,
-                                                              int penal, float penalty, unsigned char* __restrict__ mark,
-                                                              const float* __restrict__ upper, float* __restrict__ logits,
-                                                              HeadState* __restrict__ hs, Cand* __restrict__ lists) {
+// Candidate scan over this CTA's contiguous rows, exact logits of the wanted rows (gathered through the cp.async ring,
+// one row per thread), optional sampler stage 1, mark clearing.
+__global__ void __launch_bounds__(head_tile_rows(DT_Q8_0), 1) k_sl_cands(DMat W8, HeadIn hin, StreamPlan sp, int n_valid,
+                                                                         int n_list, int penal, float penalty,
+                                                                         unsigned char* __restrict__ mark,
+                                                                         const float* __restrict__ upper,
+                                                                         float* __restrict__ logits,
+                                                                         HeadState* __restrict__ hs, Cand* __restrict__ lists) {
+    constexpr int TR = head_tile_rows(DT_Q8_0);
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ Cand slist[kHeadWarps * 32];
+    __shared__ Cand slist[TR];
     __shared__ int s_count;
     pdl_launch_dependents();
-    const int cols = W8.cols, nb = cols / QK, cpr = cols / 16, TR = sp.tile_rows, tstride = nb | 1;
-    HeadAct act;
-    act.sx = reinterpret_cast<int8_t*>(smem);
-    act.sdx = reinterpret_cast<float*>(smem + sp.act_bytes - nb * 12);
-    act.ssum = reinterpret_cast<int*>(act.sdx + nb);
-    act.sxn = nullptr;
-    float* sterm = reinterpret_cast<float*>(smem + sp.act_bytes);
+    const int cols = W8.cols, nb = cols / QK, cpr = cols / 16, S = sp.stages;
+    const HeadAct act = carve_act(smem, cols, false);
     int* list = reinterpret_cast<int*>(smem + sp.list_off);
     unsigned char* ring = smem + sp.ring_off;
     const int V = W8.rows;
@@ -415,7 +495,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_sl_cands(DMat W8, HeadIn hi
     const float tau = __ldcg(&hs->tau);
     const int lane = threadIdx.x & 31;
     // scan + compaction (order inside the list does not affect any value)
-    for (int base = r0; base < r1; base += blockDim.x) {
+    for (int base = r0; base < r1; base += TR) {
         const int r = base + threadIdx.x;
         bool want = false;
         if (r < r1 && r < n_valid) {
@@ -431,43 +511,42 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_sl_cands(DMat W8, HeadIn hi
     __syncthreads();
     const int n = s_count;
     const int n_tiles = (n + TR - 1) / TR;
+    const int dpr = nb / 4;  // 8-byte scale groups per row (rows of scales are 8-byte aligned, not 16)
     auto issue = [&](int t) {
         if (t < n_tiles) {
-            unsigned char* st = ring + size_t(t % kStages) * sp.stage_bytes;
+            unsigned char* st = ring + size_t(t % S) * sp.stage_bytes;
             const int nrows = min(TR, n - t * TR);
-            for (int c = threadIdx.x; c < nrows * cpr; c += blockDim.x) {
-                const int rr = c / cpr, cc = c - rr * cpr;
-                cp_async16(st + c * 16, W8.q + size_t(list[t * TR + rr]) * cols + size_t(cc) * 16);
+            for (int c = threadIdx.x; c < nrows * cpr; c += TR) {
+                const int rr = int(fast_div(unsigned(c), sp.cpr_magic)), cc = c - rr * cpr;
+                cp_async16(st + rr * sp.qstride + cc * 16, W8.q + size_t(list[t * TR + rr]) * cols + size_t(cc) * 16);
             }
-            const int half_pairs = nb / 2;  // fp16 scales copied 4 bytes at a time (rows are not 16-byte aligned)
-            for (int c = threadIdx.x; c < nrows * half_pairs; c += blockDim.x) {
-                const int rr = c / half_pairs, cc = c - rr * half_pairs;
-                cp_async4(st + sp.d_off + (rr * nb + 2 * cc) * 2,
-                          reinterpret_cast<const uint8_t*>(W8.d) + (size_t(list[t * TR + rr]) * nb + 2 * cc) * 2);
+            for (int c = threadIdx.x; c < nrows * dpr; c += TR) {
+                const int rr = c / dpr, cc = c - rr * dpr;
+                cp_async8(st + sp.d_off + (rr * nb + 4 * cc) * 2,
+                          reinterpret_cast<const uint8_t*>(W8.d) + (size_t(list[t * TR + rr]) * nb + 4 * cc) * 2);
             }
         }
         cp_commit();
     };
-#pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) issue(s);
+    for (int s = 0; s < S - 1; ++s) issue(s);
     for (int t = 0; t < n_tiles; ++t) {
-        issue(t + kStages - 1);
-        cp_wait<kStages - 1>();
+        issue(t + S - 1);
+        cp_wait_upto(S - 1);
         __syncthreads();
-        const unsigned char* st = ring + size_t(t % kStages) * sp.stage_bytes;
+        const unsigned char* st = ring + size_t(t % S) * sp.stage_bytes;
         const int nrows = min(TR, n - t * TR);
-        smem_terms<DT_Q8_0>(st, reinterpret_cast<const __half*>(st + sp.d_off), nrows, cpr, sp.cpr_magic, nb, tstride, act,
-                            sterm);
-        __syncthreads();
-        if (int(threadIdx.x) < nrows) logits[list[t * TR + threadIdx.x]] = row_sum(sterm + threadIdx.x * tstride, nb);
+        if (int(threadIdx.x) < nrows)
+            logits[list[t * TR + threadIdx.x]] =
+                smem_row_value<DT_Q8_0>(reinterpret_cast<const uint4*>(st + threadIdx.x * sp.qstride),
+                                        reinterpret_cast<const uint2*>(st + sp.d_off + threadIdx.x * nb * 2), act, nb);
         __syncthreads();
     }
     cp_wait<0>();
     __syncthreads();
     // sampler stage 1 over every exact row of the range (seeds, must rows, candidates), marks cleared
-    WarpTopK L;
+    WarpTop32 L;
     L.init();
-    for (int base = r0; base < r1; base += blockDim.x) {
+    for (int base = r0; base < r1; base += TR) {
         const int r = base + threadIdx.x;
         bool ok = false;
         float cv = -INFINITY;
@@ -502,7 +581,7 @@ __global__ void __launch_bounds__(kThreads) k_topk_partial(const float* logits, 
     __shared__ Cand slist[kWarps * 32];
     pdl_launch_dependents();
     pdl_wait();
-    WarpTopK L;
+    WarpTop32 L;
     L.init();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = int((long long)blockIdx.x * n_valid / gridDim.x), r1 = int((long long)(blockIdx.x + 1) * n_valid / gridDim.x);
@@ -539,19 +618,22 @@ __global__ void __launch_bounds__(kHeadThreads) k_sample_final(const Cand* __res
     __shared__ Cand slist[kHeadWarps * 32];
     pdl_launch_dependents();
     pdl_wait();
-    cta_merge_global(parts, n_lists * K, K, slist);
-    if (threadIdx.x != 0) return;
-    int n = 0;
-    while (n < K && slist[n].id != INT_MAX) ++n;
-    int pick = n > 0 ? slist[0].id : 0;
-    if (sa.temperature > 0.f && n > 0) {
-        float p[32];
+    __shared__ float p[32];
+    cta_merge_sorted(parts, n_lists, K, slist);
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const int n = __popc(__ballot_sync(0xffffffffu, lane < K && slist[lane].id != INT_MAX));  // valid entries form a prefix
+    const bool draw = sa.temperature > 0.f && n > 0;
+    if (draw) {  // the n exps in parallel, one per lane
         const float mx = slist[0].v;
+        p[lane] = lane < n ? exp_ref(fdiv(fsub(slist[lane].v, mx), sa.temperature), sa.exptab) : 0.f;
+    }
+    __syncwarp();
+    if (lane != 0) return;
+    int pick = n > 0 ? slist[0].id : 0;
+    if (draw) {
         float sum = 0.f;
-        for (int i = 0; i < n; ++i) {
-            p[i] = exp_ref(fdiv(fsub(slist[i].v, mx), sa.temperature), sa.exptab);
-            sum = fadd(sum, p[i]);
-        }
+        for (int i = 0; i < n; ++i) sum = fadd(sum, p[i]);
         for (int i = 0; i < n; ++i) p[i] = fdiv(p[i], sum);
         int keep = n;
         if (sa.min_p > 0.f) {
@@ -605,20 +687,24 @@ size_t align16(size_t n) { return (n + 15) & ~size_t(15); }
 StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather) {
     StreamPlan p;
     const int rb = row_bytes_host(dtype, cols), cpr = rb / 16, nb = cols / QK;
-    int tr = (kHeadThreads * 4) / cpr;  // ~4 chunks per thread per tile
-    tr = std::max(8, std::min(tr, kHeadThreads) / 8 * 8);
+    const int tr = head_tile_rows(dtype);
     p.tile_rows = tr;
+    p.threads = tr;
     p.n_tiles = (rows + tr - 1) / tr;
     p.cpr_magic = div_magic(unsigned(cpr));
-    p.d_off = int(align16(size_t(tr) * rb));
+    p.qstride = rb + 16;
+    p.d_off = int(align16(size_t(tr) * p.qstride));
     p.e_off = int(p.d_off + align16(size_t(tr) * nb * 2 + 16));
     p.stage_bytes = int(coarse ? p.e_off + align16(size_t(tr) * nb * 2 + 16) : p.e_off);
-    p.act_bytes = int(align16(size_t(cols) + size_t(nb) * 12));
-    const size_t term_bytes = align16(size_t(tr) * (nb | 1) * 4);
-    p.list_off = int(p.act_bytes + term_bytes);
+    const size_t act_bytes = align16(size_t(cols) + size_t(nb) * 12);
     const size_t list_bytes = gather ? align16(size_t((rows + grid - 1) / grid + 64) * 4) : 0;
-    p.ring_off = int((p.list_off + list_bytes + 127) / 128 * 128);
-    p.smem = size_t(p.ring_off) + size_t(kStages) * p.stage_bytes;
+    p.list_off = int(act_bytes);
+    p.ring_off = int((act_bytes + list_bytes + 127) / 128 * 128);
+    const size_t budget = 227 * 1024 - size_t(tr) * sizeof(Cand) - 64;  // minus the kernels' static shared memory
+    const size_t fit = budget > size_t(p.ring_off) ? (budget - p.ring_off) / size_t(p.stage_bytes) : 0;
+    p.stages = int(std::min<size_t>(4, fit));
+    if (p.stages < 2 || nb % 4 != 0) p.stages = 0;
+    p.smem = size_t(p.ring_off) + size_t(p.stages) * p.stage_bytes;
     p.grid = grid;
     return p;
 }
@@ -630,13 +716,13 @@ cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, floa
 }
 
 cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl) {
-    if (a.n_list > 32) return cudaErrorInvalidValue;
+    if (a.plan.stages == 0) return cudaErrorInvalidValue;
     if (a.W.dtype == DT_Q8_0)
-        return launch_pdl(k_head_stream<DT_Q8_0, 0>, dim3(a.plan.grid), dim3(kHeadThreads), a.plan.smem, st, pdl, a.W,
+        return launch_pdl(k_head_rows<DT_Q8_0, 0>, dim3(a.plan.grid), dim3(a.plan.threads), a.plan.smem, st, pdl, a.W,
                           (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
                           (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
     if (a.W.dtype == DT_Q4_0)
-        return launch_pdl(k_head_stream<DT_Q4_0, 0>, dim3(a.plan.grid), dim3(kHeadThreads), a.plan.smem, st, pdl, a.W,
+        return launch_pdl(k_head_rows<DT_Q4_0, 0>, dim3(a.plan.grid), dim3(a.plan.threads), a.plan.smem, st, pdl, a.W,
                           (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
                           (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
     return cudaErrorInvalidValue;
@@ -644,18 +730,19 @@ cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStrea
 
 cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl, int* kernels) {
     const int n_seed = a.k + 8;
-    if (a.k < 1 || n_seed > 32 || a.W8.cols > 4096 || a.n_list > 32) return cudaErrorInvalidValue;
+    if (a.k < 1 || n_seed > 32 || a.W8.cols > 4096 || a.n_list > 32 || a.plan4.stages == 0 || a.plan8g.stages == 0)
+        return cudaErrorInvalidValue;
     cudaError_t e = launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, a.must, a.n_must_dev, a.n_must_host, a.window,
                                a.n_valid, a.mark);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_head_stream<DT_Q4_0, 1>, dim3(a.plan4.grid), dim3(kHeadThreads), a.plan4.smem, st, pdl, a.W4, a.err, hin,
+    e = launch_pdl(k_head_rows<DT_Q4_0, 1>, dim3(a.plan4.grid), dim3(a.plan4.threads), a.plan4.smem, st, pdl, a.W4, a.err, hin,
                    a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark, a.logits, a.coarse, a.upper,
                    reinterpret_cast<Cand*>(a.seed_buf));
     if (e != cudaSuccess) return e;
     e = launch_pdl(k_sl_seeds, dim3(1), dim3(kHeadThreads), 0, st, pdl, a.W8, hin, (const Cand*)a.seed_buf, a.plan4.grid,
                    n_seed, a.k, a.mark, a.logits, a.hs);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_sl_cands, dim3(a.plan8g.grid), dim3(kHeadThreads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
+    e = launch_pdl(k_sl_cands, dim3(a.plan8g.grid), dim3(a.plan8g.threads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
                    a.n_list, a.penal, a.penalty, a.mark, (const float*)a.upper, a.logits, a.hs,
                    reinterpret_cast<Cand*>(a.lists));
     if (kernels) *kernels += 4;

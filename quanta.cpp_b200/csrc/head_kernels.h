@@ -30,17 +30,18 @@ struct HeadState {
     int pad;
 };
 
-// Tiling of a streamed head pass (rows in tiles of tile_rows, tiles split over `grid` persistent CTAs, each tile staged
-// in a shared-memory ring slot of stage_bytes: quants at 0, scales at d_off, bounds at e_off).
+// Tiling of a streamed head pass: rows in tiles of tile_rows (one thread per row), tiles split over `grid` persistent
+// CTAs, each tile staged in one of `stages` shared-memory ring slots of stage_bytes: quants at 0 with a row stride of
+// qstride bytes (the row padded by 16 bytes), fp16 scales at d_off, bound errors at e_off (coarse pass).
 struct StreamPlan {
-    int tile_rows = 0, n_tiles = 0;
+    int tile_rows = 0, n_tiles = 0, threads = 0;
     unsigned cpr_magic = 0;
-    int d_off = 0, e_off = 0, stage_bytes = 0;
-    int act_bytes = 0, list_off = 0, ring_off = 0;
+    int qstride = 0, d_off = 0, e_off = 0, stage_bytes = 0, stages = 0;
+    int list_off = 0, ring_off = 0;
     size_t smem = 0;
     int grid = 0;
 };
-// coarse: stage the bounds too; gather: room for the CTA's compacted row list.
+// coarse: stage the bounds too; gather: room for the CTA's compacted row list.  stages == 0 when it cannot fit.
 StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather);
 
 struct HeadFullArgs {
