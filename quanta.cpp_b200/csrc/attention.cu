@@ -74,8 +74,8 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     float* E = LS + ls_len(ctx, CS);
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = __ldcg(pos_dev) + t + 1;
     const int P = (n + CS - 1) / CS, p0 = min(n, r * P), p1 = min(n, p0 + P);

@@ -27,8 +27,11 @@
 namespace qb {
 
 constexpr int kHeadThreads = 512;
-// Rows per streamed tile = threads per CTA of the row-per-thread head passes.
+// Head passes: a tile of head_tile_rows rows per pipeline stage, kRowParts threads per row (a warp covers 8 rows).
+constexpr int kRowParts = 4;
+constexpr int kMaxBpp = 16;  // blocks per part: cols <= kRowParts * kMaxBpp * 32 (kernels instantiated for 8 and 16)
 __host__ __device__ constexpr int head_tile_rows(int dtype) { return dtype == DT_Q4_0 ? 128 : 64; }
+__host__ __device__ constexpr int head_threads(int dtype) { return head_tile_rows(dtype) * kRowParts; }
 constexpr int kHeadWarps = kHeadThreads / 32;
 constexpr int kStages = 4;
 
@@ -176,10 +179,10 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
     __shared__ __align__(16) int8_t sx[2048];
     __shared__ float sdx[64];
     __shared__ int ssum[64];
-    pdl_launch_dependents();
     NormW nw;
     load_norm_w(norm_w, dim, nw);
     pdl_wait();
+    pdl_launch_dependents();
     norm_quant(X, nw, dim, eps, sx, sdx, ssum, sred);
     if (threadIdx.x == 0 && hs) {
         hs->rows_total += hs->calls ? hs->rows : 0;
@@ -232,44 +235,64 @@ __device__ __forceinline__ void load_head_act(const HeadIn& hin, int cols, const
     __syncthreads();
 }
 
-// One row's exact logit from its quants (16-byte granules, wq) and fp16 block scales (four per 8-byte load, wd) in
-// shared memory: acc = acc + (float(s_b) * dw_b) * dx_b in block order, as matvec_q_ref.  nb % 4 == 0.
+// One block's term (float(s_b) * dw_b) * dx_b of a row whose quants (16-byte granules, wq) and fp16 scales (wd) sit in
+// shared memory.
 template <int DT>
-__device__ __forceinline__ float smem_row_value(const uint4* wq, const uint2* wd, const HeadAct& a, int nb) {
-    float acc = 0.f;
-#pragma unroll 2
-    for (int b4 = 0; b4 < nb; b4 += 4) {
-        const uint2 d4 = wd[b4 >> 2];
-        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&d4.x));
-        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&d4.y));
-        const float dw[4] = {f01.x, f01.y, f23.x, f23.y};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int b = b4 + k;
-            int s;
-            if (DT == DT_Q4_0)
-                s = chunk_dot<DT>(wq[b], a.sx, b) - 8 * a.ssum[b];
-            else
-                s = chunk_dot<DT>(wq[2 * b], a.sx, 2 * b) + chunk_dot<DT>(wq[2 * b + 1], a.sx, 2 * b + 1);
-            acc = fadd(acc, block_term(s, dw[k], a.sdx[b]));
-        }
-    }
-    return acc;
+__device__ __forceinline__ float smem_block_term(const uint4* wq, const __half* wd, const HeadAct& a, int b) {
+    int s;
+    if (DT == DT_Q4_0)
+        s = chunk_dot<DT>(wq[b], a.sx, b) - 8 * a.ssum[b];
+    else
+        s = chunk_dot<DT>(wq[2 * b], a.sx, 2 * b) + chunk_dot<DT>(wq[2 * b + 1], a.sx, 2 * b + 1);
+    return block_term(s, __half2float(wd[b]), a.sdx[b]);
 }
 
-// The shortlist bound B = (sum_b err_b * |x_b| in block order) * 1.001 + 1e-5 (engine/src/model.cpp:271-277).
-__device__ __forceinline__ float smem_row_bound(const uint2* we, const float* sxn, int nb) {
-    float bound = 0.f;
-#pragma unroll 2
-    for (int b4 = 0; b4 < nb; b4 += 4) {
-        const uint2 e4 = we[b4 >> 2];
-        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&e4.x));
-        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&e4.y));
-        const float e[4] = {f01.x, f01.y, f23.x, f23.y};
+// A row's value acc = ((0 + t_0) + t_1) + ... in block order (matvec_q_ref), and with BOUND the shortlist bound
+// (sum_b err_b * |x_b| in block order) * 1.001 + 1e-5 (engine/src/model.cpp:271-277), computed by kRowParts lanes of
+// one warp: lane l holds part l / 8 of the warp's row l % 8.  Each part forms its nb / kRowParts terms in registers;
+// the chains then run part after part, each part continuing from the previous part's sum (shuffled up 8 lanes), so
+// the order of the float adds is the reference's.  The results are valid in the last part's lanes.
+template <int DT, bool BOUND, int MAXB>
+__device__ __forceinline__ void row_value_parts(const uint4* wq, const __half* wd, const __half* we, const HeadAct& a,
+                                                int nb, float& val, float& bnd) {
+    const int part = (threadIdx.x & 31) >> 3;
+    const int bpp = nb / kRowParts, b0 = part * bpp;
+    float t[MAXB], u[MAXB];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) bound = fadd(bound, fmul(e[k], sxn[b4 + k]));
+    for (int k = 0; k < MAXB; ++k) {
+        if (k < bpp) {
+            t[k] = smem_block_term<DT>(wq, wd, a, b0 + k);
+            if (BOUND) u[k] = fmul(__half2float(we[b0 + k]), a.sxn[b0 + k]);
+        }
     }
-    return fadd(fmul(bound, 1.001f), 1e-5f);
+    float acc = 0.f, bd = 0.f;
+    if (part == 0) {
+#pragma unroll
+        for (int k = 0; k < MAXB; ++k) {
+            if (k < bpp) {
+                acc = fadd(acc, t[k]);
+                if (BOUND) bd = fadd(bd, u[k]);
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 1; q < kRowParts; ++q) {
+        const float pa = __shfl_up_sync(0xffffffffu, acc, 8);
+        const float pb = BOUND ? __shfl_up_sync(0xffffffffu, bd, 8) : 0.f;
+        if (part == q) {
+            acc = pa;
+            bd = pb;
+#pragma unroll
+            for (int k = 0; k < MAXB; ++k) {
+                if (k < bpp) {
+                    acc = fadd(acc, t[k]);
+                    if (BOUND) bd = fadd(bd, u[k]);
+                }
+            }
+        }
+    }
+    val = acc;
+    bnd = BOUND ? fadd(fmul(bd, 1.001f), 1e-5f) : 0.f;
 }
 
 __device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n groups are pending (n in 0..3)
@@ -288,16 +311,15 @@ __device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n g
 //   rows among [0, n_valid) after the repetition penalty of marked rows, and clears those marks.
 // mode 1 (coarse): W = quanta.head_q4; coarse / upper / logits = -inf, and each CTA's best n_list coarse scores among
 //   valid unmarked rows (the seeds).
-template <int DT, int MODE>
-__global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
+template <int DT, int MODE, int MAXB>
+__global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
                                                                      StreamPlan sp, int n_valid, int n_list, int penal,
                                                                      float penalty, unsigned char* __restrict__ mark,
                                                                      float* __restrict__ logits, float* __restrict__ coarse,
                                                                      float* __restrict__ upper, Cand* __restrict__ lists) {
-    constexpr int TR = head_tile_rows(DT);
+    constexpr int TR = head_tile_rows(DT), NT = head_threads(DT);
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ Cand slist[TR];
-    pdl_launch_dependents();
+    __shared__ Cand slist[NT];
     const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16, S = sp.stages;
     const HeadAct act = carve_act(smem, cols, MODE == 1);
     unsigned char* ring = smem + sp.ring_off;
@@ -309,16 +331,16 @@ __global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, con
             unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
             const int row0 = t * TR, nrows = min(TR, W.rows - row0);
             const uint8_t* qsrc = W.q + size_t(row0) * rb;
-            for (int c = threadIdx.x; c < nrows * cpr; c += TR) {
+            for (int c = threadIdx.x; c < nrows * cpr; c += NT) {
                 const int rr = int(fast_div(unsigned(c), sp.cpr_magic));
                 cp_async16(st + rr * sp.qstride + (c - rr * cpr) * 16, qsrc + size_t(c) * 16);
             }
             const uint8_t* dsrc = reinterpret_cast<const uint8_t*>(W.d) + size_t(row0) * nb * 2;
             const int dch = (nrows * nb * 2 + 15) / 16;  // may read up to 15 bytes of the allocation's tail padding
-            for (int c = threadIdx.x; c < dch; c += TR) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
+            for (int c = threadIdx.x; c < dch; c += NT) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
             if (MODE == 1) {
                 const uint8_t* esrc = reinterpret_cast<const uint8_t*>(err) + size_t(row0) * nb * 2;
-                for (int c = threadIdx.x; c < dch; c += TR) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
+                for (int c = threadIdx.x; c < dch; c += NT) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
             }
         }
         cp_commit();
@@ -326,24 +348,29 @@ __global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, con
 
     for (int s = 0; s < S - 1; ++s) issue(ta + s);
     pdl_wait();
+    pdl_launch_dependents();
     load_head_act(hin, cols, act);
 
     WarpTop32 L;
     L.init();
-    const int r = threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int r = (threadIdx.x >> 5) * 8 + (lane & 7);  // this lane's row in the tile
+    const bool last_part = (lane >> 3) == kRowParts - 1;
     for (int t = ta; t < tb; ++t) {
         issue(t + S - 1);
         cp_wait_upto(S - 1);
         __syncthreads();
         const unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
         const int row0 = t * TR, nrows = min(TR, W.rows - row0);
+        float v, bound;
+        row_value_parts<DT, MODE == 1, MAXB>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
+                                       reinterpret_cast<const __half*>(st + sp.d_off + r * nb * 2),
+                                       reinterpret_cast<const __half*>(st + sp.e_off + r * nb * 2), act, nb, v, bound);
         float cv = -INFINITY;
         int row = INT_MAX;
         bool ok = false;
-        if (r < nrows) {
+        if (last_part && r < nrows) {
             row = row0 + r;
-            const float v = smem_row_value<DT>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
-                                               reinterpret_cast<const uint2*>(st + sp.d_off + r * nb * 2), act, nb);
             cv = v;
             if (MODE == 0) {
                 logits[row] = v;
@@ -358,7 +385,6 @@ __global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, con
                     }
                 }
             } else {
-                const float bound = smem_row_bound(reinterpret_cast<const uint2*>(st + sp.e_off + r * nb * 2), act.sxn, nb);
                 coarse[row] = v;
                 upper[row] = fadd(v, bound);
                 logits[row] = -INFINITY;
@@ -380,8 +406,8 @@ __global__ void __launch_bounds__(head_tile_rows(DT), 1) k_head_rows(DMat W, con
 // Marks the must ids: mark[id] = 1 for 0 <= id < n_valid (model.cpp:252-253).
 __global__ void k_sl_mark(const int* __restrict__ must, const int* __restrict__ n_must_dev, int n_must_host, int window,
                           int n_valid, unsigned char* __restrict__ mark) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     int n = n_must_dev ? __ldcg(n_must_dev) : n_must_host;
     int from = 0;
     if (window > 0 && n > window) from = n - window;
@@ -428,8 +454,8 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     __shared__ float wterm[kHeadWarps][128];
     __shared__ float exact[32];
     __shared__ int s_ns;
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cols = W8.cols, nb = cols / QK;
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
@@ -470,100 +496,126 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     }
 }
 
-// Candidate scan over this CTA's contiguous rows, exact logits of the wanted rows (gathered through the cp.async ring,
-// one row per thread), optional sampler stage 1, mark clearing.
-__global__ void __launch_bounds__(head_tile_rows(DT_Q8_0), 1) k_sl_cands(DMat W8, HeadIn hin, StreamPlan sp, int n_valid,
-                                                                         int n_list, int penal, float penalty,
-                                                                         unsigned char* __restrict__ mark,
-                                                                         const float* __restrict__ upper,
-                                                                         float* __restrict__ logits,
-                                                                         HeadState* __restrict__ hs, Cand* __restrict__ lists) {
-    constexpr int TR = head_tile_rows(DT_Q8_0);
+// Candidate pass over this CTA's contiguous rows.  One scan reads every mark / bound, clears the marks, and compacts
+// two lists: rows that need an exact logit (must ids, mark 1, and rows with upper >= tau, mark 0) and the seeds (mark
+// 2, exact already).  The exact logits of the first list are gathered through the cp.async ring (kRowParts threads per
+// row); the sampler's stage 1 then looks at the two lists only.
+template <int MAXB>
+__global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, HeadIn hin, StreamPlan sp, int n_valid,
+                                                                       int n_list, int penal, float penalty,
+                                                                       unsigned char* __restrict__ mark,
+                                                                       const float* __restrict__ upper,
+                                                                       float* __restrict__ logits,
+                                                                       HeadState* __restrict__ hs, Cand* __restrict__ lists) {
+    constexpr int TR = head_tile_rows(DT_Q8_0), NT = head_threads(DT_Q8_0);
+    constexpr int kScanPer = 8;  // rows a thread scans per batch of loads
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ Cand slist[TR];
-    __shared__ int s_count;
-    pdl_launch_dependents();
+    __shared__ Cand slist[NT];
+    __shared__ int s_count, s_seeds;
     const int cols = W8.cols, nb = cols / QK, cpr = cols / 16, S = sp.stages;
     const HeadAct act = carve_act(smem, cols, false);
-    int* list = reinterpret_cast<int*>(smem + sp.list_off);
+    int* list = reinterpret_cast<int*>(smem + sp.list_off);  // exact rows from the front (bit 30: penalised), seeds from the back
+    const int cap = sp.list_cap;
     unsigned char* ring = smem + sp.ring_off;
     const int V = W8.rows;
     const int r0 = int((long long)blockIdx.x * V / gridDim.x), r1 = int((long long)(blockIdx.x + 1) * V / gridDim.x);
-    if (threadIdx.x == 0) s_count = 0;
+    if (threadIdx.x == 0) {
+        s_count = 0;
+        s_seeds = 0;
+    }
     pdl_wait();
+    pdl_launch_dependents();
     load_head_act(hin, cols, act);
     const float tau = __ldcg(&hs->tau);
     const int lane = threadIdx.x & 31;
-    // scan + compaction (order inside the list does not affect any value)
-    for (int base = r0; base < r1; base += TR) {
-        const int r = base + threadIdx.x;
-        bool want = false;
-        if (r < r1 && r < n_valid) {
-            const unsigned char mk = __ldcg(mark + r);
-            want = mk == 1 || (mk == 0 && __ldcg(upper + r) >= tau);
+    for (int base = r0; base < r1; base += NT * kScanPer) {
+        unsigned char mk[kScanPer];
+        float up[kScanPer];
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) {  // every load of the batch first
+            const int r = base + k * NT + threadIdx.x;
+            mk[k] = r < r1 ? __ldcg(mark + r) : 0;
+            up[k] = r < r1 && r < n_valid ? __ldcg(upper + r) : -INFINITY;
         }
-        const unsigned m = __ballot_sync(0xffffffffu, want);
-        int off = 0;
-        if (lane == 0 && m) off = atomicAdd(&s_count, __popc(m));
-        off = __shfl_sync(0xffffffffu, off, 0);
-        if (want) list[off + __popc(m & ((1u << lane) - 1))] = r;
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) {
+            const int r = base + k * NT + threadIdx.x;
+            const bool in = r < r1 && r < n_valid;
+            const bool want = in && (mk[k] == 1 || (mk[k] == 0 && up[k] >= tau));
+            const bool seed = in && mk[k] == 2;
+            if (r < r1 && mk[k]) mark[r] = 0;
+            const unsigned mw = __ballot_sync(0xffffffffu, want), ms = __ballot_sync(0xffffffffu, seed);
+            int ow = 0, os = 0;
+            if (lane == 0) {
+                if (mw) ow = atomicAdd(&s_count, __popc(mw));
+                if (ms) os = atomicAdd(&s_seeds, __popc(ms));
+            }
+            ow = __shfl_sync(0xffffffffu, ow, 0);
+            os = __shfl_sync(0xffffffffu, os, 0);
+            const unsigned below = (1u << lane) - 1;
+            if (want) list[ow + __popc(mw & below)] = r | (mk[k] == 1 ? 1 << 30 : 0);
+            if (seed) list[cap - 1 - (os + __popc(ms & below))] = r;
+        }
     }
     __syncthreads();
-    const int n = s_count;
+    const int n = s_count, ns = s_seeds;
     const int n_tiles = (n + TR - 1) / TR;
     const int dpr = nb / 4;  // 8-byte scale groups per row (rows of scales are 8-byte aligned, not 16)
     auto issue = [&](int t) {
         if (t < n_tiles) {
             unsigned char* st = ring + size_t(t % S) * sp.stage_bytes;
             const int nrows = min(TR, n - t * TR);
-            for (int c = threadIdx.x; c < nrows * cpr; c += TR) {
+            for (int c = threadIdx.x; c < nrows * cpr; c += NT) {
                 const int rr = int(fast_div(unsigned(c), sp.cpr_magic)), cc = c - rr * cpr;
-                cp_async16(st + rr * sp.qstride + cc * 16, W8.q + size_t(list[t * TR + rr]) * cols + size_t(cc) * 16);
+                const int row = list[t * TR + rr] & 0x3FFFFFFF;
+                cp_async16(st + rr * sp.qstride + cc * 16, W8.q + size_t(row) * cols + size_t(cc) * 16);
             }
-            for (int c = threadIdx.x; c < nrows * dpr; c += TR) {
+            for (int c = threadIdx.x; c < nrows * dpr; c += NT) {
                 const int rr = c / dpr, cc = c - rr * dpr;
+                const int row = list[t * TR + rr] & 0x3FFFFFFF;
                 cp_async8(st + sp.d_off + (rr * nb + 4 * cc) * 2,
-                          reinterpret_cast<const uint8_t*>(W8.d) + (size_t(list[t * TR + rr]) * nb + 4 * cc) * 2);
+                          reinterpret_cast<const uint8_t*>(W8.d) + (size_t(row) * nb + 4 * cc) * 2);
             }
         }
         cp_commit();
     };
     for (int s = 0; s < S - 1; ++s) issue(s);
+    const int r = (threadIdx.x >> 5) * 8 + (lane & 7);
+    const bool last_part = (lane >> 3) == kRowParts - 1;
+    WarpTop32 L;
+    L.init();
     for (int t = 0; t < n_tiles; ++t) {
         issue(t + S - 1);
         cp_wait_upto(S - 1);
         __syncthreads();
         const unsigned char* st = ring + size_t(t % S) * sp.stage_bytes;
         const int nrows = min(TR, n - t * TR);
-        if (int(threadIdx.x) < nrows)
-            logits[list[t * TR + threadIdx.x]] =
-                smem_row_value<DT_Q8_0>(reinterpret_cast<const uint4*>(st + threadIdx.x * sp.qstride),
-                                        reinterpret_cast<const uint2*>(st + sp.d_off + threadIdx.x * nb * 2), act, nb);
+        float v, unused;
+        row_value_parts<DT_Q8_0, false, MAXB>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
+                                        reinterpret_cast<const __half*>(st + sp.d_off + r * nb * 2), nullptr, act, nb, v,
+                                        unused);
+        bool ok = false;
+        float cv = -INFINITY;
+        int row = INT_MAX;
+        if (last_part && r < nrows) {
+            const int e = list[t * TR + r];
+            row = e & 0x3FFFFFFF;
+            logits[row] = v;
+            ok = n_list > 0;
+            cv = (penal && (e >> 30)) ? penalize(v, penalty) : v;
+        }
+        if (n_list > 0) L.offer(cv, ok ? row : INT_MAX, ok, n_list);
         __syncthreads();
     }
     cp_wait<0>();
-    __syncthreads();
-    // sampler stage 1 over every exact row of the range (seeds, must rows, candidates), marks cleared
-    WarpTop32 L;
-    L.init();
-    for (int base = r0; base < r1; base += TR) {
-        const int r = base + threadIdx.x;
-        bool ok = false;
-        float cv = -INFINITY;
-        if (r < r1) {
-            const unsigned char mk = __ldcg(mark + r);
-            if (r < n_valid && n_list > 0) {
-                ok = mk != 0 || __ldcg(upper + r) >= tau;
-                if (ok) {
-                    const float l = __ldcg(logits + r);
-                    cv = (penal && mk == 1) ? penalize(l, penalty) : l;
-                }
-            }
-            if (mk) mark[r] = 0;
-        }
-        if (n_list > 0) L.offer(cv, ok ? r : INT_MAX, ok, n_list);
-    }
     if (n_list > 0) {
+        // the seeds: exact logits from the seed pass, never penalised (a must id carries mark 1, not 2)
+        for (int i0 = 0; i0 < ns; i0 += NT) {
+            const int i = i0 + threadIdx.x;
+            const bool ok = i < ns;
+            const int row = ok ? list[cap - 1 - i] : INT_MAX;
+            L.offer(ok ? __ldcg(logits + row) : -INFINITY, row, ok, n_list);
+        }
         cta_merge_lists(L, n_list, slist);
         if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
     }
@@ -579,8 +631,8 @@ __global__ void __launch_bounds__(kThreads) k_topk_partial(const float* logits, 
                                                            float penalty, unsigned char* __restrict__ mark,
                                                            Cand* __restrict__ out, float* wb) {
     __shared__ Cand slist[kWarps * 32];
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     WarpTop32 L;
     L.init();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -616,8 +668,8 @@ __global__ void __launch_bounds__(kHeadThreads) k_sample_final(const Cand* __res
                                                                SamplerState* __restrict__ ss, int* __restrict__ hist,
                                                                int hist_cap) {
     __shared__ Cand slist[kHeadWarps * 32];
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     __shared__ float p[32];
     cta_merge_sorted(parts, n_lists, K, slist);
     if (threadIdx.x >= 32) return;
@@ -689,7 +741,7 @@ StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, boo
     const int rb = row_bytes_host(dtype, cols), cpr = rb / 16, nb = cols / QK;
     const int tr = head_tile_rows(dtype);
     p.tile_rows = tr;
-    p.threads = tr;
+    p.threads = head_threads(dtype);
     p.n_tiles = (rows + tr - 1) / tr;
     p.cpr_magic = div_magic(unsigned(cpr));
     p.qstride = rb + 16;
@@ -697,13 +749,14 @@ StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, boo
     p.e_off = int(p.d_off + align16(size_t(tr) * nb * 2 + 16));
     p.stage_bytes = int(coarse ? p.e_off + align16(size_t(tr) * nb * 2 + 16) : p.e_off);
     const size_t act_bytes = align16(size_t(cols) + size_t(nb) * 12);
-    const size_t list_bytes = gather ? align16(size_t((rows + grid - 1) / grid + 64) * 4) : 0;
+    p.list_cap = gather ? (rows + grid - 1) / grid + 64 : 0;  // every row of a CTA's range fits in one of the lists
+    const size_t list_bytes = align16(size_t(p.list_cap) * 4);
     p.list_off = int(act_bytes);
     p.ring_off = int((act_bytes + list_bytes + 127) / 128 * 128);
-    const size_t budget = 227 * 1024 - size_t(tr) * sizeof(Cand) - 64;  // minus the kernels' static shared memory
+    const size_t budget = 227 * 1024 - size_t(p.threads) * sizeof(Cand) - 64;  // minus the kernels' static shared memory
     const size_t fit = budget > size_t(p.ring_off) ? (budget - p.ring_off) / size_t(p.stage_bytes) : 0;
     p.stages = int(std::min<size_t>(4, fit));
-    if (p.stages < 2 || nb % 4 != 0) p.stages = 0;
+    if (p.stages < 2 || nb % 4 != 0 || nb % kRowParts != 0 || nb / kRowParts > kMaxBpp) p.stages = 0;
     p.smem = size_t(p.ring_off) + size_t(p.stages) * p.stage_bytes;
     p.grid = grid;
     return p;
@@ -715,16 +768,20 @@ cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, floa
     return launch_pdl(k_head_input, dim3(1), dim3(kThreads), 0, st, pdl, X, norm_w, dim, eps, hin, hs, full_rows);
 }
 
+template <int DT, int MAXB>
+cudaError_t launch_full_t(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl) {
+    return launch_pdl(k_head_rows<DT, 0, MAXB>, dim3(a.plan.grid), dim3(a.plan.threads), a.plan.smem, st, pdl, a.W,
+                      (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
+                      (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
+}
+
 cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl) {
     if (a.plan.stages == 0) return cudaErrorInvalidValue;
+    const bool small = a.W.cols / QK / kRowParts <= 8;
     if (a.W.dtype == DT_Q8_0)
-        return launch_pdl(k_head_rows<DT_Q8_0, 0>, dim3(a.plan.grid), dim3(a.plan.threads), a.plan.smem, st, pdl, a.W,
-                          (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
-                          (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
+        return small ? launch_full_t<DT_Q8_0, 8>(a, hin, st, pdl) : launch_full_t<DT_Q8_0, kMaxBpp>(a, hin, st, pdl);
     if (a.W.dtype == DT_Q4_0)
-        return launch_pdl(k_head_rows<DT_Q4_0, 0>, dim3(a.plan.grid), dim3(a.plan.threads), a.plan.smem, st, pdl, a.W,
-                          (const __half*)nullptr, hin, a.plan, a.n_valid, a.n_list, a.penal, a.penalty, a.mark, a.logits,
-                          (float*)nullptr, (float*)nullptr, reinterpret_cast<Cand*>(a.lists));
+        return small ? launch_full_t<DT_Q4_0, 8>(a, hin, st, pdl) : launch_full_t<DT_Q4_0, kMaxBpp>(a, hin, st, pdl);
     return cudaErrorInvalidValue;
 }
 
@@ -735,14 +792,15 @@ cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStre
     cudaError_t e = launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, a.must, a.n_must_dev, a.n_must_host, a.window,
                                a.n_valid, a.mark);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_head_rows<DT_Q4_0, 1>, dim3(a.plan4.grid), dim3(a.plan4.threads), a.plan4.smem, st, pdl, a.W4, a.err, hin,
-                   a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark, a.logits, a.coarse, a.upper,
-                   reinterpret_cast<Cand*>(a.seed_buf));
+    const bool small = a.W8.cols / QK / kRowParts <= 8;
+    e = launch_pdl(small ? k_head_rows<DT_Q4_0, 1, 8> : k_head_rows<DT_Q4_0, 1, kMaxBpp>, dim3(a.plan4.grid),
+                   dim3(a.plan4.threads), a.plan4.smem, st, pdl, a.W4, a.err, hin, a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark,
+                   a.logits, a.coarse, a.upper, reinterpret_cast<Cand*>(a.seed_buf));
     if (e != cudaSuccess) return e;
     e = launch_pdl(k_sl_seeds, dim3(1), dim3(kHeadThreads), 0, st, pdl, a.W8, hin, (const Cand*)a.seed_buf, a.plan4.grid,
                    n_seed, a.k, a.mark, a.logits, a.hs);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_sl_cands, dim3(a.plan8g.grid), dim3(a.plan8g.threads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
+    e = launch_pdl(small ? k_sl_cands<8> : k_sl_cands<kMaxBpp>, dim3(a.plan8g.grid), dim3(a.plan8g.threads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
                    a.n_list, a.penal, a.penalty, a.mark, (const float*)a.upper, a.logits, a.hs,
                    reinterpret_cast<Cand*>(a.lists));
     if (kernels) *kernels += 4;

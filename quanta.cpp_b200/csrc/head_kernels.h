@@ -37,7 +37,7 @@ struct StreamPlan {
     int tile_rows = 0, n_tiles = 0, threads = 0;
     unsigned cpr_magic = 0;
     int qstride = 0, d_off = 0, e_off = 0, stage_bytes = 0, stages = 0;
-    int list_off = 0, ring_off = 0;
+    int list_off = 0, list_cap = 0, ring_off = 0;
     size_t smem = 0;
     int grid = 0;
 };

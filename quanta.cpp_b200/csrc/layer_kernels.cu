@@ -6,8 +6,9 @@
 //   k_o_dec       quantize(attn) -> o_proj matvec -> residual add
 //   k_gateup_dec  rmsnorm + quantize -> gate|up matvec (rows interleaved per 32-block) -> SwiGLU -> quantize
 //   k_down_dec    down_proj matvec -> residual add
-// Every kernel first triggers its dependents and loads its weight slice, then waits for the previous kernel
-// (programmatic dependent launch), so weight traffic overlaps the launch gap and the previous kernel's tail.
+// Every kernel first loads its weight slice, then waits for the previous kernel (programmatic dependent launch), and
+// only then lets the next kernel launch: weight traffic overlaps the launch gap and the previous kernel's tail, and at
+// most one kernel ahead is resident, so early launches never fill the SMs with CTAs that cannot run yet.
 // A kernel launched early this way may run on an SM whose L1 still holds lines that earlier kernels of the chain
 // have since rewritten (L1 is not coherent, and the wait does not invalidate it), so every read of data produced by
 // another kernel goes through L2 (__ldcg / ld.global.cg); only constant weights use L1 or the non-coherent path.
@@ -22,8 +23,8 @@ namespace qb {
 // ---------------------------------------------------------------- embedding (engine/src/ops_ref.cpp:162-192 get_row)
 
 __global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float* __restrict__ X, unsigned* status) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     if (t >= n_tok) return;
     int tok = __ldcg(tokens + t);
@@ -133,7 +134,6 @@ __global__ void __launch_bounds__(kThreads) k_qkv_dec(QkvArgs a, const float* __
                                                       float eps, const int* __restrict__ pos_dev, float* __restrict__ Q,
                                                       int rows_per_cta, unsigned magic) {
     extern __shared__ __align__(16) unsigned char smem[];
-    pdl_launch_dependents();
     const int dim = a.W.cols;
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, a.W.rows - row0);
     SliceSmem s = carve(smem, dim, rows_per_cta, term_stride(dim / QK));
@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_dec(QkvArgs a, const float* __
     int pos = 0;
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
+        pdl_launch_dependents();
         pos = __ldcg(pos_dev);
         if (has_pair) pair_rope(a, pr, pos, pin);
         norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
@@ -163,7 +164,6 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
                                                         const float* __restrict__ din, float* __restrict__ X,
                                                         int rows_per_cta, unsigned magic) {
     extern __shared__ __align__(16) unsigned char smem[];
-    pdl_launch_dependents();
     const int cols = W.cols;
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
     SliceSmem s = carve(smem, cols, rows_per_cta, term_stride(cols / QK));
@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
     float xres = 0.f;  // this thread's residual row (rows_per_cta <= blockDim)
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
+        pdl_launch_dependents();
         if (int(threadIdx.x) < nrows) xres = __ldcg(X + row0 + threadIdx.x);
         if (MODE == 0) quant_only(xin, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
         else load_quant(qin, din, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
@@ -186,7 +187,6 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
                                                          float eps, int8_t* __restrict__ HQ, float* __restrict__ HD,
                                                          int blocks_per_cta, unsigned magic, ExpTab tab) {
     extern __shared__ __align__(16) unsigned char smem[];
-    pdl_launch_dependents();
     const int dim = W.cols;
     const int rows_per_cta = blocks_per_cta * 64;
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
@@ -196,6 +196,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
     load_norm_w(norm_w, dim, nw);
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
+        pdl_launch_dependents();
         norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
     });
     __syncthreads();
@@ -219,10 +220,10 @@ __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __res
                                                               int dim, float eps, int8_t* __restrict__ XQ,
                                                               float* __restrict__ DX) {
     __shared__ __align__(16) float sred[32 + 2048];
-    pdl_launch_dependents();
     NormW nw;
     if (norm_w) load_norm_w(norm_w, dim, nw);
     pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     if (norm_w) norm_quant(X + size_t(t) * dim, nw, dim, eps, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr, sred);
     else quant_only(X + size_t(t) * dim, dim, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr);
@@ -231,8 +232,8 @@ __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __res
 // R [n][fused rows] raw q|k|v -> bias + RoPE + store, token t at position pos0 + t.
 __global__ void k_qkv_epilogue(QkvArgs a, const float* __restrict__ R, int n_tok, const int* __restrict__ pos_dev,
                                float* __restrict__ Q) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.y;
     const int pairs = a.W.rows / 2;
     const int pos = __ldcg(pos_dev) + t;
@@ -242,8 +243,8 @@ __global__ void k_qkv_epilogue(QkvArgs a, const float* __restrict__ R, int n_tok
 }
 
 __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, long long n) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         X[i] = fadd(__ldcg(X + i), __ldcg(R + i));
 }
@@ -251,8 +252,8 @@ __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, l
 // R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
 __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
                                float* __restrict__ HD, ExpTab tab) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
     const int nbk = ffn / QK;
     if (w >= (long long)n_tok * nbk) return;
