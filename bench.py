@@ -162,9 +162,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     m.session_begin(prompt, sp)  # compiles the graphs of the first call
     m.session_begin(prompt, sp)
+    torch.cuda.nvtx.range_push("prefill")
     t0 = time.perf_counter()
     m.session_begin(prompt, sp)
     prefill_s = time.perf_counter() - t0
+    torch.cuda.nvtx.range_pop()
     # warm-up, then exactly K steps bracketed by barrier + synchronize, CUDA events on the model's stream
     m.session_step(args.warmup)
     torch.cuda.synchronize()

@@ -9,12 +9,16 @@
 #include "quanta_b200.h"
 #include "capi_util.h"
 #include "engine.h"
+#include "gemm_tc.h"
 #include "ops.h"
 
 struct qnt_dtensor {
     qb::DMat m;
     void* q = nullptr;
     void* d = nullptr;
+    qb::TcMap wmap{};          // TMA source for the tensor-core matmul
+    bool tc = false;           // wmap is valid
+    unsigned* status = nullptr;  // device status word of this tensor's kernels
 };
 
 struct qnt_model {
@@ -92,6 +96,15 @@ int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_
     t->m.cols = cols;
     t->m.q = static_cast<const uint8_t*>(t->q);
     t->m.d = static_cast<const __half*>(t->d);
+    e = cudaMalloc(&t->status, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(t->status, 0, sizeof(unsigned));
+    if (e != cudaSuccess) {
+        cudaFree(t->q);
+        cudaFree(t->d);
+        cudaFree(t->status);
+        return cuda_err(e, "tensor status word");
+    }
+    t->tc = qb::make_weight_map(t->m, &t->wmap);
     *out = t.release();
     return QNT_OK;
 }
@@ -100,6 +113,7 @@ int qnt_tensor_free(qnt_dtensor* t) {
     if (!t) return QNT_OK;
     cudaFree(t->q);
     cudaFree(t->d);
+    cudaFree(t->status);
     delete t;
     return QNT_OK;
 }
@@ -128,8 +142,20 @@ int qnt_matvec(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, 
 int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo, int impl,
                void* stream) {
     if (!W || r0 < 0 || r1 > W->m.rows || r0 > r1 || n < 0 || ldo < r1) return set_err(QNT_ERR_INVALID, "bad matmul arguments");
-    (void)impl;
-    cudaError_t e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, static_cast<cudaStream_t>(stream));
+    if (impl < 0 || impl > 2) return set_err(QNT_ERR_INVALID, "impl must be 0 (auto), 1 (CUDA cores) or 2 (tensor cores)");
+    const bool tc = impl == 2 || (impl == 0 && W->tc && n >= qb::kTcMinTokens);
+    cudaError_t e;
+    if (tc) {
+        if (!W->tc) return set_err(QNT_ERR_UNSUPPORTED, "tensor-core matmul needs cols % 128 == 0 and a TMA-capable driver");
+        if ((reinterpret_cast<uintptr_t>(qx) | reinterpret_cast<uintptr_t>(dx)) & 15)
+            return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
+        if (n == 0 || r1 == r0) return QNT_OK;
+        qb::TcMap mq, md;
+        if (!qb::make_act_maps(qx, dx, n, W->m.cols, &mq, &md)) return set_err(QNT_ERR_CUDA, "TMA descriptor encode failed");
+        e = qb::launch_matmul_tc(W->m, W->wmap, mq, md, n, r0, r1, out, ldo, W->status, static_cast<cudaStream_t>(stream));
+    } else {
+        e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, static_cast<cudaStream_t>(stream));
+    }
     return e == cudaSuccess ? QNT_OK : cuda_err(e, "matmul");
 }
 
@@ -167,6 +193,14 @@ static int host_mm(const qnt_dtensor* W, const int8_t* qx, const float* dx, int 
     if (e == cudaSuccess) {
         rc = mv ? qnt_matvec(W, dq, dd, r0, r1, dout, nullptr) : qnt_matmul(W, dq, dd, n, r0, r1, dout, ldo, impl, nullptr);
         e = cudaDeviceSynchronize();
+    }
+    if (e == cudaSuccess && rc == QNT_OK) {
+        unsigned st = 0;
+        e = cudaMemcpy(&st, W->status, sizeof st, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && st) {
+            cudaMemset(W->status, 0, sizeof st);
+            rc = set_err(QNT_ERR_DEVICE, "matmul kernel reported status bits " + std::to_string(st));
+        }
     }
     if (e == cudaSuccess && rc == QNT_OK) {
         if (mv) {

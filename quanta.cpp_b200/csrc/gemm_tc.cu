@@ -1,1 +1,376 @@
-// tcgen05 int8 matmul (placeholder until the tensor-core path lands)
+// Tensor-core (tcgen05) int8 matmul for prefill chunks and batched decode: out[t * ldo + r] for weight rows r in
+// [r0, r1) and tokens t in [0, n), bit-identical to the CUDA-core matmul and to matvec_q_ref
+// (engine/src/ops_ref.cpp:122-160): per (row, token) acc = acc + (float(s_b) * dw_b) * dx_b over the 32-blocks b in
+// order, s_b the exact int32 block dot.
+//
+// The per-block scales rule out accumulating across blocks in the tensor core, so every quant block gets its own MMA
+// (K = 32, the int8 MMA's K) into its own TMEM slot, and the epilogue warps pull each block's int32 tile out of TMEM
+// and fold it into f32 registers in block order.  Per CTA: a tile of 128 weight rows x 64 tokens.
+//   warp 0      TMA producer: per stage four blocks of the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B
+//               packed per row), the activation tile (64 tokens x 128 B, 128B-swizzled) and its block scales
+//   warps 2-3   (Q4 only) unpack nibbles q into int8 q - 8 in the swizzled layout the MMA reads
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma.kind::i8 per block and commits to mbarriers
+//   warps 4-11  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and token columns
+//               32 ((w - 4) / 4) .. +32, one row per thread, 32 f32 accumulators
+// Every wait is bounded: a wait that gives up sets ERR_WAIT_TIMEOUT in the status word and an abort flag that ends
+// every other wait, so the kernel always returns (and frees its TMEM once its issued MMAs have completed).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm_tc.h"
+#include "kernels.cuh"
+
+namespace qb {
+
+namespace {
+
+constexpr int kTcThreads = 384;
+constexpr int kTileRows = 128, kTileTok = 64;
+constexpr int kStageBlocks = 4;          // quant blocks per pipeline stage (128 bytes of K)
+constexpr int kStages = 4;
+constexpr int kSlots = 4;                // TMEM accumulator slots, kTileTok columns each
+constexpr int kTmemCols = kSlots * kTileTok;
+constexpr int kASw = kTileRows * 128;    // swizzled int8 weight tile of a stage
+constexpr int kAPk = kTileRows * 64;     // packed Q4 tile of a stage
+constexpr int kB = kTileTok * 128;       // activation tile of a stage
+constexpr int kDX = kTileTok * kStageBlocks * 4;
+constexpr unsigned kWaitLimit = 1u << 22;
+
+struct StageOffsets {
+    int a_sw, a_pk, b, dx, bytes;
+};
+__host__ __device__ constexpr StageOffsets stage_layout(bool q4) {
+    // 1024-byte alignment for the swizzled tiles (the 128B swizzle atom)
+    return StageOffsets{0, kASw, kASw + (q4 ? kAPk : 0), kASw + (q4 ? kAPk : 0) + kB,
+                        ((kASw + (q4 ? kAPk : 0) + kB + kDX) + 1023) / 1024 * 1024};
+}
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when it gave up or another role aborted (then the caller unwinds).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, volatile int* abort_flag, unsigned* status) {
+    for (unsigned i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try(b, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    set_error(status, ERR_WAIT_TIMEOUT);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart (tcgen05 format).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+    const uint64_t addr = smem_u32(p);
+    uint64_t d = (addr >> 4) & 0x3FFF;      // start address
+    d |= uint64_t(1) << 16;                 // leading byte offset (unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
+    d |= uint64_t(1) << 46;                 // descriptor version (sm_100)
+    d |= uint64_t(2) << 61;                 // layout: 128B swizzle
+    return d;
+}
+
+// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kTileTok.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileTok >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Exact int -> float for |s| < 2^22 (block dots are at most 32 * 127 * 127 in magnitude).
+__device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x4B400000) - 12582912.0f; }
+
+// Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
+__device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
+
+template <int DT>
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
+                                                           const __grid_constant__ CUtensorMap tmB,
+                                                           const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
+    constexpr bool kQ4 = DT == DT_Q4_0;
+    constexpr StageOffsets L = stage_layout(kQ4);
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full_raw[kStages], full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots], fin;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * kTileTok;
+    const int nks = g.nb / kStageBlocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full_raw[s], 1);
+            mbar_init(&full[s], kQ4 ? 64 : 1);
+            mbar_init(&empty[s], 1 + 8);  // the MMA commit + one arrive per epilogue warp
+        }
+        for (int j = 0; j < kSlots; ++j) {
+            mbar_init(&mma_done[j], 1);
+            mbar_init(&slot_free[j], 8);
+        }
+        mbar_init(&fin, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    volatile int* ab = &abort_flag;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            const unsigned bytes = (kQ4 ? kAPk : kASw) + kB + kDX;
+            for (int ks = 0; ks < nks; ++ks) {
+                const int s = ks % kStages, round = ks / kStages;
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
+                unsigned char* st = smem + s * L.bytes;
+                uint64_t* bar = kQ4 ? &full_raw[s] : &full[s];
+                mbar_expect_tx(bar, bytes);
+                if (kQ4)
+                    tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, bar);
+                else
+                    tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, bar);
+                tma_load_2d(st + L.b, &tmB, ks * 128, t0, bar);
+                tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, bar);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            int b = 0;
+            for (int ks = 0; ks < nks && !*ab; ++ks) {
+                const int s = ks % kStages, round = ks / kStages;
+                if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
+                tc_fence_after();
+                unsigned char* st = smem + s * L.bytes;
+                bool ok = true;
+                for (int k = 0; k < kStageBlocks; ++k, ++b) {
+                    const int slot = b % kSlots, use = b / kSlots;
+                    if (use > 0 && !mbar_wait(&slot_free[slot], (use - 1) & 1, ab, g.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    mma_i8(tmem + uint32_t(slot * kTileTok), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.b + 32 * k));
+                    mma_commit(&mma_done[slot]);
+                }
+                if (!ok) break;
+                mma_commit(&empty[s]);
+            }
+            mma_commit(&fin);  // arrives once every MMA issued above has completed
+        }
+    } else if (warp < 4) {
+        if (kQ4) {  // unpack the packed Q4 tile into the swizzled int8 layout
+            const int ct = threadIdx.x - 64;
+            for (int ks = 0; ks < nks; ++ks) {
+                const int s = ks % kStages, round = ks / kStages;
+                if (!mbar_wait(&full_raw[s], round & 1, ab, g.status)) break;
+                unsigned char* st = smem + s * L.bytes;
+                for (int c = ct; c < kTileRows * kStageBlocks; c += 64) {
+                    const int r = c >> 2, blk = c & 3;
+                    const uint4 w = *reinterpret_cast<const uint4*>(st + L.a_pk + r * 64 + blk * 16);
+                    const uint4 lo = make_uint4(q4_bytes(w.x & 0x0F0F0F0Fu), q4_bytes(w.y & 0x0F0F0F0Fu),
+                                                q4_bytes(w.z & 0x0F0F0F0Fu), q4_bytes(w.w & 0x0F0F0F0Fu));
+                    const uint4 hi = make_uint4(q4_bytes((w.x >> 4) & 0x0F0F0F0Fu), q4_bytes((w.y >> 4) & 0x0F0F0F0Fu),
+                                                q4_bytes((w.z >> 4) & 0x0F0F0F0Fu), q4_bytes((w.w >> 4) & 0x0F0F0F0Fu));
+                    // row r, 16-byte chunks 2 blk and 2 blk + 1 of its 128-byte line, swizzled by (r mod 8)
+                    unsigned char* line = st + L.a_sw + (r >> 3) * 1024 + (r & 7) * 128;
+                    *reinterpret_cast<uint4*>(line + (((2 * blk) ^ (r & 7)) << 4)) = lo;
+                    *reinterpret_cast<uint4*>(line + (((2 * blk + 1) ^ (r & 7)) << 4)) = hi;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the MMA reads through the async proxy
+                mbar_arrive(&full[s]);
+            }
+        }
+    } else {  // epilogue
+        const int q = warp & 3, half = (warp - 4) >> 2;
+        const int row = m0 + q * 32 + lane;
+        const bool row_ok = row < g.r1;
+        const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        uint2 dnext = __ldg(wd);
+        int b = 0;
+        for (int ks = 0; ks < nks; ++ks) {
+            const int s = ks % kStages;
+            const uint2 dcur = dnext;
+            if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
+            const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
+            const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
+            const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
+            const float* sdx = reinterpret_cast<const float*>(smem + s * L.bytes + L.dx) + half * 32 * kStageBlocks;
+            bool ok = true;
+            for (int k = 0; k < kStageBlocks; ++k, ++b) {
+                const int slot = b % kSlots, use = b / kSlots;
+                int got = 0;
+                if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+                if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                int v[32];
+                tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kTileTok + half * 32), v);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&slot_free[slot]);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[i]), dw[k]), sdx[i * kStageBlocks + k]));
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (row_ok && !*ab) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int t = t0 + half * 32 + i;
+                if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        if (lane == 0) {  // the issued MMAs must be done before their TMEM goes (bounded: they depend on nothing)
+            for (unsigned i = 0; i < kWaitLimit && !mbar_try(&fin, 0); ++i) {
+            }
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+               uint32_t box_in, uint32_t box_out, CUtensorMapSwizzle sw) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {box_in, box_out};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const DMat& W) {
+    return (W.dtype == DT_Q8_0 || W.dtype == DT_Q4_0) && W.cols % (kStageBlocks * QK) == 0 && encode_fn() != nullptr;
+}
+
+bool make_weight_map(const DMat& W, TcMap* out) {
+    if (!gemm_tc_supported(W)) return false;
+    if (W.dtype == DT_Q8_0)
+        return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, W.q, uint64_t(W.cols), uint64_t(W.rows), uint64_t(W.cols), 128,
+                         kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, W.q, uint64_t(W.cols / 2), uint64_t(W.rows), uint64_t(W.cols / 2),
+                     64, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcMap* mq, TcMap* md) {
+    if (cols % (kStageBlocks * QK) != 0 || rows_alloc <= 0) return false;
+    const int nb = cols / QK;
+    return encode_2d(&mq->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
+                     kTileTok, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_2d(&md->m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
+                     kStageBlocks, kTileTok, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+size_t gemm_tc_smem(int dtype) { return size_t(kStages) * stage_layout(dtype == DT_Q4_0).bytes + 1024; }
+
+cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcMap& qmap, const TcMap& dmap, int n, int r0, int r1,
+                             float* out, int ldo, unsigned* status, cudaStream_t st) {
+    if (r1 <= r0 || n <= 0) return cudaSuccess;
+    if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
+    GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
+    const dim3 grid(unsigned((r1 - r0 + kTileRows - 1) / kTileRows), unsigned((n + kTileTok - 1) / kTileTok));
+    const size_t smem = gemm_tc_smem(W.dtype);
+    if (W.dtype == DT_Q8_0) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        k_gemm_tc<DT_Q8_0><<<grid, kTcThreads, smem, st>>>(wmap.m, qmap.m, dmap.m, g);
+    } else if (W.dtype == DT_Q4_0) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        k_gemm_tc<DT_Q4_0><<<grid, kTcThreads, smem, st>>>(wmap.m, qmap.m, dmap.m, g);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace qb

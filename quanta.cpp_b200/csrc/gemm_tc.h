@@ -1,0 +1,36 @@
+// tcgen05 int8 matmul (gemm_tc.cu): TMA tensor maps and the launcher.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace qb {
+
+// Token count from which qnt_matmul's automatic choice takes the tensor cores.
+constexpr int kTcMinTokens = 1 << 30;
+
+struct alignas(64) TcMap {
+    CUtensorMap m;
+};
+
+struct GemmTcArgs {
+    int r0, r1;        // weight rows [r0, r1)
+    int nb;            // 32-blocks per row
+    int n;             // tokens
+    const __half* wd;  // weight block scales [rows][nb]
+    float* out;        // out[t * ldo + r]
+    int ldo;
+    unsigned* status;  // device status word (ERR_WAIT_TIMEOUT)
+};
+
+bool gemm_tc_supported(const DMat& W);
+// The weight matrix as the kernel's TMA source (Q8_0: 128B-swizzled int8 tiles; Q4_0: packed tiles).
+bool make_weight_map(const DMat& W, TcMap* out);
+// Quantized activations q [rows_alloc][cols] int8 and their block scales d [rows_alloc][cols / 32] f32.
+bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcMap* mq, TcMap* md);
+size_t gemm_tc_smem(int dtype);
+cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcMap& qmap, const TcMap& dmap, int n, int r0, int r1,
+                             float* out, int ldo, unsigned* status, cudaStream_t st);
+
+}  // namespace qb
