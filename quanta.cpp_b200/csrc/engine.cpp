@@ -274,6 +274,12 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         HD_ = static_cast<float*>(dalloc(size_t(kChunk) * (hp_.ffn_dim / QK) * 4));
         tokens_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         pos_ = static_cast<int*>(dalloc(16));
+        // tensor-core matmul sources (a layer without them, or a driver without TMA encode, uses the CUDA cores)
+        tc_act_ = make_act_maps(XQ_, DX_, kChunk, hp_.dim, &tm_xq_, &tm_dx_) &&
+                  make_act_maps(HQ_, HD_, kChunk, hp_.ffn_dim, &tm_hq_, &tm_hd_);
+        for (Layer& L : layers_)
+            L.tc = tc_act_ && make_weight_map(L.qkv, &L.t_qkv) && make_weight_map(L.o, &L.t_o) &&
+                   make_weight_map(L.gu, &L.t_gu) && make_weight_map(L.down, &L.t_down);
 
         const int V = hp_.vocab_size, nbd = hp_.dim / QK;
         hin_.xq = static_cast<int8_t*>(dalloc(size_t(hp_.dim)));
@@ -377,8 +383,15 @@ int Engine::launch_layers_decode(const int* pos_dev) {
     return 0;
 }
 
-int Engine::launch_matmul(const DMat& W, const int8_t* xq, const float* dx, int n, float* out) {
-    QB_TRY(launch_matmul_simt(W, xq, dx, n, 0, W.rows, out, W.rows, st_));
+int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out) {
+    const int8_t* xq = ffn_in ? HQ_ : XQ_;
+    const float* dx = ffn_in ? HD_ : DX_;
+    if (wmap && n >= kTcChunkMin) {
+        QB_TRY(launch_matmul_tc(W, *wmap, ffn_in ? tm_hq_ : tm_xq_, ffn_in ? tm_hd_ : tm_dx_, n, 0, W.rows, out, W.rows,
+                                status_, st_));
+    } else {
+        QB_TRY(launch_matmul_simt(W, xq, dx, n, 0, W.rows, out, W.rows, st_));
+    }
     return 0;
 }
 
@@ -386,16 +399,16 @@ int Engine::launch_chunk(int n, const int* pos_dev) {
     const int dim = hp_.dim;
     for (const Layer& L : layers_) {
         QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
-        if (int r = launch_matmul(L.qkv, XQ_, DX_, n, R_)) return r;
+        if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
         QB_TRY(launch_qkv_epilogue(L.qa, R_, n, pos_dev, Q_, st_, pdl_));
         QB_TRY(launch_attn(L.aa, Q_, pos_dev, n, ATT_, st_, pdl_));
         QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, st_, pdl_));
-        if (int r = launch_matmul(L.o, XQ_, DX_, n, R_)) return r;
+        if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
         QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
-        if (int r = launch_matmul(L.gu, XQ_, DX_, n, R_)) return r;
+        if (int r = launch_matmul(L.gu, L.tc ? &L.t_gu : nullptr, false, n, R_)) return r;
         QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, exptab_, st_, pdl_));
-        if (int r = launch_matmul(L.down, HQ_, HD_, n, R_)) return r;
+        if (int r = launch_matmul(L.down, L.tc ? &L.t_down : nullptr, true, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
     }
     return 0;

@@ -12,6 +12,7 @@
 #include <tuple>
 #include <vector>
 
+#include "gemm_tc.h"
 #include "head_kernels.h"
 #include "layer_kernels.h"
 #include "qnt_file.h"
@@ -101,6 +102,8 @@ private:
         QkvArgs qa;
         AttnArgs aa;
         SlicePlan p_qkv, p_o, p_gu, p_down;
+        TcMap t_qkv{}, t_o{}, t_gu{}, t_down{};  // TMA sources of the tensor-core matmul (valid when tc)
+        bool tc = false;
     };
 
     bool fail(const std::string& m);
@@ -114,7 +117,8 @@ private:
     // marked must ids when penal).
     int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
                     int n_list, bool penal, float penalty);
-    int launch_matmul(const DMat& W, const int8_t* xq, const float* dx, int n, float* out);
+    // Prefill / batched matmul into R_: the tensor cores when the layer has TMA sources and n is large enough.
+    int launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out);
     int run_graph(const std::string& key, const std::function<int()>& body);
     int sync_check();
 
@@ -140,9 +144,12 @@ private:
     __half *kcache_ = nullptr, *vcache_ = nullptr;
 
     // activations (chunk of up to kChunk tokens)
-    static constexpr int kChunk = 32;
+    static constexpr int kChunk = 128;
+    static constexpr int kTcChunkMin = 16;  // fewer tokens: the CUDA-core matmul
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;
+    TcMap tm_xq_{}, tm_dx_{}, tm_hq_{}, tm_hd_{};  // activation tiles of the tensor-core matmul (dim / ffn inputs)
+    bool tc_act_ = false;
     int* tokens_ = nullptr;
     int* pos_ = nullptr;  // chunk start position (device)
 
