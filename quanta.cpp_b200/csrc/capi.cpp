@@ -150,9 +150,9 @@ int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, i
         if ((reinterpret_cast<uintptr_t>(qx) | reinterpret_cast<uintptr_t>(dx)) & 15)
             return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
         if (n == 0 || r1 == r0) return QNT_OK;
-        qb::TcMap mq, md;
-        if (!qb::make_act_maps(qx, dx, n, W->m.cols, &mq, &md)) return set_err(QNT_ERR_CUDA, "TMA descriptor encode failed");
-        e = qb::launch_matmul_tc(W->m, W->wmap, mq, md, n, r0, r1, out, ldo, W->status, static_cast<cudaStream_t>(stream));
+        qb::TcAct act;
+        if (!qb::make_act_maps(qx, dx, n, W->m.cols, &act)) return set_err(QNT_ERR_CUDA, "TMA descriptor encode failed");
+        e = qb::launch_matmul_tc(W->m, W->wmap, act, n, r0, r1, out, ldo, W->status, static_cast<cudaStream_t>(stream));
     } else {
         e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, static_cast<cudaStream_t>(stream));
     }

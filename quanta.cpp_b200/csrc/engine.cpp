@@ -275,8 +275,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         tokens_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         pos_ = static_cast<int*>(dalloc(16));
         // tensor-core matmul sources (a layer without them, or a driver without TMA encode, uses the CUDA cores)
-        tc_act_ = make_act_maps(XQ_, DX_, kChunk, hp_.dim, &tm_xq_, &tm_dx_) &&
-                  make_act_maps(HQ_, HD_, kChunk, hp_.ffn_dim, &tm_hq_, &tm_hd_);
+        tc_act_ = make_act_maps(XQ_, DX_, kChunk, hp_.dim, &tm_x_) && make_act_maps(HQ_, HD_, kChunk, hp_.ffn_dim, &tm_h_);
         for (Layer& L : layers_)
             L.tc = tc_act_ && make_weight_map(L.qkv, &L.t_qkv) && make_weight_map(L.o, &L.t_o) &&
                    make_weight_map(L.gu, &L.t_gu) && make_weight_map(L.down, &L.t_down);
@@ -387,8 +386,7 @@ int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, 
     const int8_t* xq = ffn_in ? HQ_ : XQ_;
     const float* dx = ffn_in ? HD_ : DX_;
     if (wmap && n >= kTcChunkMin) {
-        QB_TRY(launch_matmul_tc(W, *wmap, ffn_in ? tm_hq_ : tm_xq_, ffn_in ? tm_hd_ : tm_dx_, n, 0, W.rows, out, W.rows,
-                                status_, st_));
+        QB_TRY(launch_matmul_tc(W, *wmap, ffn_in ? tm_h_ : tm_x_, n, 0, W.rows, out, W.rows, status_, st_));
     } else {
         QB_TRY(launch_matmul_simt(W, xq, dx, n, 0, W.rows, out, W.rows, st_));
     }

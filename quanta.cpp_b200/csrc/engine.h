@@ -148,7 +148,7 @@ private:
     static constexpr int kTcChunkMin = 16;  // fewer tokens: the CUDA-core matmul
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;
-    TcMap tm_xq_{}, tm_dx_{}, tm_hq_{}, tm_hd_{};  // activation tiles of the tensor-core matmul (dim / ffn inputs)
+    TcAct tm_x_{}, tm_h_{};  // activation tiles of the tensor-core matmul (dim / ffn inputs)
     bool tc_act_ = false;
     int* tokens_ = nullptr;
     int* pos_ = nullptr;  // chunk start position (device)

@@ -5,13 +5,14 @@
 //
 // The per-block scales rule out accumulating across blocks in the tensor core, so every quant block gets its own MMA
 // (K = 32, the int8 MMA's K) into its own TMEM slot, and the epilogue warps pull each block's int32 tile out of TMEM
-// and fold it into f32 registers in block order.  Per CTA: a tile of 128 weight rows x 64 tokens.
+// and fold it into f32 registers in block order.  Per CTA: a tile of 128 weight rows x N tokens (N = 64, or 16 for
+// matrices with many blocks per row, which have few rows: more CTAs, fewer tokens per thread).
 //   warp 0      TMA producer: per stage four blocks of the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B
-//               packed per row), the activation tile (64 tokens x 128 B, 128B-swizzled) and its block scales
+//               packed per row), the activation tile (N tokens x 128 B, 128B-swizzled) and its block scales
 //   warps 2-3   (Q4 only) unpack nibbles q into int8 q - 8 in the swizzled layout the MMA reads
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma.kind::i8 per block and commits to mbarriers
-//   warps 4-11  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and token columns
-//               32 ((w - 4) / 4) .. +32, one row per thread, 32 f32 accumulators
+//   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and token columns
+//               TPT ((w - 4) / 4) .. +TPT (TPT = N / 4), one row per thread, TPT f32 accumulators
 // Every wait is bounded: a wait that gives up sets ERR_WAIT_TIMEOUT in the status word and an abort flag that ends
 // every other wait, so the kernel always returns (and frees its TMEM once its issued MMAs have completed).
 #include <cuda.h>
@@ -26,25 +27,23 @@ namespace qb {
 
 namespace {
 
-constexpr int kTcThreads = 384;
-constexpr int kTileRows = 128, kTileTok = 64;
+constexpr int kEpiWarps = 16;
+constexpr int kTcThreads = 128 + 32 * kEpiWarps;
+constexpr int kTileRows = 128;
 constexpr int kStageBlocks = 4;          // quant blocks per pipeline stage (128 bytes of K)
 constexpr int kStages = 4;
-constexpr int kSlots = 4;                // TMEM accumulator slots, kTileTok columns each
-constexpr int kTmemCols = kSlots * kTileTok;
+constexpr int kSlots = 4;                // TMEM accumulator slots, N columns each
 constexpr int kASw = kTileRows * 128;    // swizzled int8 weight tile of a stage
 constexpr int kAPk = kTileRows * 64;     // packed Q4 tile of a stage
-constexpr int kB = kTileTok * 128;       // activation tile of a stage
-constexpr int kDX = kTileTok * kStageBlocks * 4;
 constexpr unsigned kWaitLimit = 1u << 22;
 
 struct StageOffsets {
     int a_sw, a_pk, b, dx, bytes;
 };
-__host__ __device__ constexpr StageOffsets stage_layout(bool q4) {
-    // 1024-byte alignment for the swizzled tiles (the 128B swizzle atom)
-    return StageOffsets{0, kASw, kASw + (q4 ? kAPk : 0), kASw + (q4 ? kAPk : 0) + kB,
-                        ((kASw + (q4 ? kAPk : 0) + kB + kDX) + 1023) / 1024 * 1024};
+// Stage layout for N tokens: swizzled tiles on 1024-byte boundaries (the 128B swizzle atom).
+__host__ __device__ constexpr StageOffsets stage_layout(bool q4, int N) {
+    return StageOffsets{0, kASw, kASw + (q4 ? kAPk : 0), kASw + (q4 ? kAPk : 0) + (N * 128 + 1023) / 1024 * 1024,
+                        ((kASw + (q4 ? kAPk : 0) + (N * 128 + 1023) / 1024 * 1024 + N * kStageBlocks * 4) + 1023) / 1024 * 1024};
 }
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
@@ -98,15 +97,18 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
     return d;
 }
 
-// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kTileTok.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileTok >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N tokens.
+__host__ __device__ constexpr uint32_t idesc_i8(int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+}
 
+template <int N>
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc_i8(N)), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -116,14 +118,22 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+// TMEM -> registers: this warp's 32 lanes, TPT consecutive 32-bit columns from taddr.
+template <int TPT>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, int (&v)[TPT]);
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, int (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, int (&v)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -134,30 +144,33 @@ __device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x
 // Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
 __device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
 
-template <int DT>
+template <int DT, int N>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
     constexpr bool kQ4 = DT == DT_Q4_0;
-    constexpr StageOffsets L = stage_layout(kQ4);
+    constexpr StageOffsets L = stage_layout(kQ4, N);
+    constexpr int TPT = N / 4;                // tokens per epilogue thread
+    constexpr int kTmemCols = kSlots * N < 32 ? 32 : kSlots * N;
+    constexpr int kB = N * 128, kDX = N * kStageBlocks * 4;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t full_raw[kStages], full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots], fin;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * kTileTok;
+    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * N;
     const int nks = g.nb / kStageBlocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_raw[s], 1);
             mbar_init(&full[s], kQ4 ? 64 : 1);
-            mbar_init(&empty[s], 1 + 8);  // the MMA commit + one arrive per epilogue warp
+            mbar_init(&empty[s], 1 + kEpiWarps);  // the MMA commit + one arrive per epilogue warp
         }
         for (int j = 0; j < kSlots; ++j) {
             mbar_init(&mma_done[j], 1);
-            mbar_init(&slot_free[j], 8);
+            mbar_init(&slot_free[j], kEpiWarps);
         }
         mbar_init(&fin, 1);
         abort_flag = 0;
@@ -177,7 +190,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
-            const unsigned bytes = (kQ4 ? kAPk : kASw) + kB + kDX;
+            const unsigned bytes = (kQ4 ? kAPk : kASw) + kB + kDX;  // full boxes (TMA zero-fills out-of-range rows)
             for (int ks = 0; ks < nks; ++ks) {
                 const int s = ks % kStages, round = ks / kStages;
                 if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
@@ -208,7 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                         break;
                     }
                     tc_fence_after();
-                    mma_i8(tmem + uint32_t(slot * kTileTok), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.b + 32 * k));
+                    mma_i8<N>(tmem + uint32_t(slot * N), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.b + 32 * k));
                     mma_commit(&mma_done[slot]);
                 }
                 if (!ok) break;
@@ -240,13 +253,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             }
         }
     } else {  // epilogue
-        const int q = warp & 3, half = (warp - 4) >> 2;
+        const int q = warp & 3, cg = (warp - 4) >> 2;
         const int row = m0 + q * 32 + lane;
         const bool row_ok = row < g.r1;
         const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
-        float acc[32];
+        float acc[TPT];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        for (int i = 0; i < TPT; ++i) acc[i] = 0.f;
         uint2 dnext = __ldg(wd);
         int b = 0;
         for (int ks = 0; ks < nks; ++ks) {
@@ -256,25 +269,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
             const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
             const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
-            const float* sdx = reinterpret_cast<const float*>(smem + s * L.bytes + L.dx) + half * 32 * kStageBlocks;
+            // the stage's block scales of this thread's tokens: [token][4 blocks]; two blocks per 8-byte load
+            const float2* sdx = reinterpret_cast<const float2*>(smem + s * L.bytes + L.dx) + cg * TPT * 2;
             bool ok = true;
-            for (int k = 0; k < kStageBlocks; ++k, ++b) {
-                const int slot = b % kSlots, use = b / kSlots;
-                int got = 0;
-                if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
-                if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
-                    ok = false;
-                    break;
+            for (int kp = 0; kp < kStageBlocks; kp += 2) {  // two blocks at a time (register budget)
+                int v[2][TPT];
+                for (int k = 0; k < 2; ++k, ++b) {
+                    const int slot = b % kSlots, use = b / kSlots;
+                    int got = 0;
+                    if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+                    if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    tmem_ld<TPT>(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * N + cg * TPT), v[k]);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&slot_free[slot]);
                 }
-                tc_fence_after();
-                int v[32];
-                tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kTileTok + half * 32), v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&slot_free[slot]);
+                if (!ok) break;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[i]), dw[k]), sdx[i * kStageBlocks + k]));
+                for (int i = 0; i < TPT; ++i) {
+                    const float2 dx = sdx[i * 2 + (kp >> 1)];
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[0][i]), dw[kp]), dx.x));
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[1][i]), dw[kp + 1]), dx.y));
+                }
             }
             if (!ok) break;
             __syncwarp();
@@ -282,8 +302,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         }
         if (row_ok && !*ab) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int t = t0 + half * 32 + i;
+            for (int i = 0; i < TPT; ++i) {
+                const int t = t0 + cg * TPT + i;
                 if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
             }
         }
@@ -341,36 +361,47 @@ bool make_weight_map(const DMat& W, TcMap* out) {
                      64, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcMap* mq, TcMap* md) {
+bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out) {
     if (cols % (kStageBlocks * QK) != 0 || rows_alloc <= 0) return false;
     const int nb = cols / QK;
-    return encode_2d(&mq->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
-                     kTileTok, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_2d(&md->m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
-                     kStageBlocks, kTileTok, CU_TENSOR_MAP_SWIZZLE_NONE);
+    auto pair = [&](int N, TcMap* mq, TcMap* md) {
+        return encode_2d(&mq->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
+                         uint32_t(N), CU_TENSOR_MAP_SWIZZLE_128B) &&
+               encode_2d(&md->m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
+                         kStageBlocks, uint32_t(N), CU_TENSOR_MAP_SWIZZLE_NONE);
+    };
+    return pair(64, &out->q64, &out->d64) && pair(16, &out->q16, &out->d16);
 }
 
-size_t gemm_tc_smem(int dtype) { return size_t(kStages) * stage_layout(dtype == DT_Q4_0).bytes + 1024; }
+namespace {
 
-cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcMap& qmap, const TcMap& dmap, int n, int r0, int r1,
-                             float* out, int ldo, unsigned* status, cudaStream_t st) {
+template <int DT, int N>
+cudaError_t launch_tc_t(const DMat& W, const TcMap& wmap, const TcMap& mq, const TcMap& md, const GemmTcArgs& g, int rows,
+                        cudaStream_t st) {
+    const size_t smem = size_t(kStages) * stage_layout(DT == DT_Q4_0, N).bytes + 1024;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    const dim3 grid(unsigned((rows + kTileRows - 1) / kTileRows), unsigned((g.n + N - 1) / N));
+    k_gemm_tc<DT, N><<<grid, kTcThreads, smem, st>>>(wmap.m, mq.m, md.m, g);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
+                             unsigned* status, cudaStream_t st) {
     if (r1 <= r0 || n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
-    GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
-    const dim3 grid(unsigned((r1 - r0 + kTileRows - 1) / kTileRows), unsigned((n + kTileTok - 1) / kTileTok));
-    const size_t smem = gemm_tc_smem(W.dtype);
-    if (W.dtype == DT_Q8_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q8_0><<<grid, kTcThreads, smem, st>>>(wmap.m, qmap.m, dmap.m, g);
-    } else if (W.dtype == DT_Q4_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q4_0><<<grid, kTcThreads, smem, st>>>(wmap.m, qmap.m, dmap.m, g);
-    } else {
-        return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+    const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
+    // Matrices with many blocks per row have few rows (down projection): 16-token tiles give them more CTAs.
+    const bool narrow = W.cols / QK > 64 || n <= 16;
+    if (W.dtype == DT_Q8_0)
+        return narrow ? launch_tc_t<DT_Q8_0, 16>(W, wmap, act.q16, act.d16, g, r1 - r0, st)
+                      : launch_tc_t<DT_Q8_0, 64>(W, wmap, act.q64, act.d64, g, r1 - r0, st);
+    if (W.dtype == DT_Q4_0)
+        return narrow ? launch_tc_t<DT_Q4_0, 16>(W, wmap, act.q16, act.d16, g, r1 - r0, st)
+                      : launch_tc_t<DT_Q4_0, 64>(W, wmap, act.q64, act.d64, g, r1 - r0, st);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace qb
