@@ -144,7 +144,7 @@ private:
     __half *kcache_ = nullptr, *vcache_ = nullptr;
 
     // activations (chunk of up to kChunk tokens)
-    static constexpr int kChunk = 128;
+    static constexpr int kChunk = 512;
     static constexpr int kTcChunkMin = 16;  // fewer tokens: the CUDA-core matmul
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;

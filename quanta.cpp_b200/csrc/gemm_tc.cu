@@ -36,6 +36,7 @@ constexpr int kSlots = 4;                // TMEM accumulator slots, N columns ea
 constexpr int kASw = kTileRows * 128;    // swizzled int8 weight tile of a stage
 constexpr int kAPk = kTileRows * 64;     // packed Q4 tile of a stage
 constexpr unsigned kWaitLimit = 1u << 22;
+constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
 
 struct StageOffsets {
     int a_sw, a_pk, b, dx, bytes;
@@ -61,10 +62,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
     unsigned ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
+        : "r"(smem_u32(b)), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
