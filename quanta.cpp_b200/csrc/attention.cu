@@ -218,7 +218,150 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
 constexpr int kRingDecode = 8;  // V blocks in flight behind a decode token's softmax
 constexpr int kRingBatch = 3;   // multi-token launches: smaller footprint, more CTAs per SM
 
+// ---------------------------------------------------------------- multi-token (prefill) attention
+
+// One CTA per (kv head, token), 256 threads: warp h owns query head g * group + h.  K and V stream through one shared
+// tile (f32, converted once for all the group's heads); each warp keeps its head's scores / weights in shared memory
+// and runs its own ordered sums: lane 0 the softmax sum, every lane two output dimensions (lane, lane + 32).
+constexpr int kGmax = kWarps;                   // query heads per kv head: one warp each
+constexpr int kPfTile = 128;                    // positions per K / V tile
+constexpr int kPfStride = kHd + 1;              // f32 tile row stride
+constexpr int kPfTileBytes = kPfTile * kPfStride * 4;
+
+__global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const float* __restrict__ Q,
+                                                           const int* __restrict__ pos_dev, int n_cap,
+                                                           float* __restrict__ out) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* sq = reinterpret_cast<float*>(smem);                    // [kGmax][kHd]
+    float* tile = sq + kGmax * kHd;                                // [kPfTile][kPfStride]
+    float* E = tile + kPfTile * kPfStride;                         // [group][ecap]
+    pdl_wait();
+    pdl_launch_dependents();
+    const int g = blockIdx.x, t = blockIdx.y;
+    const int group = a.n_heads / a.n_kv;
+    const int n = __ldcg(pos_dev) + t + 1;
+    const int ecap = (n_cap + 3) & ~3;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool head = warp < group;
+    float* Eh = E + warp * ecap;
+    for (int i = tid; i < group * kHd; i += kThreads) sq[i] = __ldcg(Q + (size_t(t) * a.n_heads + size_t(g) * group) * kHd + i);
+    // loads the rows [p, p + kPfTile) of C (this kv head) as f32 into the tile; 4 granules of 16 bytes per thread
+    constexpr int U = kPfTile * 8 / kThreads;
+    uint4 buf[U];
+    auto fetch = [&](const __half* C, int p) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = u * kThreads + tid, row = i >> 3;
+            buf[u] = p + row < n ? __ldcg(reinterpret_cast<const uint4*>(C + size_t(p + row) * a.kv_dim + g * kHd) + (i & 7))
+                                 : make_uint4(0, 0, 0, 0);
+        }
+    };
+    auto store = [&] {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = u * kThreads + tid, row = i >> 3, c8 = (i & 7) * 8;
+            const __half2* h2 = reinterpret_cast<const __half2*>(&buf[u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(h2[k]);
+                tile[row * kPfStride + c8 + 2 * k] = f.x;
+                tile[row * kPfStride + c8 + 2 * k + 1] = f.y;
+            }
+        }
+    };
+    // ---- scores, four positions per lane per tile
+    float lmax = -INFINITY;
+    fetch(a.kcache, 0);
+    for (int p = 0; p < n; p += kPfTile) {
+        __syncthreads();  // the previous tile's readers are done (and the queries are visible)
+        store();
+        __syncthreads();
+        if (p + kPfTile < n) fetch(a.kcache, p + kPfTile);  // next tile in flight during this one's dots
+        if (head) {
+            const float* qh = sq + warp * kHd;
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+            for (int i = 0; i < kHd; ++i) {
+                const float qi = qh[i];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) sc[u] = fadd(sc[u], fmul(qi, tile[(lane + 32 * u) * kPfStride + i]));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = p + lane + 32 * u;
+                if (j < n) {
+                    const float v = fmul(sc[u], a.scale);
+                    Eh[j] = v;
+                    lmax = fmaxf(lmax, v);
+                }
+            }
+        }
+    }
+    // ---- softmax of this warp's head: exps in parallel, the sum in position order on lane 0
+    float inv = 0.f;
+    if (head) {
+        const float m = warp_max(lmax);
+        for (int j = lane; j < n; j += 32) Eh[j] = exp_ref(fsub(Eh[j], m), a.exptab);
+        __syncwarp();
+        if (lane == 0) inv = fdiv(1.0f, ordered_sum(Eh, n));
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int j = lane; j < n; j += 32) Eh[j] = fmul(Eh[j], inv);
+        __syncwarp();
+    }
+    // ---- outputs in position order, two dimensions per lane
+    float o0 = 0.f, o1 = 0.f;
+    fetch(a.vcache, 0);
+    for (int p = 0; p < n; p += kPfTile) {
+        __syncthreads();
+        store();
+        __syncthreads();
+        if (p + kPfTile < n) fetch(a.vcache, p + kPfTile);
+        if (head) {
+            const int rows = min(kPfTile, n - p);
+            const float* e = Eh + p;
+            int j = 0;
+            for (; j + 8 <= rows; j += 8) {
+                float av[8], v0[8], v1[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    av[k] = e[j + k];
+                    v0[k] = tile[(j + k) * kPfStride + lane];
+                    v1[k] = tile[(j + k) * kPfStride + lane + 32];
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    o0 = fadd(o0, fmul(av[k], v0[k]));
+                    o1 = fadd(o1, fmul(av[k], v1[k]));
+                }
+            }
+            for (; j < rows; ++j) {
+                o0 = fadd(o0, fmul(e[j], tile[j * kPfStride + lane]));
+                o1 = fadd(o1, fmul(e[j], tile[j * kPfStride + lane + 32]));
+            }
+        }
+    }
+    if (head) {
+        float* o = out + (size_t(t) * a.n_heads + size_t(g) * group + warp) * kHd;
+        o[lane] = o0;
+        o[lane + 32] = o1;
+    }
+}
+
+inline size_t prefill_smem_bytes(int group, int n_cap) {
+    return size_t(kGmax) * kHd * 4 + size_t(kPfTileBytes) + size_t(group) * ((n_cap + 3) & ~3) * 4;
+}
+
 }  // namespace
+
+cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
+                                cudaStream_t st, bool pdl) {
+    const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
+    if (a.head_dim != kHd || group < 1 || group > kGmax || group * a.n_kv != a.n_heads || pos_bound < n_tok)
+        return cudaErrorInvalidValue;
+    const size_t smem = prefill_smem_bytes(group, pos_bound);
+    if (smem > 227 * 1024) return launch_attn(a, Q, pos_dev, n_tok, out, st, pdl);  // very long contexts
+    return launch_pdl(k_attn_prefill, dim3(a.n_kv, n_tok), dim3(kThreads), smem, st, pdl, a, Q, pos_dev, pos_bound, out);
+}
 
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl) {
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;

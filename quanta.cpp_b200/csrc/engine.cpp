@@ -393,13 +393,13 @@ int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, 
     return 0;
 }
 
-int Engine::launch_chunk(int n, const int* pos_dev) {
+int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound) {
     const int dim = hp_.dim;
     for (const Layer& L : layers_) {
         QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
         if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
         QB_TRY(launch_qkv_epilogue(L.qa, R_, n, pos_dev, Q_, st_, pdl_));
-        QB_TRY(launch_attn(L.aa, Q_, pos_dev, n, ATT_, st_, pdl_));
+        QB_TRY(launch_attn_prefill(L.aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_));
         QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, st_, pdl_));
         if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
@@ -563,7 +563,7 @@ int Engine::forward_batch(const int* tokens, int n, int pos0, const HeadQueryC* 
         cudaMemcpyAsync(tokens_, tokens + i, size_t(m) * 4, cudaMemcpyHostToDevice, st_);
         cudaMemcpyAsync(pos_, &p, 4, cudaMemcpyHostToDevice, st_);
         QB_TRY(launch_embed(embed_, tokens_, m, X_, status_, st_, false));
-        if (int r = launch_chunk(m, pos_)) return r;
+        if (int r = launch_chunk(m, pos_, p + m)) return r;
         last = m - 1;
     }
     const int n_must = hm.shortlist ? hq->n_must : 0;

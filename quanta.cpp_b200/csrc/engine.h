@@ -112,7 +112,7 @@ private:
     DMat upload_matrix(const HostTensor& t);
     DMat upload_fused(const std::vector<const HostTensor*>& parts, int mode);
     int launch_layers_decode(const int* pos_dev);
-    int launch_chunk(int n, const int* pos_dev);
+    int launch_chunk(int n, const int* pos_dev, int pos_bound);  // positions of the chunk stay below pos_bound
     // Head pass: full or shortlist; n_list > 0 also produces the sampler's stage-1 lists (with the penalty of the
     // marked must ids when penal).
     int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
