@@ -3,16 +3,19 @@
 // (engine/src/ops_ref.cpp:122-160): per (row, token) acc = acc + (float(s_b) * dw_b) * dx_b over the 32-blocks b in
 // order, s_b the exact int32 block dot.
 //
-// The per-block scales rule out accumulating across blocks in the tensor core, so every quant block gets its own MMA
-// (K = 32, the int8 MMA's K) into its own TMEM slot, and the epilogue warps pull each block's int32 tile out of TMEM
-// and fold it into f32 registers in block order.  Per CTA: a tile of 128 weight rows x N tokens (N = 64, or 16 for
-// matrices with many blocks per row, which have few rows: more CTAs, fewer tokens per thread).
-//   warp 0      TMA producer: per stage four blocks of the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B
-//               packed per row), the activation tile (N tokens x 128 B, 128B-swizzled) and its block scales
-//   warps 2-3   (Q4 only) unpack nibbles q into int8 q - 8 in the swizzled layout the MMA reads
-//   warp 1      allocates TMEM; one lane issues tcgen05.mma.kind::i8 per block and commits to mbarriers
-//   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and token columns
-//               TPT ((w - 4) / 4) .. +TPT (TPT = N / 4), one row per thread, TPT f32 accumulators
+// The per-block scales rule out accumulating across blocks in the tensor core: every block's int32 dot has to leave
+// the MMA on its own.  One MMA (K = 128, four blocks) still yields four separate block dots per token by running
+// against a block-diagonal copy of the activation tile: row 4 t + b of it holds token t's 32 bytes of block b and zeros
+// elsewhere, so output column 4 t + b is exactly s_b for token t.  Per CTA: a tile of 128 weight rows x 32 tokens
+// (MMA N = 128 columns), four blocks per pipeline stage.
+//   warp 0      TMA producer: per stage the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B packed per row),
+//               the activation tile (32 tokens x 128 B, 128B-swizzled) and its block scales
+//   warps 2-3   build the stage's operands in shared memory: the block-diagonal activation tile (its zero chunks are
+//               written once) and, for Q4, the int8 q - 8 weights in the swizzled layout the MMA reads
+//   warp 1      allocates TMEM; one lane issues the stage's four tcgen05.mma.kind::i8 into one of four TMEM slots
+//   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and the 32 columns of tokens
+//               8 ((w - 4) / 4) .. +8 with one tcgen05.ld per stage, and folds the four blocks into 8 f32
+//               accumulators per thread in block order
 // Every wait is bounded: a wait that gives up sets ERR_WAIT_TIMEOUT in the status word and an abort flag that ends
 // every other wait, so the kernel always returns (and frees its TMEM once its issued MMAs have completed).
 #include <cuda.h>
@@ -30,21 +33,32 @@ namespace {
 constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = 128 + 32 * kEpiWarps;
 constexpr int kTileRows = 128;
-constexpr int kStageBlocks = 4;          // quant blocks per pipeline stage (128 bytes of K)
+constexpr int kTileTok = 32;                       // tokens per tile
+constexpr int kStageBlocks = 4;                    // quant blocks per pipeline stage (128 bytes of K)
+constexpr int kCols = kTileTok * kStageBlocks;     // MMA N: one column per (token, block)
+constexpr int kTpt = kTileTok / 4;                 // tokens per epilogue thread
 constexpr int kStages = 4;
-constexpr int kSlots = 4;                // TMEM accumulator slots, N columns each
-constexpr int kASw = kTileRows * 128;    // swizzled int8 weight tile of a stage
-constexpr int kAPk = kTileRows * 64;     // packed Q4 tile of a stage
+constexpr int kSlots = 4;                          // TMEM accumulator slots of kCols columns
+constexpr int kTmemCols = kSlots * kCols;          // 512: the whole TMEM of the SM (one CTA per SM)
+constexpr int kASw = kTileRows * 128;              // swizzled int8 weight tile of a stage
+constexpr int kAPk = kTileRows * 64;               // packed Q4 tile of a stage
+constexpr int kB = kTileTok * 128;                 // activation tile of a stage
+constexpr int kBD = kCols * 128;                   // block-diagonal activation tile
+constexpr int kDX = kTileTok * kStageBlocks * 4;
 constexpr unsigned kWaitLimit = 1u << 22;
 constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
 
 struct StageOffsets {
-    int a_sw, a_pk, b, dx, bytes;
+    int a_sw, a_pk, b, bd, dx, bytes;
 };
-// Stage layout for N tokens: swizzled tiles on 1024-byte boundaries (the 128B swizzle atom).
-__host__ __device__ constexpr StageOffsets stage_layout(bool q4, int N) {
-    return StageOffsets{0, kASw, kASw + (q4 ? kAPk : 0), kASw + (q4 ? kAPk : 0) + (N * 128 + 1023) / 1024 * 1024,
-                        ((kASw + (q4 ? kAPk : 0) + (N * 128 + 1023) / 1024 * 1024 + N * kStageBlocks * 4) + 1023) / 1024 * 1024};
+// Stage layout: swizzled tiles on 1024-byte boundaries (the 128B swizzle atom).
+__host__ __device__ constexpr StageOffsets stage_layout(bool q4) {
+    return StageOffsets{0,
+                        kASw,
+                        kASw + (q4 ? kAPk : 0),
+                        kASw + (q4 ? kAPk : 0) + kB,
+                        kASw + (q4 ? kAPk : 0) + kB + kBD,
+                        (kASw + (q4 ? kAPk : 0) + kB + kBD + kDX + 1023) / 1024 * 1024};
 }
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
@@ -98,18 +112,15 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
     return d;
 }
 
-// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N tokens.
-__host__ __device__ constexpr uint32_t idesc_i8(int N) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
-}
+// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kCols.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kCols >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
 
-template <int N>
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc_i8(N)), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate ? 1 : 0), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -119,25 +130,21 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-// TMEM -> registers: this warp's 32 lanes, TPT consecutive 32-bit columns from taddr.
-template <int TPT>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, int (&v)[TPT]);
-template <>
-__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, int (&v)[4]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, int (&v)[16]) {
+// TMEM -> registers: this warp's 32 lanes, 32 consecutive 32-bit columns from taddr.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+// Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row atoms of 1024 bytes).
+__device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
 
 // Exact int -> float for |s| < 2^22 (block dots are at most 32 * 127 * 127 in magnitude).
 __device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x4B400000) - 12582912.0f; }
@@ -145,28 +152,25 @@ __device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x
 // Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
 __device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
 
-template <int DT, int N>
+template <int DT>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
     constexpr bool kQ4 = DT == DT_Q4_0;
-    constexpr StageOffsets L = stage_layout(kQ4, N);
-    constexpr int TPT = N / 4;                // tokens per epilogue thread
-    constexpr int kTmemCols = kSlots * N < 32 ? 32 : kSlots * N;
-    constexpr int kB = N * 128, kDX = N * kStageBlocks * 4;
+    constexpr StageOffsets L = stage_layout(kQ4);
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t full_raw[kStages], full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots], fin;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * N;
+    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * kTileTok;
     const int nks = g.nb / kStageBlocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_raw[s], 1);
-            mbar_init(&full[s], kQ4 ? 64 : 1);
+            mbar_init(&full[s], 64);              // the operand builders (warps 2-3)
             mbar_init(&empty[s], 1 + kEpiWarps);  // the MMA commit + one arrive per epilogue warp
         }
         for (int j = 0; j < kSlots; ++j) {
@@ -177,6 +181,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    // the block-diagonal tiles are zero outside their data chunks; those chunks never move, so zero them once
+    for (int s = 0; s < kStages; ++s)
+        for (int i = threadIdx.x; i < kBD / 16; i += kTcThreads)
+            reinterpret_cast<uint4*>(smem + s * L.bytes + L.bd)[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kTmemCols)
@@ -196,47 +205,45 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 const int s = ks % kStages, round = ks / kStages;
                 if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
                 unsigned char* st = smem + s * L.bytes;
-                uint64_t* bar = kQ4 ? &full_raw[s] : &full[s];
-                mbar_expect_tx(bar, bytes);
+                mbar_expect_tx(&full_raw[s], bytes);
                 if (kQ4)
-                    tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, bar);
+                    tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, &full_raw[s]);
                 else
-                    tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, bar);
-                tma_load_2d(st + L.b, &tmB, ks * 128, t0, bar);
-                tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, bar);
+                    tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, &full_raw[s]);
+                tma_load_2d(st + L.b, &tmB, ks * 128, t0, &full_raw[s]);
+                tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, &full_raw[s]);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer
-            int b = 0;
+        if (lane == 0) {  // MMA issuer: four K = 32 steps per stage accumulate into one slot
             for (int ks = 0; ks < nks && !*ab; ++ks) {
                 const int s = ks % kStages, round = ks / kStages;
+                const int slot = ks % kSlots, use = ks / kSlots;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
+                if (use > 0 && !mbar_wait(&slot_free[slot], (use - 1) & 1, ab, g.status)) break;
                 tc_fence_after();
                 unsigned char* st = smem + s * L.bytes;
-                bool ok = true;
-                for (int k = 0; k < kStageBlocks; ++k, ++b) {
-                    const int slot = b % kSlots, use = b / kSlots;
-                    if (use > 0 && !mbar_wait(&slot_free[slot], (use - 1) & 1, ab, g.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    mma_i8<N>(tmem + uint32_t(slot * N), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.b + 32 * k));
-                    mma_commit(&mma_done[slot]);
-                }
-                if (!ok) break;
+                for (int k = 0; k < kStageBlocks; ++k)
+                    mma_i8(tmem + uint32_t(slot * kCols), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.bd + 32 * k),
+                           k > 0);
+                mma_commit(&mma_done[slot]);
                 mma_commit(&empty[s]);
             }
             mma_commit(&fin);  // arrives once every MMA issued above has completed
         }
-    } else if (warp < 4) {
-        if (kQ4) {  // unpack the packed Q4 tile into the swizzled int8 layout
-            const int ct = threadIdx.x - 64;
-            for (int ks = 0; ks < nks; ++ks) {
-                const int s = ks % kStages, round = ks / kStages;
-                if (!mbar_wait(&full_raw[s], round & 1, ab, g.status)) break;
-                unsigned char* st = smem + s * L.bytes;
+    } else if (warp < 4) {  // operand builders
+        const int ct = threadIdx.x - 64;
+        for (int ks = 0; ks < nks; ++ks) {
+            const int s = ks % kStages, round = ks / kStages;
+            if (!mbar_wait(&full_raw[s], round & 1, ab, g.status)) break;
+            unsigned char* st = smem + s * L.bytes;
+            // block-diagonal activations: row 4 t + b <- chunks 2 b, 2 b + 1 of token t
+            for (int c = ct; c < kTileTok * kStageBlocks * 2; c += 64) {
+                const int rr = c >> 1, half = c & 1, t = rr >> 2, b = rr & 3, ch = 2 * b + half;
+                *reinterpret_cast<uint4*>(st + L.bd + sw128_off(rr, ch)) =
+                    *reinterpret_cast<const uint4*>(st + L.b + sw128_off(t, ch));
+            }
+            if (kQ4) {  // unpack the packed Q4 tile into the swizzled int8 layout
                 for (int c = ct; c < kTileRows * kStageBlocks; c += 64) {
                     const int r = c >> 2, blk = c & 3;
                     const uint4 w = *reinterpret_cast<const uint4*>(st + L.a_pk + r * 64 + blk * 16);
@@ -244,67 +251,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                                                 q4_bytes(w.z & 0x0F0F0F0Fu), q4_bytes(w.w & 0x0F0F0F0Fu));
                     const uint4 hi = make_uint4(q4_bytes((w.x >> 4) & 0x0F0F0F0Fu), q4_bytes((w.y >> 4) & 0x0F0F0F0Fu),
                                                 q4_bytes((w.z >> 4) & 0x0F0F0F0Fu), q4_bytes((w.w >> 4) & 0x0F0F0F0Fu));
-                    // row r, 16-byte chunks 2 blk and 2 blk + 1 of its 128-byte line, swizzled by (r mod 8)
-                    unsigned char* line = st + L.a_sw + (r >> 3) * 1024 + (r & 7) * 128;
-                    *reinterpret_cast<uint4*>(line + (((2 * blk) ^ (r & 7)) << 4)) = lo;
-                    *reinterpret_cast<uint4*>(line + (((2 * blk + 1) ^ (r & 7)) << 4)) = hi;
+                    *reinterpret_cast<uint4*>(st + L.a_sw + sw128_off(r, 2 * blk)) = lo;
+                    *reinterpret_cast<uint4*>(st + L.a_sw + sw128_off(r, 2 * blk + 1)) = hi;
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the MMA reads through the async proxy
-                mbar_arrive(&full[s]);
             }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the MMA reads through the async proxy
+            mbar_arrive(&full[s]);
         }
     } else {  // epilogue
         const int q = warp & 3, cg = (warp - 4) >> 2;
         const int row = m0 + q * 32 + lane;
         const bool row_ok = row < g.r1;
         const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
-        float acc[TPT];
+        float acc[kTpt];
 #pragma unroll
-        for (int i = 0; i < TPT; ++i) acc[i] = 0.f;
+        for (int i = 0; i < kTpt; ++i) acc[i] = 0.f;
         uint2 dnext = __ldg(wd);
-        int b = 0;
         for (int ks = 0; ks < nks; ++ks) {
-            const int s = ks % kStages;
+            const int s = ks % kStages, slot = ks % kSlots, use = ks / kSlots;
             const uint2 dcur = dnext;
             if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
             const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
             const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
-            const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
-            // the stage's block scales of this thread's tokens: [token][4 blocks]; two blocks per 8-byte load
-            const float2* sdx = reinterpret_cast<const float2*>(smem + s * L.bytes + L.dx) + cg * TPT * 2;
-            bool ok = true;
-            for (int kp = 0; kp < kStageBlocks; kp += 2) {  // two blocks at a time (register budget)
-                int v[2][TPT];
-                for (int k = 0; k < 2; ++k, ++b) {
-                    const int slot = b % kSlots, use = b / kSlots;
-                    int got = 0;
-                    if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
-                    if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    tmem_ld<TPT>(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * N + cg * TPT), v[k]);
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&slot_free[slot]);
-                }
-                if (!ok) break;
+            int got = 0;
+            if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+            if (!__shfl_sync(0xffffffffu, got, 0)) break;  // warp-uniform before the .sync.aligned TMEM load
+            tc_fence_after();
+            int v[32];  // v[4 i + b]: block b of token cg * kTpt + i
+            tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kCols + cg * 32), v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&slot_free[slot]);
+            const float4* sdx = reinterpret_cast<const float4*>(smem + s * L.bytes + L.dx) + cg * kTpt;
 #pragma unroll
-                for (int i = 0; i < TPT; ++i) {
-                    const float2 dx = sdx[i * 2 + (kp >> 1)];
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[0][i]), dw[kp]), dx.x));
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[1][i]), dw[kp + 1]), dx.y));
-                }
+            for (int i = 0; i < kTpt; ++i) {
+                const float4 dx = sdx[i];
+                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 0]), d01.x), dx.x));
+                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 1]), d01.y), dx.y));
+                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 2]), d23.x), dx.z));
+                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 3]), d23.y), dx.w));
             }
-            if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         if (row_ok && !*ab) {
 #pragma unroll
-            for (int i = 0; i < TPT; ++i) {
-                const int t = t0 + cg * TPT + i;
+            for (int i = 0; i < kTpt; ++i) {
+                const int t = t0 + cg * kTpt + i;
                 if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
             }
         }
@@ -365,44 +358,33 @@ bool make_weight_map(const DMat& W, TcMap* out) {
 bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out) {
     if (cols % (kStageBlocks * QK) != 0 || rows_alloc <= 0) return false;
     const int nb = cols / QK;
-    auto pair = [&](int N, TcMap* mq, TcMap* md) {
-        return encode_2d(&mq->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
-                         uint32_t(N), CU_TENSOR_MAP_SWIZZLE_128B) &&
-               encode_2d(&md->m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
-                         kStageBlocks, uint32_t(N), CU_TENSOR_MAP_SWIZZLE_NONE);
-    };
-    return pair(64, &out->q64, &out->d64) && pair(16, &out->q16, &out->d16);
+    return encode_2d(&out->q.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
+                     kTileTok, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_2d(&out->d.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
+                     kStageBlocks, kTileTok, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-namespace {
-
-template <int DT, int N>
-cudaError_t launch_tc_t(const DMat& W, const TcMap& wmap, const TcMap& mq, const TcMap& md, const GemmTcArgs& g, int rows,
-                        cudaStream_t st) {
-    const size_t smem = size_t(kStages) * stage_layout(DT == DT_Q4_0, N).bytes + 1024;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    const dim3 grid(unsigned((rows + kTileRows - 1) / kTileRows), unsigned((g.n + N - 1) / N));
-    k_gemm_tc<DT, N><<<grid, kTcThreads, smem, st>>>(wmap.m, mq.m, md.m, g);
-    return cudaGetLastError();
-}
-
-}  // namespace
+size_t gemm_tc_smem(int dtype) { return size_t(kStages) * stage_layout(dtype == DT_Q4_0).bytes + 1024; }
 
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
                              unsigned* status, cudaStream_t st) {
     if (r1 <= r0 || n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
     const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
-    // Matrices with many blocks per row have few rows (down projection): 16-token tiles give them more CTAs.
-    const bool narrow = W.cols / QK > 64 || n <= 16;
-    if (W.dtype == DT_Q8_0)
-        return narrow ? launch_tc_t<DT_Q8_0, 16>(W, wmap, act.q16, act.d16, g, r1 - r0, st)
-                      : launch_tc_t<DT_Q8_0, 64>(W, wmap, act.q64, act.d64, g, r1 - r0, st);
-    if (W.dtype == DT_Q4_0)
-        return narrow ? launch_tc_t<DT_Q4_0, 16>(W, wmap, act.q16, act.d16, g, r1 - r0, st)
-                      : launch_tc_t<DT_Q4_0, 64>(W, wmap, act.q64, act.d64, g, r1 - r0, st);
-    return cudaErrorInvalidValue;
+    const dim3 grid(unsigned((r1 - r0 + kTileRows - 1) / kTileRows), unsigned((n + kTileTok - 1) / kTileTok));
+    const size_t smem = gemm_tc_smem(W.dtype);
+    if (W.dtype == DT_Q8_0) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        k_gemm_tc<DT_Q8_0><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
+    } else if (W.dtype == DT_Q4_0) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        k_gemm_tc<DT_Q4_0><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace qb

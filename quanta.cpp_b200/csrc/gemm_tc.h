@@ -27,11 +27,11 @@ struct GemmTcArgs {
 bool gemm_tc_supported(const DMat& W);
 // The weight matrix as the kernel's TMA source (Q8_0: 128B-swizzled int8 tiles; Q4_0: packed tiles).
 bool make_weight_map(const DMat& W, TcMap* out);
-// Quantized activations q [rows_alloc][cols] int8 and their block scales d [rows_alloc][cols / 32] f32, as TMA sources
-// for the two token tiles (64 and 16 tokens).
+// Quantized activations q [rows_alloc][cols] int8 and their block scales d [rows_alloc][cols / 32] f32, as TMA sources.
 struct TcAct {
-    TcMap q64, d64, q16, d16;
+    TcMap q, d;
 };
+size_t gemm_tc_smem(int dtype);
 bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out);
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
                              unsigned* status, cudaStream_t st);
