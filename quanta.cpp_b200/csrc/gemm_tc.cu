@@ -6,8 +6,9 @@
 // The per-block scales rule out accumulating across blocks in the tensor core: every block's int32 dot has to leave
 // the MMA on its own.  One MMA (K = 128, four blocks) still yields four separate block dots per token by running
 // against a block-diagonal copy of the activation tile: row 4 t + b of it holds token t's 32 bytes of block b and zeros
-// elsewhere, so output column 4 t + b is exactly s_b for token t.  Per CTA: a tile of 128 weight rows x 32 tokens
-// (MMA N = 128 columns), four blocks per pipeline stage.
+// elsewhere, so output column 4 t + b is exactly s_b for token t.  Tiles of 128 weight rows x 32 tokens (MMA N = 128
+// columns), four blocks per pipeline stage; persistent CTAs (one per SM) walk their tiles with the pipeline running
+// across tile boundaries.
 //   warp 0      TMA producer: per stage the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B packed per row),
 //               the activation tile (32 tokens x 128 B, 128B-swizzled) and its block scales
 //   warps 2-3   build the stage's operands in shared memory: the block-diagonal activation tile (its zero chunks are
@@ -21,6 +22,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gemm_tc.h"
@@ -164,8 +166,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = g.r0 + blockIdx.x * kTileRows, t0 = blockIdx.y * kTileTok;
     const int nks = g.nb / kStageBlocks;
+    const int n_tt = (g.n + kTileTok - 1) / kTileTok, n_tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * n_tt;
+    // tile -> (first weight row, first token); tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+    auto tile_m0 = [&](int tile) { return g.r0 + (tile / n_tt) * kTileRows; };
+    auto tile_t0 = [&](int tile) { return (tile % n_tt) * kTileTok; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -201,24 +206,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
             const unsigned bytes = (kQ4 ? kAPk : kASw) + kB + kDX;  // full boxes (TMA zero-fills out-of-range rows)
-            for (int ks = 0; ks < nks; ++ks) {
-                const int s = ks % kStages, round = ks / kStages;
-                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
-                unsigned char* st = smem + s * L.bytes;
-                mbar_expect_tx(&full_raw[s], bytes);
-                if (kQ4)
-                    tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, &full_raw[s]);
-                else
-                    tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, &full_raw[s]);
-                tma_load_2d(st + L.b, &tmB, ks * 128, t0, &full_raw[s]);
-                tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, &full_raw[s]);
+            int step = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*ab; tile += gridDim.x) {
+                const int m0 = tile_m0(tile), t0 = tile_t0(tile);
+                for (int ks = 0; ks < nks; ++ks, ++step) {
+                    const int s = step % kStages, round = step / kStages;
+                    if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
+                    unsigned char* st = smem + s * L.bytes;
+                    mbar_expect_tx(&full_raw[s], bytes);
+                    if (kQ4)
+                        tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, &full_raw[s]);
+                    else
+                        tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, &full_raw[s]);
+                    tma_load_2d(st + L.b, &tmB, ks * 128, t0, &full_raw[s]);
+                    tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, &full_raw[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer: four K = 32 steps per stage accumulate into one slot
-            for (int ks = 0; ks < nks && !*ab; ++ks) {
-                const int s = ks % kStages, round = ks / kStages;
-                const int slot = ks % kSlots, use = ks / kSlots;
+            const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
+            for (int step = 0; step < steps && !*ab; ++step) {
+                const int s = step % kStages, round = step / kStages;
+                const int slot = step % kSlots, use = step / kSlots;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
                 if (use > 0 && !mbar_wait(&slot_free[slot], (use - 1) & 1, ab, g.status)) break;
                 tc_fence_after();
@@ -233,8 +243,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         }
     } else if (warp < 4) {  // operand builders
         const int ct = threadIdx.x - 64;
-        for (int ks = 0; ks < nks; ++ks) {
-            const int s = ks % kStages, round = ks / kStages;
+        const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
+        for (int step = 0; step < steps; ++step) {
+            const int s = step % kStages, round = step / kStages;
             if (!mbar_wait(&full_raw[s], round & 1, ab, g.status)) break;
             unsigned char* st = smem + s * L.bytes;
             // block-diagonal activations: row 4 t + b <- chunks 2 b, 2 b + 1 of token t
@@ -260,45 +271,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         }
     } else {  // epilogue
         const int q = warp & 3, cg = (warp - 4) >> 2;
-        const int row = m0 + q * 32 + lane;
-        const bool row_ok = row < g.r1;
-        const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
-        float acc[kTpt];
+        int step = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int m0 = tile_m0(tile), t0 = tile_t0(tile);
+            const int row = m0 + q * 32 + lane;
+            const bool row_ok = row < g.r1;
+            const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
+            float acc[kTpt];
 #pragma unroll
-        for (int i = 0; i < kTpt; ++i) acc[i] = 0.f;
-        uint2 dnext = __ldg(wd);
-        for (int ks = 0; ks < nks; ++ks) {
-            const int s = ks % kStages, slot = ks % kSlots, use = ks / kSlots;
-            const uint2 dcur = dnext;
-            if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
-            const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
-            const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
-            int got = 0;
-            if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
-            if (!__shfl_sync(0xffffffffu, got, 0)) break;  // warp-uniform before the .sync.aligned TMEM load
-            tc_fence_after();
-            int v[32];  // v[4 i + b]: block b of token cg * kTpt + i
-            tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kCols + cg * 32), v);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&slot_free[slot]);
-            const float4* sdx = reinterpret_cast<const float4*>(smem + s * L.bytes + L.dx) + cg * kTpt;
+            for (int i = 0; i < kTpt; ++i) acc[i] = 0.f;
+            uint2 dnext = __ldg(wd);
+            bool ok = true;
+            for (int ks = 0; ks < nks; ++ks, ++step) {
+                const int s = step % kStages, slot = step % kSlots, use = step / kSlots;
+                const uint2 dcur = dnext;
+                if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
+                const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
+                const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
+                int got = 0;
+                if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+                if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                int v[32];  // v[4 i + b]: block b of token cg * kTpt + i
+                tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kCols + cg * 32), v);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&slot_free[slot]);
+                const float4* sdx = reinterpret_cast<const float4*>(smem + s * L.bytes + L.dx) + cg * kTpt;
 #pragma unroll
-            for (int i = 0; i < kTpt; ++i) {
-                const float4 dx = sdx[i];
-                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 0]), d01.x), dx.x));
-                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 1]), d01.y), dx.y));
-                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 2]), d23.x), dx.z));
-                acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 3]), d23.y), dx.w));
+                for (int i = 0; i < kTpt; ++i) {
+                    const float4 dx = sdx[i];
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 0]), d01.x), dx.x));
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 1]), d01.y), dx.y));
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 2]), d23.x), dx.z));
+                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 3]), d23.y), dx.w));
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        if (row_ok && !*ab) {
+            if (!ok) break;
+            if (row_ok) {
 #pragma unroll
-            for (int i = 0; i < kTpt; ++i) {
-                const int t = t0 + cg * kTpt + i;
-                if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+                for (int i = 0; i < kTpt; ++i) {
+                    const int t = t0 + cg * kTpt + i;
+                    if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+                }
             }
         }
     }
@@ -371,7 +391,15 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
     if (r1 <= r0 || n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
     const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
-    const dim3 grid(unsigned((r1 - r0 + kTileRows - 1) / kTileRows), unsigned((n + kTileTok - 1) / kTileTok));
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const int tiles = ((r1 - r0 + kTileRows - 1) / kTileRows) * ((n + kTileTok - 1) / kTileTok);
+    const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
     const size_t smem = gemm_tc_smem(W.dtype);
     if (W.dtype == DT_Q8_0) {
         cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
