@@ -147,6 +147,20 @@ int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_s
 int qnt_session_step(qnt_model* m, int n);
 int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* stats);
 
+/* Batched serving of many independent sequences on one model (the multi-sequence API qnt_prefill_batch /
+ * qnt_decode_batch of the drop-in boundary; the reference serves one Session at a time, engine/src/session.cpp:13-52).
+ * Each sequence has its own f16 KV cache; a decode step advances n distinct sequences by one token each through the
+ * tensor-core matmul (tokens as the matmul's N), and the greedy head is one tensor-core pass over the Q8 lm_head with
+ * the argmax fused (Sampler::sample at temperature 0: the first maximum over ids < n_valid).
+ *   qnt_batch_init     allocates the caches of max_seqs sequences of ctx_len positions (lengths reset to 0)
+ *   qnt_prefill_batch  feeds n prompt tokens to sequence seq; *next_id = its greedy next token (may be NULL)
+ *   qnt_decode_batch   n <= 512 distinct sequences, tokens[i] appended to seq_ids[i]; next_ids[i] its greedy next token
+ *   qnt_batch_reset    forgets sequence seq (length 0) */
+int qnt_batch_init(qnt_model* m, int max_seqs, int ctx_len);
+int qnt_prefill_batch(qnt_model* m, int seq, const int* tokens, int n, int* next_id);
+int qnt_decode_batch(qnt_model* m, const int* seq_ids, const int* tokens, int n, int* next_ids);
+int qnt_batch_reset(qnt_model* m, int seq);
+
 /* Sampler (engine/src/sampler.h:20-38): Sampler::sample (sampler.cpp:22-85) on logits that are already in device
  * memory -- repetition penalty -> greedy argmax (first max) or top-k -> softmax(T) -> min-p -> top-p -> xorshift64*
  * draw, with the reference's float operations, so the same logits, history and seed give the same ids.

@@ -230,7 +230,7 @@ constexpr int kPfTileBytes = kPfTile * kPfStride * 4;
 
 __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const float* __restrict__ Q,
                                                            const int* __restrict__ pos_dev, int n_cap,
-                                                           float* __restrict__ out) {
+                                                           float* __restrict__ out, TokMap tm) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* sq = reinterpret_cast<float*>(smem);                    // [kGmax][kHd]
     float* tile = sq + kGmax * kHd;                                // [kPfTile][kPfStride]
@@ -239,7 +239,12 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
     pdl_launch_dependents();
     const int g = blockIdx.x, t = blockIdx.y;
     const int group = a.n_heads / a.n_kv;
-    const int n = __ldcg(pos_dev) + t + 1;
+    const int n = (tm.pos ? __ldcg(tm.pos + t) : __ldcg(pos_dev) + t) + 1;
+    if (tm.pos) {  // this token's sequence cache
+        const long long off = __ldcg(tm.off + t);
+        a.kcache += off;
+        a.vcache += off;
+    }
     const int ecap = (n_cap + 3) & ~3;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool head = warp < group;
@@ -354,13 +359,16 @@ inline size_t prefill_smem_bytes(int group, int n_cap) {
 }  // namespace
 
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
-                                cudaStream_t st, bool pdl) {
+                                cudaStream_t st, bool pdl, TokMap tm) {
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
-    if (a.head_dim != kHd || group < 1 || group > kGmax || group * a.n_kv != a.n_heads || pos_bound < n_tok)
+    if (a.head_dim != kHd || group < 1 || group > kGmax || group * a.n_kv != a.n_heads || pos_bound < (tm.pos ? 1 : n_tok))
         return cudaErrorInvalidValue;
     const size_t smem = prefill_smem_bytes(group, pos_bound);
-    if (smem > 227 * 1024) return launch_attn(a, Q, pos_dev, n_tok, out, st, pdl);  // very long contexts
-    return launch_pdl(k_attn_prefill, dim3(a.n_kv, n_tok), dim3(kThreads), smem, st, pdl, a, Q, pos_dev, pos_bound, out);
+    if (smem > 227 * 1024) {  // very long contexts (single sequence only)
+        if (tm.pos) return cudaErrorInvalidValue;
+        return launch_attn(a, Q, pos_dev, n_tok, out, st, pdl);
+    }
+    return launch_pdl(k_attn_prefill, dim3(a.n_kv, n_tok), dim3(kThreads), smem, st, pdl, a, Q, pos_dev, pos_bound, out, tm);
 }
 
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl) {

@@ -363,6 +363,26 @@ int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* sta
     return r;
 }
 
+int qnt_batch_init(qnt_model* m, int max_seqs, int ctx_len) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.batch_init(max_seqs, ctx_len));
+}
+
+int qnt_prefill_batch(qnt_model* m, int seq, const int* tokens, int n, int* next_id) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.batch_prefill(seq, tokens, n, next_id));
+}
+
+int qnt_decode_batch(qnt_model* m, const int* seq_ids, const int* tokens, int n, int* next_ids) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.batch_decode(seq_ids, tokens, n, next_ids));
+}
+
+int qnt_batch_reset(qnt_model* m, int seq) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.batch_reset(seq));
+}
+
 int qnt_model_debug_buffer(qnt_model* m, int what, float* out) {
     if (!m || !out) return set_err(QNT_ERR_INVALID, "null argument");
     return m->eng.debug_buffer(what, out);

@@ -18,6 +18,8 @@ Engine::~Engine() {
     if (st_) cudaStreamSynchronize(st_);
     for (auto& g : graphs_) cudaGraphExecDestroy(g.second);
     for (void* p : allocs_) cudaFree(p);
+    cudaFree(bkcache_);
+    cudaFree(bvcache_);
     if (st_) cudaStreamDestroy(st_);
 }
 
@@ -308,6 +310,11 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         part_buf_ = dalloc(size_t(n_lists_) * 32 * sizeof(Cand));
         status_ = static_cast<unsigned*>(dalloc(16));
         cudaMemset(status_, 0, 16);
+        tok_pos_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
+        tok_off_ = static_cast<long long*>(dalloc(size_t(kChunk) * 8));
+        head_tc_ = make_weight_map(lm_head_, &t_head_);
+        bcand_ = dalloc(size_t(argmax_parts(hp_.vocab_size)) * kChunk * sizeof(Cand));
+        bids_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         host_tmp_.resize(size_t(V));
     } catch (const std::exception& ex) {
         return bad(ex.what());
@@ -393,13 +400,24 @@ int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, 
     return 0;
 }
 
-int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound) {
+int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm) {
     const int dim = hp_.dim;
-    for (const Layer& L : layers_) {
+    const int kv_dim = hp_.n_kv_heads * hp_.head_dim;
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        const Layer& L = layers_[l];
+        QkvArgs qa = L.qa;
+        AttnArgs aa = L.aa;
+        if (tm.pos) {  // the batch caches: this layer's slice of sequence 0 (tok_off adds the token's sequence)
+            qa.kcache = bkcache_ + l * size_t(bctx_) * kv_dim;
+            qa.vcache = bvcache_ + l * size_t(bctx_) * kv_dim;
+            aa.kcache = qa.kcache;
+            aa.vcache = qa.vcache;
+            aa.max_chunks = (bctx_ + 63) / 64;
+        }
         QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
         if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_qkv_epilogue(L.qa, R_, n, pos_dev, Q_, st_, pdl_));
-        QB_TRY(launch_attn_prefill(L.aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_));
+        QB_TRY(launch_qkv_epilogue(qa, R_, n, pos_dev, Q_, st_, pdl_, tm));
+        QB_TRY(launch_attn_prefill(aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_, tm));
         QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, st_, pdl_));
         if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
@@ -749,6 +767,138 @@ int Engine::generate(const int* prompt, int n_prompt, const SamplerParamsC& sp, 
     cudaEventDestroy(e1);
     cudaEventDestroy(e2);
     return r;
+}
+
+}  // namespace qb
+
+namespace qb {
+
+// ---------------------------------------------------------------- batched serving
+
+int Engine::batch_init(int max_seqs, int ctx) {
+    if (max_seqs <= 0 || ctx <= 1 || ctx > ctx_) {
+        err_ = "batch_init: need max_seqs > 0 and 1 < ctx <= the model's context length";
+        return -1;
+    }
+    if (!tc_act_ || !head_tc_) {
+        err_ = "batched serving needs the tensor-core matmul (cols % 128 == 0 and a TMA-capable driver)";
+        return -4;
+    }
+    for (const Layer& L : layers_)
+        if (!L.tc) {
+            err_ = "batched serving needs tensor-core sources for every layer";
+            return -4;
+        }
+    cudaStreamSynchronize(st_);
+    cudaFree(bkcache_);
+    cudaFree(bvcache_);
+    bkcache_ = bvcache_ = nullptr;
+    const size_t kv_dim = size_t(hp_.n_kv_heads) * hp_.head_dim;
+    const size_t elems = size_t(max_seqs) * hp_.n_layers * size_t(ctx) * kv_dim;
+    cudaError_t e = cudaMalloc(&bkcache_, elems * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&bvcache_, elems * 2);
+    if (e != cudaSuccess) {
+        cudaFree(bkcache_);
+        bkcache_ = nullptr;
+        err_ = std::string("batch KV caches: ") + cudaGetErrorString(e);
+        return -2;
+    }
+    bmax_ = max_seqs;
+    bctx_ = ctx;
+    blens_.assign(size_t(max_seqs), 0);
+    return 0;
+}
+
+int Engine::batch_reset(int seq) {
+    if (seq < 0 || seq >= bmax_) {
+        err_ = "batch_reset: bad sequence id";
+        return -1;
+    }
+    blens_[size_t(seq)] = 0;
+    return 0;
+}
+
+int Engine::batch_head(int n, int* host_ids) {
+    QB_TRY(launch_norm_quant_rows(X_, final_norm_, n, hp_.dim, hp_.norm_eps, XQ_, DX_, st_, false));
+    QB_TRY(launch_matmul_tc_argmax(lm_head_, t_head_, tm_x_, n, n_valid_default(), bcand_, status_, st_));
+    QB_TRY(launch_argmax_reduce(bcand_, argmax_parts(lm_head_.rows), n, bids_, nullptr, st_));
+    cudaMemcpyAsync(host_ids, bids_, size_t(n) * 4, cudaMemcpyDeviceToHost, st_);
+    return sync_check();
+}
+
+int Engine::batch_prefill(int seq, const int* tokens, int n, int* next_id) {
+    if (bmax_ == 0) {
+        err_ = "batch_init first";
+        return -1;
+    }
+    if (seq < 0 || seq >= bmax_ || n <= 0 || !tokens) {
+        err_ = "batch_prefill: bad sequence id or tokens";
+        return -1;
+    }
+    const int len = blens_[size_t(seq)];
+    if (len + n > bctx_) {
+        err_ = "batch_prefill: sequence exceeds its context";
+        return -5;
+    }
+    const long long stride = (long long)hp_.n_layers * bctx_ * hp_.n_kv_heads * hp_.head_dim;
+    int last = 0;
+    for (int i = 0; i < n; i += kChunk) {
+        const int m = std::min(kChunk, n - i);
+        h_pos_.resize(size_t(m));
+        h_off_.assign(size_t(m), stride * seq);
+        for (int t = 0; t < m; ++t) h_pos_[size_t(t)] = len + i + t;
+        cudaMemcpyAsync(tokens_, tokens + i, size_t(m) * 4, cudaMemcpyHostToDevice, st_);
+        cudaMemcpyAsync(tok_pos_, h_pos_.data(), size_t(m) * 4, cudaMemcpyHostToDevice, st_);
+        cudaMemcpyAsync(tok_off_, h_off_.data(), size_t(m) * 8, cudaMemcpyHostToDevice, st_);
+        QB_TRY(launch_embed(embed_, tokens_, m, X_, status_, st_, false));
+        if (int r = launch_chunk(m, pos_, len + i + m, TokMap{tok_pos_, tok_off_})) return r;
+        cudaStreamSynchronize(st_);  // the host position arrays are rewritten by the next chunk
+        last = m - 1;
+    }
+    blens_[size_t(seq)] = len + n;
+    if (!next_id) return sync_check();
+    // the head of the last prompt token
+    if (last > 0) cudaMemcpyAsync(X_, X_ + size_t(last) * hp_.dim, size_t(hp_.dim) * 4, cudaMemcpyDeviceToDevice, st_);
+    return batch_head(1, next_id);
+}
+
+int Engine::batch_decode(const int* seq_ids, const int* tokens, int n, int* next_ids) {
+    if (bmax_ == 0) {
+        err_ = "batch_init first";
+        return -1;
+    }
+    if (n <= 0 || n > kChunk || !seq_ids || !tokens || !next_ids) {
+        err_ = "batch_decode: need 1 <= n <= " + std::to_string(kChunk) + " sequences";
+        return -1;
+    }
+    const long long stride = (long long)hp_.n_layers * bctx_ * hp_.n_kv_heads * hp_.head_dim;
+    h_pos_.resize(size_t(n));
+    h_off_.resize(size_t(n));
+    std::vector<char> seen(size_t(bmax_), 0);
+    int bound = 0;
+    for (int i = 0; i < n; ++i) {
+        const int s = seq_ids[i];
+        if (s < 0 || s >= bmax_ || seen[size_t(s)]) {
+            err_ = "batch_decode: sequence ids must be distinct and < max_seqs";
+            return -1;
+        }
+        seen[size_t(s)] = 1;
+        if (blens_[size_t(s)] + 1 > bctx_) {
+            err_ = "batch_decode: a sequence exceeds its context";
+            return -5;
+        }
+        h_pos_[size_t(i)] = blens_[size_t(s)];
+        h_off_[size_t(i)] = stride * s;
+        bound = std::max(bound, blens_[size_t(s)] + 1);
+    }
+    cudaMemcpyAsync(tokens_, tokens, size_t(n) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(tok_pos_, h_pos_.data(), size_t(n) * 4, cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(tok_off_, h_off_.data(), size_t(n) * 8, cudaMemcpyHostToDevice, st_);
+    QB_TRY(launch_embed(embed_, tokens_, n, X_, status_, st_, false));
+    if (int r = launch_chunk(n, pos_, bound, TokMap{tok_pos_, tok_off_})) return r;
+    if (int r = batch_head(n, next_ids)) return r;
+    for (int i = 0; i < n; ++i) blens_[size_t(seq_ids[i])] += 1;
+    return 0;
 }
 
 }  // namespace qb

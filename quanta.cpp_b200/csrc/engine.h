@@ -1,6 +1,7 @@
 // Model engine: the device-side replacement of quanta::Model + Session (engine/src/model.h:31-102,
 // engine/src/session.h:13-80).  One Engine owns one model in HBM, one sequence's f16 KV cache and the buffers of a
-// 32-token prefill chunk; forward / forward_batch / head keep the reference's contracts.
+// 512-token prefill chunk; forward / forward_batch / head keep the reference's contracts.  batch_* serve many
+// independent sequences at once (their own KV caches), one token each per decode step, greedy.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -73,6 +74,16 @@ public:
     int session_step(int n);
     int session_read(int* out_ids, int max_ids, GenStats* stats);
 
+    // Batched serving (greedy): up to max_seqs sequences of up to ctx positions each, KV caches of their own.
+    int batch_init(int max_seqs, int ctx);
+    // Prefills n prompt tokens of sequence seq (after its current length); *next_id = its greedy next token.
+    int batch_prefill(int seq, const int* tokens, int n, int* next_id);
+    // One decode step of n distinct sequences: tokens[i] goes to seq_ids[i] at its next position; next_ids[i] is the
+    // greedy next token (std::max_element over the logits: first maximum among ids < n_valid).
+    int batch_decode(const int* seq_ids, const int* tokens, int n, int* next_ids);
+    int batch_reset(int seq);
+    int batch_len(int seq) const { return seq >= 0 && seq < int(blens_.size()) ? blens_[size_t(seq)] : -1; }
+
     const HParams& hparams() const { return hp_; }
     int ctx_len() const { return ctx_; }
     int n_valid_default() const;
@@ -112,7 +123,9 @@ private:
     DMat upload_matrix(const HostTensor& t);
     DMat upload_fused(const std::vector<const HostTensor*>& parts, int mode);
     int launch_layers_decode(const int* pos_dev);
-    int launch_chunk(int n, const int* pos_dev, int pos_bound);  // positions of the chunk stay below pos_bound
+    // positions of the chunk stay below pos_bound; with tm.pos set, tokens of the batch caches (their own positions)
+    int launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm = TokMap{});
+    int batch_head(int n, int* host_ids);  // greedy ids of the n rows of X_
     // Head pass: full or shortlist; n_list > 0 also produces the sampler's stage-1 lists (with the penalty of the
     // marked must ids when penal).
     int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
@@ -181,6 +194,19 @@ private:
     int kernels_per_step_ = 0;
     int kernel_count_ = 0;  // launches issued since the last reset (counted by the launch helpers)
     std::map<std::string, cudaGraphExec_t> graphs_;
+
+    // batched serving
+    int bmax_ = 0, bctx_ = 0;
+    __half *bkcache_ = nullptr, *bvcache_ = nullptr;  // [seq][layer][bctx][kv_dim]
+    std::vector<int> blens_;
+    int* tok_pos_ = nullptr;              // [kChunk] device
+    long long* tok_off_ = nullptr;        // [kChunk] device
+    std::vector<int> h_pos_;
+    std::vector<long long> h_off_;
+    TcMap t_head_{};
+    bool head_tc_ = false;
+    void* bcand_ = nullptr;               // argmax candidates [argmax_parts(V)][kChunk]
+    int* bids_ = nullptr;                 // [kChunk]
     std::vector<float> host_tmp_;
 };
 

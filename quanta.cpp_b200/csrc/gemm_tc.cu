@@ -25,7 +25,10 @@
 #include <algorithm>
 #include <mutex>
 
+#include <climits>
+
 #include "gemm_tc.h"
+#include "head_kernels.h"
 #include "kernels.cuh"
 
 namespace qb {
@@ -154,7 +157,12 @@ __device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x
 // Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
 __device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
 
-template <int DT>
+__device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid) {
+    return av > bv || (av == bv && aid < bid);
+}
+
+// EPI 0: store the rows; EPI 1: per 32-row group and token, the best (value, id) into g.cand.
+template <int DT, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
@@ -313,11 +321,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (!ok) break;
-            if (row_ok) {
+            if (EPI == 0) {
+                if (row_ok) {
+#pragma unroll
+                    for (int i = 0; i < kTpt; ++i) {
+                        const int t = t0 + cg * kTpt + i;
+                        if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+                    }
+                }
+            } else {
+                const int mt = tile / n_tt;
 #pragma unroll
                 for (int i = 0; i < kTpt; ++i) {
+                    float v = row_ok && row < g.n_valid ? acc[i] : -INFINITY;
+                    int id = row_ok && row < g.n_valid ? row : INT_MAX;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float pv = __shfl_xor_sync(0xffffffffu, v, o);
+                        const int pid = __shfl_xor_sync(0xffffffffu, id, o);
+                        if (cand_better(pv, pid, v, id)) {
+                            v = pv;
+                            id = pid;
+                        }
+                    }
                     const int t = t0 + cg * kTpt + i;
-                    if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+                    if (lane == 0 && t < g.n) static_cast<Cand*>(g.cand)[(size_t(mt) * 4 + q) * g.n + t] = Cand{v, id};
                 }
             }
         }
@@ -386,11 +414,10 @@ bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, 
 
 size_t gemm_tc_smem(int dtype) { return size_t(kStages) * stage_layout(dtype == DT_Q4_0).bytes + 1024; }
 
-cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
-                             unsigned* status, cudaStream_t st) {
-    if (r1 <= r0 || n <= 0) return cudaSuccess;
-    if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
-    const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status};
+namespace {
+
+template <int EPI>
+cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, const GemmTcArgs& g, cudaStream_t st) {
     static int sms = 0;
     if (sms == 0) {
         int dev = 0;
@@ -398,20 +425,86 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
-    const int tiles = ((r1 - r0 + kTileRows - 1) / kTileRows) * ((n + kTileTok - 1) / kTileTok);
+    const int tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * ((g.n + kTileTok - 1) / kTileTok);
     const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
     const size_t smem = gemm_tc_smem(W.dtype);
     if (W.dtype == DT_Q8_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q8_0><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
+        k_gemm_tc<DT_Q8_0, EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
     } else if (W.dtype == DT_Q4_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q4_0><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
+        k_gemm_tc<DT_Q4_0, EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
     } else {
         return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+// One CTA per token: the best (value desc, id asc) of its n_parts candidates.
+__global__ void __launch_bounds__(256) k_argmax_reduce(const Cand* __restrict__ cand, int n_parts, int n, int* __restrict__ ids,
+                                                       float* __restrict__ vals) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float v = -INFINITY;
+    int id = INT_MAX;
+    for (int p = threadIdx.x; p < n_parts; p += blockDim.x) {
+        const Cand c = cand[size_t(p) * n + t];
+        if (cand_better(c.v, c.id, v, id)) {
+            v = c.v;
+            id = c.id;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float pv = __shfl_xor_sync(0xffffffffu, v, o);
+        const int pid = __shfl_xor_sync(0xffffffffu, id, o);
+        if (cand_better(pv, pid, v, id)) {
+            v = pv;
+            id = pid;
+        }
+    }
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = id;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < int(blockDim.x >> 5); ++w)
+            if (cand_better(sv[w], si[w], v, id)) {
+                v = sv[w];
+                id = si[w];
+            }
+        ids[t] = id == INT_MAX ? 0 : id;
+        if (vals) vals[t] = v;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
+                             unsigned* status, cudaStream_t st) {
+    if (r1 <= r0 || n <= 0) return cudaSuccess;
+    if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
+    const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status, 0, nullptr};
+    return launch_tc_any<0>(W, wmap, act, g, st);
+}
+
+int argmax_parts(int rows) { return ((rows + kTileRows - 1) / kTileRows) * 4; }
+
+cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int n_valid, void* cand,
+                                    unsigned* status, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
+    const GemmTcArgs g{0, W.rows, W.cols / QK, n, W.d, nullptr, 0, status, n_valid, cand};
+    return launch_tc_any<1>(W, wmap, act, g, st);
+}
+
+cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids, float* vals, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_argmax_reduce<<<n, 256, 0, st>>>(static_cast<const Cand*>(cand), n_parts, n, ids, vals);
     return cudaGetLastError();
 }
 

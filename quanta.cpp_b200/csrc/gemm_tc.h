@@ -22,6 +22,8 @@ struct GemmTcArgs {
     float* out;        // out[t * ldo + r]
     int ldo;
     unsigned* status;  // device status word (ERR_WAIT_TIMEOUT)
+    int n_valid;       // argmax epilogue: rows >= n_valid never win
+    void* cand;        // argmax epilogue: Cand [row tiles * 4][n], each 32-row group's best (value, id) per token
 };
 
 bool gemm_tc_supported(const DMat& W);
@@ -35,5 +37,13 @@ size_t gemm_tc_smem(int dtype);
 bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out);
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
                              unsigned* status, cudaStream_t st);
+
+// Greedy head: the exact logits of rows [0, W.rows) for n tokens never leave the kernel; each 32-row group's best
+// (value desc, id asc) per token goes to cand, and launch_argmax_reduce picks each token's winner (the first maximum
+// over rows < n_valid, as std::max_element).  cand holds argmax_parts(W.rows) * n entries.
+int argmax_parts(int rows);
+cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int n_valid, void* cand,
+                                    unsigned* status, cudaStream_t st);
+cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids, float* vals, cudaStream_t st);
 
 }  // namespace qb

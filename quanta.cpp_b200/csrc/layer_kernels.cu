@@ -231,12 +231,17 @@ __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __res
 
 // R [n][fused rows] raw q|k|v -> bias + RoPE + store, token t at position pos0 + t.
 __global__ void k_qkv_epilogue(QkvArgs a, const float* __restrict__ R, int n_tok, const int* __restrict__ pos_dev,
-                               float* __restrict__ Q) {
+                               float* __restrict__ Q, TokMap tm) {
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.y;
     const int pairs = a.W.rows / 2;
-    const int pos = __ldcg(pos_dev) + t;
+    const int pos = tm.pos ? __ldcg(tm.pos + t) : __ldcg(pos_dev) + t;
+    if (tm.pos) {  // this token's sequence cache
+        const long long off = __ldcg(tm.off + t);
+        a.kcache += off;
+        a.vcache += off;
+    }
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x)
         qkv_pair_out(a, 2 * p, __ldcg(R + size_t(t) * a.W.rows + 2 * p), __ldcg(R + size_t(t) * a.W.rows + 2 * p + 1), pos,
                      Q + size_t(t) * a.n_heads * a.head_dim);
@@ -352,10 +357,10 @@ cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_to
 }
 
 cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
-                                bool pdl) {
+                                bool pdl, TokMap tm) {
     const int pairs = a.W.rows / 2;
     return launch_pdl(k_qkv_epilogue, dim3((pairs + kThreads - 1) / kThreads, n_tok), dim3(kThreads), 0, st, pdl, a, R, n_tok,
-                      pos_dev, Q);
+                      pos_dev, Q, tm);
 }
 
 cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl) {

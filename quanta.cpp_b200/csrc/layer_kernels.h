@@ -28,6 +28,13 @@ struct AttnArgs {
     ExpTab exptab;           // host libm expf exceptions (exp_table.h)
 };
 
+// Multi-token launches over tokens of different sequences: token t sits at position pos[t] and its sequence's KV cache
+// starts off[t] elements after the layer's cache pointer.  pos == nullptr: one sequence, token t at pos_dev[0] + t.
+struct TokMap {
+    const int* pos = nullptr;
+    const long long* off = nullptr;
+};
+
 struct SlicePlan {
     int rows_per_cta = 0, grid = 0, u = 0;
     unsigned magic = 0;
@@ -46,11 +53,11 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl);
 // n_tok > 1 consecutive tokens whose positions stay below pos_bound (known on the host): one CTA per (kv head, token).
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
-                                cudaStream_t st, bool pdl);
+                                cudaStream_t st, bool pdl, TokMap tm = TokMap{});
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
                                    cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
-                                bool pdl);
+                                bool pdl, TokMap tm = TokMap{});
 cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl);
 cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st,
                                 bool pdl);

@@ -115,6 +115,10 @@ def lib() -> C.CDLL:
         L.qnt_session_read.argtypes = [P, P, I, C.POINTER(GenStatsC)]
         L.qnt_model_stream.argtypes = [P]
         L.qnt_model_stream.restype = P
+        L.qnt_batch_init.argtypes = [P, I, I]
+        L.qnt_prefill_batch.argtypes = [P, I, P, I, C.POINTER(I)]
+        L.qnt_decode_batch.argtypes = [P, P, P, I, P]
+        L.qnt_batch_reset.argtypes = [P, I]
         L.qnt_sampler_create.argtypes = [C.POINTER(SamplerParamsC), C.POINTER(P)]
         L.qnt_sampler_sample.argtypes = [P, P, I, P, I, C.POINTER(I), P]
         L.qnt_sampler_free.argtypes = [P]
@@ -335,6 +339,28 @@ class Model:
 
 
     # Session in pieces (qnt_session_begin / step / read)
+    # ---- batched serving (greedy): many sequences with their own KV caches
+    def batch_init(self, max_seqs: int, ctx_len: int):
+        _check(lib().qnt_batch_init(self.h, max_seqs, ctx_len))
+
+    def prefill_batch(self, seq: int, tokens) -> int:
+        """Feeds the prompt of one sequence; returns its greedy next token."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        nxt = C.c_int(-1)
+        _check(lib().qnt_prefill_batch(self.h, seq, _ptr(t), t.size, C.byref(nxt)))
+        return nxt.value
+
+    def decode_batch(self, seq_ids, tokens) -> np.ndarray:
+        """One greedy step of several distinct sequences; returns their next tokens."""
+        s = np.ascontiguousarray(seq_ids, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(s.size, np.int32)
+        _check(lib().qnt_decode_batch(self.h, _ptr(s), _ptr(t), s.size, _ptr(out)))
+        return out
+
+    def batch_reset(self, seq: int):
+        _check(lib().qnt_batch_reset(self.h, seq))
+
     def session_begin(self, prompt, sp: SamplerParams, shortlist: bool = True, batch_prefill: bool = True):
         p = np.ascontiguousarray(prompt, np.int32)
         spc = SamplerParamsC(sp.temperature, sp.top_k, sp.top_p, sp.min_p, sp.repeat_penalty, sp.repeat_window, sp.seed)
