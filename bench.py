@@ -218,6 +218,39 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
     e2e_value = world * len(ids_e2e) / float(e2e_local.item())
 
+    # config 5 style throughput serving on this rank: BATCH sequences of PROMPT tokens, then greedy steps of all of
+    # them at once (qnt_decode_batch: tensor-core layers, fused greedy head); device time with CUDA events
+    batch = None
+    if args.batch > 0:
+        B, bsteps = args.batch, args.batch_steps
+        m.batch_init(B, PROMPT + bsteps + 8)
+        rngb = np.random.default_rng(SEED + 7 + rank)
+        prompts = rngb.integers(0, m.hp.n_tokens, (B, PROMPT)).astype(np.int32)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        last = np.array([m.prefill_batch(s, prompts[s]) for s in range(B)], np.int32)
+        torch.cuda.synchronize()
+        bprefill_s = time.perf_counter() - t0
+        seqs = np.arange(B, dtype=np.int32)
+        for _ in range(2):  # warm-up steps
+            last = m.decode_batch(seqs, last)
+        torch.cuda.synchronize()
+        eb = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        eb[0].record(stream)
+        for _ in range(bsteps):
+            last = m.decode_batch(seqs, last)
+        eb[1].record(stream)
+        torch.cuda.synchronize()
+        bms = torch.tensor([eb[0].elapsed_time(eb[1])], device="cuda")
+        if dist:
+            dist.all_reduce(bms, op=dist.ReduceOp.MAX)
+        bms = float(bms.item())
+        batch = {"workload": f"config5 style: {B} sequences x {PROMPT}-token prompts per GPU, greedy, batched decode",
+                 "value": round(world * B * bsteps / (bms / 1e3), 1), "unit": "tok/s", "steps": bsteps,
+                 "ms_per_step": round(bms / bsteps, 3), "prefill_tok_s": round(B * PROMPT / bprefill_s, 1),
+                 "note": "each step: one token for every sequence, ids copied to the host"}
+        m.batch_init(1, 2)  # release the batch caches
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -243,6 +276,7 @@ def run_ours(args, rank, world, local_rank):
             "kernels_per_step": kps,
             "clocks": clk.summary(),
             "cpu_baseline": base,
+            "batch_decode": batch,
         }
         print(json.dumps(out))
     m.close()
@@ -257,6 +291,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=256, help="sequences of the batched-serving measurement (0: skip)")
+    ap.add_argument("--batch-steps", type=int, default=32)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
