@@ -36,6 +36,11 @@ METRIC = "decode tok/s (q4mix 0.5B + shortlist head, b=1)"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
+# DRAM bytes of one decode step of this workload, summed over its launches from one ncu capture (the command and the
+# per-kernel table are in profiles/decode_step_traffic_q4mix_sl.md)
+STEP_TRAFFIC_BYTES = 338_190_000
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
@@ -269,7 +274,9 @@ def run_ours(args, rank, world, local_rank):
             "bytes_per_token": int(step_bytes),
             "roofline": {"bound": "hbm", "kernel": "whole decode step (all kernels of one graph replay)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "traffic": None},
+                         "peak_kind": peak_kind, "traffic": STEP_TRAFFIC_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over one step's launches "
+                                           "(profiles/decode_step_traffic_q4mix_sl.md)"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": round(PROMPT * 4 / args.steps, 1),
                     "d2h_bytes_per_step": 4, "note": "qnt_generate wall clock incl. 512-token prefill"},
             "gpu_launches": kps * args.steps,
