@@ -98,7 +98,8 @@ int qnt_model_hparams(const qnt_model* m, qnt_hparams* out);
  * top_k <= 0: full head).  logits: host buffer of vocab_size floats or NULL.  QNT_ERR_RANGE if pos >= ctx_len. */
 int qnt_model_forward(qnt_model* m, int token, int pos, const qnt_head_query* hq, float* logits);
 
-/* Model::forward_batch (engine/src/model.h:44): n tokens at pos0..pos0+n-1 in 32-token chunks; logits of the last. */
+/* Model::forward_batch (engine/src/model.h:44): n tokens at pos0..pos0+n-1 (device chunks of up to 512 tokens; the
+ * results do not depend on the chunking); logits of the last. */
 int qnt_model_forward_batch(qnt_model* m, const int* tokens, int n, int pos0, const qnt_head_query* hq, float* logits);
 
 /* Model::head (engine/src/model.h:47) for the last token; coarse / upper (may be NULL) receive the shortlist pass's
