@@ -28,6 +28,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "quanta.cpp_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
+import dp  # noqa: E402  (quanta.cpp_b200/dp.py: data-parallel plumbing)
 
 MODEL_DIR = Path(os.environ.get("QNT_MODEL_DIR", "/tmp/qnt_models"))
 PROMPT = 512
@@ -103,7 +104,7 @@ def model_path():
 
 
 def prompt_ids(rank, n_tokens):
-    return np.random.default_rng(SEED + rank).integers(0, n_tokens, PROMPT).astype(np.int32)
+    return np.random.default_rng(dp.rank_seed(SEED, rank)).integers(0, n_tokens, PROMPT).astype(np.int32)
 
 
 def cpu_baseline(path, steps):
@@ -190,11 +191,7 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     ids, st = m.session_read()
     kps = st["kernels_per_step"]
-    # max over ranks
-    t = torch.tensor([ms], device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = dp.max_over_ranks(ms, dist, device="cuda")  # the slowest rank's time is the job's
     value = world * args.steps / (ms_max / 1e3)
 
     # algorithmic bytes of one decode step (layers + head + KV), per rank
@@ -218,10 +215,7 @@ def run_ours(args, rank, world, local_rank):
     t0 = time.perf_counter()
     ids_e2e, st_e2e = m.generate(pin_prompt, sp, args.steps)
     e2e_s = time.perf_counter() - t0
-    e2e_local = torch.tensor([e2e_s], device="cuda")
-    if dist:
-        dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
-    e2e_value = world * len(ids_e2e) / float(e2e_local.item())
+    e2e_value = world * len(ids_e2e) / dp.max_over_ranks(e2e_s, dist, device="cuda")
 
     # config 5 style throughput serving on this rank: BATCH sequences of PROMPT tokens, then greedy steps of all of
     # them at once (qnt_decode_batch: tensor-core layers, fused greedy head); device time with CUDA events
@@ -229,7 +223,7 @@ def run_ours(args, rank, world, local_rank):
     if args.batch > 0:
         B, bsteps = args.batch, args.batch_steps
         m.batch_init(B, PROMPT + bsteps + 8)
-        rngb = np.random.default_rng(SEED + 7 + rank)
+        rngb = np.random.default_rng(dp.rank_seed(SEED + 7, rank))
         prompts = rngb.integers(0, m.hp.n_tokens, (B, PROMPT)).astype(np.int32)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -246,10 +240,7 @@ def run_ours(args, rank, world, local_rank):
             last = m.decode_batch(seqs, last)
         eb[1].record(stream)
         torch.cuda.synchronize()
-        bms = torch.tensor([eb[0].elapsed_time(eb[1])], device="cuda")
-        if dist:
-            dist.all_reduce(bms, op=dist.ReduceOp.MAX)
-        bms = float(bms.item())
+        bms = dp.max_over_ranks(eb[0].elapsed_time(eb[1]), dist, device="cuda")
         batch = {"workload": f"config5 style: {B} sequences x {PROMPT}-token prompts per GPU, greedy, batched decode",
                  "value": round(world * B * bsteps / (bms / 1e3), 1), "unit": "tok/s", "steps": bsteps,
                  "ms_per_step": round(bms / bsteps, 3), "prefill_tok_s": round(B * PROMPT / bprefill_s, 1),
