@@ -148,11 +148,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// registers -> TMEM: the same 32 lanes x 32 columns (every register holds the same value here).
+__device__ __forceinline__ void tmem_st32_fill(uint32_t taddr, unsigned x) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(x)
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// The accumulators start at the bits of 2^23 + 2^22 (kMagic): the MMA then leaves 12582912 + s, whose float value
+// carries the exact block dot s, and fma(f, dw, -12582912 * dw) rounds s * dw once, exactly like
+// fmul(float(s), dw): 12582912 * dw is exact in f32 for an fp16 dw, and |s| < 2^22.
+constexpr unsigned kMagic = 0x4B400000u;
+constexpr float kMagicF = 12582912.0f;
+
 // Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row atoms of 1024 bytes).
 __device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
 
-// Exact int -> float for |s| < 2^22 (block dots are at most 32 * 127 * 127 in magnitude).
-__device__ __forceinline__ float exact_i2f(int s) { return __int_as_float(s + 0x4B400000) - 12582912.0f; }
 
 // Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
 __device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
@@ -238,12 +252,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 const int s = step % kStages, round = step / kStages;
                 const int slot = step % kSlots, use = step / kSlots;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
-                if (use > 0 && !mbar_wait(&slot_free[slot], (use - 1) & 1, ab, g.status)) break;
+                // phase `use` of slot_free: the epilogue refilled the slot with the magic (phase 0: the initial fill)
+                if (!mbar_wait(&slot_free[slot], use & 1, ab, g.status)) break;
                 tc_fence_after();
                 unsigned char* st = smem + s * L.bytes;
-                for (int k = 0; k < kStageBlocks; ++k)
+                for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled slot
                     mma_i8(tmem + uint32_t(slot * kCols), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.bd + 32 * k),
-                           k > 0);
+                           true);
                 mma_commit(&mma_done[slot]);
                 mma_commit(&empty[s]);
             }
@@ -279,6 +294,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         }
     } else {  // epilogue
         const int q = warp & 3, cg = (warp - 4) >> 2;
+        const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * 32);
+        for (int j = 0; j < kSlots; ++j) tmem_st32_fill(my_cols + uint32_t(j * kCols), kMagic);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int j = 0; j < kSlots; ++j) mbar_arrive(&slot_free[j]);
         int step = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
@@ -296,6 +317,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
                 const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
                 const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
+                const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
+                const float nmdw[4] = {-fmul(kMagicF, d01.x), -fmul(kMagicF, d01.y), -fmul(kMagicF, d23.x),
+                                       -fmul(kMagicF, d23.y)};
                 int got = 0;
                 if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
                 if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
@@ -303,8 +327,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                     break;
                 }
                 tc_fence_after();
-                int v[32];  // v[4 i + b]: block b of token cg * kTpt + i
-                tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kCols + cg * 32), v);
+                int v[32];  // v[4 i + b]: kMagic + block b's dot of token cg * kTpt + i
+                tmem_ld32(my_cols + uint32_t(slot * kCols), v);
+                tmem_st32_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&slot_free[slot]);
@@ -312,10 +337,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
 #pragma unroll
                 for (int i = 0; i < kTpt; ++i) {
                     const float4 dx = sdx[i];
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 0]), d01.x), dx.x));
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 1]), d01.y), dx.y));
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 2]), d23.x), dx.z));
-                    acc[i] = fadd(acc[i], fmul(fmul(exact_i2f(v[4 * i + 3]), d23.y), dx.w));
+                    const float dxv[4] = {dx.x, dx.y, dx.z, dx.w};
+#pragma unroll
+                    for (int b = 0; b < 4; ++b)  // acc = acc + (float(s) * dw) * dx, each rounded as in the reference
+                        acc[i] = fadd(acc[i], fmul(__fmaf_rn(__int_as_float(v[4 * i + b]), dw[b], nmdw[b]), dxv[b]));
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
