@@ -18,6 +18,7 @@ struct qnt_dtensor {
     void* d = nullptr;
     qb::TcMap wmap{};          // TMA source for the tensor-core matmul
     bool tc = false;           // wmap is valid
+    void* i8 = nullptr;        // Q4_0: the int8 copy (q - 8) that wmap reads
     unsigned* status = nullptr;  // device status word of this tensor's kernels
 };
 
@@ -104,7 +105,21 @@ int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_
         cudaFree(t->status);
         return cuda_err(e, "tensor status word");
     }
-    t->tc = qb::make_weight_map(t->m, &t->wmap);
+    if (qb::gemm_tc_supported(t->m)) {
+        if (const size_t b = qb::tc_weight_copy_bytes(t->m)) {
+            e = cudaMalloc(&t->i8, b);
+            if (e == cudaSuccess) e = qb::unpack_q4_i8(t->m, static_cast<int8_t*>(t->i8), nullptr);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+            if (e != cudaSuccess) {
+                cudaFree(t->q);
+                cudaFree(t->d);
+                cudaFree(t->status);
+                cudaFree(t->i8);
+                return cuda_err(e, "tensor int8 copy");
+            }
+        }
+        t->tc = qb::make_weight_map(t->m, static_cast<const int8_t*>(t->i8), &t->wmap);
+    }
     *out = t.release();
     return QNT_OK;
 }
@@ -114,6 +129,7 @@ int qnt_tensor_free(qnt_dtensor* t) {
     cudaFree(t->q);
     cudaFree(t->d);
     cudaFree(t->status);
+    cudaFree(t->i8);
     delete t;
     return QNT_OK;
 }

@@ -40,6 +40,17 @@ void* Engine::dalloc(size_t bytes) {
     return p;
 }
 
+bool Engine::tc_weights(const DMat& W, TcMap* map) {
+    if (!gemm_tc_supported(W)) return false;
+    int8_t* copy = nullptr;
+    if (const size_t b = tc_weight_copy_bytes(W)) {
+        copy = static_cast<int8_t*>(dalloc(b));
+        if (unpack_q4_i8(W, copy, st_) != cudaSuccess) return false;
+        tc_copy_bytes_ += b;
+    }
+    return make_weight_map(W, copy, map);
+}
+
 int Engine::n_valid_default() const {
     return std::min(file_.tokenizer().n_tokens > 0 ? file_.tokenizer().n_tokens : hp_.vocab_size, hp_.vocab_size);
 }
@@ -279,8 +290,8 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         // tensor-core matmul sources (a layer without them, or a driver without TMA encode, uses the CUDA cores)
         tc_act_ = make_act_maps(XQ_, DX_, kChunk, hp_.dim, &tm_x_) && make_act_maps(HQ_, HD_, kChunk, hp_.ffn_dim, &tm_h_);
         for (Layer& L : layers_)
-            L.tc = tc_act_ && make_weight_map(L.qkv, &L.t_qkv) && make_weight_map(L.o, &L.t_o) &&
-                   make_weight_map(L.gu, &L.t_gu) && make_weight_map(L.down, &L.t_down);
+            L.tc = tc_act_ && tc_weights(L.qkv, &L.t_qkv) && tc_weights(L.o, &L.t_o) && tc_weights(L.gu, &L.t_gu) &&
+                   tc_weights(L.down, &L.t_down);
 
         const int V = hp_.vocab_size, nbd = hp_.dim / QK;
         hin_.xq = static_cast<int8_t*>(dalloc(size_t(hp_.dim)));
@@ -312,7 +323,8 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         cudaMemset(status_, 0, 16);
         tok_pos_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         tok_off_ = static_cast<long long*>(dalloc(size_t(kChunk) * 8));
-        head_tc_ = make_weight_map(lm_head_, &t_head_);
+        head_tc_ = tc_weights(lm_head_, &t_head_);
+        if (cudaStreamSynchronize(st_) != cudaSuccess) return bad("unpacking the tensor-core weights failed");
         bcand_ = dalloc(size_t(argmax_parts(hp_.vocab_size)) * kChunk * sizeof(Cand));
         bids_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         host_tmp_.resize(size_t(V));

@@ -89,6 +89,8 @@ public:
     int n_valid_default() const;
     size_t weight_bytes() const { return weight_bytes_; }
     size_t kv_cache_bytes() const { return kv_bytes_; }
+    // int8 copies of Q4_0 weights that the tensor-core matmul reads (q - 8 per element)
+    size_t tc_copy_bytes() const { return tc_copy_bytes_; }
     const std::string& error() const { return err_; }
     void set_matmul_impl(int impl) { mm_impl_ = impl; }
     void set_use_graphs(bool on) { use_graphs_ = on; }
@@ -132,6 +134,8 @@ private:
                     int n_list, bool penal, float penalty);
     // Prefill / batched matmul into R_: the tensor cores when the layer has TMA sources and n is large enough.
     int launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out);
+    // TMA source of W for the tensor-core matmul (a Q4_0 matrix gets its int8 copy here); false: CUDA cores only
+    bool tc_weights(const DMat& W, TcMap* map);
     int run_graph(const std::string& key, const std::function<int()>& body);
     int sync_check();
 
@@ -145,7 +149,7 @@ private:
     int device_ = 0, n_sm_ = 148;
 
     std::vector<void*> allocs_;
-    size_t weight_bytes_ = 0, kv_bytes_ = 0, layer_bytes_ = 0;
+    size_t weight_bytes_ = 0, kv_bytes_ = 0, layer_bytes_ = 0, tc_copy_bytes_ = 0;
 
     DMat embed_{}, lm_head_{};
     const float* final_norm_ = nullptr;

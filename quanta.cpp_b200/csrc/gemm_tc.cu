@@ -4,19 +4,22 @@
 // order, s_b the exact int32 block dot.
 //
 // The per-block scales rule out accumulating across blocks in the tensor core: every block's int32 dot has to leave
-// the MMA on its own.  One MMA (K = 128, four blocks) still yields four separate block dots per token by running
-// against a block-diagonal copy of the activation tile: row 4 t + b of it holds token t's 32 bytes of block b and zeros
-// elsewhere, so output column 4 t + b is exactly s_b for token t.  Tiles of 128 weight rows x 32 tokens (MMA N = 128
-// columns), four blocks per pipeline stage; persistent CTAs (one per SM) walk their tiles with the pipeline running
-// across tile boundaries.
-//   warp 0      TMA producer: per stage the weight tile (Q8: 128 B per row, 128B-swizzled; Q4: 64 B packed per row),
-//               the activation tile (32 tokens x 128 B, 128B-swizzled) and its block scales
-//   warps 2-3   build the stage's operands in shared memory: the block-diagonal activation tile (its zero chunks are
-//               written once) and, for Q4, the int8 q - 8 weights in the swizzled layout the MMA reads
-//   warp 1      allocates TMEM; one lane issues the stage's four tcgen05.mma.kind::i8 into one of four TMEM slots
-//   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and the 32 columns of tokens
-//               8 ((w - 4) / 4) .. +8 with one tcgen05.ld per stage, and folds the four blocks into 8 f32
-//               accumulators per thread in block order
+// the MMA on its own.  A tcgen05.mma.kind::i8 step is K = 32 deep, exactly one quant block, so each block gets one
+// MMA (M = 128 weight rows, N = 32 tokens) into 32 TMEM columns of its own; a TMEM slot of 128 columns holds the four
+// blocks of a pipeline stage.  Tiles of 128 weight rows x 32 tokens; persistent CTAs (one per SM) walk their tiles
+// with the pipeline running across tile boundaries.
+// Weights are int8 rows: Q8_0 as stored, Q4_0 through an int8 copy of q - 8 made once (unpack_q4_i8), so that
+// every operand reaches shared memory by TMA alone.
+//   warp 0      TMA producers: per stage the weight tile (128 rows x 128 B, 128B-swizzled) and the activation tile
+//               (32 tokens x 128 B, 128B-swizzled) into the stage ring, the stage's block scales of the activations
+//               into a separate, deeper ring that the epilogue frees.  A thread's bulk loads complete one after
+//               another, so 12 lanes issue them: lane 4 k + p loads kind k (weights, activations, scales) of the
+//               steps p, p + 4, ...
+//   warp 1      allocates TMEM; one lane issues the stage's four MMAs into one of four TMEM slots; their completion
+//               frees the stage
+//   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and, for each block, the
+//               columns of tokens 8 ((w - 4) / 4) .. +8, and folds the four blocks into 8 f32 accumulators per
+//               thread in block order
 // Every wait is bounded: a wait that gives up sets ERR_WAIT_TIMEOUT in the status word and an abort flag that ends
 // every other wait, so the kernel always returns (and frees its TMEM once its issued MMAs have completed).
 #include <cuda.h>
@@ -38,33 +41,22 @@ namespace {
 constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = 128 + 32 * kEpiWarps;
 constexpr int kTileRows = 128;
-constexpr int kTileTok = 32;                       // tokens per tile
+constexpr int kTileTok = 32;                       // tokens per tile (MMA N)
 constexpr int kStageBlocks = 4;                    // quant blocks per pipeline stage (128 bytes of K)
-constexpr int kCols = kTileTok * kStageBlocks;     // MMA N: one column per (token, block)
+constexpr int kCols = kTileTok * kStageBlocks;     // TMEM columns of a stage: block b of token t in column 32 b + t
 constexpr int kTpt = kTileTok / 4;                 // tokens per epilogue thread
-constexpr int kStages = 4;
 constexpr int kSlots = 4;                          // TMEM accumulator slots of kCols columns
 constexpr int kTmemCols = kSlots * kCols;          // 512: the whole TMEM of the SM (one CTA per SM)
 constexpr int kASw = kTileRows * 128;              // swizzled int8 weight tile of a stage
-constexpr int kAPk = kTileRows * 64;               // packed Q4 tile of a stage
 constexpr int kB = kTileTok * 128;                 // activation tile of a stage
-constexpr int kBD = kCols * 128;                   // block-diagonal activation tile
-constexpr int kDX = kTileTok * kStageBlocks * 4;
+constexpr int kDX = kTileTok * kStageBlocks * 4;   // activation block scales of a stage
+constexpr int kDxRing = 16;                        // >= stages + slots: the scales never hold the producer back
 constexpr unsigned kWaitLimit = 1u << 22;
 constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
 
-struct StageOffsets {
-    int a_sw, a_pk, b, bd, dx, bytes;
-};
-// Stage layout: swizzled tiles on 1024-byte boundaries (the 128B swizzle atom).
-__host__ __device__ constexpr StageOffsets stage_layout(bool q4) {
-    return StageOffsets{0,
-                        kASw,
-                        kASw + (q4 ? kAPk : 0),
-                        kASw + (q4 ? kAPk : 0) + kB,
-                        kASw + (q4 ? kAPk : 0) + kB + kBD,
-                        (kASw + (q4 ? kAPk : 0) + kB + kBD + kDX + 1023) / 1024 * 1024};
-}
+constexpr int kStages = 8;
+constexpr int kStageBytes = kASw + kB;             // weight tile, then activation tile (both 1024-byte aligned)
+constexpr int kProdPhases = 4;                     // producer lanes per kind of load
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 
@@ -117,8 +109,8 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
     return d;
 }
 
-// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kCols.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kCols >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kTileTok.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileTok >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, bool accumulate) {
     asm volatile(
@@ -135,27 +127,33 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-// TMEM -> registers: this warp's 32 lanes, 32 consecutive 32-bit columns from taddr.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+// TMEM -> registers: this warp's 32 lanes, 8 consecutive 32-bit columns at each of taddr + 32 b (b = 0..3):
+// v[8 b + i] = column 32 b + i.
+__device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%34];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%24,%25,%26,%27,%28,%29,%30,%31}, [%35];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
           "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
           "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
           "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr), "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u)
+        : "memory");
 }
 
-// registers -> TMEM: the same 32 lanes x 32 columns (every register holds the same value here).
-__device__ __forceinline__ void tmem_st32_fill(uint32_t taddr, unsigned x) {
+// registers -> TMEM: the same 32 lanes x 4 x 8 columns, all set to x.
+__device__ __forceinline__ void tmem_st8x4_fill(uint32_t taddr, unsigned x) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(x)
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%3], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u), "r"(x)
         : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // The accumulators start at the bits of 2^23 + 2^22 (kMagic): the MMA then leaves 12582912 + s, whose float value
@@ -168,23 +166,21 @@ constexpr float kMagicF = 12582912.0f;
 __device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
 
 
-// Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
-__device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
-
 __device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid) {
     return av > bv || (av == bv && aid < bid);
 }
 
 // EPI 0: store the rows; EPI 1: per 32-row group and token, the best (value, id) into g.cand.
-template <int DT, int EPI>
+template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
-    constexpr bool kQ4 = DT == DT_Q4_0;
-    constexpr StageOffsets L = stage_layout(kQ4);
+    constexpr int S = kStages;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full_raw[kStages], full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots], fin;
+    unsigned char* dx_ring = smem + S * kStageBytes;
+    __shared__ uint64_t full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots];
+    __shared__ uint64_t dx_full[kDxRing], dx_empty[kDxRing], fin;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -193,26 +189,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     // tile -> (first weight row, first token); tiles blockIdx.x, blockIdx.x + gridDim.x, ...
     auto tile_m0 = [&](int tile) { return g.r0 + (tile / n_tt) * kTileRows; };
     auto tile_t0 = [&](int tile) { return (tile % n_tt) * kTileTok; };
+    const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full_raw[s], 1);
-            mbar_init(&full[s], 64);              // the operand builders (warps 2-3)
-            mbar_init(&empty[s], 1 + kEpiWarps);  // the MMA commit + one arrive per epilogue warp
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 2);   // the weight and activation producers (one arrive.expect_tx each)
+            mbar_init(&empty[s], 1);  // the MMA commit
         }
         for (int j = 0; j < kSlots; ++j) {
             mbar_init(&mma_done[j], 1);
             mbar_init(&slot_free[j], kEpiWarps);
         }
+        for (int d = 0; d < kDxRing; ++d) {
+            mbar_init(&dx_full[d], 1);
+            mbar_init(&dx_empty[d], kEpiWarps);
+        }
         mbar_init(&fin, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // the block-diagonal tiles are zero outside their data chunks; those chunks never move, so zero them once
-    for (int s = 0; s < kStages; ++s)
-        for (int i = threadIdx.x; i < kBD / 16; i += kTcThreads)
-            reinterpret_cast<uint4*>(smem + s * L.bytes + L.bd)[i] = make_uint4(0, 0, 0, 0);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kTmemCols)
@@ -226,76 +221,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     volatile int* ab = &abort_flag;
 
     if (warp == 0) {
-        if (lane == 0) {  // TMA producer
-            const unsigned bytes = (kQ4 ? kAPk : kASw) + kB + kDX;  // full boxes (TMA zero-fills out-of-range rows)
+        if (lane < 3 * kProdPhases) {  // TMA producers: kind (0 weights, 1 activations, 2 scales), phase
+            const int kind = lane / kProdPhases, ph = lane % kProdPhases;
             int step = 0;
-            for (int tile = blockIdx.x; tile < n_tiles && !*ab; tile += gridDim.x) {
+            bool go = true;
+            for (int tile = blockIdx.x; tile < n_tiles && go; tile += gridDim.x) {
                 const int m0 = tile_m0(tile), t0 = tile_t0(tile);
                 for (int ks = 0; ks < nks; ++ks, ++step) {
-                    const int s = step % kStages, round = step / kStages;
-                    if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) break;
-                    unsigned char* st = smem + s * L.bytes;
-                    mbar_expect_tx(&full_raw[s], bytes);
-                    if (kQ4)
-                        tma_load_2d(st + L.a_pk, &tmA, ks * 64, m0, &full_raw[s]);
-                    else
-                        tma_load_2d(st + L.a_sw, &tmA, ks * 128, m0, &full_raw[s]);
-                    tma_load_2d(st + L.b, &tmB, ks * 128, t0, &full_raw[s]);
-                    tma_load_2d(st + L.dx, &tmDX, ks * kStageBlocks, t0, &full_raw[s]);
+                    if (step % kProdPhases != ph) continue;
+                    if (kind < 2) {
+                        const int s = step % S, round = step / S;
+                        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) {
+                            go = false;
+                            break;
+                        }
+                        unsigned char* st = smem + s * kStageBytes;
+                        if (kind == 0) {  // full boxes: TMA zero-fills rows past the matrix
+                            mbar_expect_tx(&full[s], kASw);
+                            tma_load_2d(st, &tmA, ks * 128, m0, &full[s]);
+                        } else {
+                            mbar_expect_tx(&full[s], kB);
+                            tma_load_2d(st + kASw, &tmB, ks * 128, t0, &full[s]);
+                        }
+                    } else {
+                        const int d = step % kDxRing, dround = step / kDxRing;
+                        if (dround > 0 && !mbar_wait(&dx_empty[d], (dround - 1) & 1, ab, g.status)) {
+                            go = false;
+                            break;
+                        }
+                        mbar_expect_tx(&dx_full[d], kDX);
+                        tma_load_2d(dx_ring + d * kDX, &tmDX, ks * kStageBlocks, t0, &dx_full[d]);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer: four K = 32 steps per stage accumulate into one slot
-            const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
+        if (lane == 0) {  // MMA issuer: one K = 32 MMA per block, into the block's columns of the stage's slot
             for (int step = 0; step < steps && !*ab; ++step) {
-                const int s = step % kStages, round = step / kStages;
+                const int s = step % S, round = step / S;
                 const int slot = step % kSlots, use = step / kSlots;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
                 // phase `use` of slot_free: the epilogue refilled the slot with the magic (phase 0: the initial fill)
                 if (!mbar_wait(&slot_free[slot], use & 1, ab, g.status)) break;
                 tc_fence_after();
-                unsigned char* st = smem + s * L.bytes;
-                for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled slot
-                    mma_i8(tmem + uint32_t(slot * kCols), sw128_desc(st + L.a_sw + 32 * k), sw128_desc(st + L.bd + 32 * k),
-                           true);
+                unsigned char* st = smem + s * kStageBytes;
+#pragma unroll
+                for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled columns
+                    mma_i8(tmem + uint32_t(slot * kCols + k * kTileTok), sw128_desc(st + 32 * k),
+                           sw128_desc(st + kASw + 32 * k), true);
                 mma_commit(&mma_done[slot]);
                 mma_commit(&empty[s]);
             }
             mma_commit(&fin);  // arrives once every MMA issued above has completed
         }
-    } else if (warp < 4) {  // operand builders
-        const int ct = threadIdx.x - 64;
-        const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
-        for (int step = 0; step < steps; ++step) {
-            const int s = step % kStages, round = step / kStages;
-            if (!mbar_wait(&full_raw[s], round & 1, ab, g.status)) break;
-            unsigned char* st = smem + s * L.bytes;
-            // block-diagonal activations: row 4 t + b <- chunks 2 b, 2 b + 1 of token t
-            for (int c = ct; c < kTileTok * kStageBlocks * 2; c += 64) {
-                const int rr = c >> 1, half = c & 1, t = rr >> 2, b = rr & 3, ch = 2 * b + half;
-                *reinterpret_cast<uint4*>(st + L.bd + sw128_off(rr, ch)) =
-                    *reinterpret_cast<const uint4*>(st + L.b + sw128_off(t, ch));
-            }
-            if (kQ4) {  // unpack the packed Q4 tile into the swizzled int8 layout
-                for (int c = ct; c < kTileRows * kStageBlocks; c += 64) {
-                    const int r = c >> 2, blk = c & 3;
-                    const uint4 w = *reinterpret_cast<const uint4*>(st + L.a_pk + r * 64 + blk * 16);
-                    const uint4 lo = make_uint4(q4_bytes(w.x & 0x0F0F0F0Fu), q4_bytes(w.y & 0x0F0F0F0Fu),
-                                                q4_bytes(w.z & 0x0F0F0F0Fu), q4_bytes(w.w & 0x0F0F0F0Fu));
-                    const uint4 hi = make_uint4(q4_bytes((w.x >> 4) & 0x0F0F0F0Fu), q4_bytes((w.y >> 4) & 0x0F0F0F0Fu),
-                                                q4_bytes((w.z >> 4) & 0x0F0F0F0Fu), q4_bytes((w.w >> 4) & 0x0F0F0F0Fu));
-                    *reinterpret_cast<uint4*>(st + L.a_sw + sw128_off(r, 2 * blk)) = lo;
-                    *reinterpret_cast<uint4*>(st + L.a_sw + sw128_off(r, 2 * blk + 1)) = hi;
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the MMA reads through the async proxy
-            mbar_arrive(&full[s]);
-        }
-    } else {  // epilogue
+    } else if (warp >= 4) {  // epilogue
         const int q = warp & 3, cg = (warp - 4) >> 2;
-        const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * 32);
-        for (int j = 0; j < kSlots; ++j) tmem_st32_fill(my_cols + uint32_t(j * kCols), kMagic);
+        const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * kTpt);
+        for (int j = 0; j < kSlots; ++j) tmem_st8x4_fill(my_cols + uint32_t(j * kCols), kMagic);
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
@@ -312,7 +294,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             uint2 dnext = __ldg(wd);
             bool ok = true;
             for (int ks = 0; ks < nks; ++ks, ++step) {
-                const int s = step % kStages, slot = step % kSlots, use = step / kSlots;
+                const int slot = step % kSlots, use = step / kSlots;
+                const int d = step % kDxRing, dround = step / kDxRing;
                 const uint2 dcur = dnext;
                 if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
                 const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
@@ -321,29 +304,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 const float nmdw[4] = {-fmul(kMagicF, d01.x), -fmul(kMagicF, d01.y), -fmul(kMagicF, d23.x),
                                        -fmul(kMagicF, d23.y)};
                 int got = 0;
-                if (lane == 0) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+                if (lane == 0)
+                    got = mbar_wait(&mma_done[slot], use & 1, ab, g.status) &&
+                          mbar_wait(&dx_full[d], dround & 1, ab, g.status);
                 if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                int v[32];  // v[4 i + b]: kMagic + block b's dot of token cg * kTpt + i
-                tmem_ld32(my_cols + uint32_t(slot * kCols), v);
-                tmem_st32_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
+                int v[32];  // v[8 b + i]: kMagic + block b's dot of token cg * kTpt + i
+                tmem_ld8x4(my_cols + uint32_t(slot * kCols), v);
+                tmem_st8x4_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&slot_free[slot]);
-                const float4* sdx = reinterpret_cast<const float4*>(smem + s * L.bytes + L.dx) + cg * kTpt;
+                const float4* sdx = reinterpret_cast<const float4*>(dx_ring + d * kDX) + cg * kTpt;
 #pragma unroll
                 for (int i = 0; i < kTpt; ++i) {
                     const float4 dx = sdx[i];
                     const float dxv[4] = {dx.x, dx.y, dx.z, dx.w};
 #pragma unroll
                     for (int b = 0; b < 4; ++b)  // acc = acc + (float(s) * dw) * dx, each rounded as in the reference
-                        acc[i] = fadd(acc[i], fmul(__fmaf_rn(__int_as_float(v[4 * i + b]), dw[b], nmdw[b]), dxv[b]));
+                        acc[i] = fadd(acc[i], fmul(__fmaf_rn(__int_as_float(v[8 * b + i]), dw[b], nmdw[b]), dxv[b]));
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                if (lane == 0) mbar_arrive(&dx_empty[d]);
             }
             if (!ok) break;
             if (EPI == 0) {
@@ -419,13 +404,42 @@ bool gemm_tc_supported(const DMat& W) {
     return (W.dtype == DT_Q8_0 || W.dtype == DT_Q4_0) && W.cols % (kStageBlocks * QK) == 0 && encode_fn() != nullptr;
 }
 
-bool make_weight_map(const DMat& W, TcMap* out) {
-    if (!gemm_tc_supported(W)) return false;
-    if (W.dtype == DT_Q8_0)
-        return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, W.q, uint64_t(W.cols), uint64_t(W.rows), uint64_t(W.cols), 128,
-                         kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
-    return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, W.q, uint64_t(W.cols / 2), uint64_t(W.rows), uint64_t(W.cols / 2),
-                     64, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+size_t tc_weight_copy_bytes(const DMat& W) { return W.dtype == DT_Q4_0 ? size_t(W.rows) * size_t(W.cols) : 0; }
+
+namespace {
+
+// Unpacks a packed Q4 word (4 low nibbles = elements j..j+3 or 4 high nibbles = j+16..j+19) into 4 int8 (q - 8).
+__device__ __forceinline__ unsigned q4_bytes(unsigned nib) { return ((nib | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
+
+// One thread per 32-element block: its 16 packed bytes (byte j = element j | element j + 16 << 4) -> 32 int8 q - 8.
+__global__ void __launch_bounds__(256) k_unpack_q4_i8(const uint4* __restrict__ q, uint4* __restrict__ out, size_t n_blocks) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n_blocks; i += size_t(gridDim.x) * blockDim.x) {
+        const uint4 w = __ldg(q + i);
+        out[2 * i] = make_uint4(q4_bytes(w.x & 0x0F0F0F0Fu), q4_bytes(w.y & 0x0F0F0F0Fu), q4_bytes(w.z & 0x0F0F0F0Fu),
+                                q4_bytes(w.w & 0x0F0F0F0Fu));
+        out[2 * i + 1] = make_uint4(q4_bytes((w.x >> 4) & 0x0F0F0F0Fu), q4_bytes((w.y >> 4) & 0x0F0F0F0Fu),
+                                    q4_bytes((w.z >> 4) & 0x0F0F0F0Fu), q4_bytes((w.w >> 4) & 0x0F0F0F0Fu));
+    }
+}
+
+}  // namespace
+
+cudaError_t unpack_q4_i8(const DMat& W, int8_t* dst, cudaStream_t st) {
+    if (W.dtype != DT_Q4_0 || W.cols % QK != 0 || reinterpret_cast<uintptr_t>(W.q) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(dst) % 16 != 0)
+        return cudaErrorInvalidValue;
+    const size_t n_blocks = size_t(W.rows) * size_t(W.cols / QK);
+    const unsigned grid = unsigned(std::min<size_t>((n_blocks + 255) / 256, 148 * 16));
+    if (n_blocks == 0) return cudaSuccess;
+    k_unpack_q4_i8<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(W.q), reinterpret_cast<uint4*>(dst), n_blocks);
+    return cudaGetLastError();
+}
+
+bool make_weight_map(const DMat& W, const int8_t* i8, TcMap* out) {
+    if (!gemm_tc_supported(W) || (W.dtype == DT_Q4_0 && !i8)) return false;
+    const void* src = W.dtype == DT_Q8_0 ? static_cast<const void*>(W.q) : static_cast<const void*>(i8);
+    return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, src, uint64_t(W.cols), uint64_t(W.rows), uint64_t(W.cols), 128,
+                     kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out) {
@@ -437,7 +451,7 @@ bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, 
                      kStageBlocks, kTileTok, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-size_t gemm_tc_smem(int dtype) { return size_t(kStages) * stage_layout(dtype == DT_Q4_0).bytes + 1024; }
+size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kDxRing) * kDX + 1024; }
 
 namespace {
 
@@ -452,18 +466,11 @@ cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, co
     }
     const int tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * ((g.n + kTileTok - 1) / kTileTok);
     const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
-    const size_t smem = gemm_tc_smem(W.dtype);
-    if (W.dtype == DT_Q8_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q8_0, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q8_0, EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
-    } else if (W.dtype == DT_Q4_0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<DT_Q4_0, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        k_gemm_tc<DT_Q4_0, EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
-    } else {
-        return cudaErrorInvalidValue;
-    }
+    const size_t smem = gemm_tc_smem();
+    if (W.dtype != DT_Q8_0 && W.dtype != DT_Q4_0) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    k_gemm_tc<EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
     return cudaGetLastError();
 }
 

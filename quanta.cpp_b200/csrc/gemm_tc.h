@@ -27,13 +27,17 @@ struct GemmTcArgs {
 };
 
 bool gemm_tc_supported(const DMat& W);
-// The weight matrix as the kernel's TMA source (Q8_0: 128B-swizzled int8 tiles; Q4_0: packed tiles).
-bool make_weight_map(const DMat& W, TcMap* out);
+// The kernel reads int8 weight rows: Q8_0 matrices as stored, Q4_0 through an int8 copy of q - 8 (rows x cols
+// bytes, tc_weight_copy_bytes; 0 for Q8_0) that unpack_q4_i8 writes once.
+size_t tc_weight_copy_bytes(const DMat& W);
+cudaError_t unpack_q4_i8(const DMat& W, int8_t* dst, cudaStream_t st);
+// The int8 weights as the kernel's TMA source (128B-swizzled 128 x 128-byte tiles): W.q for Q8_0, i8 for Q4_0.
+bool make_weight_map(const DMat& W, const int8_t* i8, TcMap* out);
 // Quantized activations q [rows_alloc][cols] int8 and their block scales d [rows_alloc][cols / 32] f32, as TMA sources.
 struct TcAct {
     TcMap q, d;
 };
-size_t gemm_tc_smem(int dtype);
+size_t gemm_tc_smem();
 bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out);
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
                              unsigned* status, cudaStream_t st);
