@@ -18,7 +18,7 @@ struct qnt_dtensor {
     void* d = nullptr;
     qb::TcMap wmap{};          // TMA source for the tensor-core matmul
     bool tc = false;           // wmap is valid
-    void* i8 = nullptr;        // Q4_0: the int8 copy (q - 8) that wmap reads
+    void* tcbuf = nullptr;     // the copies wmap reads (stage-major scales; Q4_0: int8 q - 8)
     unsigned* status = nullptr;  // device status word of this tensor's kernels
 };
 
@@ -106,19 +106,17 @@ int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_
         return cuda_err(e, "tensor status word");
     }
     if (qb::gemm_tc_supported(t->m)) {
-        if (const size_t b = qb::tc_weight_copy_bytes(t->m)) {
-            e = cudaMalloc(&t->i8, b);
-            if (e == cudaSuccess) e = qb::unpack_q4_i8(t->m, static_cast<int8_t*>(t->i8), nullptr);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
-            if (e != cudaSuccess) {
-                cudaFree(t->q);
-                cudaFree(t->d);
-                cudaFree(t->status);
-                cudaFree(t->i8);
-                return cuda_err(e, "tensor int8 copy");
-            }
+        e = cudaMalloc(&t->tcbuf, qb::tc_weight_bytes(t->m));
+        if (e == cudaSuccess) e = qb::tc_prepare_weights(t->m, t->tcbuf, &t->wmap, nullptr);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+        if (e != cudaSuccess) {
+            cudaFree(t->q);
+            cudaFree(t->d);
+            cudaFree(t->status);
+            cudaFree(t->tcbuf);
+            return cuda_err(e, "tensor-core weight copies");
         }
-        t->tc = qb::make_weight_map(t->m, static_cast<const int8_t*>(t->i8), &t->wmap);
+        t->tc = true;
     }
     *out = t.release();
     return QNT_OK;
@@ -129,7 +127,7 @@ int qnt_tensor_free(qnt_dtensor* t) {
     cudaFree(t->q);
     cudaFree(t->d);
     cudaFree(t->status);
-    cudaFree(t->i8);
+    cudaFree(t->tcbuf);
     delete t;
     return QNT_OK;
 }
@@ -166,9 +164,18 @@ int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, i
         if ((reinterpret_cast<uintptr_t>(qx) | reinterpret_cast<uintptr_t>(dx)) & 15)
             return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
         if (n == 0 || r1 == r0) return QNT_OK;
+        // the kernel reads the activation scales block-major: a stream-ordered transposed copy
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const int nb = W->m.cols / 32, ldt = (n + 31) & ~31;
+        float* dxt = nullptr;
+        e = cudaMallocAsync(reinterpret_cast<void**>(&dxt), size_t(nb) * ldt * 4, s);
+        if (e != cudaSuccess) return cuda_err(e, "matmul scale copy");
         qb::TcAct act;
-        if (!qb::make_act_maps(qx, dx, n, W->m.cols, &act)) return set_err(QNT_ERR_CUDA, "TMA descriptor encode failed");
-        e = qb::launch_matmul_tc(W->m, W->wmap, act, n, r0, r1, out, ldo, W->status, static_cast<cudaStream_t>(stream));
+        e = qb::launch_transpose_scales(dx, n, nb, dxt, ldt, s);
+        if (e == cudaSuccess && !qb::make_act_maps(qx, dxt, n, ldt, W->m.cols, &act)) e = cudaErrorInvalidValue;
+        if (e == cudaSuccess) e = qb::launch_matmul_tc(W->m, W->wmap, act, n, r0, r1, out, ldo, W->status, s);
+        const cudaError_t ef = cudaFreeAsync(dxt, s);
+        if (e == cudaSuccess) e = ef;
     } else {
         e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, static_cast<cudaStream_t>(stream));
     }

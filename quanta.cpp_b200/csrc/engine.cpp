@@ -42,13 +42,10 @@ void* Engine::dalloc(size_t bytes) {
 
 bool Engine::tc_weights(const DMat& W, TcMap* map) {
     if (!gemm_tc_supported(W)) return false;
-    int8_t* copy = nullptr;
-    if (const size_t b = tc_weight_copy_bytes(W)) {
-        copy = static_cast<int8_t*>(dalloc(b));
-        if (unpack_q4_i8(W, copy, st_) != cudaSuccess) return false;
-        tc_copy_bytes_ += b;
-    }
-    return make_weight_map(W, copy, map);
+    const size_t b = tc_weight_bytes(W);
+    void* buf = dalloc(b);
+    tc_copy_bytes_ += b;
+    return tc_prepare_weights(W, buf, map, st_) == cudaSuccess;
 }
 
 int Engine::n_valid_default() const {
@@ -285,10 +282,13 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         DX_ = static_cast<float*>(dalloc(size_t(kChunk) * (wmax / QK) * 4));
         HQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * hp_.ffn_dim));
         HD_ = static_cast<float*>(dalloc(size_t(kChunk) * (hp_.ffn_dim / QK) * 4));
+        DXT_ = static_cast<float*>(dalloc(size_t(kChunk) * (wmax / QK) * 4));
+        HDT_ = static_cast<float*>(dalloc(size_t(kChunk) * (hp_.ffn_dim / QK) * 4));
         tokens_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         pos_ = static_cast<int*>(dalloc(16));
         // tensor-core matmul sources (a layer without them, or a driver without TMA encode, uses the CUDA cores)
-        tc_act_ = make_act_maps(XQ_, DX_, kChunk, hp_.dim, &tm_x_) && make_act_maps(HQ_, HD_, kChunk, hp_.ffn_dim, &tm_h_);
+        tc_act_ = make_act_maps(XQ_, DXT_, kChunk, kChunk, hp_.dim, &tm_x_) &&
+                  make_act_maps(HQ_, HDT_, kChunk, kChunk, hp_.ffn_dim, &tm_h_);
         for (Layer& L : layers_)
             L.tc = tc_act_ && tc_weights(L.qkv, &L.t_qkv) && tc_weights(L.o, &L.t_o) && tc_weights(L.gu, &L.t_gu) &&
                    tc_weights(L.down, &L.t_down);
@@ -426,16 +426,16 @@ int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm) {
             aa.vcache = qa.vcache;
             aa.max_chunks = (bctx_ + 63) / 64;
         }
-        QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
+        QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, pdl_));
         if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
         QB_TRY(launch_qkv_epilogue(qa, R_, n, pos_dev, Q_, st_, pdl_, tm));
         QB_TRY(launch_attn_prefill(aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_, tm));
-        QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, st_, pdl_));
+        QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, DXT_, kChunk, st_, pdl_));
         if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
-        QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, st_, pdl_));
+        QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, pdl_));
         if (int r = launch_matmul(L.gu, L.tc ? &L.t_gu : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, exptab_, st_, pdl_));
+        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, exptab_, st_, pdl_));
         if (int r = launch_matmul(L.down, L.tc ? &L.t_down : nullptr, true, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
     }
@@ -831,7 +831,7 @@ int Engine::batch_reset(int seq) {
 }
 
 int Engine::batch_head(int n, int* host_ids) {
-    QB_TRY(launch_norm_quant_rows(X_, final_norm_, n, hp_.dim, hp_.norm_eps, XQ_, DX_, st_, false));
+    QB_TRY(launch_norm_quant_rows(X_, final_norm_, n, hp_.dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, false));
     QB_TRY(launch_matmul_tc_argmax(lm_head_, t_head_, tm_x_, n, n_valid_default(), bcand_, status_, st_));
     QB_TRY(launch_argmax_reduce(bcand_, argmax_parts(lm_head_.rows), n, bids_, nullptr, st_));
     cudaMemcpyAsync(host_ids, bids_, size_t(n) * 4, cudaMemcpyDeviceToHost, st_);

@@ -89,7 +89,7 @@ public:
     int n_valid_default() const;
     size_t weight_bytes() const { return weight_bytes_; }
     size_t kv_cache_bytes() const { return kv_bytes_; }
-    // int8 copies of Q4_0 weights that the tensor-core matmul reads (q - 8 per element)
+    // copies the tensor-core matmul reads beside the weights: stage-major block scales, int8 q - 8 of Q4_0 matrices
     size_t tc_copy_bytes() const { return tc_copy_bytes_; }
     const std::string& error() const { return err_; }
     void set_matmul_impl(int impl) { mm_impl_ = impl; }
@@ -165,6 +165,7 @@ private:
     static constexpr int kTcChunkMin = 16;  // fewer tokens: the CUDA-core matmul
     float *X_ = nullptr, *Q_ = nullptr, *ATT_ = nullptr, *R_ = nullptr, *DX_ = nullptr, *HD_ = nullptr;
     int8_t *XQ_ = nullptr, *HQ_ = nullptr;
+    float *DXT_ = nullptr, *HDT_ = nullptr;  // block scales of XQ_ / HQ_ block-major ([block][kChunk])
     TcAct tm_x_{}, tm_h_{};  // activation tiles of the tensor-core matmul (dim / ffn inputs)
     bool tc_act_ = false;
     int* tokens_ = nullptr;

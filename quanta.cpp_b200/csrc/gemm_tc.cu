@@ -8,18 +8,18 @@
 // MMA (M = 128 weight rows, N = 32 tokens) into 32 TMEM columns of its own; a TMEM slot of 128 columns holds the four
 // blocks of a pipeline stage.  Tiles of 128 weight rows x 32 tokens; persistent CTAs (one per SM) walk their tiles
 // with the pipeline running across tile boundaries.
-// Weights are int8 rows: Q8_0 as stored, Q4_0 through an int8 copy of q - 8 made once (unpack_q4_i8), so that
-// every operand reaches shared memory by TMA alone.
-//   warp 0      TMA producers: per stage the weight tile (128 rows x 128 B, 128B-swizzled) and the activation tile
-//               (32 tokens x 128 B, 128B-swizzled) into the stage ring, the stage's block scales of the activations
-//               into a separate, deeper ring that the epilogue frees.  A thread's bulk loads complete one after
-//               another, so 12 lanes issue them: lane 4 k + p loads kind k (weights, activations, scales) of the
-//               steps p, p + 4, ...
-//   warp 1      allocates TMEM; one lane issues the stage's four MMAs into one of four TMEM slots; their completion
-//               frees the stage
+// Weights are int8 rows: Q8_0 as stored, Q4_0 through an int8 copy of q - 8 made once (tc_prepare_weights).
+// A TMA instruction costs the SM about the same whatever its size (about 0.12 us of its TMA unit), so each one moves
+// two K-steps: a stage is 2 x (128 weight rows x 128 B) and 2 x (32 tokens x 128 B), 128B-swizzled, through 3-D
+// tensor maps, and the stage's block scales (weights: 4 f16 per row and K-step, from a stage-major copy; activations:
+// f32 [block][token], from a block-major copy) come in two more loads into a deeper ring that the epilogue frees.
+//   warp 0      TMA producers, one lane per kind of load (weights, activations, weight scales, activation scales)
+//               and parity of the stage (a thread's bulk loads complete one after another)
+//   warp 1      allocates TMEM; one lane issues each K-step's four MMAs into one of four TMEM slots; the stage is
+//               free again when its last MMA completes
 //   warps 4-19  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 (its 32 weight rows) and, for each block, the
 //               columns of tokens 8 ((w - 4) / 4) .. +8, and folds the four blocks into 8 f32 accumulators per
-//               thread in block order
+//               thread in block order, two tokens per instruction (f32x2: every lane rounds as the scalar op)
 // Every wait is bounded: a wait that gives up sets ERR_WAIT_TIMEOUT in the status word and an abort flag that ends
 // every other wait, so the kernel always returns (and frees its TMEM once its issued MMAs have completed).
 #include <cuda.h>
@@ -42,21 +42,23 @@ constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = 128 + 32 * kEpiWarps;
 constexpr int kTileRows = 128;
 constexpr int kTileTok = 32;                       // tokens per tile (MMA N)
-constexpr int kStageBlocks = 4;                    // quant blocks per pipeline stage (128 bytes of K)
-constexpr int kCols = kTileTok * kStageBlocks;     // TMEM columns of a stage: block b of token t in column 32 b + t
+constexpr int kStageBlocks = 4;                    // quant blocks per K-step (128 bytes of K)
+constexpr int kCols = kTileTok * kStageBlocks;     // TMEM columns of a K-step: block b of token t in column 32 b + t
 constexpr int kTpt = kTileTok / 4;                 // tokens per epilogue thread
 constexpr int kSlots = 4;                          // TMEM accumulator slots of kCols columns
 constexpr int kTmemCols = kSlots * kCols;          // 512: the whole TMEM of the SM (one CTA per SM)
-constexpr int kASw = kTileRows * 128;              // swizzled int8 weight tile of a stage
-constexpr int kB = kTileTok * 128;                 // activation tile of a stage
-constexpr int kDX = kTileTok * kStageBlocks * 4;   // activation block scales of a stage
-constexpr int kDxRing = 16;                        // >= stages + slots: the scales never hold the producer back
+constexpr int kASw = kTileRows * 128;              // swizzled int8 weight tile of a K-step
+constexpr int kB = kTileTok * 128;                 // activation tile of a K-step
+constexpr int kKPS = 2;                            // K-steps per stage (per TMA instruction)
+constexpr int kStages = 4;
+constexpr int kStageBytes = kKPS * (kASw + kB);    // kKPS weight tiles, then kKPS activation tiles
+constexpr int kDWRows = kTileRows + 2;             // weight-scale rows per load (from an even row: 16-byte start)
+constexpr int kEpiDX = kKPS * kStageBlocks * kTileTok * 4;  // activation scales of a stage: [block][token] f32
+constexpr int kEpiDW = 2176;                       // weight scales of a stage: [K-step][kDWRows] x 4 f16 (padded)
+constexpr int kEpi = kEpiDX + kEpiDW;              // epilogue ring entry (TMA destinations on 128-byte boundaries)
+constexpr int kEpiRing = 8;                        // >= stages + slots / kKPS: the scales never hold the producer back
 constexpr unsigned kWaitLimit = 1u << 22;
 constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
-
-constexpr int kStages = 8;
-constexpr int kStageBytes = kASw + kB;             // weight tile, then activation tile (both 1024-byte aligned)
-constexpr int kProdPhases = 4;                     // producer lanes per kind of load
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 
@@ -97,6 +99,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart (tcgen05 format).
 __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
@@ -127,6 +135,18 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+// registers -> TMEM: the same 32 lanes x 4 x 8 columns, all set to x.
+__device__ __forceinline__ void tmem_st8x4_fill(uint32_t taddr, unsigned x) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%3], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u), "r"(x)
+        : "memory");
+}
+
 // TMEM -> registers: this warp's 32 lanes, 8 consecutive 32-bit columns at each of taddr + 32 b (b = 0..3):
 // v[8 b + i] = column 32 b + i.
 __device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
@@ -144,26 +164,41 @@ __device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
         : "memory");
 }
 
-// registers -> TMEM: the same 32 lanes x 4 x 8 columns, all set to x.
-__device__ __forceinline__ void tmem_st8x4_fill(uint32_t taddr, unsigned x) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%3], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-        "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u), "r"(x)
-        : "memory");
-}
-
 // The accumulators start at the bits of 2^23 + 2^22 (kMagic): the MMA then leaves 12582912 + s, whose float value
-// carries the exact block dot s, and fma(f, dw, -12582912 * dw) rounds s * dw once, exactly like
-// fmul(float(s), dw): 12582912 * dw is exact in f32 for an fp16 dw, and |s| < 2^22.
+// carries the exact block dot s (|s| < 2^22), and fma(f, dw, -12582912 * dw) rounds s * dw once, exactly like
+// fmul(float(s), dw): 12582912 * dw is exact in f32 for an fp16 dw.
 constexpr unsigned kMagic = 0x4B400000u;
 constexpr float kMagicF = 12582912.0f;
 
-// Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row atoms of 1024 bytes).
-__device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+// Two f32 lanes in one 64-bit register: each lane rounds to nearest like fmaf / fmul / fadd, no flush to zero.
+// ptxas contracts a mul.rn.f32x2 that feeds an add.rn.f32x2 into one fma (a single rounding), so the products are
+// taken as fma(a, b, -0.0) with the -0.0 a kernel argument: round(a * b) exactly, and nothing left to contract.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_pack_bits(int lo, int hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 
 
 __device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid) {
@@ -174,25 +209,25 @@ __device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
+                                                           const __grid_constant__ CUtensorMap tmDW,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
-    constexpr int S = kStages;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* dx_ring = smem + S * kStageBytes;
+    unsigned char* epi_ring = smem + kStages * kStageBytes;
     __shared__ uint64_t full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots];
-    __shared__ uint64_t dx_full[kDxRing], dx_empty[kDxRing], fin;
+    __shared__ uint64_t epi_full[kEpiRing], epi_empty[kEpiRing], fin;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nks = g.nb / kStageBlocks;
+    const int nks = g.nb / kStageBlocks, nst = (nks + kKPS - 1) / kKPS;  // K-steps and stages per tile
     const int n_tt = (g.n + kTileTok - 1) / kTileTok, n_tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * n_tt;
     // tile -> (first weight row, first token); tiles blockIdx.x, blockIdx.x + gridDim.x, ...
     auto tile_m0 = [&](int tile) { return g.r0 + (tile / n_tt) * kTileRows; };
     auto tile_t0 = [&](int tile) { return (tile % n_tt) * kTileTok; };
-    const int steps = ((n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)) * nks;
+    const int my_tiles = (n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 2);   // the weight and activation producers (one arrive.expect_tx each)
             mbar_init(&empty[s], 1);  // the MMA commit
         }
@@ -200,9 +235,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             mbar_init(&mma_done[j], 1);
             mbar_init(&slot_free[j], kEpiWarps);
         }
-        for (int d = 0; d < kDxRing; ++d) {
-            mbar_init(&dx_full[d], 1);
-            mbar_init(&dx_empty[d], kEpiWarps);
+        for (int d = 0; d < kEpiRing; ++d) {
+            mbar_init(&epi_full[d], 2);  // the two scale producers
+            mbar_init(&epi_empty[d], kEpiWarps);
         }
         mbar_init(&fin, 1);
         abort_flag = 0;
@@ -221,56 +256,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     volatile int* ab = &abort_flag;
 
     if (warp == 0) {
-        if (lane < 3 * kProdPhases) {  // TMA producers: kind (0 weights, 1 activations, 2 scales), phase
-            const int kind = lane / kProdPhases, ph = lane % kProdPhases;
-            int step = 0;
+        if (lane < 8) {  // TMA producers: kind = lane / 2 (weights, activations, their scales), parity of the stage
+            const int kind = lane >> 1, ph = lane & 1;
+            int u = 0;
             bool go = true;
             for (int tile = blockIdx.x; tile < n_tiles && go; tile += gridDim.x) {
                 const int m0 = tile_m0(tile), t0 = tile_t0(tile);
-                for (int ks = 0; ks < nks; ++ks, ++step) {
-                    if (step % kProdPhases != ph) continue;
+                for (int j = 0; j < nst; ++j, ++u) {
+                    if ((u & 1) != ph) continue;
+                    // full boxes: TMA zero-fills rows, tokens, K-chunks and blocks past the tensor
                     if (kind < 2) {
-                        const int s = step % S, round = step / S;
+                        const int s = u % kStages, round = u / kStages;
                         if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, ab, g.status)) {
                             go = false;
                             break;
                         }
                         unsigned char* st = smem + s * kStageBytes;
-                        if (kind == 0) {  // full boxes: TMA zero-fills rows past the matrix
-                            mbar_expect_tx(&full[s], kASw);
-                            tma_load_2d(st, &tmA, ks * 128, m0, &full[s]);
+                        if (kind == 0) {
+                            mbar_expect_tx(&full[s], kKPS * kASw);
+                            tma_load_3d(st, &tmA, 0, m0, j * kKPS, &full[s]);
                         } else {
-                            mbar_expect_tx(&full[s], kB);
-                            tma_load_2d(st + kASw, &tmB, ks * 128, t0, &full[s]);
+                            mbar_expect_tx(&full[s], kKPS * kB);
+                            tma_load_3d(st + kKPS * kASw, &tmB, 0, t0, j * kKPS, &full[s]);
                         }
                     } else {
-                        const int d = step % kDxRing, dround = step / kDxRing;
-                        if (dround > 0 && !mbar_wait(&dx_empty[d], (dround - 1) & 1, ab, g.status)) {
+                        const int d = u % kEpiRing, dround = u / kEpiRing;
+                        if (dround > 0 && !mbar_wait(&epi_empty[d], (dround - 1) & 1, ab, g.status)) {
                             go = false;
                             break;
                         }
-                        mbar_expect_tx(&dx_full[d], kDX);
-                        tma_load_2d(dx_ring + d * kDX, &tmDX, ks * kStageBlocks, t0, &dx_full[d]);
+                        unsigned char* e = epi_ring + d * kEpi;
+                        if (kind == 2) {  // x even: a TMA start must be 16-byte aligned
+                            mbar_expect_tx(&epi_full[d], kKPS * kDWRows * 8);
+                            tma_load_2d(e + kEpiDX, &tmDW, m0 & ~1, j * kKPS, &epi_full[d]);
+                        } else {
+                            mbar_expect_tx(&epi_full[d], kEpiDX);
+                            tma_load_2d(e, &tmDX, t0, j * kKPS * kStageBlocks, &epi_full[d]);
+                        }
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer: one K = 32 MMA per block, into the block's columns of the stage's slot
-            for (int step = 0; step < steps && !*ab; ++step) {
-                const int s = step % S, round = step / S;
-                const int slot = step % kSlots, use = step / kSlots;
+        if (lane == 0) {  // MMA issuer: one K = 32 MMA per block, into the block's columns of the K-step's slot
+            int step = 0;
+            bool go = true;
+            for (int u = 0; u < my_tiles * nst && go; ++u) {
+                const int s = u % kStages, round = u / kStages;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
-                // phase `use` of slot_free: the epilogue refilled the slot with the magic (phase 0: the initial fill)
-                if (!mbar_wait(&slot_free[slot], use & 1, ab, g.status)) break;
-                tc_fence_after();
+                const int j = u % nst, kk = min(kKPS, nks - j * kKPS);  // K-steps of this stage in its tile
                 unsigned char* st = smem + s * kStageBytes;
+                for (int h = 0; h < kk; ++h, ++step) {
+                    const int slot = step % kSlots, use = step / kSlots;
+                    // phase `use` of slot_free: the epilogue refilled the slot with the magic (phase 0: the initial fill)
+                    if (!mbar_wait(&slot_free[slot], use & 1, ab, g.status)) {
+                        go = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const unsigned char* a = st + h * kASw;
+                    const unsigned char* b = st + kKPS * kASw + h * kB;
 #pragma unroll
-                for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled columns
-                    mma_i8(tmem + uint32_t(slot * kCols + k * kTileTok), sw128_desc(st + 32 * k),
-                           sw128_desc(st + kASw + 32 * k), true);
-                mma_commit(&mma_done[slot]);
-                mma_commit(&empty[s]);
+                    for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled columns
+                        mma_i8(tmem + uint32_t(slot * kCols + k * kTileTok), sw128_desc(a + 32 * k), sw128_desc(b + 32 * k),
+                               true);
+                    mma_commit(&mma_done[slot]);
+                }
+                if (go) mma_commit(&empty[s]);
             }
             mma_commit(&fin);  // arrives once every MMA issued above has completed
         }
@@ -282,68 +334,79 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         __syncwarp();
         if (lane == 0)
             for (int j = 0; j < kSlots; ++j) mbar_arrive(&slot_free[j]);
-        int step = 0;
-        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const unsigned long long nz2 = f2_pack(__int_as_float(int(g.nzero)), __int_as_float(int(g.nzero)));
+        int step = 0, u = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
             const int row = m0 + q * 32 + lane;
             const bool row_ok = row < g.r1;
-            const uint2* wd = reinterpret_cast<const uint2*>(g.wd + size_t(row_ok ? row : g.r0) * g.nb);
-            float acc[kTpt];
+            unsigned long long acc[kTpt / 2];  // tokens (2 j, 2 j + 1) of this thread's 8
 #pragma unroll
-            for (int i = 0; i < kTpt; ++i) acc[i] = 0.f;
-            uint2 dnext = __ldg(wd);
-            bool ok = true;
-            for (int ks = 0; ks < nks; ++ks, ++step) {
-                const int slot = step % kSlots, use = step / kSlots;
-                const int d = step % kDxRing, dround = step / kDxRing;
-                const uint2 dcur = dnext;
-                if (ks + 1 < nks) dnext = __ldg(wd + ks + 1);
-                const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.x));
-                const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dcur.y));
-                const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
-                const float nmdw[4] = {-fmul(kMagicF, d01.x), -fmul(kMagicF, d01.y), -fmul(kMagicF, d23.x),
-                                       -fmul(kMagicF, d23.y)};
-                int got = 0;
-                if (lane == 0)
-                    got = mbar_wait(&mma_done[slot], use & 1, ab, g.status) &&
-                          mbar_wait(&dx_full[d], dround & 1, ab, g.status);
-                if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
-                    ok = false;
-                    break;
+            for (int j = 0; j < kTpt / 2; ++j) acc[j] = 0ull;
+            for (int j = 0; j < nst && ok; ++j, ++u) {
+                const int d = u % kEpiRing, dround = u / kEpiRing, kk = min(kKPS, nks - j * kKPS);
+                const unsigned char* e = epi_ring + d * kEpi;
+                int got = 1;
+                if (lane == 0) got = mbar_wait(&epi_full[d], dround & 1, ab, g.status);
+                for (int h = 0; h < kk; ++h, ++step) {
+                    const int slot = step % kSlots, use = step / kSlots;
+                    if (lane == 0 && got) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
+                    if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    int v[32];  // v[8 b + i]: kMagic + block b's dot of token cg * kTpt + i
+                    tmem_ld8x4(my_cols + uint32_t(slot * kCols), v);
+                    tmem_st8x4_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&slot_free[slot]);
+                    const uint2 dq =
+                        *reinterpret_cast<const uint2*>(e + kEpiDX + (h * kDWRows + (m0 & 1) + q * 32 + lane) * 8);
+                    const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dq.x));
+                    const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dq.y));
+                    const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {  // acc = acc + (float(s) * dw) * dx, each rounded as in the reference
+                        const unsigned long long dw2 = f2_pack(dw[b], dw[b]);
+                        const float nm = -fmul(kMagicF, dw[b]);
+                        const unsigned long long nm2 = f2_pack(nm, nm);
+                        const float4* sdx = reinterpret_cast<const float4*>(e + ((h * kStageBlocks + b) * kTileTok + cg * kTpt) * 4);
+                        const float4 x0 = sdx[0], x1 = sdx[1];
+                        const unsigned long long dx2[4] = {f2_pack(x0.x, x0.y), f2_pack(x0.z, x0.w), f2_pack(x1.x, x1.y),
+                                                           f2_pack(x1.z, x1.w)};
+#pragma unroll
+                        for (int i = 0; i < kTpt / 2; ++i)
+                            acc[i] = f2_add(acc[i], f2_fma(f2_fma(f2_pack_bits(v[8 * b + 2 * i], v[8 * b + 2 * i + 1]), dw2, nm2),
+                                                           dx2[i], nz2));
+                    }
                 }
-                tc_fence_after();
-                int v[32];  // v[8 b + i]: kMagic + block b's dot of token cg * kTpt + i
-                tmem_ld8x4(my_cols + uint32_t(slot * kCols), v);
-                tmem_st8x4_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&slot_free[slot]);
-                const float4* sdx = reinterpret_cast<const float4*>(dx_ring + d * kDX) + cg * kTpt;
-#pragma unroll
-                for (int i = 0; i < kTpt; ++i) {
-                    const float4 dx = sdx[i];
-                    const float dxv[4] = {dx.x, dx.y, dx.z, dx.w};
-#pragma unroll
-                    for (int b = 0; b < 4; ++b)  // acc = acc + (float(s) * dw) * dx, each rounded as in the reference
-                        acc[i] = fadd(acc[i], fmul(__fmaf_rn(__int_as_float(v[8 * b + i]), dw[b], nmdw[b]), dxv[b]));
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&dx_empty[d]);
+                __syncwarp();  // the ring entry is read before it is freed
+                if (lane == 0 && ok) mbar_arrive(&epi_empty[d]);
             }
             if (!ok) break;
+            float res[kTpt];
+#pragma unroll
+            for (int i = 0; i < kTpt / 2; ++i) {
+                const float2 p = f2_unpack(acc[i]);
+                res[2 * i] = p.x;
+                res[2 * i + 1] = p.y;
+            }
             if (EPI == 0) {
                 if (row_ok) {
 #pragma unroll
                     for (int i = 0; i < kTpt; ++i) {
                         const int t = t0 + cg * kTpt + i;
-                        if (t < g.n) g.out[size_t(t) * g.ldo + row] = acc[i];
+                        if (t < g.n) g.out[size_t(t) * g.ldo + row] = res[i];
                     }
                 }
             } else {
                 const int mt = tile / n_tt;
 #pragma unroll
                 for (int i = 0; i < kTpt; ++i) {
-                    float v = row_ok && row < g.n_valid ? acc[i] : -INFINITY;
+                    float v = row_ok && row < g.n_valid ? res[i] : -INFINITY;
                     int id = row_ok && row < g.n_valid ? row : INT_MAX;
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
@@ -386,6 +449,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// 3-D view of a [rows][cols] int8 matrix as (128-byte K-chunk x rows x chunks): a box of 128 x box_rows x kKPS lands
+// as kKPS consecutive 128B-swizzled [box_rows][128 B] tiles, one per K-step.
 bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
                uint32_t box_in, uint32_t box_out, CUtensorMapSwizzle sw) {
     auto fn = encode_fn();
@@ -398,13 +463,22 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_kchunks(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn || cols % 128 != 0) return false;
+    const cuuint64_t dims[3] = {128, rows, cols / 128};
+    const cuuint64_t strides[2] = {cols, 128};
+    const cuuint32_t box[3] = {128, box_rows, kKPS};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool gemm_tc_supported(const DMat& W) {
     return (W.dtype == DT_Q8_0 || W.dtype == DT_Q4_0) && W.cols % (kStageBlocks * QK) == 0 && encode_fn() != nullptr;
 }
-
-size_t tc_weight_copy_bytes(const DMat& W) { return W.dtype == DT_Q4_0 ? size_t(W.rows) * size_t(W.cols) : 0; }
 
 namespace {
 
@@ -422,41 +496,86 @@ __global__ void __launch_bounds__(256) k_unpack_q4_i8(const uint4* __restrict__ 
     }
 }
 
+// out[g * ldr + r] = the 4 scales of row r, K-step g (blocks 4 g .. 4 g + 3).
+__global__ void __launch_bounds__(256) k_scale_copy(const uint2* __restrict__ d, int rows, int ng, uint2* __restrict__ out, int ldr) {
+    const size_t n = size_t(rows) * ng;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+        const int g = int(i / rows), r = int(i - size_t(g) * rows);
+        out[size_t(g) * ldr + r] = __ldg(d + size_t(r) * ng + g);
+    }
+}
+
+int rows_pad(int rows) { return (rows + 1) & ~1; }  // scale-copy pitch: a multiple of 16 bytes
+
+__global__ void __launch_bounds__(256) k_transpose_scales(const float* __restrict__ dx, int n, int nb, float* __restrict__ dxt,
+                                                          int ldt) {
+    const size_t total = size_t(n) * nb;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int t = int(i / nb), b = int(i - size_t(t) * nb);
+        dxt[size_t(b) * ldt + t] = dx[i];
+    }
+}
+
+unsigned grid_for(size_t n) { return unsigned(std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 148 * 16))); }
+
 }  // namespace
 
-cudaError_t unpack_q4_i8(const DMat& W, int8_t* dst, cudaStream_t st) {
-    if (W.dtype != DT_Q4_0 || W.cols % QK != 0 || reinterpret_cast<uintptr_t>(W.q) % 16 != 0 ||
-        reinterpret_cast<uintptr_t>(dst) % 16 != 0)
+size_t tc_weight_bytes(const DMat& W) {
+    const size_t sc = (size_t(W.cols / (kStageBlocks * QK)) * size_t(rows_pad(W.rows)) * 8 + 255) / 256 * 256;
+    return sc + (W.dtype == DT_Q4_0 ? size_t(W.rows) * size_t(W.cols) : 0);
+}
+
+cudaError_t tc_prepare_weights(const DMat& W, void* buf, TcMap* out, cudaStream_t st) {
+    if (!gemm_tc_supported(W) || !buf || reinterpret_cast<uintptr_t>(buf) % 256 != 0 || reinterpret_cast<uintptr_t>(W.q) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(W.d) % 8 != 0)
         return cudaErrorInvalidValue;
-    const size_t n_blocks = size_t(W.rows) * size_t(W.cols / QK);
-    const unsigned grid = unsigned(std::min<size_t>((n_blocks + 255) / 256, 148 * 16));
-    if (n_blocks == 0) return cudaSuccess;
-    k_unpack_q4_i8<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(W.q), reinterpret_cast<uint4*>(dst), n_blocks);
+    const int ng = W.cols / (kStageBlocks * QK), ldr = rows_pad(W.rows);
+    unsigned char* sc = static_cast<unsigned char*>(buf);
+    const size_t sc_bytes = (size_t(ng) * ldr * 8 + 255) / 256 * 256;
+    k_scale_copy<<<grid_for(size_t(W.rows) * ng), 256, 0, st>>>(reinterpret_cast<const uint2*>(W.d), W.rows, ng,
+                                                                reinterpret_cast<uint2*>(sc), ldr);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const void* rows8 = W.q;
+    if (W.dtype == DT_Q4_0) {
+        void* i8 = sc + sc_bytes;
+        const size_t n_blocks = size_t(W.rows) * size_t(W.cols / QK);
+        k_unpack_q4_i8<<<grid_for(n_blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(W.q), static_cast<uint4*>(i8),
+                                                          n_blocks);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        rows8 = i8;
+    }
+    // weight scales: kDWRows rows from an even row (the tile's first row is m0 or m0 - 1 in the box), kKPS K-steps
+    return encode_kchunks(&out->m, rows8, uint64_t(W.rows), uint64_t(W.cols), kTileRows) &&
+                   encode_2d(&out->s, CU_TENSOR_MAP_DATA_TYPE_UINT64, sc, uint64_t(ldr), uint64_t(ng), uint64_t(ldr) * 8, kDWRows,
+                             kKPS, CU_TENSOR_MAP_SWIZZLE_NONE)
+               ? cudaSuccess
+               : cudaErrorInvalidValue;
+}
+
+bool make_act_maps(const int8_t* qx, const float* dxt, int rows, int ldt, int cols, TcAct* out) {
+    if (cols % (kStageBlocks * QK) != 0 || rows <= 0 || ldt % kTileTok != 0 || ldt < rows ||
+        reinterpret_cast<uintptr_t>(dxt) % 16 != 0)
+        return false;
+    const int nb = cols / QK;
+    return encode_kchunks(&out->q.m, qx, uint64_t(rows), uint64_t(cols), kTileTok) &&
+           encode_2d(&out->d.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxt, uint64_t(rows), uint64_t(nb), uint64_t(ldt) * 4, kTileTok,
+                     kKPS * kStageBlocks, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, int ldt, cudaStream_t st) {
+    if (n <= 0 || nb <= 0) return cudaSuccess;
+    k_transpose_scales<<<grid_for(size_t(n) * nb), 256, 0, st>>>(dx, n, nb, dxt, ldt);
     return cudaGetLastError();
 }
 
-bool make_weight_map(const DMat& W, const int8_t* i8, TcMap* out) {
-    if (!gemm_tc_supported(W) || (W.dtype == DT_Q4_0 && !i8)) return false;
-    const void* src = W.dtype == DT_Q8_0 ? static_cast<const void*>(W.q) : static_cast<const void*>(i8);
-    return encode_2d(&out->m, CU_TENSOR_MAP_DATA_TYPE_UINT8, src, uint64_t(W.cols), uint64_t(W.rows), uint64_t(W.cols), 128,
-                     kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
-}
-
-bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out) {
-    if (cols % (kStageBlocks * QK) != 0 || rows_alloc <= 0) return false;
-    const int nb = cols / QK;
-    return encode_2d(&out->q.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, uint64_t(cols), uint64_t(rows_alloc), uint64_t(cols), 128,
-                     kTileTok, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_2d(&out->d.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, uint64_t(nb), uint64_t(rows_alloc), uint64_t(nb) * 4,
-                     kStageBlocks, kTileTok, CU_TENSOR_MAP_SWIZZLE_NONE);
-}
-
-size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kDxRing) * kDX + 1024; }
+size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kEpiRing) * kEpi + 1024; }
 
 namespace {
 
 template <int EPI>
-cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, const GemmTcArgs& g, cudaStream_t st) {
+cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, GemmTcArgs g, cudaStream_t st) {
+    g.nzero = 0x80000000u;
     static int sms = 0;
     if (sms == 0) {
         int dev = 0;
@@ -470,7 +589,7 @@ cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, co
     if (W.dtype != DT_Q8_0 && W.dtype != DT_Q4_0) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    k_gemm_tc<EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, act.d.m, g);
+    k_gemm_tc<EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, wmap.s, act.d.m, g);
     return cudaGetLastError();
 }
 
@@ -520,7 +639,14 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
                              unsigned* status, cudaStream_t st) {
     if (r1 <= r0 || n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
-    const GemmTcArgs g{r0, r1, W.cols / QK, n, W.d, out, ldo, status, 0, nullptr};
+    GemmTcArgs g{};
+    g.r0 = r0;
+    g.r1 = r1;
+    g.nb = W.cols / QK;
+    g.n = n;
+    g.out = out;
+    g.ldo = ldo;
+    g.status = status;
     return launch_tc_any<0>(W, wmap, act, g, st);
 }
 
@@ -530,7 +656,14 @@ cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAc
                                     unsigned* status, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
-    const GemmTcArgs g{0, W.rows, W.cols / QK, n, W.d, nullptr, 0, status, n_valid, cand};
+    GemmTcArgs g{};
+    g.r0 = 0;
+    g.r1 = W.rows;
+    g.nb = W.cols / QK;
+    g.n = n;
+    g.status = status;
+    g.n_valid = n_valid;
+    g.cand = cand;
     return launch_tc_any<1>(W, wmap, act, g, st);
 }
 

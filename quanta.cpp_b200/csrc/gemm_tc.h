@@ -10,35 +10,42 @@ namespace qb {
 // Token count from which qnt_matmul's automatic choice takes the tensor cores.
 constexpr int kTcMinTokens = 1 << 30;
 
+// A weight matrix as the kernel's TMA sources: m its int8 rows (two 128B-swizzled 128 x 128-byte tiles per load),
+// s its block scales in K-step-major order (4 f16 per row and K-step).
 struct alignas(64) TcMap {
-    CUtensorMap m;
+    CUtensorMap m, s;
 };
 
 struct GemmTcArgs {
     int r0, r1;        // weight rows [r0, r1)
     int nb;            // 32-blocks per row
     int n;             // tokens
-    const __half* wd;  // weight block scales [rows][nb]
     float* out;        // out[t * ldo + r]
     int ldo;
     unsigned* status;  // device status word (ERR_WAIT_TIMEOUT)
     int n_valid;       // argmax epilogue: rows >= n_valid never win
     void* cand;        // argmax epilogue: Cand [row tiles * 4][n], each 32-row group's best (value, id) per token
+    unsigned nzero;    // 0x80000000 (-0.0f): the addend that turns an fma into the exact product (see the kernel)
 };
 
 bool gemm_tc_supported(const DMat& W);
-// The kernel reads int8 weight rows: Q8_0 matrices as stored, Q4_0 through an int8 copy of q - 8 (rows x cols
-// bytes, tc_weight_copy_bytes; 0 for Q8_0) that unpack_q4_i8 writes once.
-size_t tc_weight_copy_bytes(const DMat& W);
-cudaError_t unpack_q4_i8(const DMat& W, int8_t* dst, cudaStream_t st);
-// The int8 weights as the kernel's TMA source (128B-swizzled 128 x 128-byte tiles): W.q for Q8_0, i8 for Q4_0.
-bool make_weight_map(const DMat& W, const int8_t* i8, TcMap* out);
-// Quantized activations q [rows_alloc][cols] int8 and their block scales d [rows_alloc][cols / 32] f32, as TMA sources.
+// Device bytes the tensor-core path keeps beside W: a K-step-major copy of its block scales and, for Q4_0, an int8
+// copy of q - 8 (the kernel reads int8 rows only; Q8_0 rows are read where they are).
+size_t tc_weight_bytes(const DMat& W);
+// Writes those copies into buf (tc_weight_bytes(W) bytes, 256-byte aligned) on st and encodes the TMA sources.
+cudaError_t tc_prepare_weights(const DMat& W, void* buf, TcMap* out, cudaStream_t st);
+// Quantized activations as TMA sources: q [rows][cols] int8 (32-token boxes) and the block scales in block-major
+// order, dxt[b * ldt + t] = scale of block b of token t (ldt >= rows, a multiple of 32).
+struct TcActMap {
+    CUtensorMap m;
+};
 struct TcAct {
-    TcMap q, d;
+    TcActMap q, d;
 };
 size_t gemm_tc_smem();
-bool make_act_maps(const int8_t* qx, const float* dx, int rows_alloc, int cols, TcAct* out);
+bool make_act_maps(const int8_t* qx, const float* dxt, int rows, int ldt, int cols, TcAct* out);
+// dxt[b * ldt + t] = dx[t * nb + b] for t < n (the block-major scales from the token-major ones).
+cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, int ldt, cudaStream_t st);
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
                              unsigned* status, cudaStream_t st);
 

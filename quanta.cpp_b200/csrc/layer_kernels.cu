@@ -216,9 +216,10 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
 // ---------------------------------------------------------------- batched (prefill) elementwise kernels
 
 // One CTA per token: rmsnorm + quantize (norm_w != null) or quantize only.
+// DXT (optional): the block scales also in block-major order, DXT[b * ldt + t].
 __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __restrict__ X, const float* __restrict__ norm_w,
                                                               int dim, float eps, int8_t* __restrict__ XQ,
-                                                              float* __restrict__ DX) {
+                                                              float* __restrict__ DX, float* __restrict__ DXT, int ldt) {
     __shared__ __align__(16) float sred[32 + 2048];
     NormW nw;
     if (norm_w) load_norm_w(norm_w, dim, nw);
@@ -227,6 +228,10 @@ __global__ void __launch_bounds__(kThreads) k_norm_quant_rows(const float* __res
     const int t = blockIdx.x;
     if (norm_w) norm_quant(X + size_t(t) * dim, nw, dim, eps, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr, sred);
     else quant_only(X + size_t(t) * dim, dim, XQ + size_t(t) * dim, DX + size_t(t) * (dim / QK), nullptr);
+    if (DXT) {
+        __syncthreads();  // this CTA's scale stores are visible to it
+        for (int b = threadIdx.x; b < dim / QK; b += blockDim.x) DXT[size_t(b) * ldt + t] = DX[size_t(t) * (dim / QK) + b];
+    }
 }
 
 // R [n][fused rows] raw q|k|v -> bias + RoPE + store, token t at position pos0 + t.
@@ -256,7 +261,7 @@ __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, l
 
 // R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
 __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
-                               float* __restrict__ HD, ExpTab tab) {
+                               float* __restrict__ HD, float* __restrict__ HDT, int ldt, ExpTab tab) {
     pdl_wait();
     pdl_launch_dependents();
     const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
@@ -268,7 +273,10 @@ __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, 
     float d;
     const int8_t q = quantize_lane(h, &d);
     HQ[size_t(t) * ffn + j * QK + lane] = q;
-    if (lane == 0) HD[size_t(t) * nbk + j] = d;
+    if (lane == 0) {
+        HD[size_t(t) * nbk + j] = d;
+        if (HDT) HDT[size_t(j) * ldt + t] = d;
+    }
 }
 
 // ---------------------------------------------------------------- launchers
@@ -352,8 +360,8 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
 }
 
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
-                                   cudaStream_t st, bool pdl) {
-    return launch_pdl(k_norm_quant_rows, dim3(n_tok), dim3(kThreads), 0, st, pdl, X, norm_w, dim, eps, XQ, DX);
+                                   float* DXT, int ldt, cudaStream_t st, bool pdl) {
+    return launch_pdl(k_norm_quant_rows, dim3(n_tok), dim3(kThreads), 0, st, pdl, X, norm_w, dim, eps, XQ, DX, DXT, ldt);
 }
 
 cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
@@ -368,11 +376,11 @@ cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t 
     return launch_pdl(k_residual, dim3(grid), dim3(kThreads), 0, st, pdl, X, R, n);
 }
 
-cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st,
-                                bool pdl) {
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, const ExpTab& tab,
+                                cudaStream_t st, bool pdl) {
     const long long warps = (long long)n_tok * (ffn / QK);
     return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD,
-                      tab);
+                      HDT, ldt, tab);
 }
 
 }  // namespace qb

@@ -54,12 +54,13 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
 // n_tok > 1 consecutive tokens whose positions stay below pos_bound (known on the host): one CTA per (kv head, token).
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
                                 cudaStream_t st, bool pdl, TokMap tm = TokMap{});
+// DXT (optional): the block scales also block-major, DXT[b * ldt + t] (the tensor-core matmul's layout).
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
-                                   cudaStream_t st, bool pdl);
+                                   float* DXT, int ldt, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, const int* pos_dev, float* Q, cudaStream_t st,
                                 bool pdl, TokMap tm = TokMap{});
 cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl);
-cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st,
-                                bool pdl);
+cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, const ExpTab& tab,
+                                cudaStream_t st, bool pdl);
 
 }  // namespace qb
