@@ -178,17 +178,45 @@ __device__ __forceinline__ void load_norm_w(const float* __restrict__ w, int dim
     }
 }
 
-// quantize one round's element (whole warp participates when the round is valid for the warp).
-__device__ __forceinline__ void quant_round(float v, int i, int8_t* sx, float* sdx, int* ssum) {
-    const int lane = threadIdx.x & 31;
-    float d;
-    const int8_t q = quantize_lane(v, &d);
-    sx[i] = q;
-    if (ssum) {
-        const int s = warp_sum_i(int(q));
-        if (lane == 0) ssum[i / QK] = s;
+// quantize_q8 of a whole activation held in registers, v[k] = element k * blockDim + tid (0 past n): the rounds'
+// warp reductions, divisions and roundings are interleaved (independent per round), which keeps the dependent
+// latency of a decode prologue to about one round's.  Same results as quant_round on every round.
+template <int NR>
+__device__ __forceinline__ void quant_rounds_n(const float* v, int n, int8_t* sx, float* sdx, int* ssum) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, T = blockDim.x;
+    float amax[NR];
+#pragma unroll
+    for (int k = 0; k < NR; ++k) amax[k] = fabsf(v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int k = 0; k < NR; ++k) amax[k] = fmaxf(amax[k], __shfl_xor_sync(0xffffffffu, amax[k], o));
     }
-    if (lane == 0) sdx[i / QK] = d;
+    int q[NR];
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+        const float d = fdiv(amax[k], 127.0f);
+        const float inv = d > 0.f ? fdiv(1.0f, d) : 0.0f;
+        q[k] = int((int8_t)lroundf(fmul(v[k], inv)));
+        if (k * T + warp * 32 < n) {
+            sx[k * T + tid] = int8_t(q[k]);
+            if (lane == 0) sdx[(k * T + tid) / QK] = d;
+        }
+    }
+    if (ssum) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int k = 0; k < NR; ++k) q[k] += __shfl_xor_sync(0xffffffffu, q[k], o);
+        }
+#pragma unroll
+        for (int k = 0; k < NR; ++k)
+            if (k * T + warp * 32 < n && lane == 0) ssum[(k * T + tid) / QK] = q[k];
+    }
+}
+__device__ __forceinline__ void quant_rounds(const float (&v)[kMaxRounds], int n, int8_t* sx, float* sdx, int* ssum) {
+    if (n <= 4 * int(blockDim.x)) quant_rounds_n<4>(v, n, sx, sdx, ssum);
+    else quant_rounds_n<kMaxRounds>(v, n, sx, sdx, ssum);
 }
 
 // Sum of squares in element order, ((x0*x0 + x1*x1) + x2*x2) + ..., the reference's sequential loop
@@ -232,7 +260,7 @@ __device__ __forceinline__ float ordered_sum(const float* v, int n, float s = 0.
 // sred: scratch of >= dim + 32 floats.  Bit-identical to the reference.  dim <= kMaxRounds * blockDim.
 __device__ __forceinline__ void norm_quant(const float* __restrict__ x, const NormW& nw, int dim, float eps, int8_t* sx,
                                            float* sdx, int* ssum, float* sred) {
-    const int tid = threadIdx.x, warp = tid >> 5, T = blockDim.x;
+    const int tid = threadIdx.x, T = blockDim.x;
     float xv[kMaxRounds];
 #pragma unroll
     for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < dim ? __ldcg(x + tid + k * T) : 0.f;
@@ -245,23 +273,20 @@ __device__ __forceinline__ void norm_quant(const float* __restrict__ x, const No
     __syncthreads();
     const float tot = sred[0];
     const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(tot, float(dim)), eps)));
+    float y[kMaxRounds];
 #pragma unroll
-    for (int k = 0; k < kMaxRounds; ++k) {
-        const int i = tid + k * T;
-        if (k * T + warp * 32 < dim) quant_round(fmul(fmul(xv[k], scale), nw.w[k]), i, sx, sdx, ssum);
-    }
+    for (int k = 0; k < kMaxRounds; ++k) y[k] = fmul(fmul(xv[k], scale), nw.w[k]);  // 0 past dim
+    quant_rounds(y, dim, sx, sdx, ssum);
     __syncthreads();
 }
 
 // quantize_q8 of x[n] (no norm) into sx / sdx (and block sums); n <= kMaxRounds * blockDim.
 __device__ __forceinline__ void quant_only(const float* __restrict__ x, int n, int8_t* sx, float* sdx, int* ssum) {
-    const int tid = threadIdx.x, warp = tid >> 5, T = blockDim.x;
+    const int tid = threadIdx.x, T = blockDim.x;
     float xv[kMaxRounds];
 #pragma unroll
     for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < n ? __ldcg(x + tid + k * T) : 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxRounds; ++k)
-        if (k * T + warp * 32 < n) quant_round(xv[k], tid + k * T, sx, sdx, ssum);
+    quant_rounds(xv, n, sx, sdx, ssum);
     __syncthreads();
 }
 
