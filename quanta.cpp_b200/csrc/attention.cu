@@ -13,8 +13,12 @@
 //   2. cluster barrier; every CTA reads the CS maxima, exponentiates its own scores and stores the weights straight
 //      into the leader's weight row (distributed shared memory).
 //   3. cluster barrier; the other CTAs exit.  The leader sums the row in position order on one thread and normalises
-//      it.  Six warps stream V rows through a cp.async ring (the first blocks requested inside the second barrier, so
-//      they land during the sum); two warps, one lane per dimension, chain o_d += a_j * v_jd in position order.
+//      it.  Six producer warps stream V rows through a cp.async ring and turn each 64-row block into the products
+//      a_j * v_jd (f32, the reference's separately rounded multiply) in one of two buffers; two chain warps, one lane
+//      per dimension, add them in position order, o_d += p_jd, one load and one add per row.
+// K and V rows below the launch's first position were written by earlier launches, so they are requested before the
+// programmatic-launch wait (the first K tile into registers, the leading V blocks into the ring) and land while the
+// previous kernel finishes; only rows of this launch's own tokens and the query wait.
 // Decode launches CS = min(8, chunks); multi-token (prefill) launches use CS = 1, one CTA per (head, token), which
 // keeps the SMs busy with many tokens at once.  The cluster barriers are hardware barriers (no spin loops).
 #include <cooperative_groups.h>
@@ -37,22 +41,30 @@ constexpr int kMaxCluster = 8;      // portable cluster size limit
 constexpr int kKfStride = kHd + 1;  // f32 K tile row stride (conflict-free column walks)
 constexpr int kSlotBytes = kVBlk * kHd * 2;  // one f16 V block
 
-// Dynamic shared memory layout (byte offsets), the same for every CTA of a launch.  The K tile (scores) and the V
-// ring (outputs) share one region: the ring is first written after the first cluster barrier.
+// Dynamic shared memory layout (byte offsets), the same for every CTA of a launch.
 constexpr int kOffQ = 0;                        // f32 [kHd] query
 constexpr int kOffMax = kOffQ + kHd * 4;        // f32 [kMaxCluster] local maxima (the leader's copy is used)
-constexpr int kOffRegion = kOffMax + 256;       // f32 [kTile][kKfStride] K tile | f16 [R][kVBlk][kHd] V ring
+constexpr int kOffK = kOffMax + 256;            // f32 [kTile][kKfStride] K tile
 constexpr int kKfBytes = kTile * kKfStride * 4;
-static_assert(kOffRegion % 16 == 0 && kKfBytes % 16 == 0, "16-byte aligned regions");
+constexpr int kOffRing = kOffK + kKfBytes;      // f16 [R][kVBlk][kHd] V ring
+constexpr int kProdBytes = kVBlk * kHd * 4;     // f32 [kVBlk][kHd] products of one V block
+static_assert(kOffK % 16 == 0 && kKfBytes % 16 == 0, "16-byte aligned regions");
 static_assert(kThreads == 256 && kTile * 8 % kThreads == 0, "K tile loader");
+constexpr int kProducers = kThreads - kOutThreads;
+// named barriers (0 is __syncthreads): the producers among themselves; product buffer b full / free
+constexpr int kBarProd = 1, kBarFull = 2, kBarFree = 4;
 
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+template <int ID>
+__device__ __forceinline__ void bar_sync(int count) { asm volatile("bar.sync %0, %1;" ::"n"(ID), "r"(count) : "memory"); }
+template <int ID>
+__device__ __forceinline__ void bar_arrive(int count) { asm volatile("bar.arrive %0, %1;" ::"n"(ID), "r"(count) : "memory"); }
 
-__host__ __device__ constexpr int region_bytes(int ring) { return ring * kSlotBytes > kKfBytes ? ring * kSlotBytes : kKfBytes; }
 __host__ __device__ inline int ls_len(int ctx, int cs) { return ((ctx + cs - 1) / cs + 3) & ~3; }
-// then f32 [ls_len] own scores, f32 [ctx] weights
-__host__ __device__ inline int off_ls(int ring) { return kOffRegion + region_bytes(ring); }
+__host__ __device__ constexpr int off_prod(int ring) { return kOffRing + ring * kSlotBytes; }
+// then f32 [2][kVBlk][kHd] products, f32 [ls_len] own scores, f32 [ctx] weights
+__host__ __device__ constexpr int off_ls(int ring) { return off_prod(ring) + 2 * kProdBytes; }
 inline size_t attn_smem_bytes(int ctx, int cs, int ring) {
     return size_t(off_ls(ring)) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4;
 }
@@ -68,43 +80,59 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     const int ctx = a.max_chunks * kPosChunk;
     float* sq = reinterpret_cast<float*>(smem + kOffQ);
     float* smx = reinterpret_cast<float*>(smem + kOffMax);
-    float* kf = reinterpret_cast<float*>(smem + kOffRegion);
-    __half* ring = reinterpret_cast<__half*>(smem + kOffRegion);
+    float* kf = reinterpret_cast<float*>(smem + kOffK);
+    __half* ring = reinterpret_cast<__half*>(smem + kOffRing);
+    float* prod = reinterpret_cast<float*>(smem + off_prod(R));
     float* LS = reinterpret_cast<float*>(smem + off_ls(R));
     float* E = LS + ls_len(ctx, CS);
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
-    pdl_wait();
-    pdl_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = __ldcg(pos_dev) + t + 1;
+    // The launch's first position was written by an earlier launch (the host or the step's first kernel); K / V rows
+    // below it are final, rows from it on are this launch's (the previous kernel's) and wait for it.
+    const int pos0 = __ldcg(pos_dev);
+    const int n = pos0 + t + 1;
     const int P = (n + CS - 1) / CS, p0 = min(n, r * P), p1 = min(n, p0 + P);
     const bool leader = r == 0, producer = tid >= kOutThreads;
     const int nblk = (n + kVBlk - 1) / kVBlk;
     const __half* V = a.vcache + g * kHd;
+    const __half* K = a.kcache + g * kHd;
     auto issue_v = [&](int b) {  // V rows [64 b, min(64 b + 64, n)) into slot b % R (producer threads); empty past the end
         if (b < nblk) {
             const int r0 = b * kVBlk, rows = min(kVBlk, n - r0);
             __half* dst = ring + (b % R) * kVBlk * kHd;
-            for (int i = tid - kOutThreads; i < rows * 8; i += kThreads - kOutThreads)
+            for (int i = tid - kOutThreads; i < rows * 8; i += kProducers)
                 cp_async16(dst + (i >> 3) * kHd + (i & 7) * 8, V + size_t(r0 + (i >> 3)) * a.kv_dim + (i & 7) * 8);
         }
         cp_commit();
     };
-    if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
-
-    // ---- 1. scores of [p0, p1), one position per thread
-    const __half* K = a.kcache + g * kHd;
-    for (int tile0 = p0; tile0 < p1; tile0 += kTile) {
-        const int tl = min(kTile, p1 - tile0);
-        constexpr int U = kTile * 8 / kThreads;
-        uint4 kv[U];
+    constexpr int U = kTile * 8 / kThreads;
+    uint4 kv[U];
+    // K rows [tile0, tile0 + tl) of the scored range, rows >= pos0 only when `late`
+    auto load_k = [&](int tile0, int tl, bool late) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int i = u * kThreads + tid, row = i >> 3;
-            kv[u] = row < tl ? __ldcg(reinterpret_cast<const uint4*>(K + size_t(tile0 + row) * a.kv_dim) + (i & 7))
-                             : make_uint4(0, 0, 0, 0);
+            if (row < tl && (tile0 + row < pos0) != late)
+                kv[u] = __ldcg(reinterpret_cast<const uint4*>(K + size_t(tile0 + row) * a.kv_dim) + (i & 7));
+            else if (!late)
+                kv[u] = make_uint4(0, 0, 0, 0);
         }
+    };
+    // ---- before the wait: the first K tile's final rows; the leader's leading V blocks (those below pos0)
+    load_k(p0, min(kTile, p1 - p0), false);
+    int issued = 0;  // V blocks requested so far (in order)
+    if (leader && producer)
+        while (issued < R - 1 && (issued + 1) * kVBlk <= pos0) issue_v(issued++);
+    pdl_wait();
+    pdl_launch_dependents();
+    if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
+
+    // ---- 1. scores of [p0, p1), one position per thread
+    for (int tile0 = p0; tile0 < p1; tile0 += kTile) {
+        const int tl = min(kTile, p1 - tile0);
+        if (tile0 != p0) load_k(tile0, tl, false);  // the first tile's final rows came before the wait
+        load_k(tile0, tl, true);
         __syncthreads();  // the previous tile's readers are done (and the query is visible)
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -152,67 +180,89 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
         const float m = s_m;
         for (int j = tid; j < p1 - p0; j += kThreads) lead_E[p0 + j] = exp_ref(fsub(LS[j], m), a.exptab);
     }
-    // Split cluster barrier: the leader's producer warps request the first V blocks between arrive and wait (the
-    // K tile space is free: every thread passed the barrier after its last score).
+    // the leader's producers request the rest of the leading V blocks (rows of this launch) while the cluster meets
     cluster_arrive();
     if (leader && producer)
-        for (int b = 0; b < R - 1; ++b) issue_v(b);
+        while (issued < R - 1) issue_v(issued++);
     cluster_wait();
     if (!leader) return;
 
-    // ---- 3. leader: ordered sum, normalise, output chains
+    // ---- 3. leader: ordered sum, normalise, products and output chains
     if (tid == 0) s_inv = fdiv(1.0f, ordered_sum(E, n));
     __syncthreads();
     {
         const float iv = s_inv;
         for (int j = tid; j < n; j += kThreads) E[j] = fmul(E[j], iv);
     }
-    // V blocks stream through the ring: the producer warps (2-7) only copy; the chain threads (warps 0-1, one lane per
-    // dimension) form a_j * v_jd (the reference's separately rounded multiply) and add it in position order, the next
-    // 16 rows' loads ahead of the current 16 rows' adds.  One barrier per block publishes the landed block and frees
-    // the slot the previous block used.
-    float o = 0.f;
-    for (int it = 0; it < nblk; ++it) {
-        if (producer) cp_wait<R - 2>();  // V block `it` has landed (for this thread's copies)
-        __syncthreads();
-        if (producer) {
-            issue_v(it + R - 1);  // into the slot block it-1 used, which the chain threads have finished with
-        } else {
-            const int r0 = it * kVBlk, rows = min(kVBlk, n - r0);
-            const __half* v = ring + (it % R) * kVBlk * kHd + tid;
-            const float* e = E + r0;
-            if (rows == kVBlk) {
-                float ac[16], an[16];
-                __half vc[16], vn[16];
+    __syncthreads();
+    if (producer) {
+        // block b: its copies landed (own wait + producer barrier), products into buffer b % 2 once the chains are
+        // done with block b - 2, then its ring slot takes block b + R - 1
+        const int ptid = tid - kOutThreads;
+        for (int b = 0; b < nblk; ++b) {
+            cp_wait<R - 2>();
+            bar_sync<kBarProd>(kProducers);
+            if (b >= 2) {
+                if (b & 1) bar_sync<kBarFree + 1>(kThreads);
+                else bar_sync<kBarFree>(kThreads);
+            }
+            const int r0 = b * kVBlk, rows = min(kVBlk, n - r0);
+            const __half2* v2 = reinterpret_cast<const __half2*>(ring + (b % R) * kVBlk * kHd);
+            float2* p2 = reinterpret_cast<float2*>(prod + (b & 1) * kVBlk * kHd);
+            constexpr int kPP = (kVBlk * kHd / 2 + kProducers - 1) / kProducers;  // pairs per producer thread
+            float2 vv[kPP];
+            float av[kPP];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    ac[k] = e[k];
-                    vc[k] = v[k * kHd];
+            for (int k = 0; k < kPP; ++k) {  // all loads first: the pairs are independent
+                const int i = ptid + k * kProducers;
+                if (i < rows * (kHd / 2)) {
+                    vv[k] = __half22float2(v2[i]);
+                    av[k] = E[r0 + i / (kHd / 2)];
                 }
+            }
+#pragma unroll
+            for (int k = 0; k < kPP; ++k) {
+                const int i = ptid + k * kProducers;
+                if (i < rows * (kHd / 2)) p2[i] = make_float2(fmul(av[k], vv[k].x), fmul(av[k], vv[k].y));
+            }
+            if (b & 1) bar_arrive<kBarFull + 1>(kThreads);
+            else bar_arrive<kBarFull>(kThreads);
+            issue_v(b + R - 1);  // into the slot of block b - 1, whose products every producer has written
+        }
+        cp_wait<0>();
+    } else {
+        // chain threads: dimension tid, o = ((0 + p_0) + p_1) + ... in position order, 16 rows' loads ahead
+        float o = 0.f;
+        for (int b = 0; b < nblk; ++b) {
+            if (b & 1) bar_sync<kBarFull + 1>(kThreads);
+            else bar_sync<kBarFull>(kThreads);
+            const int rows = min(kVBlk, n - b * kVBlk);
+            const float* pb = prod + (b & 1) * kVBlk * kHd + tid;
+            if (rows == kVBlk) {
+                float pc[16], pn[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) pc[k] = pb[k * kHd];
 #pragma unroll
                 for (int g16 = 0; g16 < kVBlk / 16; ++g16) {
                     if (g16 + 1 < kVBlk / 16) {
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) {
-                            an[k] = e[(g16 + 1) * 16 + k];
-                            vn[k] = v[((g16 + 1) * 16 + k) * kHd];
-                        }
+                        for (int k = 0; k < 16; ++k) pn[k] = pb[((g16 + 1) * 16 + k) * kHd];
                     }
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) o = fadd(o, fmul(ac[k], __half2float(vc[k])));
+                    for (int k = 0; k < 16; ++k) o = fadd(o, pc[k]);
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        ac[k] = an[k];
-                        vc[k] = vn[k];
-                    }
+                    for (int k = 0; k < 16; ++k) pc[k] = pn[k];
                 }
             } else {
-                for (int j = 0; j < rows; ++j) o = fadd(o, fmul(e[j], __half2float(v[j * kHd])));
+                for (int j = 0; j < rows; ++j) o = fadd(o, pb[j * kHd]);
+            }
+            if (b + 2 < nblk) {  // the producers of block b + 2 wait for it
+                if (b & 1) bar_arrive<kBarFree + 1>(kThreads);
+                else bar_arrive<kBarFree>(kThreads);
             }
         }
+        out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
     }
-    if (producer) cp_wait<0>();
-    else out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
 }
 
 constexpr int kRingDecode = 8;  // V blocks in flight behind a decode token's softmax
