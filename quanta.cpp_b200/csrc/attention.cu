@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     if (!leader) return;
 
     // ---- 3. leader: ordered sum, normalise, products and output chains
-    if (tid == 0) s_inv = fdiv(1.0f, ordered_sum(E, n));
+    if (tid == 0) s_inv = __frcp_rn(ordered_sum(E, n));  // = 1.0f / sum (IEEE round to nearest)
     __syncthreads();
     {
         const float iv = s_inv;
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
         const float m = warp_max(lmax);
         for (int j = lane; j < n; j += 32) Eh[j] = exp_ref(fsub(Eh[j], m), a.exptab);
         __syncwarp();
-        if (lane == 0) inv = fdiv(1.0f, ordered_sum(Eh, n));
+        if (lane == 0) inv = __frcp_rn(ordered_sum(Eh, n));  // = 1.0f / sum (IEEE round to nearest)
         inv = __shfl_sync(0xffffffffu, inv, 0);
         for (int j = lane; j < n; j += 32) Eh[j] = fmul(Eh[j], inv);
         __syncwarp();

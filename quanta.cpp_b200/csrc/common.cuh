@@ -76,12 +76,30 @@ __device__ __forceinline__ void set_error(unsigned* status, unsigned bit) {
 
 // Quantize 32 consecutive floats held one per lane of a warp (engine/src/ops_ref.cpp:69-83):
 // d = amax/127, inv = d > 0 ? 1/d : 0, q = lround(x * inv).  Returns q for this lane; *d_out gets d.
+// a / 127 correctly rounded, for a >= 0 (the quantizer's scale): one correction step of the product with RN(1/127)
+// (Markstein), infinity passed through.  Checked equal to a / 127.0f for every non-negative float bit pattern.  The
+// reciprocal of the scale is __frcp_rn (IEEE round to nearest, equal to 1.0f / d for every d >= 0, checked the same way).
+__device__ __forceinline__ float div127(float a) {
+    const float r127 = 7.8740157186985015869140625e-3f;  // RN(1 / 127)
+    const float q0 = __fmul_rn(a, r127);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, 127.0f, a), r127, q0);
+    return isinf(a) ? a : q1;
+}
+
+// lroundf (half away from zero) for |y| < 2^22 with two round-toward-zero adds: floor(|y| + 0.5) + 2^23 lands in the
+// low mantissa bits.  Checked equal to lroundf for every float of that range.
+__device__ __forceinline__ int round_away(float y) {
+    const float s = __fadd_rz(__fadd_rz(fabsf(y), 0.5f), 8388608.0f);
+    const int q = __float_as_int(s) - 0x4B000000;
+    return y < 0.f ? -q : q;
+}
+
 __device__ __forceinline__ int8_t quantize_lane(float x, float* d_out) {
     const float amax = warp_max(fabsf(x));
-    const float d = fdiv(amax, 127.0f);
-    const float inv = d > 0.f ? fdiv(1.0f, d) : 0.0f;
+    const float d = div127(amax);
+    const float inv = d > 0.f ? __frcp_rn(d) : 0.0f;
     *d_out = d;
-    return (int8_t)lroundf(fmul(x, inv));
+    return (int8_t)round_away(fmul(x, inv));  // |x * inv| <= 127 (plus rounding)
 }
 
 // Launches `kernel`, optionally as a programmatic dependent of the previous launch on the stream (the kernel then

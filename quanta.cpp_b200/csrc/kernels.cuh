@@ -204,9 +204,9 @@ __device__ __forceinline__ void quant_rounds_n(const float* v, int n, int8_t* sx
     int q[NR];
 #pragma unroll
     for (int k = 0; k < NR; ++k) {
-        const float d = fdiv(amax[k], 127.0f);
-        const float inv = d > 0.f ? fdiv(1.0f, d) : 0.0f;
-        q[k] = int((int8_t)lroundf(fmul(v[k], inv)));
+        const float d = div127(amax[k]);
+        const float inv = d > 0.f ? __frcp_rn(d) : 0.0f;
+        q[k] = int((int8_t)round_away(fmul(v[k], inv)));
         if (k * T + warp * 32 < n) {
             sx[k * T + tid] = int8_t(q[k]);
             if (lane == 0) sdx[(k * T + tid) / QK] = d;
@@ -281,7 +281,7 @@ __device__ __forceinline__ void norm_quant(const float* __restrict__ x, const No
     if (tid == 0) sred[0] = ordered_sum(sq, dim);
     __syncthreads();
     const float tot = sred[0];
-    const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(tot, float(dim)), eps)));
+    const float scale = __frcp_rn(__fsqrt_rn(fadd(fdiv(tot, float(dim)), eps)));  // 1.0f / sqrt(...), IEEE round to nearest
     float y[kMaxRounds];
 #pragma unroll
     for (int k = 0; k < kMaxRounds; ++k) y[k] = fmul(fmul(xv[k], scale), nw.w[k]);  // 0 past dim
