@@ -98,6 +98,49 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tc_matmul_measure(tokens, iters=20):
+    """The tensor-core int8 matmul alone on the gate|up shape (9728 x 896, GPTQ-style Q4 weights, their int8 copy L2
+    resident) at `tokens` tokens, through qnt_matmul(impl=2) with device buffers: CUDA-event time per call and the
+    int8 rate against twice the measured dense bf16 rate (int8 dense peak = 2 x bf16 on this GPU)."""
+    import torch
+    import quanta_b200 as qb
+    rows, cols = 9728, 896
+    rng = np.random.default_rng(SEED + 11)
+    qi = (rng.integers(-8, 8, (rows, cols)) + 8).astype(np.uint8).reshape(-1, 32)
+    packed = (qi[:, :16] & 0xF) | (qi[:, 16:] << 4)
+    d = (0.02 / 4.6 * rng.uniform(0.75, 1.25, (rows, cols // 32))).astype(np.float16)
+    W = qb.DeviceTensor(3, rows, cols, np.concatenate([packed.astype(np.uint8).ravel(), d.view(np.uint8).ravel()]))
+    L = qb.lib()
+    x = torch.randn(tokens, cols, device="cuda")
+    qx = torch.empty(tokens, cols, dtype=torch.int8, device="cuda")
+    dx = torch.empty(tokens, cols // 32, device="cuda")
+    out = torch.empty(tokens, rows, device="cuda")
+    st = torch.cuda.current_stream()
+    sp = C.c_void_p(st.cuda_stream)
+    qb._check(L.qnt_quantize_q8(C.c_void_p(x.data_ptr()), tokens, cols, C.c_void_p(qx.data_ptr()), C.c_void_p(dx.data_ptr()), sp))
+    call = lambda: qb._check(L.qnt_matmul(W.h, C.c_void_p(qx.data_ptr()), C.c_void_p(dx.data_ptr()), tokens, 0, rows,
+                                          C.c_void_p(out.data_ptr()), rows, 2, sp))
+    for _ in range(3):
+        call()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        call()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    tops = 2.0 * rows * cols * tokens / (us * 1e-6) / 1e12
+    try:
+        bf16 = json.loads(PEAKS.read_text())["bf16_tflops"]
+        peak, kind = 2 * bf16, "measured (2 x bf16 dense)"
+    except Exception:
+        peak, kind = 2 * 1590.0, "fallback (2 x bf16 dense)"
+    W.close()
+    return {"shape": f"{rows}x{cols} Q4 (gate|up) x {tokens} tokens", "us_per_call": round(us, 2),
+            "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s", "frac": round(tops / peak, 4),
+            "peak_kind": kind, "bound": "epilogue: three rounded f32 ops per (row, token, 32-block)"}
+
+
 def model_path():
     import quanta_b200 as qb
     return qb.synth_model(MODEL_DIR / "q4mix_sl.qnt", shape=qb.QWEN05B, mlp_q4=True, shortlist=True, seed=SEED)
@@ -244,7 +287,8 @@ def run_ours(args, rank, world, local_rank):
         batch = {"workload": f"config5 style: {B} sequences x {PROMPT}-token prompts per GPU, greedy, batched decode",
                  "value": round(world * B * bsteps / (bms / 1e3), 1), "unit": "tok/s", "steps": bsteps,
                  "ms_per_step": round(bms / bsteps, 3), "prefill_tok_s": round(B * PROMPT / bprefill_s, 1),
-                 "note": "each step: one token for every sequence, ids copied to the host"}
+                 "note": "each step: one token for every sequence, ids copied to the host",
+                 "tc_matmul": tc_matmul_measure(B)}
         m.batch_init(1, 2)  # release the batch caches
 
     base = None

@@ -262,6 +262,11 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
             }
         }
         out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
+        if (a.xq && n_tok == 1) {  // quantize_q8 of this head's 64 outputs: warp w holds block 2 h + w
+            float d;
+            a.xq[h * kHd + tid] = quantize_lane(o, &d);
+            if (lane == 0) a.dx[h * (kHd / QK) + warp] = d;
+        }
     }
 }
 
@@ -275,16 +280,17 @@ constexpr int kRingBatch = 3;   // multi-token launches: smaller footprint, more
 // and runs its own ordered sums: lane 0 the softmax sum, every lane two output dimensions (lane, lane + 32).
 constexpr int kGmax = kWarps;                   // query heads per kv head: one warp each
 constexpr int kPfTile = 128;                    // positions per K / V tile
-constexpr int kPfStride = kHd + 1;              // f32 tile row stride
-constexpr int kPfTileBytes = kPfTile * kPfStride * 4;
+constexpr int kPfStride = kHd + 1;              // f32 K tile row stride (conflict-free column walks)
+constexpr int kPfStrideV = kHd + 2;             // f32 V tile row stride (8-byte aligned dimension pairs)
+constexpr int kPfTileBytes = kPfTile * kPfStrideV * 4;
 
 __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const float* __restrict__ Q,
                                                            const int* __restrict__ pos_dev, int n_cap,
                                                            float* __restrict__ out, TokMap tm) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* sq = reinterpret_cast<float*>(smem);                    // [kGmax][kHd]
-    float* tile = sq + kGmax * kHd;                                // [kPfTile][kPfStride]
-    float* E = tile + kPfTile * kPfStride;                         // [group][ecap]
+    float* tile = sq + kGmax * kHd;                                // [kPfTile][kPfStride] K, [kPfTile][kPfStrideV] V
+    float* E = tile + kPfTile * kPfStrideV;                        // [group][ecap]
     pdl_wait();
     pdl_launch_dependents();
     const int g = blockIdx.x, t = blockIdx.y;
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
                                  : make_uint4(0, 0, 0, 0);
         }
     };
-    auto store = [&] {
+    auto store = [&](int stride) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int i = u * kThreads + tid, row = i >> 3, c8 = (i & 7) * 8;
@@ -319,8 +325,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const float2 f = __half22float2(h2[k]);
-                tile[row * kPfStride + c8 + 2 * k] = f.x;
-                tile[row * kPfStride + c8 + 2 * k + 1] = f.y;
+                tile[row * stride + c8 + 2 * k] = f.x;
+                tile[row * stride + c8 + 2 * k + 1] = f.y;
             }
         }
     };
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
     fetch(a.kcache, 0);
     for (int p = 0; p < n; p += kPfTile) {
         __syncthreads();  // the previous tile's readers are done (and the queries are visible)
-        store();
+        store(kPfStride);
         __syncthreads();
         if (p + kPfTile < n) fetch(a.kcache, p + kPfTile);  // next tile in flight during this one's dots
         if (head) {
@@ -363,42 +369,38 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
         for (int j = lane; j < n; j += 32) Eh[j] = fmul(Eh[j], inv);
         __syncwarp();
     }
-    // ---- outputs in position order, two dimensions per lane
-    float o0 = 0.f, o1 = 0.f;
+    // ---- outputs in position order, dimensions (2 lane, 2 lane + 1) per lane as one f32x2 pair: the product
+    // a_j * v_jd as fma(v, a, -0.0) (exactly fmul's rounding; a mul feeding the add would be contracted), then the add
+    unsigned long long o2 = 0ull;
+    const unsigned long long nz2 = f2_pack(a.neg_zero, a.neg_zero);
     fetch(a.vcache, 0);
     for (int p = 0; p < n; p += kPfTile) {
         __syncthreads();
-        store();
+        store(kPfStrideV);
         __syncthreads();
         if (p + kPfTile < n) fetch(a.vcache, p + kPfTile);
         if (head) {
             const int rows = min(kPfTile, n - p);
             const float* e = Eh + p;
+            const unsigned long long* v2 = reinterpret_cast<const unsigned long long*>(tile) + lane;
             int j = 0;
             for (; j + 8 <= rows; j += 8) {
-                float av[8], v0[8], v1[8];
+                float av[8];
+                unsigned long long vv[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     av[k] = e[j + k];
-                    v0[k] = tile[(j + k) * kPfStride + lane];
-                    v1[k] = tile[(j + k) * kPfStride + lane + 32];
+                    vv[k] = v2[(j + k) * (kPfStrideV / 2)];
                 }
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    o0 = fadd(o0, fmul(av[k], v0[k]));
-                    o1 = fadd(o1, fmul(av[k], v1[k]));
-                }
+                for (int k = 0; k < 8; ++k) o2 = f2_add(o2, f2_fma(vv[k], f2_pack(av[k], av[k]), nz2));
             }
-            for (; j < rows; ++j) {
-                o0 = fadd(o0, fmul(e[j], tile[j * kPfStride + lane]));
-                o1 = fadd(o1, fmul(e[j], tile[j * kPfStride + lane + 32]));
-            }
+            for (; j < rows; ++j) o2 = f2_add(o2, f2_fma(v2[j * (kPfStrideV / 2)], f2_pack(e[j], e[j]), nz2));
         }
     }
     if (head) {
-        float* o = out + (size_t(t) * a.n_heads + size_t(g) * group + warp) * kHd;
-        o[lane] = o0;
-        o[lane + 32] = o1;
+        float2* o = reinterpret_cast<float2*>(out + (size_t(t) * a.n_heads + size_t(g) * group + warp) * kHd);
+        o[lane] = f2_unpack(o2);
     }
 }
 

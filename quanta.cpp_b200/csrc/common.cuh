@@ -76,6 +76,35 @@ __device__ __forceinline__ void set_error(unsigned* status, unsigned bit) {
 
 // Quantize 32 consecutive floats held one per lane of a warp (engine/src/ops_ref.cpp:69-83):
 // d = amax/127, inv = d > 0 ? 1/d : 0, q = lround(x * inv).  Returns q for this lane; *d_out gets d.
+// Two f32 lanes in one 64-bit register: each lane rounds to nearest like fmaf / fmul / fadd, no flush to zero.
+// ptxas contracts a mul.rn.f32x2 that feeds an add.rn.f32x2 into one fma (a single rounding), so the products are
+// taken as fma(a, b, -0.0) with the -0.0 a kernel argument: round(a * b) exactly, and nothing left to contract.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_pack_bits(int lo, int hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // a / 127 correctly rounded, for a >= 0 (the quantizer's scale): one correction step of the product with RN(1/127)
 // (Markstein), infinity passed through.  Checked equal to a / 127.0f for every non-negative float bit pattern.  The
 // reciprocal of the scale is __frcp_rn (IEEE round to nearest, equal to 1.0f / d for every d >= 0, checked the same way).

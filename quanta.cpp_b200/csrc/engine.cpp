@@ -393,8 +393,11 @@ int Engine::sync_check() {
 int Engine::launch_layers_decode(const int* pos_dev) {
     for (const Layer& L : layers_) {
         QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
-        QB_TRY(launch_attn(L.aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
-        QB_TRY(launch_resid_dec(L.o, L.p_o, ATT_, nullptr, nullptr, X_, st_, pdl_));
+        AttnArgs aa = L.aa;  // the attention also hands o_proj its quantized input (XQ_ / DX_ are prefill scratch)
+        aa.xq = XQ_;
+        aa.dx = DX_;
+        QB_TRY(launch_attn(aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
+        QB_TRY(launch_resid_dec(L.o, L.p_o, nullptr, XQ_, DX_, X_, st_, pdl_));
         QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_));
         QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_));
     }

@@ -170,34 +170,6 @@ __device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
 constexpr unsigned kMagic = 0x4B400000u;
 constexpr float kMagicF = 12582912.0f;
 
-// Two f32 lanes in one 64-bit register: each lane rounds to nearest like fmaf / fmul / fadd, no flush to zero.
-// ptxas contracts a mul.rn.f32x2 that feeds an add.rn.f32x2 into one fma (a single rounding), so the products are
-// taken as fma(a, b, -0.0) with the -0.0 a kernel argument: round(a * b) exactly, and nothing left to contract.
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_pack_bits(int lo, int hi) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-    return r;
-}
-__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
 
 
 

@@ -26,6 +26,9 @@ struct AttnArgs {
     float scale;             // 1/sqrt(head_dim)
     int max_chunks;          // ceil(ctx / 64): the KV cache holds max_chunks * 64 >= ctx positions of room
     ExpTab exptab;           // host libm expf exceptions (exp_table.h)
+    float neg_zero = -0.0f;  // -0.0 as a runtime value: the addend of the exact f32x2 products (common.cuh)
+    int8_t* xq = nullptr;    // decode (one token): the output also quantized (quantize_q8) for the next matvec,
+    float* dx = nullptr;     //   xq[n_heads * head_dim] int8 and dx[n_heads * head_dim / 32] block scales
 };
 
 // Multi-token launches over tokens of different sequences: token t sits at position pos[t] and its sequence's KV cache
