@@ -6,21 +6,23 @@
 //   weight e_j = exp(s_j - m); sum = e_0 + e_1 + ... in position order; a_j = e_j * (1 / sum)
 //   output o_i = a_0 v_0i + a_1 v_1i + ... in position order
 // The two sums are sequential chains (the reference's float order), so each query head gets its own SM resources:
-// one thread-block cluster of CS CTAs per (query head, token), grid (CS * n_heads, n_tok), 256 threads per CTA.
+// one thread-block cluster of CS CTAs per (query head, token), grid (CS * n_heads, n_tok), 256 threads per CTA,
+// CS a power of two up to 8.
 //   1. CTA r of the cluster scores the contiguous positions [r P, r P + P) (P = ceil((pos + 1) / CS)), one thread per
 //      position (K tiles staged as f32 in shared memory), and posts its local maximum to the leader (rank 0) through
 //      distributed shared memory.
-//   2. cluster barrier; every CTA reads the CS maxima, exponentiates its own scores and stores the weights straight
-//      into the leader's weight row (distributed shared memory).
-//   3. cluster barrier; the other CTAs exit.  The leader sums the row in position order on one thread and normalises
-//      it.  Six producer warps stream V rows through a cp.async ring and turn each 64-row block into the products
-//      a_j * v_jd (f32, the reference's separately rounded multiply) in one of two buffers; two chain warps, one lane
-//      per dimension, add them in position order, o_d += p_jd, one load and one add per row.
-// K and V rows below the launch's first position were written by earlier launches, so they are requested before the
-// programmatic-launch wait (the first K tile into registers, the leading V blocks into the ring) and land while the
-// previous kernel finishes; only rows of this launch's own tokens and the query wait.
-// Decode launches CS = min(8, chunks); multi-token (prefill) launches use CS = 1, one CTA per (head, token), which
-// keeps the SMs busy with many tokens at once.  The cluster barriers are hardware barriers (no spin loops).
+//   2. cluster barrier; every CTA reads the CS maxima, exponentiates its own scores and stores the weights into the
+//      weight row of every CTA of the cluster (distributed shared memory).
+//   3. cluster barrier; every CTA sums the whole row in position order on one thread (the same sum, the same bits) and
+//      owns 64 / CS output dimensions: its producer warps form the products a_j * v_jd (f32, the reference's separately
+//      rounded multiply) of its dimensions for 512-row blocks into one of two buffers, and one lane per dimension adds
+//      them in position order.  Splitting the dimensions spreads the f16 -> f32 conversions and the product traffic
+//      over the cluster; each chain is still one load and one add per row.
+//   4. with a quantized output requested, the CTAs post their outputs into the leader, which quantizes them.
+// K rows and each CTA's V columns below the launch's first position were written by earlier launches, so they are
+// requested before the programmatic-launch wait (the first K tile into registers, the V columns by cp.async into
+// shared memory) and land while the previous kernel finishes; only this launch's own rows and the query wait.
+// The cluster barriers and named barriers are hardware barriers (no spin loops).
 #include <cooperative_groups.h>
 
 #include "kernels.cuh"
@@ -35,24 +37,23 @@ namespace {
 constexpr int kPosChunk = 64;       // KV positions per chunk (the unit of max_chunks)
 constexpr int kHd = 64;             // supported head_dim
 constexpr int kTile = 128;          // positions scored per K tile (one thread each)
-constexpr int kVBlk = 64;           // V rows per ring slot
-constexpr int kOutThreads = 64;     // chain threads of the leader (one per dimension, warps 0-1)
+constexpr int kOutThreads = 64;     // warps 0-1: the chain lanes (one per owned dimension) and the quantizer
 constexpr int kMaxCluster = 8;      // portable cluster size limit
 constexpr int kKfStride = kHd + 1;  // f32 K tile row stride (conflict-free column walks)
-constexpr int kSlotBytes = kVBlk * kHd * 2;  // one f16 V block
+constexpr int kPB = 512;            // rows per product block (fewer blocks: each hand-over costs a barrier round trip)
 
-// Dynamic shared memory layout (byte offsets), the same for every CTA of a launch.
+// Dynamic shared memory layout (byte offsets), the same for every CTA of a launch; dpc = 64 / CS dimensions per CTA.
 constexpr int kOffQ = 0;                        // f32 [kHd] query
 constexpr int kOffMax = kOffQ + kHd * 4;        // f32 [kMaxCluster] local maxima (the leader's copy is used)
-constexpr int kOffK = kOffMax + 256;            // f32 [kTile][kKfStride] K tile
+constexpr int kOffOut = kOffMax + 256;          // f32 [kHd] the head's outputs, gathered in the leader
+constexpr int kOffK = kOffOut + kHd * 4;        // f32 [kTile][kKfStride] K tile
 constexpr int kKfBytes = kTile * kKfStride * 4;
-constexpr int kOffRing = kOffK + kKfBytes;      // f16 [R][kVBlk][kHd] V ring
-constexpr int kProdBytes = kVBlk * kHd * 4;     // f32 [kVBlk][kHd] products of one V block
+constexpr int kOffProd = kOffK + kKfBytes;      // f32 [2][dpc][pb_rows + 4] products, dimension-major
 static_assert(kOffK % 16 == 0 && kKfBytes % 16 == 0, "16-byte aligned regions");
 static_assert(kThreads == 256 && kTile * 8 % kThreads == 0, "K tile loader");
 constexpr int kProducers = kThreads - kOutThreads;
-// named barriers (0 is __syncthreads): the producers among themselves; product buffer b full / free
-constexpr int kBarProd = 1, kBarFull = 2, kBarFree = 4;
+// named barriers (0 is __syncthreads): product buffer b full / free
+constexpr int kBarFull = 2, kBarFree = 4;
 
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
@@ -62,28 +63,33 @@ template <int ID>
 __device__ __forceinline__ void bar_arrive(int count) { asm volatile("bar.arrive %0, %1;" ::"n"(ID), "r"(count) : "memory"); }
 
 __host__ __device__ inline int ls_len(int ctx, int cs) { return ((ctx + cs - 1) / cs + 3) & ~3; }
-__host__ __device__ constexpr int off_prod(int ring) { return kOffRing + ring * kSlotBytes; }
-// then f32 [2][kVBlk][kHd] products, f32 [ls_len] own scores, f32 [ctx] weights
-__host__ __device__ constexpr int off_ls(int ring) { return off_prod(ring) + 2 * kProdBytes; }
-inline size_t attn_smem_bytes(int ctx, int cs, int ring) {
-    return size_t(off_ls(ring)) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4;
-}
+// then f16 [ctx][dpc] V columns, f32 [ls_len] own scores, f32 [ctx] weights
+__host__ __device__ inline int pb_rows(int ctx) { return ctx < kPB ? ctx : kPB; }
+// a dimension's products are contiguous (float4 loads by its chain lane); the +4 keeps the lanes' rows in distinct banks
+__host__ __device__ inline int pb_stride(int ctx) { return pb_rows(ctx) + 4; }
+__host__ __device__ inline int off_vs(int ctx, int cs) { return kOffProd + 2 * pb_stride(ctx) * (kHd / cs) * 4; }
+__host__ __device__ inline int off_ls(int ctx, int cs) { return off_vs(ctx, cs) + ctx * (kHd / cs) * 2; }
+inline size_t attn_smem_bytes(int ctx, int cs) { return size_t(off_ls(ctx, cs)) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4; }
 
-template <int R>
+template <int CS>
 __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
                                                    int n_tok, float* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
     cg::cluster_group cluster = cg::this_cluster();
-    const int CS = int(cluster.num_blocks()), r = int(cluster.block_rank());
+    const int r = int(cluster.block_rank());  // CS = cluster.num_blocks(), fixed by the launch
     const int h = blockIdx.x / CS, t = blockIdx.y;
     const int group = a.n_heads / a.n_kv, g = h / group;
     const int ctx = a.max_chunks * kPosChunk;
+    constexpr int dpc = kHd / CS;  // this CTA's output dimensions [d0, d0 + dpc)
+    const int d0 = r * dpc;
     float* sq = reinterpret_cast<float*>(smem + kOffQ);
     float* smx = reinterpret_cast<float*>(smem + kOffMax);
+    float* so = reinterpret_cast<float*>(smem + kOffOut);
     float* kf = reinterpret_cast<float*>(smem + kOffK);
-    __half* ring = reinterpret_cast<__half*>(smem + kOffRing);
-    float* prod = reinterpret_cast<float*>(smem + off_prod(R));
-    float* LS = reinterpret_cast<float*>(smem + off_ls(R));
+    float* prod = reinterpret_cast<float*>(smem + kOffProd);
+    __half* vs = reinterpret_cast<__half*>(smem + off_vs(ctx, CS));
+    const int pbr = pb_rows(ctx), pbs = pb_stride(ctx);  // rows per product block, a dimension's stride
+    float* LS = reinterpret_cast<float*>(smem + off_ls(ctx, CS));
     float* E = LS + ls_len(ctx, CS);
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
@@ -93,16 +99,16 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     const int pos0 = __ldcg(pos_dev);
     const int n = pos0 + t + 1;
     const int P = (n + CS - 1) / CS, p0 = min(n, r * P), p1 = min(n, p0 + P);
-    const bool leader = r == 0, producer = tid >= kOutThreads;
-    const int nblk = (n + kVBlk - 1) / kVBlk;
-    const __half* V = a.vcache + g * kHd;
+    const bool producer = tid >= kOutThreads;
+    const int nblk = (n + pb_rows(ctx) - 1) / pb_rows(ctx);
+    const __half* V = a.vcache + g * kHd + d0;
     const __half* K = a.kcache + g * kHd;
-    auto issue_v = [&](int b) {  // V rows [64 b, min(64 b + 64, n)) into slot b % R (producer threads); empty past the end
-        if (b < nblk) {
-            const int r0 = b * kVBlk, rows = min(kVBlk, n - r0);
-            __half* dst = ring + (b % R) * kVBlk * kHd;
-            for (int i = tid - kOutThreads; i < rows * 8; i += kProducers)
-                cp_async16(dst + (i >> 3) * kHd + (i & 7) * 8, V + size_t(r0 + (i >> 3)) * a.kv_dim + (i & 7) * 8);
+    // this CTA's V columns of rows [j0, j1) into vs (16-byte granules, dpc / 8 per row), one cp.async group
+    auto load_v = [&](int j0, int j1) {
+        constexpr int gpr = dpc / 8;
+        for (int i = tid; i < (j1 - j0) * gpr; i += kThreads) {
+            const int row = j0 + i / gpr, c = i % gpr;
+            cp_async16(vs + size_t(row) * dpc + c * 8, V + size_t(row) * a.kv_dim + c * 8);
         }
         cp_commit();
     };
@@ -119,13 +125,12 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
                 kv[u] = make_uint4(0, 0, 0, 0);
         }
     };
-    // ---- before the wait: the first K tile's final rows; the leader's leading V blocks (those below pos0)
+    // ---- before the wait: the first K tile's final rows, this CTA's V columns of the final rows
     load_k(p0, min(kTile, p1 - p0), false);
-    int issued = 0;  // V blocks requested so far (in order)
-    if (leader && producer)
-        while (issued < R - 1 && (issued + 1) * kVBlk <= pos0) issue_v(issued++);
+    load_v(0, min(pos0, n));
     pdl_wait();
     pdl_launch_dependents();
+    load_v(min(pos0, n), n);  // this launch's own rows
     if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
 
     // ---- 1. scores of [p0, p1), one position per thread
@@ -168,110 +173,75 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     }
     cluster.sync();
 
-    // ---- 2. weights of [p0, p1) into the leader's row
+    // ---- 2. weights of [p0, p1) into every CTA's row
     if (warp == 0) {
         float m = lane < CS ? lead_max[lane] : -INFINITY;
         m = warp_max(m);
         if (lane == 0) s_m = m;
     }
     __syncthreads();
-    {
-        float* lead_E = cluster.map_shared_rank(E, 0);
-        const float m = s_m;
-        for (int j = tid; j < p1 - p0; j += kThreads) lead_E[p0 + j] = exp_ref(fsub(LS[j], m), a.exptab);
+    for (int j = tid; j < p1 - p0; j += kThreads) {
+        const float e = exp_ref(fsub(LS[j], s_m), a.exptab);
+        for (int q = 0; q < CS; ++q) cluster.map_shared_rank(E, q)[p0 + j] = e;
     }
-    // the leader's producers request the rest of the leading V blocks (rows of this launch) while the cluster meets
+    cp_wait<0>();  // this thread's V copies (the barriers below publish them)
     cluster_arrive();
-    if (leader && producer)
-        while (issued < R - 1) issue_v(issued++);
     cluster_wait();
-    if (!leader) return;
 
-    // ---- 3. leader: ordered sum, normalise, products and output chains
+    // ---- 3. every CTA: the ordered sum, then the products and chains of its dimensions
     if (tid == 0) s_inv = __frcp_rn(ordered_sum(E, n));  // = 1.0f / sum (IEEE round to nearest)
     __syncthreads();
-    {
-        const float iv = s_inv;
-        for (int j = tid; j < n; j += kThreads) E[j] = fmul(E[j], iv);
-    }
-    __syncthreads();
+    const float inv = s_inv;
+    float o = 0.f;
     if (producer) {
-        // block b: its copies landed (own wait + producer barrier), products into buffer b % 2 once the chains are
-        // done with block b - 2, then its ring slot takes block b + R - 1
+        // block b: products of rows [128 b, ..) and dims [d0, d0 + dpc) into buffer b % 2, once the chains are done
+        // with block b - 2
         const int ptid = tid - kOutThreads;
+        constexpr int hp = dpc / 2;
         for (int b = 0; b < nblk; ++b) {
-            cp_wait<R - 2>();
-            bar_sync<kBarProd>(kProducers);
             if (b >= 2) {
                 if (b & 1) bar_sync<kBarFree + 1>(kThreads);
                 else bar_sync<kBarFree>(kThreads);
             }
-            const int r0 = b * kVBlk, rows = min(kVBlk, n - r0);
-            const __half2* v2 = reinterpret_cast<const __half2*>(ring + (b % R) * kVBlk * kHd);
-            float2* p2 = reinterpret_cast<float2*>(prod + (b & 1) * kVBlk * kHd);
-            constexpr int kPP = (kVBlk * kHd / 2 + kProducers - 1) / kProducers;  // pairs per producer thread
-            float2 vv[kPP];
-            float av[kPP];
-#pragma unroll
-            for (int k = 0; k < kPP; ++k) {  // all loads first: the pairs are independent
-                const int i = ptid + k * kProducers;
-                if (i < rows * (kHd / 2)) {
-                    vv[k] = __half22float2(v2[i]);
-                    av[k] = E[r0 + i / (kHd / 2)];
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kPP; ++k) {
-                const int i = ptid + k * kProducers;
-                if (i < rows * (kHd / 2)) p2[i] = make_float2(fmul(av[k], vv[k].x), fmul(av[k], vv[k].y));
+            const int r0 = b * pbr, rows = min(pbr, n - r0);
+            const __half2* v2 = reinterpret_cast<const __half2*>(vs + size_t(r0) * dpc);
+            float* pbuf = prod + (b & 1) * dpc * pbs;
+            for (int i = ptid; i < rows * hp; i += kProducers) {
+                const int j = i / hp, q = i - j * hp;
+                const float aj = fmul(E[r0 + j], inv);
+                const float2 v = __half22float2(v2[i]);
+                pbuf[(2 * q) * pbs + j] = fmul(aj, v.x);
+                pbuf[(2 * q + 1) * pbs + j] = fmul(aj, v.y);
             }
             if (b & 1) bar_arrive<kBarFull + 1>(kThreads);
             else bar_arrive<kBarFull>(kThreads);
-            issue_v(b + R - 1);  // into the slot of block b - 1, whose products every producer has written
         }
-        cp_wait<0>();
     } else {
-        // chain threads: dimension tid, o = ((0 + p_0) + p_1) + ... in position order, 16 rows' loads ahead
-        float o = 0.f;
+        // chain lanes tid < dpc: dimension d0 + tid, o = ((0 + p_0) + p_1) + ... in position order, 16 rows ahead
         for (int b = 0; b < nblk; ++b) {
             if (b & 1) bar_sync<kBarFull + 1>(kThreads);
             else bar_sync<kBarFull>(kThreads);
-            const int rows = min(kVBlk, n - b * kVBlk);
-            const float* pb = prod + (b & 1) * kVBlk * kHd + tid;
-            if (rows == kVBlk) {
-                float pc[16], pn[16];
-#pragma unroll
-                for (int k = 0; k < 16; ++k) pc[k] = pb[k * kHd];
-#pragma unroll
-                for (int g16 = 0; g16 < kVBlk / 16; ++g16) {
-                    if (g16 + 1 < kVBlk / 16) {
-#pragma unroll
-                        for (int k = 0; k < 16; ++k) pn[k] = pb[((g16 + 1) * 16 + k) * kHd];
-                    }
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) o = fadd(o, pc[k]);
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) pc[k] = pn[k];
-                }
-            } else {
-                for (int j = 0; j < rows; ++j) o = fadd(o, pb[j * kHd]);
-            }
+            const int rows = min(pbr, n - b * pbr);
+            if (tid < dpc) o = ordered_sum(prod + ((b & 1) * dpc + tid) * pbs, rows, o);  // float4 loads ahead of the adds
             if (b + 2 < nblk) {  // the producers of block b + 2 wait for it
                 if (b & 1) bar_arrive<kBarFree + 1>(kThreads);
                 else bar_arrive<kBarFree>(kThreads);
             }
         }
-        out[(size_t(t) * a.n_heads + h) * kHd + tid] = o;
-        if (a.xq && n_tok == 1) {  // quantize_q8 of this head's 64 outputs: warp w holds block 2 h + w
+        if (tid < dpc) out[(size_t(t) * a.n_heads + h) * kHd + d0 + tid] = o;
+    }
+    if (a.xq && n_tok == 1) {  // quantize_q8 of the head's 64 outputs in the leader: warp w holds block 2 h + w
+        if (tid < dpc) cluster.map_shared_rank(so, 0)[d0 + tid] = o;
+        cluster_arrive();
+        cluster_wait();
+        if (r == 0 && tid < kHd) {
             float d;
-            a.xq[h * kHd + tid] = quantize_lane(o, &d);
+            a.xq[h * kHd + tid] = quantize_lane(so[tid], &d);
             if (lane == 0) a.dx[h * (kHd / QK) + warp] = d;
         }
     }
 }
 
-constexpr int kRingDecode = 8;  // V blocks in flight behind a decode token's softmax
-constexpr int kRingBatch = 3;   // multi-token launches: smaller footprint, more CTAs per SM
 
 // ---------------------------------------------------------------- multi-token (prefill) attention
 
@@ -427,12 +397,11 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
     if (a.head_dim != kHd || group < 1 || group * a.n_kv != a.n_heads || a.max_chunks < 1) return cudaErrorInvalidValue;
     const int ctx = a.max_chunks * kPosChunk;
-    // Decode: a cluster per head and a deep V ring; multi-token launches: one CTA per (head, token), a short ring.
-    const bool decode = n_tok == 1;
-    const int cs = decode ? std::min(kMaxCluster, a.max_chunks) : 1;
-    const int ring = decode ? kRingDecode : kRingBatch;
-    auto kern = decode ? k_attn<kRingDecode> : k_attn<kRingBatch>;
-    const size_t smem = attn_smem_bytes(ctx, cs, ring);
+    // a cluster of cs CTAs per (head, token): the largest power of two up to 8 and the chunk count
+    int cs = 1;
+    while (cs * 2 <= std::min(kMaxCluster, a.max_chunks)) cs *= 2;
+    auto kern = cs == 8 ? k_attn<8> : cs == 4 ? k_attn<4> : cs == 2 ? k_attn<2> : k_attn<1>;
+    const size_t smem = attn_smem_bytes(ctx, cs);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
