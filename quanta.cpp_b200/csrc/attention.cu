@@ -44,7 +44,7 @@ constexpr int kPB = 512;            // rows per product block (fewer blocks: eac
 
 // Dynamic shared memory layout (byte offsets), the same for every CTA of a launch; dpc = 64 / CS dimensions per CTA.
 constexpr int kOffQ = 0;                        // f32 [kHd] query
-constexpr int kOffMax = kOffQ + kHd * 4;        // f32 [kMaxCluster] local maxima (the leader's copy is used)
+constexpr int kOffMax = kOffQ + kHd * 4;        // f32 [kMaxCluster] the cluster CTAs' local maxima (each CTA a copy)
 constexpr int kOffOut = kOffMax + 256;          // f32 [kHd] the head's outputs, gathered in the leader
 constexpr int kOffK = kOffOut + kHd * 4;        // f32 [kTile][kKfStride] K tile
 constexpr int kKfBytes = kTile * kKfStride * 4;
@@ -125,8 +125,25 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
                 kv[u] = make_uint4(0, 0, 0, 0);
         }
     };
-    // ---- before the wait: the first K tile's final rows, this CTA's V columns of the final rows
+    // K tile rows -> f32 in shared memory: the rows below pos0 (early), from pos0 on (late), or all of them
+    auto store_k = [&](int tile0, int which) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = u * kThreads + tid, row = i >> 3, c8 = (i & 7) * 8;
+            if (which == 1 && tile0 + row >= pos0) continue;
+            if (which == 2 && tile0 + row < pos0) continue;
+            const __half2* h2 = reinterpret_cast<const __half2*>(&kv[u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(h2[k]);
+                kf[row * kKfStride + c8 + 2 * k] = f.x;
+                kf[row * kKfStride + c8 + 2 * k + 1] = f.y;
+            }
+        }
+    };
+    // ---- before the wait: the first K tile's final rows (loaded and converted), this CTA's V columns of them
     load_k(p0, min(kTile, p1 - p0), false);
+    store_k(p0, 1);
     load_v(0, min(pos0, n));
     pdl_wait();
     pdl_launch_dependents();
@@ -136,21 +153,16 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     // ---- 1. scores of [p0, p1), one position per thread
     for (int tile0 = p0; tile0 < p1; tile0 += kTile) {
         const int tl = min(kTile, p1 - tile0);
-        if (tile0 != p0) load_k(tile0, tl, false);  // the first tile's final rows came before the wait
-        load_k(tile0, tl, true);
-        __syncthreads();  // the previous tile's readers are done (and the query is visible)
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = u * kThreads + tid, row = i >> 3, c8 = (i & 7) * 8;
-            const __half2* h2 = reinterpret_cast<const __half2*>(&kv[u]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 f = __half22float2(h2[k]);
-                kf[row * kKfStride + c8 + 2 * k] = f.x;
-                kf[row * kKfStride + c8 + 2 * k + 1] = f.y;
-            }
+        if (tile0 == p0) {  // the first tile's final rows came (and were converted) before the wait
+            load_k(tile0, tl, true);
+            store_k(tile0, 2);
+        } else {
+            load_k(tile0, tl, false);
+            load_k(tile0, tl, true);
+            __syncthreads();  // the previous tile's readers are done
+            store_k(tile0, 0);
         }
-        __syncthreads();
+        __syncthreads();  // the tile (and the query) are visible
         if (tid < tl) {
             const float* kj = kf + tid * kKfStride;
             float s = 0.f;
@@ -165,17 +177,16 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     lm = warp_max(lm);
     if (lane == 0) sred[warp] = lm;
     __syncthreads();
-    float* lead_max = cluster.map_shared_rank(smx, 0);
-    if (tid == 0) {
+    if (tid < CS) {  // this CTA's maximum into slot r of every CTA's table
         float m = sred[0];
         for (int k = 1; k < kWarps; ++k) m = fmaxf(m, sred[k]);
-        lead_max[r] = m;
+        cluster.map_shared_rank(smx, tid)[r] = m;
     }
     cluster.sync();
 
     // ---- 2. weights of [p0, p1) into every CTA's row
     if (warp == 0) {
-        float m = lane < CS ? lead_max[lane] : -INFINITY;
+        float m = lane < CS ? smx[lane] : -INFINITY;
         m = warp_max(m);
         if (lane == 0) s_m = m;
     }
