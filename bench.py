@@ -278,10 +278,12 @@ def run_ours(args, rank, world, local_rank):
             last = m.decode_batch(seqs, last)
         torch.cuda.synchronize()
         eb = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.nvtx.range_push("batch")  # lets a profiler select the timed batched steps
         eb[0].record(stream)
         for _ in range(bsteps):
             last = m.decode_batch(seqs, last)
         eb[1].record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         bms = dp.max_over_ranks(eb[0].elapsed_time(eb[1]), dist, device="cuda")
         batch = {"workload": f"config5 style: {B} sequences x {PROMPT}-token prompts per GPU, greedy, batched decode",
