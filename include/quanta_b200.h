@@ -40,7 +40,9 @@ int qnt_set_device(int device); /* cudaSetDevice for the calling thread */
 typedef struct qnt_dtensor qnt_dtensor;
 
 /* Uploads a quantized weight matrix given in the .qnt layout (quants, then fp16 scales: engine/src/model_file.h:25-38,
- * scripts/export.py:10-13) to device memory.  Replaces passing `const Tensor& W` (engine/src/ops.h:57,68). */
+ * scripts/export.py:10-13) to device memory.  Replaces passing `const Tensor& W` (engine/src/ops.h:57,68).
+ * When cols % 128 == 0 it also keeps what the tensor-core matmul reads: a K-step-major copy of the scales and, for
+ * Q4_0, an int8 copy of q - 8 (rows * cols bytes). */
 int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_dtensor** out);
 int qnt_tensor_free(qnt_dtensor* t);
 int qnt_tensor_shape(const qnt_dtensor* t, int* dtype, int* rows, int* cols);
@@ -54,7 +56,8 @@ int qnt_quantize_q8(const float* x, int n_tok, int n, int8_t* q, float* d, void*
 int qnt_matvec(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, int r1, float* out, void* stream);
 
 /* MatmulQFn (engine/src/ops.h:68): n activations (q [n][cols], d [n][cols/32]), out[t * ldo + r]; device pointers.
- * Per (row, token) bit-identical to qnt_matvec.  impl: 0 auto, 1 CUDA cores, 2 tensor cores (tcgen05). */
+ * Per (row, token) bit-identical to qnt_matvec.  impl: 0 auto, 1 CUDA cores, 2 tensor cores (tcgen05; q and d
+ * 16-byte aligned; the call makes a stream-ordered block-major copy of d with cudaMallocAsync). */
 int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo,
                int impl, void* stream);
 
