@@ -19,6 +19,9 @@
 //      them in position order.  Splitting the dimensions spreads the f16 -> f32 conversions and the product traffic
 //      over the cluster; each chain is still one load and one add per row.
 //   4. with a quantized output requested, the CTAs post their outputs into the leader, which quantizes them.
+// Decode can also take the layer's q|k|v rows into the same launch (k_attn<8, UW>, launch_qkv_attn): each CTA first
+// computes 24 of its head's q / k / v rows (rmsnorm + quantize prologue, integer matvec, bias, RoPE) and the cluster
+// exchanges them through distributed shared memory, so the q|k|v kernel and its launch gap disappear.
 // K rows and each CTA's V columns below the launch's first position were written by earlier launches, so they are
 // requested before the programmatic-launch wait (the first K tile into registers, the V columns by cp.async into
 // shared memory) and land while the previous kernel finishes; only this launch's own rows and the query wait.
@@ -70,10 +73,25 @@ __host__ __device__ inline int pb_stride(int ctx) { return pb_rows(ctx) + 4; }
 __host__ __device__ inline int off_vs(int ctx, int cs) { return kOffProd + 2 * pb_stride(ctx) * (kHd / cs) * 4; }
 __host__ __device__ inline int off_ls(int ctx, int cs) { return off_vs(ctx, cs) + ctx * (kHd / cs) * 2; }
 inline size_t attn_smem_bytes(int ctx, int cs) { return size_t(off_ls(ctx, cs)) + size_t(ls_len(ctx, cs)) * 4 + size_t(ctx) * 4; }
+// decode with the q|k|v rows fused in: after the weight row, sx [dim] int8, sdx [dim/32], the norm's scratch
+// [32 + dim], terms [24][dim/32 | 1], the current token's k and v [64] each (f32 of the f16 values)
+constexpr int kQkvRows = 24;  // 8 rows of each of the head's q, k and v units per CTA (cluster of 8)
+inline size_t qkv_smem_bytes(int dim) {
+    const int nb = dim / QK;
+    return size_t(dim) + size_t(nb) * 4 + size_t(32 + dim) * 4 + size_t(kQkvRows) * (nb | 1) * 4 + 2 * kHd * 4;
+}
 
-template <int CS>
-__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __restrict__ Q, const int* __restrict__ pos_dev,
-                                                   int n_tok, float* __restrict__ out) {
+// UW > 0: decode only (one token, CS = 8), with the layer's q|k|v matvec fused in front (UW weight chunks per
+// thread): every CTA of the head's cluster computes 8 rows of each of the head's q, k and v units (the k and v units
+// of the kv head are recomputed by each of its query heads' clusters, the same bits), applies bias and RoPE, and
+// posts q and the f16-rounded k, v of the token into every CTA of the cluster; the first query head of each kv
+// head also stores k, v into the cache.  This removes the q|k|v kernel, its launch gap and the attention's reads of
+// q and of the token's own K/V row.  Bit-identical to k_qkv_dec followed by the unfused attention.
+template <int CS, int UW>
+__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, const float* __restrict__ X,
+                                                   const float* __restrict__ norm_w, float eps, float* __restrict__ Qout,
+                                                   const float* __restrict__ Q, const int* __restrict__ pos_dev, int n_tok,
+                                                   float* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int r = int(cluster.block_rank());  // CS = cluster.num_blocks(), fixed by the launch
@@ -94,6 +112,8 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // every CTA of the cluster has started before any remote shared-memory access (the wait comes before the first)
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
     // The launch's first position was written by an earlier launch (the host or the step's first kernel); K / V rows
     // below it are final, rows from it on are this launch's (the previous kernel's) and wait for it.
     const int pos0 = __ldcg(pos_dev);
@@ -141,26 +161,126 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, const float* __re
             }
         }
     };
+    // fused q|k|v (UW > 0): virtual row vr of this CTA = unit vr / 8 (the head's q, its kv head's k, v), row 8 r + vr % 8
+    const int qdim = qa.W.cols, qnb = qdim / QK, qcpr = qdim / 16, qts = qnb | 1, qtotal = kQkvRows * qcpr;
+    auto qrow = [&](int vr) {
+        const int u = vr >> 3;
+        return (u == 0 ? h : u == 1 ? qa.n_heads + g : qa.n_heads + qa.n_kv + g) * kHd + 8 * r + (vr & 7);
+    };
+    constexpr int UWn = UW > 0 ? UW : 1;
+    uint4 wv[UWn];
+    __half wdv[UWn];
+    NormW nw;
+    float pba = 0.f, pbb = 0.f, pc = 1.f, ps = 0.f;  // pair lanes (tid < 12): bias of the two rows, RoPE cos / sin
+    if constexpr (UW > 0) {  // the CTA's weight chunks, the norm weights and the pair constants before the wait
+        load_norm_w(norm_w, qdim, nw);
+        if (tid < kQkvRows / 2) {
+            const int vr = 2 * tid, fr = qrow(vr), i = (8 * r + (vr & 7)) >> 1;
+            pba = qa.bias[fr];
+            pbb = qa.bias[fr + 1];
+            if ((vr >> 3) < 2) {
+                pc = qa.rope_cos[size_t(pos0) * (kHd / 2) + i];
+                ps = qa.rope_sin[size_t(pos0) * (kHd / 2) + i];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UW; ++u) {
+            const int f = u * kThreads + tid;
+            if (f < qtotal) {
+                const int vr = f / qcpr, c = f - vr * qcpr, fr = qrow(vr);
+                wv[u] = ld_stream(reinterpret_cast<const uint4*>(qa.W.q + size_t(fr) * qdim) + c);
+                wdv[u] = qa.W.d[size_t(fr) * qnb + (c >> 1)];
+            } else {
+                wv[u] = make_uint4(0, 0, 0, 0);
+                wdv[u] = __float2half(0.f);
+            }
+        }
+    }
     // ---- before the wait: the first K tile's final rows (loaded and converted), this CTA's V columns of them
     load_k(p0, min(kTile, p1 - p0), false);
     store_k(p0, 1);
     load_v(0, min(pos0, n));
     pdl_wait();
     pdl_launch_dependents();
-    load_v(min(pos0, n), n);  // this launch's own rows
-    if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
+    float* kc = nullptr;  // (fused) the token's k and v, f32 of their f16 values
+    float* vc = nullptr;
+    if constexpr (UW == 0) {
+        load_v(min(pos0, n), n);  // this launch's own rows
+        if (tid < kHd) sq[tid] = __ldcg(Q + (size_t(t) * a.n_heads + h) * kHd + tid);
+        asm volatile("barrier.cluster.wait;" ::: "memory");
+    } else {
+        unsigned char* qs = smem + off_ls(ctx, CS) + (ls_len(ctx, CS) + ctx) * 4;
+        int8_t* sx = reinterpret_cast<int8_t*>(qs);
+        float* sdx = reinterpret_cast<float*>(qs + qdim);
+        float* sredq = sdx + qnb;
+        float* sterm = sredq + 32 + qdim;
+        kc = sterm + kQkvRows * qts;
+        vc = kc + kHd;
+        norm_quant(X, nw, qdim, eps, sx, sdx, nullptr, sredq);
+#pragma unroll
+        for (int u = 0; u < UW; ++u) {  // block terms (Q8_0: a block's two chunks sit in adjacent lanes)
+            if (u * kThreads >= qtotal) break;
+            const int f = u * kThreads + tid;
+            const int vr = f / qcpr, c = f - vr * qcpr;
+            int sdot = f < qtotal ? chunk_dot<DT_Q8_0>(wv[u], sx, c) : 0;
+            sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+            if (f < qtotal && !(c & 1)) sterm[vr * qts + (c >> 1)] = block_term(sdot, __half2float(wdv[u]), sdx[c >> 1]);
+        }
+        __syncthreads();
+        asm volatile("barrier.cluster.wait;" ::: "memory");
+        // warp 0: lane l < 24 sums row l; lane p < 12 then takes rows 2 p, 2 p + 1 (dimensions i, i + 32 of its unit)
+        if (warp == 0) {
+            const float rs = lane < kQkvRows ? row_sum(sterm + lane * qts, qnb) : 0.f;
+            const float ra = __shfl_sync(0xffffffffu, rs, (2 * lane) & 31);
+            const float rb = __shfl_sync(0xffffffffu, rs, (2 * lane + 1) & 31);
+            if (lane < kQkvRows / 2) {
+                const int vr = 2 * lane, u = vr >> 3, i = (8 * r + (vr & 7)) >> 1;
+                float va = fadd(ra, pba), vb = fadd(rb, pbb);
+                if (u < 2) rope_pair(va, vb, pc, ps);
+                if (u == 0) {
+                    for (int q = 0; q < CS; ++q) {
+                        float* dst = cluster.map_shared_rank(sq, q);
+                        dst[i] = va;
+                        dst[i + kHd / 2] = vb;
+                    }
+                    Qout[h * kHd + i] = va;
+                    Qout[h * kHd + i + kHd / 2] = vb;
+                } else {
+                    const __half ha = __float2half_rn(va), hb = __float2half_rn(vb);
+                    for (int q = 0; q < CS; ++q) {
+                        float* dst = cluster.map_shared_rank(u == 1 ? kc : vc, q);
+                        dst[i] = __half2float(ha);
+                        dst[i + kHd / 2] = __half2float(hb);
+                    }
+                    if (h == g * group) {  // one cluster per kv head writes the cache
+                        __half* C = (u == 1 ? qa.kcache : qa.vcache) + size_t(pos0) * qa.kv_dim + g * kHd;
+                        C[i] = ha;
+                        C[i + kHd / 2] = hb;
+                    }
+                }
+            }
+        }
+        cluster_arrive();  // q, k and v of the token are in every CTA
+        cluster_wait();
+        if (tid < dpc) vs[size_t(pos0) * dpc + tid] = __float2half_rn(vc[d0 + tid]);  // exact: vc holds f16 values
+    }
 
     // ---- 1. scores of [p0, p1), one position per thread
     for (int tile0 = p0; tile0 < p1; tile0 += kTile) {
         const int tl = min(kTile, p1 - tile0);
         if (tile0 == p0) {  // the first tile's final rows came (and were converted) before the wait
-            load_k(tile0, tl, true);
-            store_k(tile0, 2);
+            if constexpr (UW == 0) {
+                load_k(tile0, tl, true);
+                store_k(tile0, 2);
+            }
         } else {
             load_k(tile0, tl, false);
-            load_k(tile0, tl, true);
+            if constexpr (UW == 0) load_k(tile0, tl, true);
             __syncthreads();  // the previous tile's readers are done
-            store_k(tile0, 0);
+            store_k(tile0, UW == 0 ? 0 : 1);
+        }
+        if constexpr (UW > 0) {  // the token's own row (position pos0) from the posted k
+            if (pos0 >= tile0 && pos0 < tile0 + tl && tid < kHd) kf[(pos0 - tile0) * kKfStride + tid] = kc[tid];
         }
         __syncthreads();  // the tile (and the query) are visible
         if (tid < tl) {
@@ -411,7 +531,7 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     // a cluster of cs CTAs per (head, token): the largest power of two up to 8 and the chunk count
     int cs = 1;
     while (cs * 2 <= std::min(kMaxCluster, a.max_chunks)) cs *= 2;
-    auto kern = cs == 8 ? k_attn<8> : cs == 4 ? k_attn<4> : cs == 2 ? k_attn<2> : k_attn<1>;
+    auto kern = cs == 8 ? k_attn<8, 0> : cs == 4 ? k_attn<4, 0> : cs == 2 ? k_attn<2, 0> : k_attn<1, 0>;
     const size_t smem = attn_smem_bytes(ctx, cs);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -430,7 +550,43 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, a, Q, pos_dev, n_tok, out);
+    return cudaLaunchKernelEx(&cfg, kern, a, QkvArgs{}, static_cast<const float*>(nullptr), static_cast<const float*>(nullptr),
+                              0.f, static_cast<float*>(nullptr), Q, pos_dev, n_tok, out);
+}
+
+cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
+                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl) {
+    const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
+    const int dim = qa.W.cols;
+    // the fused form covers the decode shapes it was built for; anything else takes the two kernels
+    if (a.head_dim != kHd || group < 1 || group * a.n_kv != a.n_heads || a.max_chunks < kMaxCluster ||
+        qa.W.dtype != DT_Q8_0 || qa.head_dim != kHd || dim % QK != 0 || dim > kMaxRounds * kThreads ||
+        qa.W.rows != (a.n_heads + 2 * a.n_kv) * kHd)
+        return cudaErrorNotSupported;
+    const int chunks = kQkvRows * (dim / 16);
+    const int uw = (chunks + kThreads - 1) / kThreads;
+    if (uw > 12) return cudaErrorNotSupported;
+    const int ctx = a.max_chunks * kPosChunk;
+    const size_t smem = attn_smem_bytes(ctx, kMaxCluster) + qkv_smem_bytes(dim);
+    if (smem > 227 * 1024) return cudaErrorNotSupported;
+    auto kern = uw <= 6 ? k_attn<kMaxCluster, 6> : k_attn<kMaxCluster, 12>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(kMaxCluster * a.n_heads), 1u);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(kMaxCluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, qa, X, norm_w, eps, Qout, static_cast<const float*>(nullptr), pos_dev, 1, out);
 }
 
 }  // namespace qb

@@ -147,6 +147,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     // Launch-mode switches for diagnosis (defaults: programmatic dependent launch on, CUDA graphs on).
     if (const char* v = std::getenv("QNT_PDL")) pdl_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_GRAPHS")) use_graphs_ = std::atoi(v) != 0;
+    if (const char* v = std::getenv("QNT_FUSE_QKV")) fuse_qkv_attn_ = std::atoi(v) != 0;
     try {
         const HostTensor& emb = file_.get("model.embed_tokens.weight");
         embed_ = upload_matrix(emb);
@@ -392,11 +393,23 @@ int Engine::sync_check() {
 
 int Engine::launch_layers_decode(const int* pos_dev) {
     for (const Layer& L : layers_) {
-        QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
         AttnArgs aa = L.aa;  // the attention also hands o_proj its quantized input (XQ_ / DX_ are prefill scratch)
         aa.xq = XQ_;
         aa.dx = DX_;
-        QB_TRY(launch_attn(aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
+        bool fused = false;  // q|k|v inside the attention kernel where its shape allows
+        if (fuse_qkv_attn_) {
+            const cudaError_t fe = launch_qkv_attn(L.qa, aa, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, ATT_, st_, pdl_);
+            if (fe == cudaSuccess) {
+                ++kernel_count_;
+                fused = true;
+            } else if (fe != cudaErrorNotSupported) {
+                return cuda_fail(fe, "launch_qkv_attn");
+            }
+        }
+        if (!fused) {
+            QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
+            QB_TRY(launch_attn(aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
+        }
         QB_TRY(launch_resid_dec(L.o, L.p_o, nullptr, XQ_, DX_, X_, st_, pdl_));
         QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_));
         QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_));

@@ -145,6 +145,7 @@ private:
     std::string err_;
     cudaStream_t st_ = nullptr;
     bool pdl_ = true, use_graphs_ = true;
+    bool fuse_qkv_attn_ = true;  // decode: q|k|v matvec fused into the attention kernel (QNT_FUSE_QKV=0: two kernels)
     int mm_impl_ = MM_AUTO;
     int device_ = 0, n_sm_ = 148;
 

@@ -1,6 +1,7 @@
 // Per-layer kernels of the Qwen2 forward (engine/src/model.cpp:165-228 decode, :363-433 prefill chunk).
 //
-// Decode (one token) runs five kernels per layer, each fusing its neighbours:
+// Decode (one token) runs five kernels per layer, each fusing its neighbours (four where the first two merge into
+// one, attention.cu's launch_qkv_attn):
 //   k_qkv_dec     rmsnorm + quantize (prologue) -> fused q|k|v integer matvec -> bias + RoPE -> q, f16 K/V store
 //   k_attn        GQA attention over the f16 KV cache (attention.cu)
 //   k_o_dec       quantize(attn) -> o_proj matvec -> residual add

@@ -55,6 +55,10 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
                               int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl);
 // n_tok > 1 consecutive tokens whose positions stay below pos_bound (known on the host): one CTA per (kv head, token).
+// Decode (one token): the layer's q|k|v matvec (with its rmsnorm prologue, bias, RoPE and K/V store) fused into the
+// attention; cudaErrorNotSupported for shapes the fused form does not cover (then k_qkv_dec + launch_attn).
+cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
+                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
                                 cudaStream_t st, bool pdl, TokMap tm = TokMap{});
 // DXT (optional): the block scales also block-major, DXT[b * ldt + t] (the tensor-core matmul's layout).

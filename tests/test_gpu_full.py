@@ -67,3 +67,39 @@ def test_config4_shortlist_matches_full_head(qb, models):
         prompt = hist
     print("config4 rel errors:", ["%.2e" % e for e in errs])
     assert max(errs) < TOL, errs
+
+
+_FUSE_SCRIPT = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+import quanta_b200 as qb
+m = qb.Model(sys.argv[2], ctx_len=4096)
+prompt = np.random.default_rng(21).integers(0, m.hp.n_tokens, 300)
+ids, st = m.generate(prompt, qb.SamplerParams(seed=99), 48, shortlist=True, batch_prefill=True)
+print(json.dumps({"ids": [int(i) for i in ids], "kps": st["kernels_per_step"], "layers": m.hp.n_layers}))
+"""
+
+
+def test_fused_qkv_attention_decode_equals_two_kernels(qb, models):
+    """Decode with the q|k|v matvec fused into the attention kernel (the default where the shape allows) against the
+    two-kernel path (QNT_FUSE_QKV=0): the same sampled ids on the full-size q4mix model, and one launch fewer per
+    layer, so the fused kernel is the one that ran."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    path = models("q4mix_sl")
+    pkg = str(Path(qb.__file__).resolve().parent)
+    out = {}
+    for fuse in ("1", "0"):
+        env = dict(os.environ, QNT_FUSE_QKV=fuse)
+        r = subprocess.run([sys.executable, "-c", _FUSE_SCRIPT, pkg, str(path)], env=env, capture_output=True,
+                           text=True, timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        out[fuse] = json.loads(r.stdout.strip().splitlines()[-1])
+    assert len(out["1"]["ids"]) == 48
+    assert out["1"]["ids"] == out["0"]["ids"]
+    assert out["0"]["kps"] - out["1"]["kps"] == out["1"]["layers"], (out["0"]["kps"], out["1"]["kps"])
