@@ -87,8 +87,11 @@ inline size_t qkv_smem_bytes(int dim) {
 // posts q and the f16-rounded k, v of the token into every CTA of the cluster; the first query head of each kv
 // head also stores k, v into the cache.  This removes the q|k|v kernel, its launch gap and the attention's reads of
 // q and of the token's own K/V row.  Bit-identical to k_qkv_dec followed by the unfused attention.
-template <int CS, int UW>
-__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, const float* __restrict__ X,
+// UO > 0 (with UW > 0): o_proj folded in as well.  After the output chain every CTA holds the head's 64 outputs,
+// quantizes them (the same bits as the leader's quantize for o_proj) and forms the o_proj block terms of the head's two
+// 32-blocks for its eighth of the rows (UO weight chunks per thread, loaded before the wait) into oa.T.
+template <int CS, int UW, int UO>
+__global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs oa, const float* __restrict__ X,
                                                    const float* __restrict__ norm_w, float eps, float* __restrict__ Qout,
                                                    const float* __restrict__ Q, const int* __restrict__ pos_dev, int n_tok,
                                                    float* __restrict__ out) {
@@ -170,6 +173,25 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, const
     constexpr int UWn = UW > 0 ? UW : 1;
     uint4 wv[UWn];
     __half wdv[UWn];
+    // o_proj (UO > 0): chunk f of this CTA = row orow0 + f / 4, chunk f % 4 of the head's 64 columns (two per 32-block)
+    constexpr int UOn = UO > 0 ? UO : 1;
+    const int ocols = oa.W.cols, onb = ocols / QK, orpc = (oa.W.rows + CS - 1) / CS, orow0 = r * orpc;
+    const int onr = UO > 0 ? min(orpc, oa.W.rows - orow0) : 0;
+    uint4 wo[UOn];
+    __half wdo[UOn];
+    if constexpr (UO > 0) {
+#pragma unroll
+        for (int u = 0; u < UO; ++u) {
+            const int f = u * kThreads + tid, orow = orow0 + (f >> 2), c = f & 3;
+            if ((f >> 2) < onr) {
+                wo[u] = ld_stream(reinterpret_cast<const uint4*>(oa.W.q + size_t(orow) * ocols + h * kHd) + c);
+                wdo[u] = oa.W.d[size_t(orow) * onb + 2 * h + (c >> 1)];
+            } else {
+                wo[u] = make_uint4(0, 0, 0, 0);
+                wdo[u] = __float2half(0.f);
+            }
+        }
+    }
     NormW nw;
     float pba = 0.f, pbb = 0.f, pc = 1.f, ps = 0.f;  // pair lanes (tid < 12): bias of the two rows, RoPE cos / sin
     if constexpr (UW > 0) {  // the CTA's weight chunks, the norm weights and the pair constants before the wait
@@ -361,7 +383,31 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, const
         }
         if (tid < dpc) out[(size_t(t) * a.n_heads + h) * kHd + d0 + tid] = o;
     }
-    if (a.xq && n_tok == 1) {  // quantize_q8 of the head's 64 outputs in the leader: warp w holds block 2 h + w
+    if constexpr (UO > 0) {  // every CTA: the head's outputs, their quantization, this CTA's o_proj terms
+        __shared__ __align__(16) int8_t sxo[kHd];
+        __shared__ float sdo[kHd / QK];
+        if (tid < dpc) {
+#pragma unroll
+            for (int q = 0; q < CS; ++q) cluster.map_shared_rank(so, q)[d0 + tid] = o;
+        }
+        cluster_arrive();
+        cluster_wait();
+        if (tid < kHd) {  // warp w quantizes block 2 h + w
+            float d;
+            sxo[tid] = quantize_lane(so[tid], &d);
+            if (lane == 0) sdo[warp] = d;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < UO; ++u) {  // a block's two chunks sit in adjacent lanes
+            const int f = u * kThreads + tid, c = f & 3;
+            const bool ok = (f >> 2) < onr;
+            int sdot = ok ? chunk_dot<DT_Q8_0>(wo[u], sxo, c) : 0;
+            sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+            if (ok && !(c & 1))
+                oa.T[size_t(orow0 + (f >> 2)) * onb + 2 * h + (c >> 1)] = block_term(sdot, __half2float(wdo[u]), sdo[c >> 1]);
+        }
+    } else if (a.xq && n_tok == 1) {  // quantize_q8 of the head's 64 outputs in the leader: warp w holds block 2 h + w
         if (tid < dpc) cluster.map_shared_rank(so, 0)[d0 + tid] = o;
         cluster_arrive();
         cluster_wait();
@@ -531,7 +577,7 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     // a cluster of cs CTAs per (head, token): the largest power of two up to 8 and the chunk count
     int cs = 1;
     while (cs * 2 <= std::min(kMaxCluster, a.max_chunks)) cs *= 2;
-    auto kern = cs == 8 ? k_attn<8, 0> : cs == 4 ? k_attn<4, 0> : cs == 2 ? k_attn<2, 0> : k_attn<1, 0>;
+    auto kern = cs == 8 ? k_attn<8, 0, 0> : cs == 4 ? k_attn<4, 0, 0> : cs == 2 ? k_attn<2, 0, 0> : k_attn<1, 0, 0>;
     const size_t smem = attn_smem_bytes(ctx, cs);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -550,26 +596,39 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, a, QkvArgs{}, static_cast<const float*>(nullptr), static_cast<const float*>(nullptr),
+    return cudaLaunchKernelEx(&cfg, kern, a, QkvArgs{}, OArgs{}, static_cast<const float*>(nullptr), static_cast<const float*>(nullptr),
                               0.f, static_cast<float*>(nullptr), Q, pos_dev, n_tok, out);
 }
 
-cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
-                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl) {
+namespace {
+// weight chunks per thread of the fused forms: q|k|v (24 rows per CTA), o_proj (an eighth of the rows, 4 chunks each)
+int qkv_uw(int dim) { return (kQkvRows * (dim / 16) + kThreads - 1) / kThreads; }
+int o_uo(const DMat& o) { return ((o.rows + kMaxCluster - 1) / kMaxCluster * 4 + kThreads - 1) / kThreads; }
+}  // namespace
+
+bool qkv_attn_supported(const QkvArgs& qa, const AttnArgs& a, const DMat* o) {
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
     const int dim = qa.W.cols;
-    // the fused form covers the decode shapes it was built for; anything else takes the two kernels
     if (a.head_dim != kHd || group < 1 || group * a.n_kv != a.n_heads || a.max_chunks < kMaxCluster ||
         qa.W.dtype != DT_Q8_0 || qa.head_dim != kHd || dim % QK != 0 || dim > kMaxRounds * kThreads ||
-        qa.W.rows != (a.n_heads + 2 * a.n_kv) * kHd)
-        return cudaErrorNotSupported;
-    const int chunks = kQkvRows * (dim / 16);
-    const int uw = (chunks + kThreads - 1) / kThreads;
-    if (uw > 12) return cudaErrorNotSupported;
-    const int ctx = a.max_chunks * kPosChunk;
-    const size_t smem = attn_smem_bytes(ctx, kMaxCluster) + qkv_smem_bytes(dim);
-    if (smem > 227 * 1024) return cudaErrorNotSupported;
-    auto kern = uw <= 6 ? k_attn<kMaxCluster, 6> : k_attn<kMaxCluster, 12>;
+        qa.W.rows != (a.n_heads + 2 * a.n_kv) * kHd || qkv_uw(dim) > 12)
+        return false;
+    if (o && (o->dtype != DT_Q8_0 || o->cols != a.n_heads * kHd || o_uo(*o) > 4 || o->rows < kMaxCluster)) return false;
+    const size_t smem = attn_smem_bytes(a.max_chunks * kPosChunk, kMaxCluster) + qkv_smem_bytes(dim);
+    return smem <= 227 * 1024;
+}
+
+cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
+                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl, const OArgs* o) {
+    // the fused form covers the decode shapes it was built for; anything else takes the separate kernels
+    if (!qkv_attn_supported(qa, a, o ? &o->W : nullptr)) return cudaErrorNotSupported;
+    const int dim = qa.W.cols;
+    const size_t smem = attn_smem_bytes(a.max_chunks * kPosChunk, kMaxCluster) + qkv_smem_bytes(dim);
+    const bool u6 = qkv_uw(dim) <= 6;
+    const int uo = o ? (o_uo(o->W) <= 2 ? 2 : 4) : 0;
+    auto kern = uo == 0 ? (u6 ? k_attn<kMaxCluster, 6, 0> : k_attn<kMaxCluster, 12, 0>)
+              : uo == 2 ? (u6 ? k_attn<kMaxCluster, 6, 2> : k_attn<kMaxCluster, 12, 2>)
+                        : (u6 ? k_attn<kMaxCluster, 6, 4> : k_attn<kMaxCluster, 12, 4>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -586,7 +645,8 @@ cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, a, qa, X, norm_w, eps, Qout, static_cast<const float*>(nullptr), pos_dev, 1, out);
+    return cudaLaunchKernelEx(&cfg, kern, a, qa, o ? *o : OArgs{}, X, norm_w, eps, Qout, static_cast<const float*>(nullptr),
+                              pos_dev, 1, out);
 }
 
 }  // namespace qb

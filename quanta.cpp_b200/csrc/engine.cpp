@@ -148,6 +148,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     if (const char* v = std::getenv("QNT_PDL")) pdl_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_GRAPHS")) use_graphs_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_FUSE_QKV")) fuse_qkv_attn_ = std::atoi(v) != 0;
+    if (const char* v = std::getenv("QNT_FUSE_O")) fuse_o_ = std::atoi(v) != 0;
     try {
         const HostTensor& emb = file_.get("model.embed_tokens.weight");
         embed_ = upload_matrix(emb);
@@ -253,6 +254,9 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
             L.p_o = plan_rows(L.o.dtype, L.o.rows, L.o.cols, n_sm_, 2);
             L.p_gu = plan_rows(L.gu.dtype, L.gu.rows, L.gu.cols, n_sm_, 64);
             L.p_down = plan_rows(L.down.dtype, L.down.rows, L.down.cols, n_sm_, 2);
+            L.f_qkv = fuse_qkv_attn_ && qkv_attn_supported(L.qa, L.aa, nullptr);
+            L.f_o = L.f_qkv && fuse_o_ && L.o.rows == hp_.dim && qkv_attn_supported(L.qa, L.aa, &L.o) &&
+                    gateup_rt_supported(L.gu, L.p_gu, L.o.cols / QK);
         }
         layer_bytes_ = weight_bytes_ - before_layers + size_t(hp_.dim) * 4;
 
@@ -279,6 +283,8 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         Q_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
         ATT_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
         R_ = static_cast<float*>(dalloc(size_t(kChunk) * rmax * 4));
+        OT_ = static_cast<float*>(dalloc(size_t(hp_.dim) * (layers_[0].o.cols / QK) * 4));
+        X2_ = static_cast<float*>(dalloc(size_t(hp_.dim) * 4));
         XQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * wmax));
         DX_ = static_cast<float*>(dalloc(size_t(kChunk) * (wmax / QK) * 4));
         HQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * hp_.ffn_dim));
@@ -396,17 +402,17 @@ int Engine::launch_layers_decode(const int* pos_dev) {
         AttnArgs aa = L.aa;  // the attention also hands o_proj its quantized input (XQ_ / DX_ are prefill scratch)
         aa.xq = XQ_;
         aa.dx = DX_;
-        bool fused = false;  // q|k|v inside the attention kernel where its shape allows
-        if (fuse_qkv_attn_) {
-            const cudaError_t fe = launch_qkv_attn(L.qa, aa, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, ATT_, st_, pdl_);
-            if (fe == cudaSuccess) {
-                ++kernel_count_;
-                fused = true;
-            } else if (fe != cudaErrorNotSupported) {
-                return cuda_fail(fe, "launch_qkv_attn");
-            }
+        if (L.f_o) {  // three kernels: attention (+ q|k|v, + o_proj terms), gate|up (+ o_proj residual), down
+            const OArgs oa{L.o, OT_};
+            QB_TRY(launch_qkv_attn(L.qa, aa, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, ATT_, st_, pdl_, &oa));
+            QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_, OT_,
+                                     L.o.cols / QK, X2_));
+            QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_, X2_));
+            continue;
         }
-        if (!fused) {
+        if (L.f_qkv) {
+            QB_TRY(launch_qkv_attn(L.qa, aa, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, ATT_, st_, pdl_));
+        } else {
             QB_TRY(launch_qkv_dec(L.qa, L.p_qkv, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, st_, pdl_));
             QB_TRY(launch_attn(aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
         }

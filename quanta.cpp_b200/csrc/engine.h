@@ -115,6 +115,7 @@ private:
         QkvArgs qa;
         AttnArgs aa;
         SlicePlan p_qkv, p_o, p_gu, p_down;
+        bool f_qkv = false, f_o = false;  // decode: q|k|v inside the attention kernel; o_proj folded in as well
         TcMap t_qkv{}, t_o{}, t_gu{}, t_down{};  // TMA sources of the tensor-core matmul (valid when tc)
         bool tc = false;
     };
@@ -146,6 +147,8 @@ private:
     cudaStream_t st_ = nullptr;
     bool pdl_ = true, use_graphs_ = true;
     bool fuse_qkv_attn_ = true;  // decode: q|k|v matvec fused into the attention kernel (QNT_FUSE_QKV=0: two kernels)
+    bool fuse_o_ = true;         // decode: o_proj folded into the attention + gate|up kernels (QNT_FUSE_O=0: its own kernel)
+    float *OT_ = nullptr, *X2_ = nullptr;  // o_proj block terms [dim][n_heads * 2] and the o_proj residual [dim]
     int mm_impl_ = MM_AUTO;
     int device_ = 0, n_sm_ = 148;
 

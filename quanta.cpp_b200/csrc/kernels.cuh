@@ -267,12 +267,10 @@ __device__ __forceinline__ float ordered_sum(const float* v, int n, float s = 0.
 
 // rmsnorm (engine/src/ops_ref.cpp:194-199) then quantize_q8 (:69-83) of x[dim] into sx / sdx (and block sums).
 // sred: scratch of >= dim + 32 floats.  Bit-identical to the reference.  dim <= kMaxRounds * blockDim.
-__device__ __forceinline__ void norm_quant(const float* __restrict__ x, const NormW& nw, int dim, float eps, int8_t* sx,
-                                           float* sdx, int* ssum, float* sred) {
+// norm_quant_v: the same on values already in registers, xv[k] = element tid + k * blockDim (0 past dim).
+__device__ __forceinline__ void norm_quant_v(const float (&xv)[kMaxRounds], const NormW& nw, int dim, float eps, int8_t* sx,
+                                             float* sdx, int* ssum, float* sred) {
     const int tid = threadIdx.x, T = blockDim.x;
-    float xv[kMaxRounds];
-#pragma unroll
-    for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < dim ? __ldcg(x + tid + k * T) : 0.f;
     float* sq = sred + 32;
 #pragma unroll
     for (int k = 0; k < kMaxRounds; ++k)
@@ -287,6 +285,14 @@ __device__ __forceinline__ void norm_quant(const float* __restrict__ x, const No
     for (int k = 0; k < kMaxRounds; ++k) y[k] = fmul(fmul(xv[k], scale), nw.w[k]);  // 0 past dim
     quant_rounds(y, dim, sx, sdx, ssum);
     __syncthreads();
+}
+__device__ __forceinline__ void norm_quant(const float* __restrict__ x, const NormW& nw, int dim, float eps, int8_t* sx,
+                                           float* sdx, int* ssum, float* sred) {
+    const int tid = threadIdx.x, T = blockDim.x;
+    float xv[kMaxRounds];
+#pragma unroll
+    for (int k = 0; k < kMaxRounds; ++k) xv[k] = tid + k * T < dim ? __ldcg(x + tid + k * T) : 0.f;
+    norm_quant_v(xv, nw, dim, eps, sx, sdx, ssum, sred);
 }
 
 // quantize_q8 of x[n] (no norm) into sx / sdx (and block sums); n <= kMaxRounds * blockDim.

@@ -16,10 +16,15 @@
 //
 // Prefill runs the matmul (tensor-core or CUDA-core) on whole chunks and the same elementwise helpers as the
 // decode kernels' epilogues, so batched and token-by-token give the same bits.
+#include <cooperative_groups.h>
+
 #include "kernels.cuh"
 #include "layer_kernels.h"
 
 namespace qb {
+
+namespace cg = cooperative_groups;
+constexpr int kRtMaxNb = 32;  // o_proj blocks per row that the gate|up residual-terms form takes (o_proj cols <= 1024)
 
 // ---------------------------------------------------------------- embedding (engine/src/ops_ref.cpp:162-192 get_row)
 
@@ -161,9 +166,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv_dec(QkvArgs a, const float* __
 
 // out rows -> X[row] += value (residual).  mode 0: input is f32 attn output to quantize; mode 1: pre-quantized.
 template <int DT, int U, int MODE>
+// Xres: where the residual is read (X itself when null; the gate|up kernel's X2 after an o_proj folded into it).
 __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __restrict__ xin, const int8_t* __restrict__ qin,
                                                         const float* __restrict__ din, float* __restrict__ X,
-                                                        int rows_per_cta, unsigned magic) {
+                                                        int rows_per_cta, unsigned magic, const float* __restrict__ Xres) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int cols = W.cols;
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
         pdl_launch_dependents();
-        if (int(threadIdx.x) < nrows) xres = __ldcg(X + row0 + threadIdx.x);
+        if (int(threadIdx.x) < nrows) xres = __ldcg((Xres ? Xres : X) + row0 + threadIdx.x);
         if (MODE == 0) quant_only(xin, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
         else load_quant(qin, din, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
     });
@@ -183,11 +189,20 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
 
 // gate|up rows interleaved per 32-block: fused row 64j + i = gate row 32j + i, 64j + 32 + i = up row 32j + i.
 // Each CTA owns whole ffn blocks, so it finishes SwiGLU and the block's int8 quantization itself.
-template <int DT, int U>
+//
+// RT (residual terms, decode with o_proj folded into the attention): launched in clusters of 8.  After the wait, CTA c
+// of each cluster forms rows [c R, c R + R) (R = dim / 8) of the o_proj residual, X + ((0 + T_r0) + T_r1) + ... in
+// block order (k_resid_dec's arithmetic on the attention's terms), posts them into all 8 CTAs (distributed shared
+// memory) and the first cluster stores them into X2; every CTA then norms the whole vector from shared memory.
+template <int DT, int U, bool RT>
 __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __restrict__ X, const float* __restrict__ norm_w,
                                                          float eps, int8_t* __restrict__ HQ, float* __restrict__ HD,
-                                                         int blocks_per_cta, unsigned magic, ExpTab tab) {
+                                                         int blocks_per_cta, unsigned magic, ExpTab tab,
+                                                         const float* __restrict__ T, int nbo, float* __restrict__ X2,
+                                                         int xn_off) {
     extern __shared__ __align__(16) unsigned char smem[];
+    // every CTA of the cluster has started before the first remote store (the wait comes before it)
+    if constexpr (RT) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
     const int dim = W.cols;
     const int rows_per_cta = blocks_per_cta * 64;
     const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, W.rows - row0);
@@ -198,7 +213,47 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
         pdl_launch_dependents();
-        norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+        if constexpr (RT) {
+            cg::cluster_group cl = cg::this_cluster();
+            const int cr = int(cl.block_rank()), rpc = (dim + 7) / 8, rr0 = cr * rpc, nr = min(rpc, dim - rr0);
+            float* sxn = reinterpret_cast<float*>(smem + xn_off);
+            const int i = threadIdx.x;
+            float xn = 0.f;
+            if (i < nr) {
+                const int row = rr0 + i;
+                const float xo = __ldcg(X + row);
+                const float4* t4 = reinterpret_cast<const float4*>(T + size_t(row) * nbo);
+                float4 tv[kRtMaxNb / 4];
+#pragma unroll
+                for (int j = 0; j < kRtMaxNb / 4; ++j)
+                    if (j < nbo / 4) tv[j] = __ldcg(t4 + j);
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < kRtMaxNb / 4; ++j) {
+                    if (j < nbo / 4) {
+                        acc = fadd(acc, tv[j].x);
+                        acc = fadd(acc, tv[j].y);
+                        acc = fadd(acc, tv[j].z);
+                        acc = fadd(acc, tv[j].w);
+                    }
+                }
+                xn = fadd(xo, acc);
+                if (blockIdx.x < 8) X2[row] = xn;  // the first cluster stores the residual for the down kernel
+            }
+            asm volatile("barrier.cluster.wait;" ::: "memory");
+            if (i < nr) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) cl.map_shared_rank(sxn, q)[rr0 + i] = xn;
+            }
+            asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+            asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+            float xv[kMaxRounds];
+#pragma unroll
+            for (int k = 0; k < kMaxRounds; ++k) xv[k] = i + k * int(blockDim.x) < dim ? sxn[i + k * blockDim.x] : 0.f;
+            norm_quant_v(xv, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+        } else {
+            norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+        }
     });
     __syncthreads();
     for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
@@ -333,29 +388,69 @@ cudaError_t launch_qkv_dec(const QkvArgs& a, const SlicePlan& p, const float* X,
 }
 
 cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin, const int8_t* qin, const float* din,
-                             float* X, cudaStream_t st, bool pdl) {
+                             float* X, cudaStream_t st, bool pdl, const float* Xres) {
     cudaError_t e = cudaErrorInvalidValue;
     const bool pre = qin != nullptr;
     if (W.dtype == DT_Q8_0) {
-        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
-        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic, Xres)); }
+        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q8_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic, Xres)); }
     } else if (W.dtype == DT_Q4_0) {
-        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
-        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic)); }
+        if (pre) { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 1>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic, Xres)); }
+        else { QB_DISPATCH_U(p.u, e = launch_pdl(k_resid_dec<DT_Q4_0, UU, 0>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, xin, qin, din, X, p.rows_per_cta, p.magic, Xres)); }
     }
     return e;
 }
 
+namespace {
+size_t rt_xn_off(const SlicePlan& p) { return (p.smem + 15) & ~size_t(15); }
+}  // namespace
+
+bool gateup_rt_supported(const DMat& W, const SlicePlan& p, int nbo) {
+    const int dim = W.cols;
+    return (W.dtype == DT_Q8_0 || W.dtype == DT_Q4_0) && p.grid % 8 == 0 && dim % QK == 0 && dim <= kMaxRounds * kThreads &&
+           nbo > 0 && nbo % 4 == 0 && nbo <= kRtMaxNb && rt_xn_off(p) + size_t(dim) * 4 <= 227 * 1024;
+}
+
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
-                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl) {
+                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl,
+                              const float* T, int nbo, float* X2) {
     cudaError_t e = cudaErrorInvalidValue;
     const int bpc = p.rows_per_cta / 64;
+    if (T) {  // residual-terms form: clusters of 8
+        if (!gateup_rt_supported(W, p, nbo)) return cudaErrorNotSupported;
+        const size_t smem = rt_xn_off(p) + size_t(W.cols) * 4;
+        const int xo = int(rt_xn_off(p));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(p.grid));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 8;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 2 : 1;
+        auto go = [&](auto kern) {
+            cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (r != cudaSuccess) return r;
+            return cudaLaunchKernelEx(&cfg, kern, W, X, norm_w, eps, HQ, HD, bpc, p.magic, tab, T, nbo, X2, xo);
+        };
+        if (W.dtype == DT_Q8_0) { QB_DISPATCH_U(p.u, e = go(k_gateup_dec<DT_Q8_0, UU, true>)); }
+        else { QB_DISPATCH_U(p.u, e = go(k_gateup_dec<DT_Q4_0, UU, true>)); }
+        return e;
+    }
     if (W.dtype == DT_Q8_0) {
-        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q8_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
-                                          eps, HQ, HD, bpc, p.magic, tab));
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q8_0, UU, false>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X,
+                                          norm_w, eps, HQ, HD, bpc, p.magic, tab, static_cast<const float*>(nullptr), 0,
+                                          static_cast<float*>(nullptr), 0));
     } else if (W.dtype == DT_Q4_0) {
-        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q4_0, UU>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X, norm_w,
-                                          eps, HQ, HD, bpc, p.magic, tab));
+        QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q4_0, UU, false>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X,
+                                          norm_w, eps, HQ, HD, bpc, p.magic, tab, static_cast<const float*>(nullptr), 0,
+                                          static_cast<float*>(nullptr), 0));
     }
     return e;
 }

@@ -19,6 +19,13 @@ struct QkvArgs {
     int n_heads, n_kv, head_dim, kv_dim;
 };
 
+// o_proj folded into the decode attention: T [W.rows][W.cols / 32] receives each row's block terms
+// (float(s_b) * dw_b) * dx_b; the gate|up kernel adds them in block order onto the residual.
+struct OArgs {
+    DMat W;
+    float* T = nullptr;
+};
+
 struct AttnArgs {
     const __half* kcache;    // this layer's [ctx][kv_dim]
     const __half* vcache;
@@ -50,15 +57,22 @@ cudaError_t launch_embed(const DMat& E, const int* tokens, int n_tok, float* X, 
 cudaError_t launch_qkv_dec(const QkvArgs& a, const SlicePlan& p, const float* X, const float* norm_w, float eps,
                            const int* pos_dev, float* Q, cudaStream_t st, bool pdl);
 cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin, const int8_t* qin, const float* din,
-                             float* X, cudaStream_t st, bool pdl);
+                             float* X, cudaStream_t st, bool pdl, const float* Xres = nullptr);
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
-                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl);
+                              int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl,
+                              const float* T = nullptr, int nbo = 0, float* X2 = nullptr);
+// residual-terms form of gate|up (T != nullptr): clusters of 8 CTAs first form X2 = X + (o_proj terms T summed in block
+// order), the o_proj residual, then norm it; launched only where gateup_rt_supported.
+bool gateup_rt_supported(const DMat& W, const SlicePlan& p, int nbo);
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl);
 // n_tok > 1 consecutive tokens whose positions stay below pos_bound (known on the host): one CTA per (kv head, token).
 // Decode (one token): the layer's q|k|v matvec (with its rmsnorm prologue, bias, RoPE and K/V store) fused into the
 // attention; cudaErrorNotSupported for shapes the fused form does not cover (then k_qkv_dec + launch_attn).
+// With `o` (o_proj Q8_0, [dim][n_heads * 64]), the kernel also forms the o_proj block terms of its head into o->T
+// (o_proj then runs inside launch_gateup_dec's residual-terms form).  qkv_attn_supported: whether the shapes allow it.
+bool qkv_attn_supported(const QkvArgs& qa, const AttnArgs& a, const DMat* o);
 cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
-                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl);
+                            const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl, const OArgs* o = nullptr);
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
                                 cudaStream_t st, bool pdl, TokMap tm = TokMap{});
 // DXT (optional): the block scales also block-major, DXT[b * ldt + t] (the tensor-core matmul's layout).

@@ -81,10 +81,13 @@ print(json.dumps({"ids": [int(i) for i in ids], "kps": st["kernels_per_step"], "
 """
 
 
-def test_fused_qkv_attention_decode_equals_two_kernels(qb, models):
-    """Decode with the q|k|v matvec fused into the attention kernel (the default where the shape allows) against the
-    two-kernel path (QNT_FUSE_QKV=0): the same sampled ids on the full-size q4mix model, and one launch fewer per
-    layer, so the fused kernel is the one that ran."""
+def test_fused_decode_layers_equal_separate_kernels(qb, models):
+    """The three decode forms on the full-size q4mix model give the same sampled ids:
+    - default: q|k|v inside the attention kernel, and o_proj folded into the attention (block terms) and the gate|up
+      kernel (residual), three kernels per layer;
+    - QNT_FUSE_O=0: o_proj as a kernel of its own, four per layer;
+    - QNT_FUSE_QKV=0: q|k|v as a kernel of its own as well, five per layer.
+    The per-step launch counts differ by one per layer between them, so each form is the one that ran."""
     import json
     import os
     import subprocess
@@ -94,12 +97,16 @@ def test_fused_qkv_attention_decode_equals_two_kernels(qb, models):
     path = models("q4mix_sl")
     pkg = str(Path(qb.__file__).resolve().parent)
     out = {}
-    for fuse in ("1", "0"):
-        env = dict(os.environ, QNT_FUSE_QKV=fuse)
+    for name, env_add in (("both", {}), ("qkv", {"QNT_FUSE_O": "0"}), ("none", {"QNT_FUSE_QKV": "0"})):
+        env = dict(os.environ, **env_add)
+        env.pop("QNT_FUSE_O", None) if name == "both" else None
+        env.pop("QNT_FUSE_QKV", None) if name != "none" else None
         r = subprocess.run([sys.executable, "-c", _FUSE_SCRIPT, pkg, str(path)], env=env, capture_output=True,
                            text=True, timeout=600)
         assert r.returncode == 0, r.stdout + r.stderr
-        out[fuse] = json.loads(r.stdout.strip().splitlines()[-1])
-    assert len(out["1"]["ids"]) == 48
-    assert out["1"]["ids"] == out["0"]["ids"]
-    assert out["0"]["kps"] - out["1"]["kps"] == out["1"]["layers"], (out["0"]["kps"], out["1"]["kps"])
+        out[name] = json.loads(r.stdout.strip().splitlines()[-1])
+    layers = out["both"]["layers"]
+    assert len(out["both"]["ids"]) == 48
+    assert out["both"]["ids"] == out["qkv"]["ids"] == out["none"]["ids"]
+    assert out["qkv"]["kps"] - out["both"]["kps"] == layers, (out["both"]["kps"], out["qkv"]["kps"])
+    assert out["none"]["kps"] - out["qkv"]["kps"] == layers, (out["qkv"]["kps"], out["none"]["kps"])
