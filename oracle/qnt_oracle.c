@@ -289,6 +289,11 @@ OModel* orc_model_open(const char* path, int ctx, char* err, int errlen) {
     m->tied = rd_u32(&r) != 0;
     m->qkv_bias = rd_u32(&r) != 0;
     m->flags = version >= 2 ? rd_u32(&r) : 0;
+    if ((m->flags & 1u) && m->ffn % 256 != 0) { /* engine/src/model.cpp:39-42 */
+        snprintf(err, (size_t)errlen, "FLAG_HADAMARD_DOWN needs ffn_dim %% 256 == 0");
+        orc_model_close(m);
+        return NULL;
+    }
     const uint32_t tok_len = rd_u32(&r);
     if (!r.bad) {
         Rd t = {r.p, r.p + tok_len, 0};
@@ -426,6 +431,24 @@ static void add_bias(float* v, const OTensor* b) { /* engine/src/model.cpp:159-1
 }
 
 /* attend<_Float16> (engine/src/model.cpp:115-137). */
+/* Block Walsh-Hadamard transform in place (engine/src/ops_ref.cpp:228-241): in each block, stages h = 1, 2, ..,
+ * block / 2 replace (v[j], v[j + h]) by (v[j] + v[j + h], v[j] - v[j + h]) within 2h-blocks, then scale by
+ * 1 / sqrt(block). */
+static void fwht_blocks(float* x, int n, int block) {
+    const float norm = 1.0f / sqrtf((float)block);
+    for (int b0 = 0; b0 < n; b0 += block) {
+        float* v = x + b0;
+        for (int h = 1; h < block; h *= 2)
+            for (int i = 0; i < block; i += 2 * h)
+                for (int j = i; j < i + h; ++j) {
+                    const float a = v[j], c = v[j + h];
+                    v[j] = a + c;
+                    v[j + h] = a - c;
+                }
+        for (int i = 0; i < block; ++i) v[i] *= norm;
+    }
+}
+
 static void attend(OModel* m, const uint16_t* kc, const uint16_t* vc, int pos) {
     const int hd = m->hd, kvd = m->n_kv * hd, group = m->n_heads / m->n_kv;
     const float scale = 1.0f / sqrtf((float)hd);
@@ -499,6 +522,7 @@ int orc_forward(OModel* m, int token, int pos, int top_k, int n_valid, const int
             const float g = m->hb[i];
             m->hb[i] = g / (1.0f + ref_expf(-g)) * m->hb2[i];
         }
+        if (m->flags & 1u) fwht_blocks(m->hb, m->ffn, 256); /* FLAG_HADAMARD_DOWN, engine/src/model.cpp:219 */
         orc_quantize_q8(m->hb, m->ffn, m->hq, m->hd_);
         linear(m, m->xb2, L[11], m->hq, m->hd_);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];

@@ -136,7 +136,9 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     if (hp_.head_dim != 64) return bad("the device attention kernel needs head_dim == 64");
     if (hp_.n_heads / hp_.n_kv_heads > 8) return bad("the device attention kernel needs <= 8 query heads per kv head");
     if (hp_.dim % QK || hp_.ffn_dim % QK || hp_.dim > 8192 || hp_.ffn_dim > 16384) return bad("unsupported dims");
-    if (hp_.flags & 1u) return bad("FLAG_HADAMARD_DOWN files are not supported on the device yet");
+    // FLAG_HADAMARD_DOWN (block-256 transform of the SwiGLU output before down), validated as model.cpp:39 does
+    hadamard_ = (hp_.flags & 1u) != 0;
+    if (hadamard_ && hp_.ffn_dim % 256 != 0) return bad("FLAG_HADAMARD_DOWN needs ffn_dim % 256 == 0");
     ctx_ = (ctx_len > 0 && ctx_len < hp_.max_seq) ? ctx_len : hp_.max_seq;
     if (cudaGetDevice(&device_) != cudaSuccess) return bad("no CUDA device");
     cudaDeviceProp prop;
@@ -284,6 +286,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         ATT_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.dim * 4));
         R_ = static_cast<float*>(dalloc(size_t(kChunk) * rmax * 4));
         OT_ = static_cast<float*>(dalloc(size_t(hp_.dim) * (layers_[0].o.cols / QK) * 4));
+        if (hadamard_) HF_ = static_cast<float*>(dalloc(size_t(kChunk) * hp_.ffn_dim * 4));
         X2_ = static_cast<float*>(dalloc(size_t(hp_.dim) * 4));
         XQ_ = static_cast<int8_t*>(dalloc(size_t(kChunk) * wmax));
         DX_ = static_cast<float*>(dalloc(size_t(kChunk) * (wmax / QK) * 4));
@@ -406,7 +409,8 @@ int Engine::launch_layers_decode(const int* pos_dev) {
             const OArgs oa{L.o, OT_};
             QB_TRY(launch_qkv_attn(L.qa, aa, X_, L.attn_norm, hp_.norm_eps, pos_dev, Q_, ATT_, st_, pdl_, &oa));
             QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_, OT_,
-                                     L.o.cols / QK, X2_));
+                                     L.o.cols / QK, X2_, HF_));
+            if (hadamard_) QB_TRY(launch_fwht_quant(HF_, 1, hp_.ffn_dim, HQ_, HD_, nullptr, 0, st_, pdl_));
             QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_, X2_));
             continue;
         }
@@ -417,7 +421,9 @@ int Engine::launch_layers_decode(const int* pos_dev) {
             QB_TRY(launch_attn(aa, Q_, pos_dev, 1, ATT_, st_, pdl_));
         }
         QB_TRY(launch_resid_dec(L.o, L.p_o, nullptr, XQ_, DX_, X_, st_, pdl_));
-        QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_));
+        QB_TRY(launch_gateup_dec(L.gu, L.p_gu, X_, L.ffn_norm, hp_.norm_eps, HQ_, HD_, exptab_, st_, pdl_, nullptr, 0, nullptr,
+                                 HF_));
+        if (hadamard_) QB_TRY(launch_fwht_quant(HF_, 1, hp_.ffn_dim, HQ_, HD_, nullptr, 0, st_, pdl_));
         QB_TRY(launch_resid_dec(L.down, L.p_down, nullptr, HQ_, HD_, X_, st_, pdl_));
     }
     return 0;
@@ -457,7 +463,8 @@ int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm) {
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
         QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, pdl_));
         if (int r = launch_matmul(L.gu, L.tc ? &L.t_gu : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, exptab_, st_, pdl_));
+        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, exptab_, st_, pdl_, HF_));
+        if (hadamard_) QB_TRY(launch_fwht_quant(HF_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, st_, pdl_));
         if (int r = launch_matmul(L.down, L.tc ? &L.t_down : nullptr, true, n, R_)) return r;
         QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
     }

@@ -149,6 +149,8 @@ private:
     bool fuse_qkv_attn_ = true;  // decode: q|k|v matvec fused into the attention kernel (QNT_FUSE_QKV=0: two kernels)
     bool fuse_o_ = true;         // decode: o_proj folded into the attention + gate|up kernels (QNT_FUSE_O=0: its own kernel)
     float *OT_ = nullptr, *X2_ = nullptr;  // o_proj block terms [dim][n_heads * 2] and the o_proj residual [dim]
+    bool hadamard_ = false;                // FLAG_HADAMARD_DOWN file
+    float* HF_ = nullptr;                  // (hadamard_) f32 SwiGLU outputs [kChunk][ffn] before the transform
     int mm_impl_ = MM_AUTO;
     int device_ = 0, n_sm_ = 148;
 

@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
                                                          float eps, int8_t* __restrict__ HQ, float* __restrict__ HD,
                                                          int blocks_per_cta, unsigned magic, ExpTab tab,
                                                          const float* __restrict__ T, int nbo, float* __restrict__ X2,
-                                                         int xn_off) {
+                                                         int xn_off, float* __restrict__ Hf) {
     extern __shared__ __align__(16) unsigned char smem[];
     // every CTA of the cluster has started before the first remote store (the wait comes before it)
     if constexpr (RT) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
@@ -261,9 +261,13 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int jb = warp; jb < nrows / 64; jb += kWarps) {
         const float h = swiglu1(s.sval[jb * 64 + lane], s.sval[jb * 64 + 32 + lane], tab);
+        const int j = row0 / 64 + jb;
+        if (Hf) {  // FLAG_HADAMARD_DOWN: k_fwht_quant transforms and quantizes
+            Hf[j * QK + lane] = h;
+            continue;
+        }
         float d;
         const int8_t q = quantize_lane(h, &d);
-        const int j = row0 / 64 + jb;
         HQ[j * QK + lane] = q;
         if (lane == 0) HD[j] = d;
     }
@@ -316,8 +320,9 @@ __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, l
 }
 
 // R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
+// Hf (files with FLAG_HADAMARD_DOWN): the f32 SwiGLU output goes to Hf[t][ffn] for k_fwht_quant instead.
 __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
-                               float* __restrict__ HD, float* __restrict__ HDT, int ldt, ExpTab tab) {
+                               float* __restrict__ HD, float* __restrict__ HDT, int ldt, ExpTab tab, float* __restrict__ Hf) {
     pdl_wait();
     pdl_launch_dependents();
     const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
@@ -326,12 +331,73 @@ __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, 
     const int t = int(w / nbk), j = int(w - (long long)t * nbk), lane = threadIdx.x & 31;
     const float* r = R + size_t(t) * 2 * ffn + size_t(j) * 64;
     const float h = swiglu1(__ldcg(r + lane), __ldcg(r + 32 + lane), tab);
+    if (Hf) {
+        Hf[size_t(t) * ffn + j * QK + lane] = h;
+        return;
+    }
     float d;
     const int8_t q = quantize_lane(h, &d);
     HQ[size_t(t) * ffn + j * QK + lane] = q;
     if (lane == 0) {
         HD[size_t(t) * nbk + j] = d;
         if (HDT) HDT[size_t(j) * ldt + t] = d;
+    }
+}
+
+// fwht_blocks(h, ffn, 256) (engine/src/ops_ref.cpp:228-241, model.cpp:219,424) then quantize_q8 of the result for the
+// down projection.  One warp per (token, 256-block); lane l holds elements [8 l, 8 l + 8).  Stage h pairs element j
+// with j + h inside each 2h-block as (a + c, a - c): stages 1, 2, 4 stay inside a lane, stages 8 .. 128 pair lane l
+// with lane l ^ (h / 8).  Every butterfly reads the previous stage's two values, so any order of the butterflies of a
+// stage gives the reference's bits; the final scale 1 / sqrt(256) = 1/16 is exact.
+__global__ void k_fwht_quant(const float* __restrict__ Hf, int n_tok, int ffn, int8_t* __restrict__ HQ,
+                             float* __restrict__ HD, float* __restrict__ HDT, int ldt) {
+    __shared__ __align__(16) float sv[kWarps][256];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long w = blockIdx.x * (long long)kWarps + warp;
+    const int nblk = ffn / 256;
+    if (w >= (long long)n_tok * nblk) return;
+    const int t = int(w / nblk), k = int(w - (long long)t * nblk);
+    const float4* src = reinterpret_cast<const float4*>(Hf + size_t(t) * ffn + size_t(k) * 256) + 2 * lane;
+    const float4 a0 = __ldcg(src), a1 = __ldcg(src + 1);
+    float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+    for (int h = 1; h < 8; h *= 2) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2 * h) {
+#pragma unroll
+            for (int j = i; j < i + h; ++j) {
+                const float a = v[j], c = v[j + h];
+                v[j] = fadd(a, c);
+                v[j + h] = fsub(a, c);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 1; m < 32; m *= 2) {  // stage h = 8 m
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
+            v[j] = upper ? fsub(o, v[j]) : fadd(v[j], o);
+        }
+    }
+    float* s = sv[warp];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[8 * lane + j] = fmul(v[j], 0.0625f);
+    __syncwarp();
+    const int nbk = ffn / QK;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {  // the eight 32-blocks of this 256-block
+        float d;
+        const int8_t q = quantize_lane(s[32 * b + lane], &d);
+        const int jb = k * 8 + b;
+        HQ[size_t(t) * ffn + jb * QK + lane] = q;
+        if (lane == 0) {
+            HD[size_t(t) * nbk + jb] = d;
+            if (HDT) HDT[size_t(jb) * ldt + t] = d;
+        }
     }
 }
 
@@ -413,7 +479,7 @@ bool gateup_rt_supported(const DMat& W, const SlicePlan& p, int nbo) {
 
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
                               int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl,
-                              const float* T, int nbo, float* X2) {
+                              const float* T, int nbo, float* X2, float* Hf) {
     cudaError_t e = cudaErrorInvalidValue;
     const int bpc = p.rows_per_cta / 64;
     if (T) {  // residual-terms form: clusters of 8
@@ -437,7 +503,7 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
         auto go = [&](auto kern) {
             cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
             if (r != cudaSuccess) return r;
-            return cudaLaunchKernelEx(&cfg, kern, W, X, norm_w, eps, HQ, HD, bpc, p.magic, tab, T, nbo, X2, xo);
+            return cudaLaunchKernelEx(&cfg, kern, W, X, norm_w, eps, HQ, HD, bpc, p.magic, tab, T, nbo, X2, xo, Hf);
         };
         if (W.dtype == DT_Q8_0) { QB_DISPATCH_U(p.u, e = go(k_gateup_dec<DT_Q8_0, UU, true>)); }
         else { QB_DISPATCH_U(p.u, e = go(k_gateup_dec<DT_Q4_0, UU, true>)); }
@@ -446,11 +512,11 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
     if (W.dtype == DT_Q8_0) {
         QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q8_0, UU, false>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X,
                                           norm_w, eps, HQ, HD, bpc, p.magic, tab, static_cast<const float*>(nullptr), 0,
-                                          static_cast<float*>(nullptr), 0));
+                                          static_cast<float*>(nullptr), 0, Hf));
     } else if (W.dtype == DT_Q4_0) {
         QB_DISPATCH_U(p.u, e = launch_pdl(k_gateup_dec<DT_Q4_0, UU, false>, dim3(p.grid), dim3(kThreads), p.smem, st, pdl, W, X,
                                           norm_w, eps, HQ, HD, bpc, p.magic, tab, static_cast<const float*>(nullptr), 0,
-                                          static_cast<float*>(nullptr), 0));
+                                          static_cast<float*>(nullptr), 0, Hf));
     }
     return e;
 }
@@ -473,10 +539,18 @@ cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t 
 }
 
 cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, const ExpTab& tab,
-                                cudaStream_t st, bool pdl) {
+                                cudaStream_t st, bool pdl, float* Hf) {
     const long long warps = (long long)n_tok * (ffn / QK);
     return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD,
-                      HDT, ldt, tab);
+                      HDT, ldt, tab, Hf);
+}
+
+cudaError_t launch_fwht_quant(const float* Hf, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, cudaStream_t st,
+                              bool pdl) {
+    if (ffn % 256 != 0) return cudaErrorInvalidValue;
+    const long long warps = (long long)n_tok * (ffn / 256);
+    return launch_pdl(k_fwht_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, Hf, n_tok, ffn, HQ, HD,
+                      HDT, ldt);
 }
 
 }  // namespace qb

@@ -60,7 +60,7 @@ cudaError_t launch_resid_dec(const DMat& W, const SlicePlan& p, const float* xin
                              float* X, cudaStream_t st, bool pdl, const float* Xres = nullptr);
 cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X, const float* norm_w, float eps,
                               int8_t* HQ, float* HD, const ExpTab& tab, cudaStream_t st, bool pdl,
-                              const float* T = nullptr, int nbo = 0, float* X2 = nullptr);
+                              const float* T = nullptr, int nbo = 0, float* X2 = nullptr, float* Hf = nullptr);
 // residual-terms form of gate|up (T != nullptr): clusters of 8 CTAs first form X2 = X + (o_proj terms T summed in block
 // order), the o_proj residual, then norm it; launched only where gateup_rt_supported.
 bool gateup_rt_supported(const DMat& W, const SlicePlan& p, int nbo);
@@ -82,6 +82,10 @@ cudaError_t launch_qkv_epilogue(const QkvArgs& a, const float* R, int n_tok, con
                                 bool pdl, TokMap tm = TokMap{});
 cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t st, bool pdl);
 cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, const ExpTab& tab,
-                                cudaStream_t st, bool pdl);
+                                cudaStream_t st, bool pdl, float* Hf = nullptr);
+// FLAG_HADAMARD_DOWN: the block-256 Walsh-Hadamard transform of Hf[n_tok][ffn] (ffn % 256 == 0), then its quantization
+// into HQ / HD (and HDT[b * ldt + t] when given) for the down projection.
+cudaError_t launch_fwht_quant(const float* Hf, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, cudaStream_t st,
+                              bool pdl);
 
 }  // namespace qb

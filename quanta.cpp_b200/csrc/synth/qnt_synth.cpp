@@ -341,7 +341,7 @@ int qnt_synth_write(const char* path, const qnt_synth_cfg* c) {
         put_f32(head, c->norm_eps);
         put_u32(head, 1);  // tied embeddings
         put_u32(head, 1);  // qkv bias
-        put_u32(head, 0);  // flags
+        put_u32(head, c->flags);
         const std::vector<uint8_t> tok = tokenizer_section(c->n_tokens > 0 ? c->n_tokens : c->vocab_size);
         put_u32(head, uint32_t(tok.size()));
         head.insert(head.end(), tok.begin(), tok.end());

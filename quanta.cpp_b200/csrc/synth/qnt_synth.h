@@ -16,6 +16,7 @@ typedef struct qnt_synth_cfg {
     float w_std;     // weight std (0 = 0.02)
     uint64_t seed;
     int n_threads;   // 0 = all hardware threads
+    unsigned flags;  // header flags (1 = FLAG_HADAMARD_DOWN: the reference transforms the SwiGLU output before down)
 } qnt_synth_cfg;
 
 int qnt_synth_write(const char* path, const qnt_synth_cfg* cfg);  // 0 on success

@@ -54,7 +54,7 @@ class GenStatsC(C.Structure):
 class SynthCfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in "vocab_size dim n_layers n_heads n_kv_heads head_dim ffn_dim max_seq".split()] + [
         ("rope_theta", C.c_float), ("norm_eps", C.c_float)] + [(n, C.c_int) for n in "mlp_q4 q4_group shortlist n_tokens".split()] + [
-        ("w_std", C.c_float), ("seed", C.c_uint64), ("n_threads", C.c_int)]
+        ("w_std", C.c_float), ("seed", C.c_uint64), ("n_threads", C.c_int), ("flags", C.c_uint32)]
 
 
 @dataclass
@@ -390,8 +390,9 @@ TINY = dict(vocab_size=5000, dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_
 
 
 def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: bool = True, q4_group: int = 128,
-                seed: int = 1234, w_std: float = 0.02, threads: int = 0, overwrite: bool = False) -> Path:
-    """Writes a seeded random-init .qnt (q4mix = attention Q8_0 + MLP GPTQ-sym int4; or all Q8_0)."""
+                seed: int = 1234, w_std: float = 0.02, threads: int = 0, overwrite: bool = False, flags: int = 0) -> Path:
+    """Writes a seeded random-init .qnt (q4mix = attention Q8_0 + MLP GPTQ-sym int4; or all Q8_0); flags = the header
+    flags (1: FLAG_HADAMARD_DOWN)."""
     global _synth
     path = Path(path)
     if path.exists() and not overwrite:
@@ -406,7 +407,7 @@ def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: 
     cfg = SynthCfg(**{k: shape[k] for k in ("vocab_size", "dim", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn_dim",
                                              "max_seq", "rope_theta", "norm_eps", "n_tokens")},
                    mlp_q4=int(mlp_q4), q4_group=q4_group, shortlist=int(shortlist), w_std=w_std, seed=seed,
-                   n_threads=threads)
+                   n_threads=threads, flags=flags)
     path.parent.mkdir(parents=True, exist_ok=True)
     tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
     if _synth.qnt_synth_write(str(tmp).encode(), C.byref(cfg)) != 0:

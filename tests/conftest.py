@@ -47,6 +47,7 @@ def models(qb):
             "tiny_q8": dict(shape=qb.TINY, mlp_q4=False, shortlist=True, seed=7),
             "tiny_q4sl": dict(shape=qb.TINY, mlp_q4=True, shortlist=True, seed=11),
             "tiny_long": dict(shape=dict(qb.TINY, max_seq=2048), mlp_q4=True, shortlist=True, seed=13),
+            "tiny_had": dict(shape=qb.TINY, mlp_q4=True, shortlist=True, seed=17, flags=1),  # FLAG_HADAMARD_DOWN
             "q8_0": dict(shape=qb.QWEN05B, mlp_q4=False, shortlist=False, seed=1234),
             "q4mix_sl": dict(shape=qb.QWEN05B, mlp_q4=True, shortlist=True, seed=1234),
         }

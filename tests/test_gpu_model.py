@@ -20,7 +20,7 @@ def rel_err(got, want):
 @pytest.fixture(scope="module")
 def tiny(qb, models):
     out = {}
-    for name in ("tiny_q8", "tiny_q4sl"):
+    for name in ("tiny_q8", "tiny_q4sl", "tiny_had"):
         out[name] = (qb.Model(models(name)), R.RefModel(models(name), threads=4))
     yield out
     for m, r in out.values():
@@ -28,7 +28,7 @@ def tiny(qb, models):
         r.close()
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl", "tiny_had"])
 def test_forward_logits_match_reference(tiny, name):
     m, r = tiny[name]
     rng = np.random.default_rng(5)
@@ -41,7 +41,7 @@ def test_forward_logits_match_reference(tiny, name):
         assert worst < TOL, (p, worst)
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl", "tiny_had"])
 def test_batched_prefill_equals_token_by_token(tiny, name):
     """check_batch (checks.cpp:148-176) on the device: maxdiff must be 0, incl. a second turn at pos0 > 0."""
     m, r = tiny[name]
@@ -108,7 +108,7 @@ def test_shortlist_head_exact(tiny, k):
         assert rel_err(coarse, rco) < TOL
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl", "tiny_had"])
 def test_greedy_ids_match_reference(tiny, name):
     m, r = tiny[name]
     rng = np.random.default_rng(8)

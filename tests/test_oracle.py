@@ -48,7 +48,7 @@ def test_restated_ops_bit_identical_to_reference():
 
 
 @need_ref
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4sl", "tiny_had"])
 def test_restated_model_bit_identical_to_reference(models, name):
     path = models(name)
     o = R.OracleModel(path)
