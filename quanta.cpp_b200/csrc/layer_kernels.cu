@@ -321,26 +321,41 @@ __global__ void k_residual(float* __restrict__ X, const float* __restrict__ R, l
 
 // R [n][2*ffn] raw interleaved gate|up -> SwiGLU -> quantize.  One warp per (token, ffn block).
 // Hf (files with FLAG_HADAMARD_DOWN): the f32 SwiGLU output goes to Hf[t][ffn] for k_fwht_quant instead.
+// One warp per (token, kSwiBlocks consecutive 32-blocks): the warp's gate and up loads are all issued before the
+// first SwiGLU, so each warp keeps several L2 requests in flight (one block per warp left it latency-bound).
+constexpr int kSwiBlocks = 4;
 __global__ void k_swiglu_quant(const float* __restrict__ R, int n_tok, int ffn, int8_t* __restrict__ HQ,
                                float* __restrict__ HD, float* __restrict__ HDT, int ldt, ExpTab tab, float* __restrict__ Hf) {
     pdl_wait();
     pdl_launch_dependents();
     const long long w = blockIdx.x * (long long)(blockDim.x / 32) + (threadIdx.x >> 5);
-    const int nbk = ffn / QK;
-    if (w >= (long long)n_tok * nbk) return;
-    const int t = int(w / nbk), j = int(w - (long long)t * nbk), lane = threadIdx.x & 31;
-    const float* r = R + size_t(t) * 2 * ffn + size_t(j) * 64;
-    const float h = swiglu1(__ldcg(r + lane), __ldcg(r + 32 + lane), tab);
-    if (Hf) {
-        Hf[size_t(t) * ffn + j * QK + lane] = h;
-        return;
+    const int nbk = ffn / QK, ngr = (nbk + kSwiBlocks - 1) / kSwiBlocks;
+    if (w >= (long long)n_tok * ngr) return;
+    const int t = int(w / ngr), j0 = int(w - (long long)t * ngr) * kSwiBlocks, lane = threadIdx.x & 31;
+    const float* r = R + size_t(t) * 2 * ffn;
+    float gv[kSwiBlocks], uv[kSwiBlocks];
+#pragma unroll
+    for (int k = 0; k < kSwiBlocks; ++k) {
+        const int j = j0 + k;
+        gv[k] = j < nbk ? __ldcg(r + size_t(j) * 64 + lane) : 0.f;
+        uv[k] = j < nbk ? __ldcg(r + size_t(j) * 64 + 32 + lane) : 0.f;
     }
-    float d;
-    const int8_t q = quantize_lane(h, &d);
-    HQ[size_t(t) * ffn + j * QK + lane] = q;
-    if (lane == 0) {
-        HD[size_t(t) * nbk + j] = d;
-        if (HDT) HDT[size_t(j) * ldt + t] = d;
+#pragma unroll
+    for (int k = 0; k < kSwiBlocks; ++k) {
+        const int j = j0 + k;  // uniform across the warp
+        if (j >= nbk) break;
+        const float h = swiglu1(gv[k], uv[k], tab);
+        if (Hf) {
+            Hf[size_t(t) * ffn + j * QK + lane] = h;
+            continue;
+        }
+        float d;
+        const int8_t q = quantize_lane(h, &d);
+        HQ[size_t(t) * ffn + j * QK + lane] = q;
+        if (lane == 0) {
+            HD[size_t(t) * nbk + j] = d;
+            if (HDT) HDT[size_t(j) * ldt + t] = d;
+        }
     }
 }
 
@@ -540,7 +555,7 @@ cudaError_t launch_residual(float* X, const float* R, long long n, cudaStream_t 
 
 cudaError_t launch_swiglu_quant(const float* R, int n_tok, int ffn, int8_t* HQ, float* HD, float* HDT, int ldt, const ExpTab& tab,
                                 cudaStream_t st, bool pdl, float* Hf) {
-    const long long warps = (long long)n_tok * (ffn / QK);
+    const long long warps = (long long)n_tok * ((ffn / QK + kSwiBlocks - 1) / kSwiBlocks);
     return launch_pdl(k_swiglu_quant, dim3(unsigned((warps + kWarps - 1) / kWarps)), dim3(kThreads), 0, st, pdl, R, n_tok, ffn, HQ, HD,
                       HDT, ldt, tab, Hf);
 }
