@@ -21,7 +21,9 @@
 //   4. with a quantized output requested, the CTAs post their outputs into the leader, which quantizes them.
 // Decode can also take the layer's q|k|v rows into the same launch (k_attn<8, UW>, launch_qkv_attn): each CTA first
 // computes 24 of its head's q / k / v rows (rmsnorm + quantize prologue, integer matvec, bias, RoPE) and the cluster
-// exchanges them through distributed shared memory, so the q|k|v kernel and its launch gap disappear.
+// exchanges them through distributed shared memory, so the q|k|v kernel and its launch gap disappear.  With o_proj
+// folded in as well (k_attn<8, UW, UO>), every CTA then quantizes the head's outputs and writes the o_proj block terms
+// of the head's two 32-blocks for an eighth of the rows; the gate|up kernel sums them onto the residual.
 // K rows and each CTA's V columns below the launch's first position were written by earlier launches, so they are
 // requested before the programmatic-launch wait (the first K tile into registers, the V columns by cp.async into
 // shared memory) and land while the previous kernel finishes; only this launch's own rows and the query wait.

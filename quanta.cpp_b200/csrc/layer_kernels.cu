@@ -1,12 +1,14 @@
 // Per-layer kernels of the Qwen2 forward (engine/src/model.cpp:165-228 decode, :363-433 prefill chunk).
 //
-// Decode (one token) runs five kernels per layer, each fusing its neighbours (four where the first two merge into
-// one, attention.cu's launch_qkv_attn):
+// Decode (one token) runs, in its separate form, five kernels per layer, each fusing its neighbours:
 //   k_qkv_dec     rmsnorm + quantize (prologue) -> fused q|k|v integer matvec -> bias + RoPE -> q, f16 K/V store
 //   k_attn        GQA attention over the f16 KV cache (attention.cu)
-//   k_o_dec       quantize(attn) -> o_proj matvec -> residual add
+//   k_resid_dec   quantize(attn) -> o_proj matvec -> residual add
 //   k_gateup_dec  rmsnorm + quantize -> gate|up matvec (rows interleaved per 32-block) -> SwiGLU -> quantize
-//   k_down_dec    down_proj matvec -> residual add
+//   k_resid_dec   down_proj matvec -> residual add
+// Where the shapes allow, the default is three: attention.cu's launch_qkv_attn takes q|k|v in front of the attention
+// and the o_proj block terms behind it, k_gateup_dec<.., RT = true> adds those terms onto the residual before its
+// norm, and k_resid_dec does down.  Files with FLAG_HADAMARD_DOWN add k_fwht_quant between gate|up and down.
 // Every kernel first loads its weight slice, then waits for the previous kernel (programmatic dependent launch), and
 // only then lets the next kernel launch: weight traffic overlaps the launch gap and the previous kernel's tail, and at
 // most one kernel ahead is resident, so early launches never fill the SMs with CTAs that cannot run yet.
