@@ -139,3 +139,15 @@ def test_bad_position_and_token(tiny):
     with pytest.raises(Exception):
         m.forward(m.vocab + 5, 0)
     m.forward(1, 0)  # the handle stays usable
+
+
+def test_hadamard_flag_needs_ffn_multiple_of_256(qb, tmp_path):
+    """The device refuses FLAG_HADAMARD_DOWN files whose ffn_dim is not a multiple of 256, with the reference's
+    condition (engine/src/model.cpp:39-42), and loads the same shape without the flag."""
+    bad = qb.synth_model(tmp_path / "had_bad.qnt", shape=dict(qb.TINY, ffn_dim=384), mlp_q4=False, shortlist=False,
+                         seed=5, flags=1)
+    with pytest.raises(qb.QntError, match="256"):
+        qb.Model(bad)
+    plain = qb.synth_model(tmp_path / "had_plain.qnt", shape=dict(qb.TINY, ffn_dim=384), mlp_q4=False, shortlist=False,
+                           seed=5, flags=0)
+    qb.Model(plain).close()

@@ -93,3 +93,18 @@ def test_golden_vectors():
         s = R.OracleSampler(**case["params"])
         got = [s.sample(z[case["logits"]][i], case["n_valid"], z[case["history"]]) for i in range(len(case["picks"]))]
         assert got == case["picks"], case["name"]
+
+
+@need_ref
+def test_hadamard_flag_needs_ffn_multiple_of_256(qb, tmp_path):
+    """FLAG_HADAMARD_DOWN with ffn_dim % 256 != 0 is refused at load by the reference (engine/src/model.cpp:39-42) and
+    by the restated oracle alike; with ffn_dim % 256 == 0 both load it."""
+    bad = qb.synth_model(tmp_path / "had_bad.qnt", shape=dict(qb.TINY, ffn_dim=384), mlp_q4=False, shortlist=False,
+                         seed=5, flags=1)
+    with pytest.raises(RuntimeError):
+        R.RefModel(bad, threads=1)
+    with pytest.raises(RuntimeError):
+        R.OracleModel(bad)
+    good = qb.synth_model(tmp_path / "had_ok.qnt", shape=qb.TINY, mlp_q4=False, shortlist=False, seed=5, flags=1)
+    R.RefModel(good, threads=1).close()
+    R.OracleModel(good).close()
