@@ -11,8 +11,8 @@ NEAR = 0.008  # kExpNearMidpoint
 
 def _old_not_new(exp_field, top):
     bad = 0
-    for c in range(32):
-        r = np.arange(c << 24, (c + 1) << 24, dtype=np.uint64)
+    for c in range(128):  # 2^22 values per step keeps the arrays to a few hundred MB
+        r = np.arange(c << 22, (c + 1) << 22, dtype=np.uint64)
         y = ((np.uint64(exp_field) << np.uint64(52)) | (np.uint64(top) << np.uint64(29)) | r).view(np.float64)
         f = y.astype(np.float32)
         df = f.astype(np.float64)
