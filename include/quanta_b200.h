@@ -191,11 +191,13 @@ void qnt_sampler_free(qnt_sampler* s);
  *           QNT_ERR_INVALID with the limit in qnt_last_error().
  *   Scratch: one static device array of 459,008 bytes per device (sampler state, candidate lists, history copy and
  *            penalty marks) plus a static 4 MiB copy of the host exp table.  The marks must be all zero when a call
- *            starts: they start zeroed and every completed call clears the ones it set.  Calls whose GPU work overlaps
- *            (other host threads, or other streams) share that scratch and race: serialise them.
+ *            starts: they start zeroed, every completed call clears the ones it set, and a call that fails after
+ *            setting them clears them (a stream-ordered memset) before it returns its error.  Calls whose GPU work
+ *            overlaps (other host threads, or other streams) share that scratch and race: serialise them.
  *   The first call on each device does the set-up, with that device current: cudaGetSymbolAddress of the scratch and
  *            of the table, and a synchronous copy of the exp table into it.  Make that first call before any stream
- *            capture.  The call waits for its stream and writes the id to *token. */
+ *            capture begins.  Every call copies its parameters and history through pageable host memory, waits for
+ *            its stream (cudaStreamSynchronize) and writes the id to *token. */
 int qnt_sampler_sample_noalloc(const qnt_sampler_params* sp, uint64_t* rng_state, float* logits, int n_valid,
                                const int* history, int n_history, int* token, void* stream);
 

@@ -258,13 +258,7 @@ int qnt_model_open(const char* path, int ctx_len, int flags, qnt_model** out) {
     if (!path || !out) return set_err(QNT_ERR_INVALID, "null argument");
     auto m = std::make_unique<qnt_model>();
     std::string err;
-    if (!m->eng.load(path, ctx_len, &err)) {
-        const bool io = err.find("open") != std::string::npos || err.find("magic") != std::string::npos ||
-                        err.find("truncated") != std::string::npos || err.find("bounds") != std::string::npos ||
-                        err.find("offset") != std::string::npos || err.find("version") != std::string::npos ||
-                        err.find("missing tensor") != std::string::npos || err.find("ndim") != std::string::npos;
-        return set_err(io ? QNT_ERR_IO : QNT_ERR_UNSUPPORTED, err);
-    }
+    if (!m->eng.load(path, ctx_len, &err)) return set_err(m->eng.file_fault() ? QNT_ERR_IO : QNT_ERR_UNSUPPORTED, err);
     *out = m.release();
     return QNT_OK;
 }

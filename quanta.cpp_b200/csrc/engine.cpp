@@ -129,7 +129,11 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         return false;
     };
     std::string e;
-    if (!file_.open(path, &e)) return bad(e);
+    file_fault_ = false;
+    if (!file_.open(path, &e)) {
+        file_fault_ = true;
+        return bad(e);
+    }
     hp_ = file_.hparams();
     if (hp_.n_heads * hp_.head_dim != hp_.dim || hp_.n_kv_heads <= 0 || hp_.n_heads % hp_.n_kv_heads != 0)
         return bad("unsupported head configuration");
@@ -152,10 +156,10 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     if (const char* v = std::getenv("QNT_FUSE_QKV")) fuse_qkv_attn_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_FUSE_O")) fuse_o_ = std::atoi(v) != 0;
     try {
-        const HostTensor& emb = file_.get("model.embed_tokens.weight");
+        const HostTensor& emb = file_.require("model.embed_tokens.weight");
         embed_ = upload_matrix(emb);
-        lm_head_ = hp_.tied_embeddings ? embed_ : upload_matrix(file_.get("lm_head.weight"));
-        const HostTensor& fn = file_.get("model.norm.weight");
+        lm_head_ = hp_.tied_embeddings ? embed_ : upload_matrix(file_.require("lm_head.weight"));
+        const HostTensor& fn = file_.require("model.norm.weight");
         auto upload_f32 = [&](const HostTensor& t) {
             if (t.dtype != DT_F32) throw std::runtime_error("norms and biases must be f32");
             void* p = dalloc(size_t(t.cols) * t.rows * 4);
@@ -203,19 +207,19 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         for (int l = 0; l < hp_.n_layers; ++l) {
             const std::string p = "model.layers." + std::to_string(l) + ".";
             Layer& L = layers_[size_t(l)];
-            L.attn_norm = upload_f32(file_.get(p + "input_layernorm.weight"));
-            L.ffn_norm = upload_f32(file_.get(p + "post_attention_layernorm.weight"));
-            const HostTensor &wq = file_.get(p + "self_attn.q_proj.weight"), &wk = file_.get(p + "self_attn.k_proj.weight"),
-                             &wv = file_.get(p + "self_attn.v_proj.weight");
+            L.attn_norm = upload_f32(file_.require(p + "input_layernorm.weight"));
+            L.ffn_norm = upload_f32(file_.require(p + "post_attention_layernorm.weight"));
+            const HostTensor &wq = file_.require(p + "self_attn.q_proj.weight"), &wk = file_.require(p + "self_attn.k_proj.weight"),
+                             &wv = file_.require(p + "self_attn.v_proj.weight");
             L.qkv = upload_fused({&wq, &wk, &wv}, 0);
-            L.o = upload_matrix(file_.get(p + "self_attn.o_proj.weight"));
-            L.gu = upload_fused({&file_.get(p + "mlp.gate_proj.weight"), &file_.get(p + "mlp.up_proj.weight")}, 1);
-            L.down = upload_matrix(file_.get(p + "mlp.down_proj.weight"));
+            L.o = upload_matrix(file_.require(p + "self_attn.o_proj.weight"));
+            L.gu = upload_fused({&file_.require(p + "mlp.gate_proj.weight"), &file_.require(p + "mlp.up_proj.weight")}, 1);
+            L.down = upload_matrix(file_.require(p + "mlp.down_proj.weight"));
             // fused bias in the q|k|v pair-interleaved order
             std::vector<float> b(size_t(L.qkv.rows), 0.f);
             if (hp_.qkv_bias) {
-                const HostTensor* bs[3] = {&file_.get(p + "self_attn.q_proj.bias"), &file_.get(p + "self_attn.k_proj.bias"),
-                                           &file_.get(p + "self_attn.v_proj.bias")};
+                const HostTensor* bs[3] = {&file_.require(p + "self_attn.q_proj.bias"), &file_.require(p + "self_attn.k_proj.bias"),
+                                           &file_.require(p + "self_attn.v_proj.bias")};
                 int fr = 0;
                 for (const HostTensor* t : bs) {
                     if (t->dtype != DT_F32) throw std::runtime_error("qkv biases must be f32");
@@ -338,6 +342,9 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         bcand_ = dalloc(size_t(argmax_parts(hp_.vocab_size)) * kChunk * sizeof(Cand));
         bids_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
         host_tmp_.resize(size_t(V));
+    } catch (const QntMissingTensor& ex) {
+        file_fault_ = true;
+        return bad(ex.what());
     } catch (const std::exception& ex) {
         return bad(ex.what());
     }

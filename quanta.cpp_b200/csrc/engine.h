@@ -92,6 +92,8 @@ public:
     // copies the tensor-core matmul reads beside the weights: stage-major block scales, int8 q - 8 of Q4_0 matrices
     size_t tc_copy_bytes() const { return tc_copy_bytes_; }
     const std::string& error() const { return err_; }
+    // the last load failed on the file itself (unreadable, malformed, or a tensor missing), not on the device
+    bool file_fault() const { return file_fault_; }
     void set_matmul_impl(int impl) { mm_impl_ = impl; }
     void set_use_graphs(bool on) { use_graphs_ = on; }
     void set_use_pdl(bool on) { pdl_ = on; }
@@ -144,6 +146,7 @@ private:
     HParams hp_;
     int ctx_ = 0, max_chunks_ = 0;
     std::string err_;
+    bool file_fault_ = false;
     cudaStream_t st_ = nullptr;
     bool pdl_ = true, use_graphs_ = true;
     bool fuse_qkv_attn_ = true;  // decode: q|k|v matvec fused into the attention kernel (QNT_FUSE_QKV=0: two kernels)

@@ -1,16 +1,44 @@
-// Host reader for the .qnt model format: mmap + header / tokenizer / tensor-table parse, zero-copy tensor views.
-// Mirrors the reference loader's checks (engine/src/model_file.cpp:149-211): magic "QNT1", version 1..2,
-// truncation and out-of-bounds tensors are errors, ndim must be 1 or 2.
+// Host side of the .qnt model format: the file is mapped read-only, its header, tokenizer section and tensor
+// directory are decoded and validated in one pass, and every tensor becomes a zero-copy view into the mapping that
+// the engine uploads to HBM once.
+//
+// Format (writer: scripts/export.py:1-13,290-315 of Quanta.cpp; the reference reader is engine/src/model_file.cpp):
+//   "QNT1" | u32 version (1 or 2) | hyper-parameters (u32/f32, `flags` from version 2 on)
+//   | u32 length + tokenizer section (tokens, merges, specials, three code-point range lists)
+//   | u32 tensor count + directory entries (name, dtype, rank, dims, u64 byte offset)
+//   tensor data: quants row-major, then one fp16 scale per 32 values for the block-quantized dtypes.
+// The checks are the format's own invariants: a known signature and version, every field inside the file, rank 1
+// or 2, a known dtype, quantized rows made of whole 32-value blocks, every tensor's bytes inside the file.  Each
+// failed check is reported as a QntFault with a message naming the field or tensor.
 #pragma once
 
+#include <array>
 #include <cstddef>
 #include <cstdint>
+#include <stdexcept>
 #include <string>
 #include <unordered_map>
 #include <utility>
 #include <vector>
 
 namespace qb {
+
+// Which invariant of the file failed (None: the file opened).
+enum class QntFault {
+    None = 0,
+    Open,       // the path cannot be opened, sized or mapped
+    Signature,  // the first four bytes are not "QNT1"
+    Version,    // format version outside 1..2
+    Header,     // the hyper-parameter block is cut short or holds a non-positive size
+    Tokenizer,  // the tokenizer section is cut short or inconsistent
+    Directory,  // a tensor directory entry is cut short, or a name repeats
+    Rank,       // a tensor of rank other than 1 or 2
+    DType,      // an unknown dtype code
+    BlockCols,  // a block-quantized tensor whose rows are not whole 32-value blocks
+    Extent,     // a tensor's bytes reach past the end of the file
+    Missing,    // a tensor the engine needs is not in the file
+};
+const char* qnt_fault_name(QntFault f);
 
 struct HostTensor {
     int dtype = 0;  // 0 f32, 1 f16, 2 q8_0, 3 q4_0 (engine/src/model_file.h:16)
@@ -28,10 +56,18 @@ struct HParams {
     uint32_t flags = 0;
 };
 
+// The tokenizer section, decoded (its meaning: engine/src/tokenizer.h:15-39).
 struct TokenizerInfo {
     int n_tokens = 0;
-    std::vector<std::string> tokens;                         // raw bytes per id
-    std::vector<std::pair<int, std::string>> specials;       // (id, text)
+    std::vector<std::string> tokens;                       // raw bytes per id
+    std::vector<std::array<uint32_t, 3>> merges;           // (left id, right id, merged id), highest priority first
+    std::vector<std::pair<int, std::string>> specials;     // (id, text)
+    std::vector<std::pair<uint32_t, uint32_t>> letters, numbers, spaces;  // inclusive code-point ranges
+};
+
+// Thrown by QntFile::require for a tensor the file does not hold.
+struct QntMissingTensor : std::runtime_error {
+    explicit QntMissingTensor(const std::string& name);
 };
 
 class QntFile {
@@ -41,21 +77,26 @@ public:
     QntFile(const QntFile&) = delete;
     QntFile& operator=(const QntFile&) = delete;
 
+    // Maps and validates the file.  On failure returns false, fault() names the check and *err the details.
     bool open(const std::string& path, std::string* err);
+    QntFault fault() const { return fault_; }
+
     const HParams& hparams() const { return hp_; }
     const TokenizerInfo& tokenizer() const { return tok_; }
     const HostTensor* find(const std::string& name) const;
-    const HostTensor& get(const std::string& name) const;  // throws std::runtime_error if missing
+    const HostTensor& require(const std::string& name) const;  // throws QntMissingTensor
     size_t size_bytes() const { return size_; }
+    size_t tensor_count() const { return tensors_.size(); }
     int special_id(const std::string& text) const;         // -1 if absent
 
 private:
-    void unmap();
+    void release();
     HParams hp_;
     TokenizerInfo tok_;
     std::unordered_map<std::string, HostTensor> tensors_;
-    const uint8_t* base_ = nullptr;
+    const uint8_t* map_ = nullptr;
     size_t size_ = 0;
+    QntFault fault_ = QntFault::None;
 };
 
 }  // namespace qb

@@ -105,14 +105,21 @@ extern "C" int qnt_sampler_sample_noalloc(const qnt_sampler_params* sp, uint64_t
     in.rng = *rng_state;
     e = cudaMemcpyAsync(ss, &in, sizeof in, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_err(e, "sampler state in");
+    // Once marks may have been set, a failure must not leave them behind for the next call: clear the ids this call
+    // could have marked (stream-ordered memset, no allocation) before reporting it.
+    auto fail_marked = [&](cudaError_t err, const char* what) {
+        cudaMemsetAsync(mark, 0, size_t(n_valid), st);
+        return cuda_err(err, what);
+    };
     if (penal) {
         e = cudaMemcpyAsync(hist, history, size_t(n_history) * 4, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = qb::launch_mark(hist, nullptr, n_history, sp->repeat_window, n_valid, mark, st, false);
-        if (e != cudaSuccess) return cuda_err(e, "sampler penalty marks");
+        if (e != cudaSuccess) return cuda_err(e, "sampler history copy");
+        e = qb::launch_mark(hist, nullptr, n_history, sp->repeat_window, n_valid, mark, st, false);
+        if (e != cudaSuccess) return fail_marked(e, "sampler penalty marks");
     }
     e = qb::launch_topk_partial(logits, n_valid, K, penal ? 1 : 0, sp->repeat_penalty, mark, lists, s.n_lists, st, false,
                                 logits);
-    if (e != cudaSuccess) return cuda_err(e, "sampler stage 1");
+    if (e != cudaSuccess) return penal ? fail_marked(e, "sampler stage 1") : cuda_err(e, "sampler stage 1");
     const qb::SamplerArgs sa{sp->temperature, sp->top_p, sp->min_p, sp->repeat_penalty, 0, qb::ExpTab{s.tab, s.mask}};
     e = qb::launch_sample_final(lists, s.n_lists, K, sa, ss, nullptr, 0, st, false);
     if (e != cudaSuccess) return cuda_err(e, "sampler stage 2");
