@@ -120,7 +120,7 @@ size_t qnt_model_weight_bytes(const qnt_model* m);
 /* SamplerParams (engine/src/sampler.h:9-18). */
 typedef struct qnt_sampler_params {
     float temperature; /* <= 0: greedy */
-    int top_k;         /* device sampler: 1..32 when temperature > 0 */
+    int top_k;         /* 0 = disabled (every candidate), as in the reference */
     float top_p, min_p;
     float repeat_penalty;
     int repeat_window; /* 0 = whole history */
@@ -169,7 +169,9 @@ int qnt_batch_reset(qnt_model* m, int seq);
  * memory -- repetition penalty -> greedy argmax (first max) or top-k -> softmax(T) -> min-p -> top-p -> xorshift64*
  * draw, with the reference's float operations, so the same logits, history and seed give the same ids.
  *   qnt_sampler_create  = Sampler(const SamplerParams&): the xorshift state starts at (seed ? seed : fixed) | 1, on the
- *                         current device; top_k must be 1..32 when temperature > 0 (QNT_ERR_UNSUPPORTED otherwise).
+ *                         current device.  Any top_k: up to 32 the candidates come from per-CTA lists; top_k 0 (disabled)
+ *                         or above 32 sorts every logit below n_valid on the device (scratch of 16 B per id, allocated
+ *                         on first use and kept by the sampler).
  *   qnt_sampler_sample  = Sampler::sample(float* logits, int n_valid, const std::vector<int>& history): `logits` is a
  *                         DEVICE array of at least n_valid floats and is edited in place like the reference's (the
  *                         penalised ids); `history` is a host array of n_history ids.  Work is queued on `stream`

@@ -13,11 +13,12 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF_SO = HERE / "_ref" / "libquanta_ref.so"
+REF_SO = HERE / "_ref" / "libquanta_ref.so"            # the checker: no FMA contraction
+STOCK_SO = HERE / "_ref" / "stock" / "libquanta_ref.so"  # the reference's own Release flags (the timed CPU baseline)
 ORACLE_SO = HERE / "_build" / "libqnt_oracle.so"
 QK = 32
 
-_ref = None
+_refs = {}
 _orc = None
 
 
@@ -25,17 +26,18 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
-def have_ref() -> bool:
-    return REF_SO.exists()
+def have_ref(stock: bool = False) -> bool:
+    return (STOCK_SO if stock else REF_SO).exists()
 
 
-def ref() -> C.CDLL:
-    """The reference engine (raises if oracle/_ref was not built)."""
-    global _ref
-    if _ref is None:
-        if not REF_SO.exists():
-            raise RuntimeError(f"{REF_SO} missing: `make -C oracle` (needs the reference sources)")
-        L = C.CDLL(str(REF_SO))
+def ref(stock: bool = False) -> C.CDLL:
+    """The reference engine (raises if oracle/_ref was not built).  stock: the build with the reference's own Release
+    flags (FMA contraction on) instead of the contraction-free checker."""
+    so = STOCK_SO if stock else REF_SO
+    if so not in _refs:
+        if not so.exists():
+            raise RuntimeError(f"{so} missing: `make -C oracle` (needs the reference sources)")
+        L = C.CDLL(str(so))
         P, I, F = C.c_void_p, C.c_int, C.c_float
         L.ref_model_open.argtypes = [C.c_char_p, I, I, I, C.c_char_p, I]
         L.ref_model_open.restype = P
@@ -59,8 +61,8 @@ def ref() -> C.CDLL:
                                    C.POINTER(C.c_double), C.POINTER(C.c_double)]
         L.ref_check_batch.argtypes = [P, P, I, I]
         L.ref_check_head.argtypes = [P, P, I]
-        _ref = L
-    return _ref
+        _refs[so] = L
+    return _refs[so]
 
 
 def quantize_q8(x: np.ndarray):
@@ -90,35 +92,37 @@ def matmul_q(dtype: int, rows: int, cols: int, raw: np.ndarray, q: np.ndarray, d
 
 
 class RefModel:
-    """quanta::Model of the reference (CPU)."""
+    """quanta::Model of the reference (CPU).  stock=True: the build with the reference's Release flags."""
 
-    def __init__(self, path, ctx: int = 0, threads: int = 0, kv_f16: bool = True):
+    def __init__(self, path, ctx: int = 0, threads: int = 0, kv_f16: bool = True, stock: bool = False):
+        self.L = ref(stock)
         err = C.create_string_buffer(512)
-        h = ref().ref_model_open(str(path).encode(), ctx, threads, int(kv_f16), err, 512)
+        h = self.L.ref_model_open(str(path).encode(), ctx, threads, int(kv_f16), err, 512)
         if not h:
             raise RuntimeError("reference load failed: " + err.value.decode())
         self.h = h
-        self.vocab = ref().ref_vocab(h)
-        self.n_tokens = ref().ref_n_tokens(h)
+        self.vocab = self.L.ref_vocab(h)
+        self.n_tokens = self.L.ref_n_tokens(h)
+        self.threads = self.L.ref_n_threads(h)
         self.out = np.zeros(self.vocab, np.float32)
 
     def close(self):
         if getattr(self, "h", None):
-            ref().ref_model_close(self.h)
+            self.L.ref_model_close(self.h)
             self.h = None
 
     __del__ = close
 
     def forward(self, token, pos, top_k=0, n_valid=0, must=None):
         m = np.ascontiguousarray(must if must is not None else np.zeros(0), np.int32)
-        if ref().ref_forward(self.h, int(token), int(pos), top_k, n_valid, _p(m), m.size, _p(self.out)) != 0:
+        if self.L.ref_forward(self.h, int(token), int(pos), top_k, n_valid, _p(m), m.size, _p(self.out)) != 0:
             raise IndexError("reference forward failed")
         return self.out.copy()
 
     def forward_batch(self, tokens, pos0, top_k=0, n_valid=0, must=None):
         t = np.ascontiguousarray(tokens, np.int32)
         m = np.ascontiguousarray(must if must is not None else np.zeros(0), np.int32)
-        if ref().ref_forward_batch(self.h, _p(t), t.size, int(pos0), top_k, n_valid, _p(m), m.size, _p(self.out)) != 0:
+        if self.L.ref_forward_batch(self.h, _p(t), t.size, int(pos0), top_k, n_valid, _p(m), m.size, _p(self.out)) != 0:
             raise IndexError("reference forward_batch failed")
         return self.out.copy()
 
@@ -126,21 +130,21 @@ class RefModel:
         m = np.ascontiguousarray(must if must is not None else np.zeros(0), np.int32)
         coarse = np.zeros(self.vocab, np.float32) if want_bounds else None
         upper = np.zeros(self.vocab, np.float32) if want_bounds else None
-        rows = ref().ref_head(self.h, top_k, n_valid, _p(m), m.size, _p(self.out), _p(coarse), _p(upper))
+        rows = self.L.ref_head(self.h, top_k, n_valid, _p(m), m.size, _p(self.out), _p(coarse), _p(upper))
         if want_bounds:
             return self.out.copy(), coarse, upper, rows
         return self.out.copy()
 
     @property
     def last_head_rows(self):
-        return ref().ref_last_head_rows(self.h)
+        return self.L.ref_last_head_rows(self.h)
 
     def generate(self, prompt, n_gen, temperature=0.7, top_k=20, top_p=0.8, min_p=0.0, repeat_penalty=1.1, seed=1234,
                  batch_prefill=True, shortlist=True):
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max(n_gen, 1), np.int32)
         tp, td, hf = C.c_double(), C.c_double(), C.c_double()
-        n = ref().ref_generate(self.h, _p(p), p.size, int(batch_prefill), int(shortlist), temperature, top_k, top_p, min_p,
+        n = self.L.ref_generate(self.h, _p(p), p.size, int(batch_prefill), int(shortlist), temperature, top_k, top_p, min_p,
                                repeat_penalty, seed, n_gen, _p(out), C.byref(tp), C.byref(td), C.byref(hf))
         if n < 0:
             raise RuntimeError("reference generate failed")

@@ -333,6 +333,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         cudaMemset(ss_, 0, sizeof(SamplerState));
         hist_ = static_cast<int*>(dalloc(size_t(ctx_ + 1) * 4));
         part_buf_ = dalloc(size_t(n_lists_) * 32 * sizeof(Cand));
+        wide_ = wide_scratch_carve(dalloc(wide_scratch_bytes(V)), V);
         status_ = static_cast<unsigned*>(dalloc(16));
         cudaMemset(status_, 0, 16);
         tok_pos_ = static_cast<int*>(dalloc(size_t(kChunk) * 4));
@@ -680,22 +681,20 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
         return -5;
     }
     const bool greedy = sp.temperature <= 0.f;
+    // top_k <= 0 (disabled) or above the 32 candidates of the fused head lists: the sorting sampler
+    const bool wide = !greedy && (sp.top_k <= 0 || sp.top_k > 32);
     const int K = greedy ? 1 : sp.top_k;
-    if (K < 1 || K > 32) {
-        err_ = "device sampler supports 1 <= top_k <= 32";
-        return -4;
-    }
     const int nv = n_valid_default();
-    const bool sl = use_shortlist && has_shortlist();
-    if (sl && K + 8 > 32) {
-        err_ = "shortlist head supports top_k <= 24";
-        return -4;
-    }
+    // Session::head_query (session.cpp:63-79) uses the shortlist with k = top_k, and the full head when k <= 0.  The
+    // device shortlist keeps k + 8 <= 32 seeds; above that the full head gives the same exact top-k logits, so the
+    // sampled ids do not change (only the count of exact rows does).
+    const bool sl = use_shortlist && has_shortlist() && !wide && K + 8 <= 32;
     const bool penal = sp.repeat_penalty != 1.0f;
     sess_ = Sess{};
     sess_.active = false;
     sess_.sp = sp;
     sess_.sl = sl;
+    sess_.wide = wide;
     sess_.K = K;
     sess_.nv = nv;
     sess_.penal = penal;
@@ -733,9 +732,12 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
         }
     }
     cudaMemcpyAsync(ss_, &st, sizeof st, cudaMemcpyHostToDevice, st_);  // forward() used token/pos
-    // sampler stage-1 lists of the prompt's logits (the decode steps get theirs from the fused head)
-    if (penal) QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, false));
-    QB_TRY(launch_topk_partial(logits_, nv, K, penal ? 1 : 0, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, false));
+    // sampler stage-1 lists of the prompt's logits (the decode steps get theirs from the fused head); the sorting
+    // sampler starts every step from the logits themselves
+    if (!wide) {
+        if (penal) QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, false));
+        QB_TRY(launch_topk_partial(logits_, nv, K, penal ? 1 : 0, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, false));
+    }
     if (int rr = sync_check()) return rr;
     sess_.active = true;
     sess_.steps = 0;
@@ -754,12 +756,33 @@ int Engine::session_step(int n) {
     const SamplerArgs sa{sp.temperature, sp.top_p, sp.min_p, sp.repeat_penalty, 1, exptab_};
     const bool sl = sess_.sl, penal = sess_.penal;
     const int K = sess_.K, nv = sess_.nv, V = hp_.vocab_size;
-    const std::string key = "gen|" + std::to_string(sl) + "|" + std::to_string(K) + "|" + std::to_string(penal) + "|" +
-                            std::to_string(sp.repeat_window) + "|" + std::to_string(sp.temperature) + "|" +
-                            std::to_string(sp.top_p) + "|" + std::to_string(sp.min_p) + "|" + std::to_string(sp.repeat_penalty);
+    const bool wide = sess_.wide;
+    const std::string key = "gen|" + std::to_string(sl) + "|" + std::to_string(wide) + "|" + std::to_string(K) + "|" +
+                            std::to_string(penal) + "|" + std::to_string(sp.repeat_window) + "|" +
+                            std::to_string(sp.temperature) + "|" + std::to_string(sp.top_p) + "|" + std::to_string(sp.min_p) +
+                            "|" + std::to_string(sp.repeat_penalty);
     for (int s = 0; s < n; ++s) {
         const int r = run_graph(key, [&]() -> int {
             const int c0 = kernel_count_;
+            if (wide) {
+                // Sampler::sample over the whole logits: the penalty in place on the unique history ids, then the
+                // sorting sampler; the head below only writes logits
+                if (penal) {
+                    QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, pdl_));
+                    QB_TRY(launch_topk_partial(logits_, nv, 1, 1, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, pdl_,
+                                               logits_));
+                }
+                int extra = 0;
+                const cudaError_t e = launch_sample_wide(logits_, nv, K, sa, ss_, hist_, ctx_, wide_, st_, pdl_, &extra);
+                kernel_count_ += extra;
+                if (e != cudaSuccess) return cuda_fail(e, "launch_sample_wide");
+                QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
+                if (int rr = launch_layers_decode(&ss_->pos)) return rr;
+                QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, V, st_, pdl_));
+                const int rr = launch_head(false, 1, nv, nullptr, nullptr, 0, 0, 0, false, 1.0f);
+                kernels_per_step_ = kernel_count_ - c0;
+                return rr;
+            }
             QB_TRY(launch_sample_final(part_buf_, n_lists_, K, sa, ss_, hist_, ctx_, st_, pdl_));
             QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
             if (int rr = launch_layers_decode(&ss_->pos)) return rr;

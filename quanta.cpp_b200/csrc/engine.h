@@ -195,10 +195,11 @@ private:
     SamplerState* ss_ = nullptr;
     int* hist_ = nullptr;
     void* part_buf_ = nullptr;
+    WideScratch wide_{};  // the sorting sampler's scratch (top_k 0 or > 32)
     unsigned* status_ = nullptr;
 
     struct Sess {
-        bool active = false, sl = false, penal = false;
+        bool active = false, sl = false, penal = false, wide = false;
         int K = 1, nv = 0, n_prompt = 0, steps = 0;
         SamplerParamsC sp;
     } sess_;

@@ -107,4 +107,20 @@ cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int pen
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
                                 int hist_cap, cudaStream_t st, bool pdl);
 
+// The sampler for any top_k (sampler_wide.cu): top_k <= 0 (every candidate) or top_k > 32.  A stable radix sort of
+// (logit, id) over ids < n_valid, then the softmax / min-p / top-p / draw of the n best on one CTA.  Temperature > 0
+// only (greedy takes the argmax path).  Scratch: 4 arrays of n_valid words and a digit histogram.
+struct WideScratch {
+    unsigned* keys[2];
+    int* ids[2];
+    unsigned* hist;
+    int cap;  // largest n_valid the scratch holds
+};
+int wide_sort_tiles(int n_valid);
+size_t wide_scratch_bytes(int n_valid);
+WideScratch wide_scratch_carve(void* base, int n_valid);  // base: wide_scratch_bytes(n_valid) bytes, 256-byte aligned
+// Launches 13 kernels (adds 13 to *kernels).  logits: already penalised.
+cudaError_t launch_sample_wide(const float* logits, int n_valid, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
+                               int hist_cap, const WideScratch& ws, cudaStream_t st, bool pdl, int* kernels);
+
 }  // namespace qb

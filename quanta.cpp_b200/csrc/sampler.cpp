@@ -51,12 +51,15 @@ struct qnt_sampler {
     int mark_cap = 0;
     int* hist = nullptr;             // device copy of the history
     int hist_cap = 0;
+    void* wide_buf = nullptr;        // the sorting sampler's scratch (top_k 0 or > 32), grown to n_valid
+    qb::WideScratch wide{};
 
     ~qnt_sampler() {
         cudaFree(ss);
         cudaFree(lists);
         cudaFree(mark);
         cudaFree(hist);
+        cudaFree(wide_buf);
     }
 };
 
@@ -66,8 +69,6 @@ int qnt_sampler_create(const qnt_sampler_params* sp, qnt_sampler** out) {
     using namespace qnt_capi;
     if (!sp || !out) return set_err(QNT_ERR_INVALID, "qnt_sampler_create: null argument");
     *out = nullptr;
-    if (sp->temperature > 0.f && (sp->top_k < 1 || sp->top_k > 32))
-        return set_err(QNT_ERR_UNSUPPORTED, "device sampler supports 1 <= top_k <= 32 when temperature > 0");
     auto s = std::make_unique<qnt_sampler>();
     s->p = *sp;
     cudaError_t e = cudaGetDevice(&s->device);
@@ -99,9 +100,19 @@ int qnt_sampler_sample(qnt_sampler* s, float* logits, int n_valid, const int* hi
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const qnt_sampler_params& p = s->p;
     const bool greedy = p.temperature <= 0.f;
-    const int K = greedy ? 1 : std::min(p.top_k, n_valid);  // top_k >= n_valid keeps every id (sampler.cpp:45-50)
+    // top_k <= 0 keeps every id, as does top_k >= n_valid (sampler.cpp:45-50); beyond 32 the sorting sampler runs
+    const bool wide = !greedy && (p.top_k <= 0 || p.top_k > 32);
+    const int K = greedy ? 1 : wide ? 1 : std::min(p.top_k, n_valid);
     const bool penal = p.repeat_penalty != 1.0f && n_history > 0;
     cudaError_t e = cudaSuccess;
+    if (wide && s->wide.cap < n_valid) {
+        cudaFree(s->wide_buf);
+        s->wide_buf = nullptr;
+        s->wide.cap = 0;
+        e = cudaMalloc(&s->wide_buf, qb::wide_scratch_bytes(n_valid));
+        if (e != cudaSuccess) return cuda_err(e, "sampler sort scratch");
+        s->wide = qb::wide_scratch_carve(s->wide_buf, n_valid);
+    }
     if (penal) {
         if (s->mark_cap < n_valid) {
             cudaFree(s->mark);
@@ -124,11 +135,15 @@ int qnt_sampler_sample(qnt_sampler* s, float* logits, int n_valid, const int* hi
         if (e == cudaSuccess) e = qb::launch_mark(s->hist, nullptr, n_history, p.repeat_window, n_valid, s->mark, st, false);
         if (e != cudaSuccess) return cuda_err(e, "sampler penalty marks");
     }
-    e = qb::launch_topk_partial(logits, n_valid, K, penal ? 1 : 0, p.repeat_penalty, s->mark, s->lists, s->n_lists, st, false,
-                                logits);
-    if (e != cudaSuccess) return cuda_err(e, "sampler stage 1");
+    // stage 1: the penalty written back into the logits (and, for the list sampler, each CTA's best K)
+    if (!wide || penal) {
+        e = qb::launch_topk_partial(logits, n_valid, K, penal ? 1 : 0, p.repeat_penalty, s->mark, s->lists, s->n_lists, st,
+                                    false, logits);
+        if (e != cudaSuccess) return cuda_err(e, "sampler stage 1");
+    }
     const qb::SamplerArgs sa{p.temperature, p.top_p, p.min_p, p.repeat_penalty, 0, s->tab};
-    e = qb::launch_sample_final(s->lists, s->n_lists, K, sa, s->ss, nullptr, 0, st, false);
+    e = wide ? qb::launch_sample_wide(logits, n_valid, p.top_k, sa, s->ss, nullptr, 0, s->wide, st, false, nullptr)
+             : qb::launch_sample_final(s->lists, s->n_lists, K, sa, s->ss, nullptr, 0, st, false);
     if (e != cudaSuccess) return cuda_err(e, "sampler stage 2");
     int tok = -1;
     e = cudaMemcpyAsync(&tok, &s->ss->token, 4, cudaMemcpyDeviceToHost, st);

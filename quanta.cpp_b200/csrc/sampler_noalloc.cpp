@@ -86,7 +86,7 @@ extern "C" int qnt_sampler_sample_noalloc(const qnt_sampler_params* sp, uint64_t
         return set_err(QNT_ERR_INVALID, "qnt_sampler_sample_noalloc: n_history " + std::to_string(n_history) +
                                             " exceeds the no-alloc maximum of " + std::to_string(kMaxHistory));
     if (sp->temperature > 0.f && (sp->top_k < 1 || sp->top_k > kListLen))
-        return set_err(QNT_ERR_UNSUPPORTED, "device sampler supports 1 <= top_k <= 32 when temperature > 0");
+        return set_err(QNT_ERR_UNSUPPORTED, "the no-alloc sampler supports 1 <= top_k <= 32 when temperature > 0 (qnt_sampler_sample takes any top_k)");
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");

@@ -120,6 +120,19 @@ def test_greedy_ids_match_reference(tiny, name):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("top_k", [0, 40, 24, 28])
+def test_sampled_ids_match_reference_any_top_k(tiny, qb, top_k):
+    """Session::generate with sampling, against the reference, for top_k values around the device's limits: 0
+    (disabled) and 40 run the sorting sampler; 24 keeps the shortlist (k + 8 seeds = 32); 28 uses the full head."""
+    m, r = tiny["tiny_q4sl"]
+    prompt = np.random.default_rng(12).integers(0, m.hp.n_tokens, 30)
+    sp = qb.SamplerParams(temperature=0.9, top_k=top_k, top_p=0.9, repeat_penalty=1.1, seed=321)
+    got, _ = m.generate(prompt, sp, 40, shortlist=True, batch_prefill=True)
+    want, _ = r.generate(prompt, 40, temperature=0.9, top_k=top_k, top_p=0.9, repeat_penalty=1.1, seed=321,
+                         batch_prefill=True, shortlist=True)
+    assert np.array_equal(got, want)
+
+
 def test_sampled_shortlist_equals_full_head(tiny, qb):
     """bench's `decode output identical (full vs shortlist)` (checks.cpp:371-373) with Qwen defaults, seed 1234."""
     m, _ = tiny["tiny_q4sl"]
