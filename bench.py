@@ -1,16 +1,26 @@
 """Benchmark of the quantized-transformer hot path on B200 (one process per GPU).
 
-Workload (the metric's b=1 case): random-init Qwen2.5-0.5B q4mix (attention Q8_0, MLP GPTQ-sym int4
-g128) with the Exact Shortlist Head; 512 uniform-random prompt ids; decode at temperature 0.7, top-k 20, top-p 0.8,
-repetition penalty 1.1 (the reference's SamplerParams defaults), fixed seed.  One step = one decode token on the
-device: sample -> append -> 24-layer forward -> shortlist head (one CUDA-graph replay).  With N GPUs every rank
+Headline workload (the metric's b=1 case): random-init Qwen2.5-0.5B q4mix (attention Q8_0, MLP
+GPTQ-sym int4 g128) with the Exact Shortlist Head; 512 uniform-random prompt ids; decode at temperature 0.7, top-k 20,
+top-p 0.8, repetition penalty 1.1 (the reference's SamplerParams defaults), fixed seed.  One step = one decode token on
+the device: sample -> append -> 24-layer forward -> shortlist head (one CUDA-graph replay).  With N GPUs every rank
 decodes its own sequence (independent sequences, no data-path collective: weak scaling).
+
+Beside it, on the same line:
+  config5_job  BASELINE config 5 as a job: 2048 sequences x (512-token prompt + 128 greedy tokens) split over the N
+               ranks, 256 sequences per GPU per wave, through qnt_prefill_batch / qnt_decode_batch with host ids
+               (strong scaling: the job is fixed, N divides it);
+  head_shard   the vocab-sharded head's per-GPU work measured on one GPU: the batched head matmul at V rows x 256
+               tokens against V/s rows x 256 s tokens (what each of s GPUs would run after gathering every
+               sequence's hidden state);
+  tc_matmul    the tensor-core int8 matmul alone on the gate|up shape, against the measured int8 MMA peak.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Prints one JSON line (rank 0).  `value` = decode tok/s over all ranks, timed with CUDA events on the model's stream
-(max over ranks).  `e2e` = the same workload through the public C ABI call qnt_generate with host buffers
-(prompt in, ids out) timed by the host clock, prefill included.
+(max over ranks).  `e2e` = the same workload through the public C ABI call qnt_generate with host buffers (prompt in,
+ids out) timed by the host clock, prefill included.  `--impl reference` times the reference's own CPU engine (its
+Release build, oracle/_ref/stock) on the host cores, on the same workload.
 """
 import argparse
 import ctypes as C
@@ -34,11 +44,12 @@ MODEL_DIR = Path(os.environ.get("QNT_MODEL_DIR", "/tmp/qnt_models"))
 PROMPT = 512
 SEED = 1234
 METRIC = "decode tok/s (q4mix 0.5B + shortlist head, b=1)"
+WORKLOAD = "config4: q4mix 0.5B + shortlist, 512-token prompt, b=1 decode, T=0.7 k=20 p=0.8 rp=1.1"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
+JOB_SEQS, JOB_WAVE, JOB_GEN = 2048, 256, 128
 
-
-# DRAM bytes of one decode step of this workload, summed over its launches from one ncu capture (the command and the
-# per-kernel table are in profiles/decode_step_traffic_q4mix_sl.md)
+# DRAM bytes of one decode step of this workload: dram__bytes_read.sum + dram__bytes_write.sum summed over the step's
+# launches in one ncu capture of this command
 STEP_TRAFFIC_BYTES = 339_039_744
 
 
@@ -46,48 +57,80 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+def gpu_selector(local_rank: int) -> str:
+    """nvidia-smi's -i argument for the GPU this process drives (its PCI address: robust to CUDA_VISIBLE_DEVICES)."""
+    try:
+        import torch
+        p = torch.cuda.get_device_properties(local_rank)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:
+        return str(local_rank)
+
+
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi samples (every 50 ms) for the whole run; summary(t0, t1) reports the samples taken between two host
+    times.  The sampler is started before the model loads and waited for before the first timed region, so short
+    timed regions still get samples."""
 
-    def __init__(self, gpu: int):
-        self.gpu, self.rows, self.proc = gpu, [], None
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+    def __init__(self, selector: str):
+        self.sel, self.rows, self.proc, self.err = selector, [], None, None
+
+    def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.sel, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError as e:
+            self.err = str(e)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 7:
-                self.rows.append(parts)
+                self.rows.append((time.monotonic(), parts))
 
-    def __exit__(self, *a):
+    def wait_ready(self, timeout=15.0):
+        t0 = time.monotonic()
+        while not self.rows and self.proc and self.proc.poll() is None and time.monotonic() - t0 < timeout:
+            time.sleep(0.05)
+
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            if not self.rows and self.proc.stderr:
+                self.err = (self.proc.stderr.read() or "").strip()[:200] or f"nvidia-smi exited {self.proc.returncode}"
 
-    def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
+    def summary(self, t0, t1):
+        rows = [r for t, r in self.rows if t0 <= t <= t1]
+        if not rows and self.rows:  # a region shorter than the sampling period: the samples around it
+            near = sorted(self.rows, key=lambda tr: min(abs(tr[0] - t0), abs(tr[0] - t1)))[:2]
+            rows = [r for _, r in near]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"no nvidia-smi samples ({self.err or 'none'})"]}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[0]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[1]) for r in rows) if v is not None]
+        pw = [v for v in (num(r[2]) for r in rows) if v is not None]
+        reasons = sorted({self.NAMES[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "power_w_max": max(pw) if pw else None, "reasons": reasons, "samples": len(rows)}
 
 
 def peaks():
@@ -98,12 +141,23 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def tc_matmul_measure(tokens, iters=20):
+def int8_peak(qb):
+    """Dense int8 tensor-core peak of this GPU, measured by qnt_bench_mma_i8 (back-to-back tcgen05.mma.kind::i8 on every
+    SM); falls back to 2 x the measured bf16 rate when the library lacks the probe."""
+    try:
+        tops = qb.bench_mma_i8()
+        return tops, "measured (tcgen05.mma.kind::i8 issue loop, all SMs)"
+    except Exception as e:  # noqa: BLE001
+        try:
+            return 2 * json.loads(PEAKS.read_text())["bf16_tflops"], f"2 x measured bf16 ({e})"
+        except Exception:
+            return 2 * 1590.0, "fallback (2 x bf16 dense)"
+
+
+def tc_matmul_measure(qb, tokens, peak, peak_kind, iters=20):
     """The tensor-core int8 matmul alone on the gate|up shape (9728 x 896, GPTQ-style Q4 weights, their int8 copy L2
-    resident) at `tokens` tokens, through qnt_matmul(impl=2) with device buffers: CUDA-event time per call and the
-    int8 rate against twice the measured dense bf16 rate (int8 dense peak = 2 x bf16 on this GPU)."""
+    resident) at `tokens` tokens, through qnt_matmul(impl=2) with device buffers: CUDA-event time per call."""
     import torch
-    import quanta_b200 as qb
     rows, cols = 9728, 896
     rng = np.random.default_rng(SEED + 11)
     qi = (rng.integers(-8, 8, (rows, cols)) + 8).astype(np.uint8).reshape(-1, 32)
@@ -130,15 +184,49 @@ def tc_matmul_measure(tokens, iters=20):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / iters
     tops = 2.0 * rows * cols * tokens / (us * 1e-6) / 1e12
-    try:
-        bf16 = json.loads(PEAKS.read_text())["bf16_tflops"]
-        peak, kind = 2 * bf16, "measured (2 x bf16 dense)"
-    except Exception:
-        peak, kind = 2 * 1590.0, "fallback (2 x bf16 dense)"
     W.close()
     return {"shape": f"{rows}x{cols} Q4 (gate|up) x {tokens} tokens", "us_per_call": round(us, 2),
             "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s", "frac": round(tops / peak, 4),
-            "peak_kind": kind, "bound": "epilogue: three rounded f32 ops per (row, token, 32-block)"}
+            "peak_kind": peak_kind, "bound": "epilogue: three rounded f32 ops per (row, token, 32-block)"}
+
+
+def head_shard_measure(qb, shards=(1, 2, 4, 8), batch=256, iters=5):
+    """Per-GPU work of a vocab-sharded batched head, on one GPU: the head matmul (Q8_0 151936 x 896) over V/s rows for
+    s * batch tokens -- each of s GPUs' share after an all-gather of every sequence's hidden state -- against the
+    unsharded V rows x batch tokens.  CUDA-event time per call (logits written, as the head's exact pass does)."""
+    import torch
+    V, D = 151936, 896
+    rng = np.random.default_rng(SEED + 13)
+    q = rng.integers(-127, 128, (V, D), dtype=np.int8)
+    d = (0.02 / 64 * rng.uniform(0.5, 1.5, (V, D // 32))).astype(np.float16)
+    W = qb.DeviceTensor(2, V, D, np.concatenate([q.view(np.uint8).ravel(), d.view(np.uint8).ravel()]))
+    L = qb.lib()
+    st = torch.cuda.current_stream()
+    sp = C.c_void_p(st.cuda_stream)
+    res = []
+    for s in shards:
+        rows, toks = V // s, batch * s
+        x = torch.randn(toks, D, device="cuda")
+        qx = torch.empty(toks, D, dtype=torch.int8, device="cuda")
+        dx = torch.empty(toks, D // 32, device="cuda")
+        out = torch.empty(toks, rows, device="cuda")
+        qb._check(L.qnt_quantize_q8(C.c_void_p(x.data_ptr()), toks, D, C.c_void_p(qx.data_ptr()), C.c_void_p(dx.data_ptr()), sp))
+        call = lambda: qb._check(L.qnt_matmul(W.h, C.c_void_p(qx.data_ptr()), C.c_void_p(dx.data_ptr()), toks, 0, rows,
+                                              C.c_void_p(out.data_ptr()), rows, 2, sp))
+        call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(iters):
+            call()
+        e1.record(st)
+        torch.cuda.synchronize()
+        res.append({"gpus": s, "rows": rows, "tokens": toks, "us": round(e0.elapsed_time(e1) * 1e3 / iters, 1)})
+        del x, qx, dx, out
+    W.close()
+    base = res[0]["us"]
+    return {"what": "batched head matmul per GPU: V/s rows x 256*s tokens (vocab-sharded over s GPUs) vs V x 256",
+            "shards": res, "per_gpu_ratio": [round(r["us"] / base, 3) for r in res],
+            "note": "the sharded head would add two all-gathers (hidden states, then per-shard candidates) on top"}
 
 
 def model_path():
@@ -150,41 +238,125 @@ def prompt_ids(rank, n_tokens):
     return np.random.default_rng(dp.rank_seed(SEED, rank)).integers(0, n_tokens, PROMPT).astype(np.int32)
 
 
-def cpu_baseline(path, steps):
-    """The reference's own CPU path (oracle/_ref) on this host's cores, bounded sample: 512-token prefill then `steps`
-    decode tokens with the same sampler, timed by the reference's Session (engine/src/session.cpp:33-52)."""
+def host_cpu():
+    """CPU model, logical CPUs and physical cores of this host (from /proc/cpuinfo)."""
+    model, cores = "unknown", set()
+    try:
+        phys = core = None
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "model name":
+                model = v
+            elif k == "physical id":
+                phys = v
+            elif k == "core id":
+                core = v
+                cores.add((phys, core))
+    except OSError:
+        pass
+    logical = os.cpu_count() or 1
+    return model, logical, len(cores) or logical
+
+
+def cpu_reference_decode(path, n_tokens, steps, threads):
+    """The reference's Release build (oracle/_ref/stock) on this host: 512-token prefill, then `steps` decode tokens
+    of the config-4 sampler through Session::generate (engine/src/session.cpp:33-52), timed by the reference itself."""
     import ref as R
-    threads = os.cpu_count() or 1
-    if R.have_ref():
-        r = R.RefModel(path, ctx=4096, threads=threads)
-        kind = "reference"
-    else:
-        return None
-    ids, st = r.generate(prompt_ids(0, r.n_tokens), steps, temperature=0.7, top_k=20, top_p=0.8, repeat_penalty=1.1,
+    r = R.RefModel(path, ctx=4096, threads=threads, stock=True)
+    used = r.threads
+    ids, st = r.generate(prompt_ids(0, n_tokens), steps, temperature=0.7, top_k=20, top_p=0.8, repeat_penalty=1.1,
                          seed=SEED, batch_prefill=True, shortlist=True)
     r.close()
-    return {"value": round(len(ids) / st["decode_s"], 3), "unit": "tok/s", "cores": threads, "kind": kind,
-            "sample": f"512-token prompt prefilled ({st['prefill_s']:.1f} s, untimed) then {len(ids)} decode tokens",
-            "prefill_tok_s": round(PROMPT / st["prefill_s"], 2), "head_fraction": round(st["head_fraction"], 4)}
+    return {"threads": used, "decode_tok_s": round(len(ids) / st["decode_s"], 3),
+            "prefill_tok_s": round(PROMPT / st["prefill_s"], 2), "head_fraction": round(st["head_fraction"], 4),
+            "tokens": len(ids)}
+
+
+def cpu_baseline(path, n_tokens, steps):
+    """Both thread counts the reference is run with: its default min(8, hw/2) (engine/src/threadpool.cpp:21-25) and the
+    host's physical cores; `value` is the faster."""
+    import ref as R
+    if not R.have_ref(stock=True):
+        return None
+    model, logical, physical = host_cpu()
+    runs = [cpu_reference_decode(path, n_tokens, steps, t) for t in sorted({0, physical})]
+    best = max(runs, key=lambda r: r["decode_tok_s"])
+    return {"value": best["decode_tok_s"], "unit": "tok/s", "cores": best["threads"], "kind": "reference",
+            "build": "reference Release flags (-O3 -DNDEBUG, FMA contraction on), oracle/_ref/stock",
+            "sample": f"512-token prompt prefilled (untimed) then {steps} decode tokens per thread count",
+            "cpu": model, "logical_cpus": logical, "physical_cores": physical, "runs": runs}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    import quanta_b200 as qb  # noqa: F401  (only for the synthetic model writer)
     import ref as R
-    path = model_path()
-    if not R.have_ref():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libquanta_ref.so not built"}))
+    base = {"impl": "reference", "metric": METRIC}
+    if not R.have_ref(stock=True):
+        print(json.dumps(dict(base, unavailable="oracle/_ref/stock/libquanta_ref.so not built")))
         return
-    n = args.warmup + args.steps
-    base = cpu_baseline(path, n)
-    out = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "int8/int4 x int8 -> f32", "data": "synthetic",
-           "config": {"workload": "config4: q4mix 0.5B + shortlist, 512-token prompt, b=1 decode, T=0.7 k=20 p=0.8 rp=1.1"},
-           "cpu_baseline": base, "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    # the model file is written by a separate process, so this one loads only the reference engine
+    path = MODEL_DIR / "q4mix_sl.qnt"
+    if not path.exists():
+        code = (f"import sys; sys.path.insert(0, {str(ROOT / 'quanta.cpp_b200')!r}); import quanta_b200 as qb; "
+                f"qb.synth_model({str(path)!r}, shape=qb.QWEN05B, mlp_q4=True, shortlist=True, seed={SEED})")
+        subprocess.run([sys.executable, "-c", code], check=True)
+    n_tokens = 151665
+    b = cpu_baseline(path, n_tokens, args.warmup + args.steps)
+    out = dict(base, value=b["value"], unit="tok/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+               ms_per_step=round(1e3 / b["value"], 3), higher_is_better=True, scaling="weak", vs_baseline=None,
+               dtype="int8/int4 x int8 -> f32 (f16 KV)", data="synthetic", config={"workload": WORKLOAD},
+               cpu_baseline=b, e2e={"value": b["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
     print(json.dumps(out))
+
+
+def config5_job(m, rank, world, dist, stream, n_seqs=JOB_SEQS):
+    """BASELINE config 5 as one job: JOB_SEQS sequences (512 random prompt ids, JOB_GEN greedy tokens each) split over
+    the ranks, served in waves of JOB_WAVE through the public batched API with host ids.  Host clock per rank (max over
+    ranks) for the job; CUDA events around each wave's decode steps for the batched decode rate."""
+    import torch
+    mine = dp.shard(n_seqs, rank, world)
+    prompts = np.random.default_rng(SEED + 5).integers(0, m.hp.n_tokens, (n_seqs, PROMPT)).astype(np.int32)
+    m.batch_init(JOB_WAVE, PROMPT + JOB_GEN + 8)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    decode_ms, decode_steps, prefill_s = 0.0, 0, 0.0
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    generated = 0
+    for w0 in range(mine.start, mine.stop, JOB_WAVE):
+        seqs = list(range(w0, min(w0 + JOB_WAVE, mine.stop)))
+        slots = np.arange(len(seqs), dtype=np.int32)
+        tp = time.perf_counter()
+        last = np.array([m.prefill_batch(i, prompts[g]) for i, g in enumerate(seqs)], np.int32)
+        prefill_s += time.perf_counter() - tp
+        torch.cuda.nvtx.range_push("batch_decode")  # lets a profiler select the batched steps
+        ev[0].record(stream)
+        for _ in range(JOB_GEN - 1):
+            last = m.decode_batch(slots, last)
+        ev[1].record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        decode_ms += ev[0].elapsed_time(ev[1])
+        decode_steps += JOB_GEN - 1
+        generated += len(seqs) * JOB_GEN
+        for i in range(len(seqs)):
+            m.batch_reset(i)
+    torch.cuda.synchronize()
+    job_s = dp.max_over_ranks(time.perf_counter() - t0, dist, device="cuda")
+    step_ms = dp.max_over_ranks(decode_ms / max(decode_steps, 1), dist, device="cuda")
+    m.batch_init(1, 2)  # release the batch caches
+    return {"workload": f"config5: {n_seqs} sequences x ({PROMPT}-token prompt + {JOB_GEN} greedy tokens), "
+                        f"{JOB_WAVE} per GPU per wave, split over {world} GPU(s)",
+            "scaling": "strong", "sequences_per_gpu": len(mine), "waves_per_gpu": -(-len(mine) // JOB_WAVE),
+            "seconds": round(job_s, 3), "generated_tok_s": round(n_seqs * JOB_GEN / job_s, 1),
+            "prompt_tok_s": round(n_seqs * PROMPT / job_s, 1),
+            "batch_decode": {"ms_per_step": round(step_ms, 3), "sequences_per_step": JOB_WAVE,
+                             "tok_s_per_gpu": round(JOB_WAVE / (step_ms / 1e3), 1)},
+            "prefill_tok_s_per_gpu": round(len(mine) * PROMPT / prefill_s, 1),
+            "note": "host clock over the whole job (prompts in, ids out per call), max over ranks"}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -196,7 +368,8 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    clk = Clocks(gpu_selector(local_rank)).start()
     path = model_path() if rank == 0 or world == 1 else None
     if dist:
         dist.barrier()
@@ -207,7 +380,7 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(m.stream)
 
     # prefill (timed separately: prompt tok/s)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     torch.cuda.synchronize()
     m.session_begin(prompt, sp)  # compiles the graphs of the first call
     m.session_begin(prompt, sp)
@@ -219,16 +392,18 @@ def run_ours(args, rank, world, local_rank):
     # warm-up, then exactly K steps bracketed by barrier + synchronize, CUDA events on the model's stream
     m.session_step(args.warmup)
     torch.cuda.synchronize()
+    clk.wait_ready()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local_rank) as clk:
-        torch.cuda.nvtx.range_push("decode")  # lets a profiler select the timed steps (ncu --nvtx-include "decode/")
-        ev[0].record(stream)
-        m.session_step(args.steps)
-        ev[1].record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
+    tc0 = time.monotonic()
+    torch.cuda.nvtx.range_push("decode")  # lets a profiler select the timed steps (ncu --nvtx-include "decode/")
+    ev[0].record(stream)
+    m.session_step(args.steps)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    tc1 = time.monotonic()
     ms = ev[0].elapsed_time(ev[1])
     if dist:
         dist.barrier()
@@ -241,8 +416,7 @@ def run_ours(args, rank, world, local_rank):
     hp = m.hp
     head_rows_mean = st["head_rows"] / max(st["head_calls"], 1)
     layer_bytes = m.weight_bytes - (hp.vocab_size * (hp.dim + hp.dim // 32 * 2))  # minus embedding/Q8 head
-    # (the shortlist pass reads the Q4 copy + err, and head_rows exact Q8 rows)
-    q4 = hp.vocab_size * (hp.dim // 2 + hp.dim // 32 * 2)
+    q4 = hp.vocab_size * (hp.dim // 2 + hp.dim // 32 * 2)  # the shortlist pass reads the Q4 copy + err
     err = hp.vocab_size * (hp.dim // 32) * 2
     layer_only = layer_bytes - q4 - err
     pos_mid = PROMPT + args.warmup + args.steps / 2
@@ -255,48 +429,32 @@ def run_ours(args, rank, world, local_rank):
     pin_prompt = torch.from_numpy(prompt).pin_memory().numpy()
     m.generate(pin_prompt, sp, 4)
     torch.cuda.synchronize()
+    te0 = time.monotonic()
     t0 = time.perf_counter()
-    ids_e2e, st_e2e = m.generate(pin_prompt, sp, args.steps)
+    ids_e2e, _ = m.generate(pin_prompt, sp, args.steps)
     e2e_s = time.perf_counter() - t0
+    te1 = time.monotonic()
     e2e_value = world * len(ids_e2e) / dp.max_over_ranks(e2e_s, dist, device="cuda")
 
-    # config 5 style throughput serving on this rank: BATCH sequences of PROMPT tokens, then greedy steps of all of
-    # them at once (qnt_decode_batch: tensor-core layers, fused greedy head); device time with CUDA events
-    batch = None
-    if args.batch > 0:
-        B, bsteps = args.batch, args.batch_steps
-        m.batch_init(B, PROMPT + bsteps + 8)
-        rngb = np.random.default_rng(dp.rank_seed(SEED + 7, rank))
-        prompts = rngb.integers(0, m.hp.n_tokens, (B, PROMPT)).astype(np.int32)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        last = np.array([m.prefill_batch(s, prompts[s]) for s in range(B)], np.int32)
-        torch.cuda.synchronize()
-        bprefill_s = time.perf_counter() - t0
-        seqs = np.arange(B, dtype=np.int32)
-        for _ in range(2):  # warm-up steps
-            last = m.decode_batch(seqs, last)
-        torch.cuda.synchronize()
-        eb = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        torch.cuda.nvtx.range_push("batch")  # lets a profiler select the timed batched steps
-        eb[0].record(stream)
-        for _ in range(bsteps):
-            last = m.decode_batch(seqs, last)
-        eb[1].record(stream)
-        torch.cuda.nvtx.range_pop()
-        torch.cuda.synchronize()
-        bms = dp.max_over_ranks(eb[0].elapsed_time(eb[1]), dist, device="cuda")
-        batch = {"workload": f"config5 style: {B} sequences x {PROMPT}-token prompts per GPU, greedy, batched decode",
-                 "value": round(world * B * bsteps / (bms / 1e3), 1), "unit": "tok/s", "steps": bsteps,
-                 "ms_per_step": round(bms / bsteps, 3), "prefill_tok_s": round(B * PROMPT / bprefill_s, 1),
-                 "note": "each step: one token for every sequence, ids copied to the host",
-                 "tc_matmul": tc_matmul_measure(B)}
-        m.batch_init(1, 2)  # release the batch caches
+    job = None
+    tj0 = time.monotonic()
+    if args.job:
+        job = config5_job(m, rank, world, dist, stream, args.job_seqs)
+    tj1 = time.monotonic()
+    m.close()
+
+    extra = {}
+    if world == 1 and not args.no_extras:
+        i8_peak, i8_kind = int8_peak(qb)
+        extra["int8_peak_tops"] = {"value": round(i8_peak, 1), "kind": i8_kind}
+        extra["tc_matmul"] = tc_matmul_measure(qb, JOB_WAVE, i8_peak, i8_kind)
+        extra["head_shard"] = head_shard_measure(qb)
+    clk.stop()
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            base = cpu_baseline(path, 16)
+            base = cpu_baseline(path, hp.n_tokens, 16)
         except Exception as e:  # the checker is optional on a box without it
             base = {"error": str(e)}
     if rank == 0:
@@ -304,26 +462,28 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8/int4 x int8 -> f32 (f16 KV)", "data": "synthetic",
-            "config": {"workload": "config4: q4mix 0.5B + shortlist, 512-token prompt, b=1 decode, T=0.7 k=20 p=0.8 rp=1.1",
-                       "parallelism": f"dp{world} (independent sequences)", "l2": "inputs larger than L2 (~309 MB read per step)"},
+            "config": {"workload": WORKLOAD, "parallelism": f"dp{world} (independent sequences)",
+                       "l2": "inputs larger than L2 (~309 MB read per step)"},
             "prefill_tok_s": round(PROMPT / prefill_s, 1),
             "head_rows_mean": round(head_rows_mean, 1),
             "bytes_per_token": int(step_bytes),
             "roofline": {"bound": "hbm", "kernel": "whole decode step (all kernels of one graph replay)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind, "traffic": STEP_TRAFFIC_BYTES,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over one step's launches "
-                                           "(profiles/decode_step_traffic_q4mix_sl.md)"},
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over one step's "
+                                           "launches of this workload"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": round(PROMPT * 4 / args.steps, 1),
                     "d2h_bytes_per_step": 4, "note": "qnt_generate wall clock incl. 512-token prefill"},
             "gpu_launches": kps * args.steps,
             "kernels_per_step": kps,
-            "clocks": clk.summary(),
+            "clocks": clk.summary(tc0, tc1),
+            "clocks_e2e": clk.summary(te0, te1),
+            "clocks_job": clk.summary(tj0, tj1) if job else None,
             "cpu_baseline": base,
-            "batch_decode": batch,
+            "config5_job": job,
         }
+        out.update(extra)
         print(json.dumps(out))
-    m.close()
     if dist:
         dist.destroy_process_group()
 
@@ -335,8 +495,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=256, help="sequences of the batched-serving measurement (0: skip)")
-    ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--no-extras", action="store_true", help="skip the one-GPU matmul, head-shard and peak measurements")
+    ap.add_argument("--no-job", dest="job", action="store_false", help="skip the config-5 job")
+    ap.add_argument("--job-seqs", type=int, default=JOB_SEQS, help="sequences of the config-5 job (BASELINE: 2048)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -61,8 +61,15 @@ int qnt_matvec(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, 
 int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo,
                int impl, void* stream);
 
+/* No reference counterpart: waits for `stream`, then reports (and clears) the status bits that the calling thread's
+ * earlier qnt_matmul calls left -- QNT_ERR_DEVICE when a tensor-core wait gave up.  The host forms check it themselves. */
+int qnt_ops_check(void* stream);
+
 /* Synchronous host-pointer forms of the three calls above: the drop-in for the reference's function pointers
- * (a MatvecQFn / MatmulQFn shim passes QuantVec::q / QuantVec::d and the caller's output buffer). */
+ * (a MatvecQFn / MatmulQFn shim passes QuantVec::q / QuantVec::d and the caller's output buffer).  Re-entrant like the
+ * reference's kernels, which Model::linear calls from its thread pool on disjoint row ranges (engine/src/model.cpp:
+ * 150-157): each calling thread keeps its own stream, staging buffers (device and pinned host, grown on demand, so a
+ * call allocates nothing once its sizes have been seen) and kernel status word, and waits only for its own stream. */
 int qnt_quantize_q8_host(const float* x, int n, int8_t* q, float* d);
 int qnt_matvec_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, int r1, float* out);
 int qnt_matmul_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo,
@@ -211,6 +218,11 @@ int qnt_model_debug_buffer(qnt_model* m, int what, float* out);
 /* The cudaStream_t (as void*) every call on this model is queued on: lets a caller record CUDA events around
  * qnt_session_step for device timing. */
 void* qnt_model_stream(const qnt_model* m);
+
+/* Diagnostics (no reference counterpart): the dense int8 tensor-core rate of the current GPU, measured -- every SM
+ * issues 4 * iters back-to-back tcgen05.mma.kind::i8 (M 128, N 256, K 32) on operands resident in shared memory;
+ * *tops = int8 TOP/s over the slowest SM.  The roofline denominator of the tensor-core matmul. */
+int qnt_bench_mma_i8(int iters, double* tops);
 
 #ifdef __cplusplus
 }

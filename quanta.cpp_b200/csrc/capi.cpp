@@ -19,7 +19,6 @@ struct qnt_dtensor {
     qb::TcMap wmap{};          // TMA source for the tensor-core matmul
     bool tc = false;           // wmap is valid
     void* tcbuf = nullptr;     // the copies wmap reads (stage-major scales; Q4_0: int8 q - 8)
-    unsigned* status = nullptr;  // device status word of this tensor's kernels
 };
 
 struct qnt_model {
@@ -57,6 +56,106 @@ int engine_code(qb::Engine& e, int r) {
 
 bool shape_ok(int dtype, int rows, int cols) {
     return (dtype == QNT_Q8_0 || dtype == QNT_Q4_0) && rows > 0 && cols > 0 && cols % 32 == 0;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// What each calling thread keeps for the ops-level entries, per device: a status word of its own (the tensor-core
+// matmul's bounded waits report there, so concurrent callers never see or clear each other's bits), and for the
+// synchronous host entries one stream with device and pinned host staging that only grows -- a call allocates
+// nothing once its sizes have been seen, and synchronises only its own stream.
+struct ThreadOps {
+    int device = -1;
+    cudaStream_t st = nullptr;
+    unsigned* status = nullptr;     // device word
+    unsigned* status_h = nullptr;   // pinned copy read after a host call
+    unsigned char* dbuf = nullptr;  // device staging
+    size_t dcap = 0;
+    unsigned char* hbuf = nullptr;  // pinned host staging
+    size_t hcap = 0;
+
+    ~ThreadOps() { release(); }
+    void release() {
+        if (device < 0) return;
+        int cur = -1;
+        cudaGetDevice(&cur);
+        cudaSetDevice(device);
+        if (st) cudaStreamDestroy(st);
+        cudaFree(status);
+        cudaFree(dbuf);
+        cudaFreeHost(status_h);
+        cudaFreeHost(hbuf);
+        if (cur >= 0) cudaSetDevice(cur);
+        *this = ThreadOps{};
+        device = -1;
+    }
+    // the current device's stream and status word (made on first use)
+    cudaError_t ready() {
+        int dev = -1;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev == device) return cudaSuccess;
+        release();
+        device = dev;
+        e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaMalloc(&status, sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemset(status, 0, sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMallocHost(&status_h, sizeof(unsigned));
+        if (e != cudaSuccess) release();
+        return e;
+    }
+    cudaError_t staging(size_t dbytes, size_t hbytes) {
+        cudaError_t e = ready();
+        if (e == cudaSuccess && dbytes > dcap) {
+            cudaFree(dbuf);
+            dbuf = nullptr;
+            dcap = 0;
+            e = cudaMalloc(&dbuf, dbytes);
+            if (e == cudaSuccess) dcap = dbytes;
+        }
+        if (e == cudaSuccess && hbytes > hcap) {
+            cudaFreeHost(hbuf);
+            hbuf = nullptr;
+            hcap = 0;
+            e = cudaMallocHost(&hbuf, hbytes);
+            if (e == cudaSuccess) hcap = hbytes;
+        }
+        return e;
+    }
+};
+
+thread_local ThreadOps t_ops;
+
+// The tensor-core or CUDA-core matmul on device pointers.  dxt: a block-major scale buffer of nb * ((n + 31) & ~31)
+// floats, or null to take one stream-ordered from the pool for this call.
+int matmul_dev(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo, int impl,
+               cudaStream_t s, unsigned* status, float* dxt) {
+    const bool tc = impl == 2 || (impl == 0 && W->tc && n >= qb::kTcMinTokens);
+    cudaError_t e;
+    if (tc) {
+        if (!W->tc) return set_err(QNT_ERR_UNSUPPORTED, "tensor-core matmul needs cols % 128 == 0 and a TMA-capable driver");
+        if ((reinterpret_cast<uintptr_t>(qx) | reinterpret_cast<uintptr_t>(dx)) & 15)
+            return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
+        if (n == 0 || r1 == r0) return QNT_OK;
+        // the kernel reads the activation scales block-major: a stream-ordered transposed copy
+        const int nb = W->m.cols / 32, ldt = (n + 31) & ~31;
+        const bool own = dxt == nullptr;
+        if (own) {
+            e = cudaMallocAsync(reinterpret_cast<void**>(&dxt), size_t(nb) * ldt * 4, s);
+            if (e != cudaSuccess) return cuda_err(e, "matmul scale copy");
+        }
+        qb::TcAct act;
+        e = qb::launch_transpose_scales(dx, n, nb, dxt, ldt, s);
+        if (e == cudaSuccess && !qb::make_act_maps(qx, dxt, n, ldt, W->m.cols, &act)) e = cudaErrorInvalidValue;
+        if (e == cudaSuccess) e = qb::launch_matmul_tc(W->m, W->wmap, act, n, r0, r1, out, ldo, status, s);
+        if (own) {
+            const cudaError_t ef = cudaFreeAsync(dxt, s);
+            if (e == cudaSuccess) e = ef;
+        }
+    } else {
+        e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, s);
+    }
+    return e == cudaSuccess ? QNT_OK : cuda_err(e, "matmul");
 }
 
 }  // namespace
@@ -97,14 +196,6 @@ int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_
     t->m.cols = cols;
     t->m.q = static_cast<const uint8_t*>(t->q);
     t->m.d = static_cast<const __half*>(t->d);
-    e = cudaMalloc(&t->status, sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(t->status, 0, sizeof(unsigned));
-    if (e != cudaSuccess) {
-        cudaFree(t->q);
-        cudaFree(t->d);
-        cudaFree(t->status);
-        return cuda_err(e, "tensor status word");
-    }
     if (qb::gemm_tc_supported(t->m)) {
         e = cudaMalloc(&t->tcbuf, qb::tc_weight_bytes(t->m));
         if (e == cudaSuccess) e = qb::tc_prepare_weights(t->m, t->tcbuf, &t->wmap, nullptr);
@@ -112,7 +203,6 @@ int qnt_tensor_upload(int dtype, int rows, int cols, const void* host_data, qnt_
         if (e != cudaSuccess) {
             cudaFree(t->q);
             cudaFree(t->d);
-            cudaFree(t->status);
             cudaFree(t->tcbuf);
             return cuda_err(e, "tensor-core weight copies");
         }
@@ -126,7 +216,6 @@ int qnt_tensor_free(qnt_dtensor* t) {
     if (!t) return QNT_OK;
     cudaFree(t->q);
     cudaFree(t->d);
-    cudaFree(t->status);
     cudaFree(t->tcbuf);
     delete t;
     return QNT_OK;
@@ -157,88 +246,88 @@ int qnt_matmul(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, i
                void* stream) {
     if (!W || r0 < 0 || r1 > W->m.rows || r0 > r1 || n < 0 || ldo < r1) return set_err(QNT_ERR_INVALID, "bad matmul arguments");
     if (impl < 0 || impl > 2) return set_err(QNT_ERR_INVALID, "impl must be 0 (auto), 1 (CUDA cores) or 2 (tensor cores)");
-    const bool tc = impl == 2 || (impl == 0 && W->tc && n >= qb::kTcMinTokens);
-    cudaError_t e;
-    if (tc) {
-        if (!W->tc) return set_err(QNT_ERR_UNSUPPORTED, "tensor-core matmul needs cols % 128 == 0 and a TMA-capable driver");
-        if ((reinterpret_cast<uintptr_t>(qx) | reinterpret_cast<uintptr_t>(dx)) & 15)
-            return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
-        if (n == 0 || r1 == r0) return QNT_OK;
-        // the kernel reads the activation scales block-major: a stream-ordered transposed copy
-        const cudaStream_t s = static_cast<cudaStream_t>(stream);
-        const int nb = W->m.cols / 32, ldt = (n + 31) & ~31;
-        float* dxt = nullptr;
-        e = cudaMallocAsync(reinterpret_cast<void**>(&dxt), size_t(nb) * ldt * 4, s);
-        if (e != cudaSuccess) return cuda_err(e, "matmul scale copy");
-        qb::TcAct act;
-        e = qb::launch_transpose_scales(dx, n, nb, dxt, ldt, s);
-        if (e == cudaSuccess && !qb::make_act_maps(qx, dxt, n, ldt, W->m.cols, &act)) e = cudaErrorInvalidValue;
-        if (e == cudaSuccess) e = qb::launch_matmul_tc(W->m, W->wmap, act, n, r0, r1, out, ldo, W->status, s);
-        const cudaError_t ef = cudaFreeAsync(dxt, s);
-        if (e == cudaSuccess) e = ef;
-    } else {
-        e = qb::launch_matmul_simt(W->m, qx, dx, n, r0, r1, out, ldo, static_cast<cudaStream_t>(stream));
-    }
-    return e == cudaSuccess ? QNT_OK : cuda_err(e, "matmul");
+    const cudaError_t e = t_ops.ready();
+    if (e != cudaSuccess) return cuda_err(e, "matmul set-up");
+    return matmul_dev(W, qx, dx, n, r0, r1, out, ldo, impl, static_cast<cudaStream_t>(stream), t_ops.status, nullptr);
+}
+
+int qnt_ops_check(void* stream) {
+    cudaError_t e = t_ops.ready();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    unsigned st = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&st, t_ops.status, sizeof st, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && st) e = cudaMemset(t_ops.status, 0, sizeof st);
+    if (e != cudaSuccess) return cuda_err(e, "qnt_ops_check");
+    if (st) return set_err(QNT_ERR_DEVICE, "an ops-level kernel of this thread reported status bits " + std::to_string(st));
+    return QNT_OK;
 }
 
 int qnt_quantize_q8_host(const float* x, int n, int8_t* q, float* d) {
-    if (n <= 0 || n % 32) return set_err(QNT_ERR_INVALID, "n must be a positive multiple of 32");
-    float* dxv = nullptr;
-    int8_t* dq = nullptr;
-    float* dd = nullptr;
-    cudaError_t e = cudaMalloc(&dxv, size_t(n) * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&dq, size_t(n));
-    if (e == cudaSuccess) e = cudaMalloc(&dd, size_t(n / 32) * 4);
-    if (e == cudaSuccess) e = cudaMemcpy(dxv, x, size_t(n) * 4, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = qb::launch_quantize_q8(dxv, 1, n, dq, dd, nullptr);
-    if (e == cudaSuccess) e = cudaMemcpy(q, dq, size_t(n), cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemcpy(d, dd, size_t(n / 32) * 4, cudaMemcpyDeviceToHost);
-    cudaFree(dxv);
-    cudaFree(dq);
-    cudaFree(dd);
-    return e == cudaSuccess ? QNT_OK : cuda_err(e, "quantize_q8_host");
+    if (n <= 0 || n % 32 || !x || !q || !d) return set_err(QNT_ERR_INVALID, "n must be a positive multiple of 32");
+    const size_t xb = size_t(n) * 4, qb_ = align256(size_t(n)), db = size_t(n / 32) * 4;
+    const size_t qoff = align256(xb), doff = qoff + qb_, total = doff + db;
+    cudaError_t e = t_ops.staging(total, total);
+    if (e != cudaSuccess) return cuda_err(e, "quantize_q8_host staging");
+    std::memcpy(t_ops.hbuf, x, xb);
+    e = cudaMemcpyAsync(t_ops.dbuf, t_ops.hbuf, xb, cudaMemcpyHostToDevice, t_ops.st);
+    if (e == cudaSuccess)
+        e = qb::launch_quantize_q8(reinterpret_cast<const float*>(t_ops.dbuf), 1, n, reinterpret_cast<int8_t*>(t_ops.dbuf + qoff),
+                                   reinterpret_cast<float*>(t_ops.dbuf + doff), t_ops.st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(t_ops.hbuf + qoff, t_ops.dbuf + qoff, total - qoff, cudaMemcpyDeviceToHost, t_ops.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(t_ops.st);
+    if (e != cudaSuccess) return cuda_err(e, "quantize_q8_host");
+    std::memcpy(q, t_ops.hbuf + qoff, size_t(n));
+    std::memcpy(d, t_ops.hbuf + doff, db);
+    return QNT_OK;
 }
 
+// The synchronous host entries: inputs through pinned staging to the thread's device staging, the kernel on the
+// thread's stream, the used output rows back, and the thread's status word checked.  Device layout:
+// [q n x cols | d n x nb | block-major d nb x ldt | out n x r1].
 static int host_mm(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, int r0, int r1, float* out, int ldo, bool mv,
                    int impl) {
-    if (!W || r0 < 0 || r1 > W->m.rows || r0 > r1 || n <= 0) return set_err(QNT_ERR_INVALID, "bad arguments");
-    const int cols = W->m.cols;
-    int8_t* dq = nullptr;
-    float *dd = nullptr, *dout = nullptr;
-    const size_t out_elems = mv ? size_t(r1) : size_t(n - 1) * ldo + r1;
-    cudaError_t e = cudaMalloc(&dq, size_t(n) * cols);
-    if (e == cudaSuccess) e = cudaMalloc(&dd, size_t(n) * (cols / 32) * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&dout, out_elems * 4);
-    if (e == cudaSuccess) e = cudaMemcpy(dq, qx, size_t(n) * cols, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(dd, dx, size_t(n) * (cols / 32) * 4, cudaMemcpyHostToDevice);
-    int rc = QNT_OK;
-    if (e == cudaSuccess) {
-        rc = mv ? qnt_matvec(W, dq, dd, r0, r1, dout, nullptr) : qnt_matmul(W, dq, dd, n, r0, r1, dout, ldo, impl, nullptr);
-        e = cudaDeviceSynchronize();
+    if (!W || !qx || !dx || !out || r0 < 0 || r1 > W->m.rows || r0 > r1 || n <= 0)
+        return set_err(QNT_ERR_INVALID, "bad arguments");
+    if (r0 == r1) return QNT_OK;
+    const int cols = W->m.cols, nb = cols / 32, ldt = (n + 31) & ~31;
+    const size_t qbytes = size_t(n) * cols, dbytes = size_t(n) * nb * 4;
+    const size_t doff = align256(qbytes), toff = doff + align256(dbytes), ooff = toff + align256(size_t(nb) * ldt * 4);
+    const size_t obytes = size_t(n) * r1 * 4;
+    // host staging: [q | d | out], with the out block at the same offset as on the device
+    cudaError_t e = t_ops.staging(ooff + obytes, ooff + obytes);
+    if (e != cudaSuccess) return cuda_err(e, "host matvec/matmul staging");
+    unsigned char* h = t_ops.hbuf;
+    unsigned char* dv = t_ops.dbuf;
+    std::memcpy(h, qx, qbytes);
+    std::memcpy(h + doff, dx, dbytes);
+    e = cudaMemcpyAsync(dv, h, doff + dbytes, cudaMemcpyHostToDevice, t_ops.st);
+    if (e != cudaSuccess) return cuda_err(e, "host matvec/matmul input copy");
+    const int8_t* dq = reinterpret_cast<const int8_t*>(dv);
+    const float* dd = reinterpret_cast<const float*>(dv + doff);
+    float* dout = reinterpret_cast<float*>(dv + ooff);
+    int rc;
+    if (mv) {
+        if (cols > 16384) return set_err(QNT_ERR_UNSUPPORTED, "matvec supports cols <= 16384");
+        e = qb::launch_matvec(W->m, dq, dd, r0, r1, dout, t_ops.st);
+        rc = e == cudaSuccess ? QNT_OK : cuda_err(e, "matvec");
+    } else {
+        rc = matmul_dev(W, dq, dd, n, r0, r1, dout, r1, impl, t_ops.st, t_ops.status, reinterpret_cast<float*>(dv + toff));
     }
-    if (e == cudaSuccess && rc == QNT_OK) {
-        unsigned st = 0;
-        e = cudaMemcpy(&st, W->status, sizeof st, cudaMemcpyDeviceToHost);
-        if (e == cudaSuccess && st) {
-            cudaMemset(W->status, 0, sizeof st);
-            rc = set_err(QNT_ERR_DEVICE, "matmul kernel reported status bits " + std::to_string(st));
-        }
-    }
-    if (e == cudaSuccess && rc == QNT_OK) {
-        if (mv) {
-            e = cudaMemcpy(out + r0, dout + r0, size_t(r1 - r0) * 4, cudaMemcpyDeviceToHost);
-        } else {
-            for (int t = 0; t < n && e == cudaSuccess; ++t)
-                e = cudaMemcpy(out + size_t(t) * ldo + r0, dout + size_t(t) * ldo + r0, size_t(r1 - r0) * 4,
-                               cudaMemcpyDeviceToHost);
-        }
-    }
-    cudaFree(dq);
-    cudaFree(dd);
-    cudaFree(dout);
     if (rc != QNT_OK) return rc;
-    return e == cudaSuccess ? QNT_OK : cuda_err(e, "host matvec/matmul");
+    e = cudaMemcpyAsync(h + ooff, dout, obytes, cudaMemcpyDeviceToHost, t_ops.st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(t_ops.status_h, t_ops.status, sizeof(unsigned), cudaMemcpyDeviceToHost, t_ops.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(t_ops.st);
+    if (e != cudaSuccess) return cuda_err(e, "host matvec/matmul");
+    if (const unsigned st = *t_ops.status_h) {
+        cudaMemsetAsync(t_ops.status, 0, sizeof(unsigned), t_ops.st);
+        cudaStreamSynchronize(t_ops.st);
+        return set_err(QNT_ERR_DEVICE, "matmul kernel reported status bits " + std::to_string(st));
+    }
+    const float* ho = reinterpret_cast<const float*>(h + ooff);
+    for (int t = 0; t < (mv ? 1 : n); ++t)
+        std::memcpy(out + size_t(t) * ldo + r0, ho + size_t(t) * r1 + r0, size_t(r1 - r0) * 4);
+    return QNT_OK;
 }
 
 int qnt_matvec_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int r0, int r1, float* out) {
@@ -406,5 +495,14 @@ int qnt_model_debug_buffer(qnt_model* m, int what, float* out) {
 }
 
 void* qnt_model_stream(const qnt_model* m) { return m ? static_cast<void*>(m->eng.stream()) : nullptr; }
+
+int qnt_bench_mma_i8(int iters, double* tops) {
+    if (iters <= 0 || !tops) return set_err(QNT_ERR_INVALID, "qnt_bench_mma_i8: iters > 0 and an output needed");
+    unsigned status = 0;
+    const cudaError_t e = qb::bench_mma_i8(iters, tops, &status);
+    if (e != cudaSuccess) return cuda_err(e, "qnt_bench_mma_i8");
+    if (status) return set_err(QNT_ERR_DEVICE, "qnt_bench_mma_i8: the MMA completion wait timed out");
+    return QNT_OK;
+}
 
 }  // extern "C"

@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <vector>
 #include <mutex>
 
 #include <climits>
@@ -565,6 +566,73 @@ cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, Ge
     return cudaGetLastError();
 }
 
+// Peak probe: back-to-back tcgen05.mma.kind::i8 (M = 128, N = 256, K = 32, the largest single-CTA shape) on operands
+// that stay in shared memory, accumulating into one 256-column TMEM accumulator, four K offsets in turn as a real
+// K-step would.  One lane issues; the commit's mbarrier wait is bounded.  elapsed[blockIdx.x] = globaltimer ns from
+// the first issue to the last MMA's completion.
+constexpr int kPeakN = 256;
+constexpr uint32_t kPeakIdesc =
+    (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kPeakN >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+// 120 KB of shared memory keeps it to one CTA per SM (two would not fit), so each SM's time is its own tensor pipe's
+constexpr size_t kPeakSmem = 120 * 1024;
+static_assert(kPeakSmem >= size_t(kTileRows) * 128 + size_t(kPeakN) * 128 + 1024, "operand tiles fit");
+
+__global__ void __launch_bounds__(128, 1) k_mma_i8_peak(int iters, unsigned long long* elapsed, unsigned* status) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t done;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < (kTileRows + kPeakN) * 128 / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes visible to the MMA
+    if (threadIdx.x == 0) {
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(kPeakN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    if (threadIdx.x == 0) {
+        unsigned long long t0, t1;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        const unsigned char* a = smem;
+        const unsigned char* b = smem + kTileRows * 128;
+        for (int it = 0; it < iters; ++it) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\t"
+                    "setp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                    ::"r"(tmem), "l"(sw128_desc(a + 32 * k)), "l"(sw128_desc(b + 32 * k)), "r"(kPeakIdesc),
+                    "r"((it | k) ? 1 : 0)
+                    : "memory");
+            }
+        }
+        mma_commit(&done);
+        bool ok = false;
+        for (unsigned i = 0; i < kWaitLimit && !(ok = mbar_try(&done, 0)); ++i) {
+        }
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        elapsed[blockIdx.x] = t1 - t0;
+        if (!ok) set_error(status, ERR_WAIT_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPeakN) : "memory");
+    }
+}
+
 // One CTA per token: the best (value desc, id asc) of its n_parts candidates.
 __global__ void __launch_bounds__(256) k_argmax_reduce(const Cand* __restrict__ cand, int n_parts, int n, int* __restrict__ ids,
                                                        float* __restrict__ vals) {
@@ -623,6 +691,36 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
 }
 
 int argmax_parts(int rows) { return ((rows + kTileRows - 1) / kTileRows) * 4; }
+
+cudaError_t bench_mma_i8(int iters, double* tops, unsigned* status_host) {
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    unsigned long long* el = nullptr;
+    unsigned* status = nullptr;
+    e = cudaMalloc(&el, sizeof(unsigned long long) * sms);
+    if (e == cudaSuccess) e = cudaMalloc(&status, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(status, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_mma_i8_peak, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPeakSmem));
+    std::vector<unsigned long long> h(size_t(sms > 0 ? sms : 1), 0);
+    unsigned st = 0;
+    if (e == cudaSuccess) {
+        k_mma_i8_peak<<<sms, 128, kPeakSmem>>>(iters / 8, el, status);  // warm-up
+        k_mma_i8_peak<<<sms, 128, kPeakSmem>>>(iters, el, status);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), el, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&st, status, sizeof st, cudaMemcpyDeviceToHost);
+    cudaFree(el);
+    cudaFree(status);
+    if (e != cudaSuccess) return e;
+    const unsigned long long worst = *std::max_element(h.begin(), h.end());
+    const double ops = 2.0 * kTileRows * kPeakN * 32 * 4 * double(iters) * sms;
+    if (tops) *tops = worst ? ops / (double(worst) * 1e-9) / 1e12 : 0.0;
+    if (status_host) *status_host = st;
+    return cudaSuccess;
+}
 
 cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int n_valid, void* cand,
                                     unsigned* status, cudaStream_t st) {

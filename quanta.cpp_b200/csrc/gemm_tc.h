@@ -57,4 +57,8 @@ cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAc
                                     unsigned* status, cudaStream_t st);
 cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids, float* vals, cudaStream_t st);
 
+// Dense int8 tensor-core peak of this GPU: every SM issues 4 * iters back-to-back tcgen05.mma.kind::i8 of
+// M = 128, N = 256, K = 32 from shared memory; *tops = 2 M N K * MMAs / the slowest SM's time (synchronous).
+cudaError_t bench_mma_i8(int iters, double* tops, unsigned* status);
+
 }  // namespace qb

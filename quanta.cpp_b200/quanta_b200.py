@@ -92,6 +92,7 @@ def lib() -> C.CDLL:
         L.qnt_quantize_q8.argtypes = [P, I, I, P, P, P]
         L.qnt_matvec.argtypes = [P, P, P, I, I, P, P]
         L.qnt_matmul.argtypes = [P, P, P, I, I, I, P, I, I, P]
+        L.qnt_ops_check.argtypes = [P]
         L.qnt_quantize_q8_host.argtypes = [P, I, P, P]
         L.qnt_matvec_host.argtypes = [P, P, P, I, I, P]
         L.qnt_matmul_host.argtypes = [P, P, P, I, I, I, P, I, I]
@@ -123,6 +124,7 @@ def lib() -> C.CDLL:
         L.qnt_sampler_sample.argtypes = [P, P, I, P, I, C.POINTER(I), P]
         L.qnt_sampler_free.argtypes = [P]
         L.qnt_sampler_free.restype = None
+        L.qnt_bench_mma_i8.argtypes = [I, C.POINTER(C.c_double)]
         L.qnt_sampler_sample_noalloc.argtypes = [C.POINTER(SamplerParamsC), C.POINTER(C.c_uint64), P, I, P, I,
                                                  C.POINTER(I), P]
         _lib = L
@@ -247,6 +249,12 @@ def sample_noalloc(sp: SamplerParams, rng_state: int, logits, n_valid: int | Non
     _check(lib().qnt_sampler_sample_noalloc(C.byref(spc), C.byref(state), C.c_void_p(logits.data_ptr()), n_valid,
                                             _ptr(hist) if hist.size else None, hist.size, C.byref(tok), st))
     return tok.value, state.value
+
+def bench_mma_i8(iters: int = 4096) -> float:
+    """Measured dense int8 tensor-core TOP/s of the current GPU (qnt_bench_mma_i8)."""
+    v = C.c_double(0)
+    _check(lib().qnt_bench_mma_i8(iters, C.byref(v)))
+    return v.value
 
 # ---------------------------------------------------------------- model level
 
