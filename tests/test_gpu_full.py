@@ -110,3 +110,30 @@ def test_fused_decode_layers_equal_separate_kernels(qb, models):
     assert out["both"]["ids"] == out["qkv"]["ids"] == out["none"]["ids"]
     assert out["qkv"]["kps"] - out["both"]["kps"] == layers, (out["both"]["kps"], out["qkv"]["kps"])
     assert out["none"]["kps"] - out["qkv"]["kps"] == layers, (out["qkv"]["kps"], out["none"]["kps"])
+
+
+def test_config3_device_vs_stock_reference_build(qb, models):
+    """The reference built with its own Release flags (GCC's default FMA contraction, -march of the host: the stock
+    build that the CPU baseline times) against the contraction-free build the other tests use.  The two builds of the
+    same reference differ from each other by about 2.5e-2 in relative logit terms on config 3 (one fused multiply-add
+    changes an int8 activation code, and 24 layers amplify it), so no device result can be within 1e-3 of both.
+    The device equals the contraction-free build bit for bit, so its distance from the stock build is exactly that
+    build's own distance from it: checked here, with both distances recorded."""
+    if not R.have_ref(stock=True):
+        pytest.skip("oracle/_ref/stock not built")
+    path = models("q8_0")
+    m = qb.Model(path, ctx_len=512)
+    chk = R.RefModel(path, ctx=512)
+    stock = R.RefModel(path, ctx=512, stock=True)
+    prompt = np.random.default_rng(3).integers(0, m.hp.n_tokens, 128)
+    d_dev, d_chk = [], []
+    got, want, ws = m.forward_batch(prompt, 0), chk.forward_batch(prompt, 0), stock.forward_batch(prompt, 0)
+    tok = int(np.argmax(want[:m.hp.n_tokens]))
+    for p in range(128, 128 + 8):
+        assert np.array_equal(got, want)
+        d_dev.append(rel_err(got, ws))
+        d_chk.append(rel_err(want, ws))
+        got, want, ws = m.forward(tok, p), chk.forward(tok, p), stock.forward(tok, p)
+        tok = int(np.argmax(want[:m.hp.n_tokens]))
+    print("device vs stock build: max %.3e; contraction-free build vs stock build: max %.3e" % (max(d_dev), max(d_chk)))
+    assert d_dev == d_chk
