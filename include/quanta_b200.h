@@ -116,6 +116,11 @@ int qnt_model_forward_batch(qnt_model* m, const int* tokens, int n, int pos0, co
  * 4-bit scores and upper bounds (Model::head_coarse / head_upper, model.h:50-51). */
 int qnt_model_head(qnt_model* m, const qnt_head_query* hq, float* logits, float* coarse, float* upper);
 
+/* The sum behind the CLI's `ppl` (tools/cli/main.cpp:261-282): Model::forward of ids[0..n-2] in order from position 0
+ * (full head), and for each p the full-vocabulary -log softmax of ids[p + 1] over ids < n_tokens, summed in f64 into
+ * *nll; perplexity = exp(*nll / (n - 1)).  Leaves the KV cache holding those positions. */
+int qnt_model_nll(qnt_model* m, const int* ids, int n, double* nll);
+
 /* Model::last_head_rows / has_shortlist_head / kv_cache_bytes (engine/src/model.h:48-49,58). */
 int qnt_model_last_head_rows(const qnt_model* m);
 int qnt_model_has_shortlist(const qnt_model* m);
@@ -142,6 +147,8 @@ typedef struct qnt_gen_stats {
 
 #define QNT_GEN_SHORTLIST 1     /* Session::set_sampler: use the Exact Shortlist Head when the file has one */
 #define QNT_GEN_BATCH_PREFILL 2 /* Session::set_batch_prefill(true) */
+#define QNT_GEN_KEEP_RNG 4      /* qnt_session_begin: keep the previous session's xorshift state (a Chat::reset keeps
+                                   its Sampler) instead of starting from the seed */
 
 /* Session::feed + Session::generate (engine/src/session.cpp:13-52) with Sampler::sample (sampler.cpp:22-85) on the
  * device: prefill the prompt, then n_gen steps of sample -> append -> forward without host round trips.
@@ -157,6 +164,32 @@ int qnt_generate(qnt_model* m, const int* prompt, int n_prompt, const qnt_sample
 int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_sampler_params* sp, int flags);
 int qnt_session_step(qnt_model* m, int n);
 int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* stats);
+
+/* The rest of Session (engine/src/session.cpp:13-52) for multi-turn use (Chat::reply, session.cpp:94-118):
+ *   qnt_session_feed    Session::feed after the first: appends n ids to the history and prefills them at the next
+ *                       positions (the same results as feeding them with the first prompt); the sampler state carries on.
+ *   qnt_session_rewind  forgets the last n_drop history tokens -- a sampled stop token, which the reference never
+ *                       appends (session.cpp:41-42); the next call on the session must be a feed.
+ *   qnt_session_last    waits for the queued steps; *token = the last sampled id, *length = the history length. */
+int qnt_session_feed(qnt_model* m, const int* ids, int n);
+int qnt_session_rewind(qnt_model* m, int n_drop);
+int qnt_session_last(qnt_model* m, int* token, int* length);
+
+/* Text <-> ids (engine/src/tokenizer.h:15-39): byte-level BPE over the .qnt's tokenizer section, on the host (no GPU).
+ *   qnt_tokenizer_open  Tokenizer(ModelFile::tokenizer()): QNT_ERR_IO for an unreadable file or a vocabulary without
+ *                       all 256 byte tokens
+ *   qnt_tokenize        Tokenizer::encode (special literals such as "<|im_start|>" recognised): returns the id count and
+ *                       writes at most max_ids of them
+ *   qnt_token_piece     Tokenizer::decode(id): the raw bytes (possibly part of a UTF-8 sequence); returns their count and
+ *                       writes at most cap of them (an unknown id has none)
+ *   qnt_token_id        Tokenizer::token_id: a special token's id, or -1 */
+typedef struct qnt_tokenizer qnt_tokenizer;
+int qnt_tokenizer_open(const char* path, qnt_tokenizer** out);
+void qnt_tokenizer_free(qnt_tokenizer* t);
+int qnt_tokenizer_n_tokens(const qnt_tokenizer* t);
+int qnt_tokenize(const qnt_tokenizer* t, const char* text, size_t len, int* ids, int max_ids);
+int qnt_token_piece(const qnt_tokenizer* t, int id, char* buf, int cap);
+int qnt_token_id(const qnt_tokenizer* t, const char* literal);
 
 /* Batched serving of many independent sequences on one model (the multi-sequence API qnt_prefill_batch /
  * qnt_decode_batch of the drop-in boundary; the reference serves one Session at a time, engine/src/session.cpp:13-52).

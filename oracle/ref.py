@@ -59,6 +59,8 @@ def ref(stock: bool = False) -> C.CDLL:
         L.ref_sample.argtypes = [P, P, I, P, I]
         L.ref_generate.argtypes = [P, P, I, I, I, F, I, F, F, F, C.c_ulonglong, I, P, C.POINTER(C.c_double),
                                    C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        L.ref_tokenize.argtypes = [P, C.c_char_p, I, P, I]
+        L.ref_token_id.argtypes = [P, C.c_char_p]
         L.ref_check_batch.argtypes = [P, P, I, I]
         L.ref_check_head.argtypes = [P, P, I]
         _refs[so] = L
@@ -138,6 +140,16 @@ class RefModel:
     @property
     def last_head_rows(self):
         return self.L.ref_last_head_rows(self.h)
+
+    def tokenize(self, text) -> np.ndarray:
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        n = self.L.ref_tokenize(self.h, b, len(b), None, 0)
+        out = np.zeros(max(n, 1), np.int32)
+        self.L.ref_tokenize(self.h, b, len(b), _p(out), n)
+        return out[:n]
+
+    def token_id(self, literal: str) -> int:
+        return self.L.ref_token_id(self.h, literal.encode())
 
     def generate(self, prompt, n_gen, temperature=0.7, top_k=20, top_p=0.8, min_p=0.0, repeat_penalty=1.1, seed=1234,
                  batch_prefill=True, shortlist=True):

@@ -10,6 +10,7 @@
 //   quantize_q8, matvec_q_ref, matmul_q_ref (engine/src/ops.h:52-70)
 //   Sampler::sample (engine/src/sampler.h:26), Session::feed / generate / head_fraction (engine/src/session.h:27-35)
 //   kernel_selftest, check_batch, check_head (engine/src/checks.h:20-27)
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstring>
@@ -223,6 +224,15 @@ int ref_generate(void* h, const int* ids, int n_ids, int batch_prefill, int use_
     if (head_fraction) *head_fraction = s.head_fraction();
     return n;
 }
+
+// ---- tokenizer (engine/src/tokenizer.h): encode returns the id count and writes at most max of them
+int ref_tokenize(void* h, const char* text, int len, int* out, int max) {
+    const std::vector<int> ids = static_cast<RefModel*>(h)->tok->encode(std::string(text, size_t(len)));
+    std::memcpy(out, ids.data(), sizeof(int) * std::min(ids.size(), size_t(max)));
+    return int(ids.size());
+}
+
+int ref_token_id(void* h, const char* literal) { return static_cast<RefModel*>(h)->tok->token_id(literal); }
 
 // ---- the reference's own self-checks (engine/src/checks.h)
 

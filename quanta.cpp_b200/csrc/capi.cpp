@@ -1,6 +1,8 @@
 // extern "C" layer of include/quanta_b200.h over the engine and the ops-level kernels.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstdint>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -11,6 +13,7 @@
 #include "engine.h"
 #include "gemm_tc.h"
 #include "ops.h"
+#include "tokenizer.h"
 
 struct qnt_dtensor {
     qb::DMat m;
@@ -23,6 +26,11 @@ struct qnt_dtensor {
 
 struct qnt_model {
     qb::Engine eng;
+};
+
+struct qnt_tokenizer {
+    qb::QntFile file;
+    std::unique_ptr<qb::BpeTokenizer> bpe;
 };
 
 namespace qnt_capi {
@@ -446,7 +454,7 @@ int qnt_session_begin(qnt_model* m, const int* prompt, int n_prompt, const qnt_s
     p.repeat_window = sp->repeat_window;
     p.seed = sp->seed;
     return engine_code(m->eng, m->eng.session_begin(prompt, n_prompt, p, (flags & QNT_GEN_SHORTLIST) != 0,
-                                                    (flags & QNT_GEN_BATCH_PREFILL) != 0));
+                                                    (flags & QNT_GEN_BATCH_PREFILL) != 0, (flags & QNT_GEN_KEEP_RNG) != 0));
 }
 
 int qnt_session_step(qnt_model* m, int n) {
@@ -467,6 +475,67 @@ int qnt_session_read(qnt_model* m, int* out_ids, int max_ids, qnt_gen_stats* sta
         stats->kernels_per_step = m->eng.kernels_per_step();
     }
     return r;
+}
+
+int qnt_model_nll(qnt_model* m, const int* ids, int n, double* nll) {
+    if (!m || !nll || n < 0 || (n > 0 && !ids)) return set_err(QNT_ERR_INVALID, "bad argument");
+    return engine_code(m->eng, m->eng.nll(ids, n, nll));
+}
+
+int qnt_session_feed(qnt_model* m, const int* ids, int n) {
+    if (!m || (n > 0 && !ids) || n < 0) return set_err(QNT_ERR_INVALID, "bad argument");
+    return engine_code(m->eng, m->eng.session_feed(ids, n));
+}
+
+int qnt_session_rewind(qnt_model* m, int n_drop) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.session_rewind(n_drop));
+}
+
+int qnt_session_last(qnt_model* m, int* token, int* length) {
+    if (!m) return set_err(QNT_ERR_INVALID, "null model");
+    return engine_code(m->eng, m->eng.session_last(token, length));
+}
+
+// ---------------------------------------------------------------- text
+
+int qnt_tokenizer_open(const char* path, qnt_tokenizer** out) {
+    if (!path || !out) return set_err(QNT_ERR_INVALID, "null argument");
+    *out = nullptr;
+    auto t = std::make_unique<qnt_tokenizer>();
+    std::string err;
+    if (!t->file.open(path, &err)) return set_err(QNT_ERR_IO, err);
+    try {
+        t->bpe = std::make_unique<qb::BpeTokenizer>(t->file.tokenizer());
+    } catch (const std::exception& e) {
+        return set_err(QNT_ERR_IO, e.what());
+    }
+    *out = t.release();
+    return QNT_OK;
+}
+
+void qnt_tokenizer_free(qnt_tokenizer* t) { delete t; }
+
+int qnt_tokenizer_n_tokens(const qnt_tokenizer* t) { return t ? t->bpe->n_tokens() : 0; }
+
+int qnt_tokenize(const qnt_tokenizer* t, const char* text, size_t len, int* ids, int max_ids) {
+    if (!t || (len > 0 && !text) || max_ids < 0 || (max_ids > 0 && !ids)) return set_err(QNT_ERR_INVALID, "bad argument");
+    const std::vector<int> v = t->bpe->encode(std::string(text ? text : "", len));
+    if (v.size() > size_t(INT32_MAX)) return set_err(QNT_ERR_RANGE, "text encodes to too many tokens");
+    std::memcpy(ids, v.data(), std::min(v.size(), size_t(max_ids)) * sizeof(int));
+    return int(v.size());
+}
+
+int qnt_token_piece(const qnt_tokenizer* t, int id, char* buf, int cap) {
+    if (!t || cap < 0 || (cap > 0 && !buf)) return set_err(QNT_ERR_INVALID, "bad argument");
+    const std::string& p = t->bpe->piece(id);
+    std::memcpy(buf, p.data(), std::min(p.size(), size_t(cap)));
+    return int(p.size());
+}
+
+int qnt_token_id(const qnt_tokenizer* t, const char* literal) {
+    if (!t || !literal) return -1;
+    return t->bpe->special_id(literal);
 }
 
 int qnt_batch_init(qnt_model* m, int max_seqs, int ctx_len) {

@@ -608,6 +608,40 @@ int Engine::forward(int token, int pos, const HeadQueryC* hq, float* out) {
     return 0;
 }
 
+int Engine::nll(const int* ids, int n, double* total) {
+    if (!ids || !total || n < 0) {
+        err_ = "nll: bad argument";
+        return -1;
+    }
+    *total = 0.0;
+    if (n < 2) return 0;
+    if (n > ctx_) {
+        err_ = "nll: more tokens than the context holds";
+        return -5;
+    }
+    if (!nll_acc_) nll_acc_ = static_cast<double*>(dalloc(sizeof(double)));
+    const int V = hp_.vocab_size, nv = n_valid_default();
+    cudaMemsetAsync(nll_acc_, 0, sizeof(double), st_);
+    // Model::forward of every position but the last (full head), each followed by its target's term; one sync at the end
+    for (int p = 0; p + 1 < n; ++p) {
+        const int tp[2] = {ids[p], p};  // SamplerState::token, then (after n_hist) ::pos
+        cudaMemcpyAsync(&ss_->token, &tp[0], 4, cudaMemcpyHostToDevice, st_);
+        cudaMemcpyAsync(&ss_->pos, &tp[1], 4, cudaMemcpyHostToDevice, st_);
+        const int r = run_graph("fwd|full", [&]() -> int {  // the same graph as forward() with the full head
+            QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
+            if (int rr = launch_layers_decode(&ss_->pos)) return rr;
+            QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, V, st_, pdl_));
+            return launch_head(false, 0, V, must_, n_must_, 0, 0, 0, false, 1.f);
+        });
+        if (r) return r;
+        QB_TRY(launch_token_nll(logits_, nv, ids[p + 1], nll_acc_, st_, false));
+    }
+    cudaMemcpyAsync(total, nll_acc_, sizeof(double), cudaMemcpyDeviceToHost, st_);
+    if (int rr = sync_check()) return rr;
+    last_head_rows_ = V;
+    return 0;
+}
+
 int Engine::forward_batch(const int* tokens, int n, int pos0, const HeadQueryC* hq, float* out) {
     if (n <= 0) {
         err_ = "forward_batch needs at least one token";
@@ -675,8 +709,9 @@ int Engine::head(const HeadQueryC* hq, float* out, float* coarse, float* upper) 
     return 0;
 }
 
-int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill) {
-    if (n_prompt <= 0 || n_prompt + 1 >= ctx_) {
+int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill,
+                          bool keep_rng) {
+    if (n_prompt <= 0 || n_prompt >= ctx_) {  // Session::feed: pos() + n >= ctx_len is refused (session.cpp:14)
         err_ = "prompt does not fit in the context";
         return -5;
     }
@@ -702,6 +737,10 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
     // session state: history = prompt, rng = seed | 1 (engine/src/sampler.cpp:15-20)
     SamplerState st{};
     st.rng = (sp.seed ? sp.seed : 0x9E3779B97F4A7C15ULL) | 1ULL;
+    if (keep_rng && sess_.active) {  // Chat::reset keeps its Sampler: the xorshift state carries on
+        if (int rr = sync_check()) return rr;
+        cudaMemcpy(&st.rng, &ss_->rng, sizeof st.rng, cudaMemcpyDeviceToHost);
+    }
     st.n_hist = n_prompt;
     st.pos = n_prompt - 1;
     cudaMemcpyAsync(hist_, prompt, size_t(n_prompt) * 4, cudaMemcpyHostToDevice, st_);
@@ -741,6 +780,7 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
     if (int rr = sync_check()) return rr;
     sess_.active = true;
     sess_.steps = 0;
+    sess_.len = n_prompt;
     return 0;
 }
 
@@ -749,7 +789,11 @@ int Engine::session_step(int n) {
         err_ = "no active session";
         return -1;
     }
-    const int room = ctx_ - 1 - (sess_.n_prompt + sess_.steps);
+    if (sess_.stale) {
+        err_ = "the session was rewound: feed tokens before the next step";
+        return -1;
+    }
+    const int room = ctx_ - 1 - sess_.len;
     n = std::min(n, room);
     if (n <= 0) return 0;
     const SamplerParamsC& sp = sess_.sp;
@@ -796,12 +840,82 @@ int Engine::session_step(int n) {
         if (r) return r;
     }
     sess_.steps += n;
+    sess_.len += n;
     return n;
+}
+
+int Engine::session_feed(const int* ids, int n) {
+    if (!sess_.active) {
+        err_ = "no active session";
+        return -1;
+    }
+    if (n <= 0) return 0;
+    if (sess_.len + n >= ctx_) {  // Session::feed refuses a prompt that reaches the last position (session.cpp:14)
+        err_ = "the fed tokens do not fit in the context";
+        return -5;
+    }
+    const int L = sess_.len;
+    const SamplerParamsC& sp = sess_.sp;
+    cudaMemcpyAsync(hist_ + L, ids, size_t(n) * 4, cudaMemcpyHostToDevice, st_);
+    // the head query of the last fed token (session.cpp:63-79): must = the penalised window of the whole history
+    HeadQueryC hq;
+    std::vector<int> must;
+    if (sess_.sl) {
+        hq.top_k = sess_.K;
+        hq.n_valid = sess_.nv;
+        if (sess_.penal) {
+            const int total = L + n, from = (sp.repeat_window > 0 && total > sp.repeat_window) ? total - sp.repeat_window : 0;
+            must.resize(size_t(total - from));
+            cudaMemcpyAsync(must.data(), hist_ + from, must.size() * 4, cudaMemcpyDeviceToHost, st_);
+            if (int rr = sync_check()) return rr;
+        }
+        hq.must = must.data();
+        hq.n_must = int(must.size());
+    }
+    if (int r = forward_batch(ids, n, L, sess_.sl ? &hq : nullptr, nullptr)) return r;
+    const int counters[2] = {L + n, L + n - 1};  // SamplerState::n_hist, ::pos (adjacent)
+    cudaMemcpyAsync(&ss_->n_hist, counters, sizeof counters, cudaMemcpyHostToDevice, st_);
+    if (!sess_.wide) {
+        if (sess_.penal) QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, sess_.nv, mark_, st_, false));
+        QB_TRY(launch_topk_partial(logits_, sess_.nv, sess_.K, sess_.penal ? 1 : 0, sp.repeat_penalty, mark_, part_buf_,
+                                   n_lists_, st_, false));
+    }
+    if (int rr = sync_check()) return rr;
+    sess_.len = L + n;
+    sess_.stale = false;
+    return 0;
+}
+
+int Engine::session_rewind(int n_drop) {
+    if (!sess_.active || n_drop < 0 || n_drop >= sess_.len) {
+        err_ = "session_rewind: needs an active session and 0 <= n_drop < its length";
+        return -1;
+    }
+    if (n_drop == 0) return 0;
+    sess_.len -= n_drop;
+    const int counters[2] = {sess_.len, sess_.len - 1};
+    cudaMemcpyAsync(&ss_->n_hist, counters, sizeof counters, cudaMemcpyHostToDevice, st_);
+    if (int rr = sync_check()) return rr;
+    sess_.stale = true;  // the logits belong to a dropped token
+    return 0;
+}
+
+int Engine::session_last(int* token, int* length) {
+    if (!sess_.active) {
+        err_ = "no active session";
+        return -1;
+    }
+    if (int rr = sync_check()) return rr;
+    int t = -1;
+    cudaMemcpy(&t, &ss_->token, 4, cudaMemcpyDeviceToHost);
+    if (token) *token = t;
+    if (length) *length = sess_.len;
+    return 0;
 }
 
 int Engine::session_read(int* out_ids, int max_ids, GenStats* stats) {
     if (int rr = sync_check()) return rr;
-    const int n = std::min(sess_.steps, max_ids);
+    const int n = std::min(sess_.len - sess_.n_prompt, max_ids);
     if (n > 0) cudaMemcpy(out_ids, hist_ + sess_.n_prompt, size_t(n) * 4, cudaMemcpyDeviceToHost);
     if (stats) {
         HeadState h;

@@ -60,6 +60,9 @@ public:
     // Model::head (model.h:47): head of the last token again.  coarse/upper get the shortlist pass's scores.
     int head(const HeadQueryC* hq, float* out, float* coarse, float* upper);
     int last_head_rows() const { return last_head_rows_; }
+    // The perplexity's sum (tools/cli/main.cpp:261-282): token by token, the full head's -log softmax of ids[p + 1]
+    // after ids[0..p], summed over p < n - 1 into *total.
+    int nll(const int* ids, int n, double* total);
     bool has_shortlist() const { return head_q4_ != nullptr; }
 
     // Session::feed + Session::generate (session.cpp:13-52) with sampling on the device: the prompt is prefilled,
@@ -70,9 +73,18 @@ public:
 
     // The same loop in pieces: prefill the prompt, run n decode steps (sample -> append -> forward, one CUDA graph
     // replay each), read the sampled ids.  generate() = begin + step(n_gen) + read.
-    int session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill);
+    int session_begin(const int* prompt, int n_prompt, const SamplerParamsC& sp, bool use_shortlist, bool batch_prefill,
+                      bool keep_rng = false);
     int session_step(int n);
     int session_read(int* out_ids, int max_ids, GenStats* stats);
+    // Session::feed after the first (session.cpp:13-31): appends ids to the history and prefills them at the next
+    // positions; the next step samples from the last one's logits.  The sampler state (xorshift) carries on.
+    int session_feed(const int* ids, int n);
+    // Forgets the last n_drop history tokens (a sampled stop token, which the reference never appends); a feed must
+    // come before the next step.
+    int session_rewind(int n_drop);
+    // Waits for the queued steps: the last sampled id and the history length.
+    int session_last(int* token, int* length);
 
     // Batched serving (greedy): up to max_seqs sequences of up to ctx positions each, KV caches of their own.
     int batch_init(int max_seqs, int ctx);
@@ -197,10 +209,13 @@ private:
     void* part_buf_ = nullptr;
     WideScratch wide_{};  // the sorting sampler's scratch (top_k 0 or > 32)
     unsigned* status_ = nullptr;
+    double* nll_acc_ = nullptr;  // the perplexity's running sum
 
     struct Sess {
         bool active = false, sl = false, penal = false, wide = false;
+        bool stale = false;  // rewound: the logits are not the last token's until the next feed
         int K = 1, nv = 0, n_prompt = 0, steps = 0;
+        int len = 0;         // history length (= positions in the KV cache)
         SamplerParamsC sp;
     } sess_;
     ExpTab exptab_{};

@@ -107,6 +107,9 @@ cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int pen
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
                                 int hist_cap, cudaStream_t st, bool pdl);
 
+// nll.cu: *acc += -log softmax(logits[0..n_valid))[target] (the perplexity's term), f64 accumulation.
+cudaError_t launch_token_nll(const float* logits, int n_valid, int target, double* acc, cudaStream_t st, bool pdl);
+
 // The sampler for any top_k (sampler_wide.cu): top_k <= 0 (every candidate) or top_k > 32.  A stable radix sort of
 // (logit, id) over ids < n_valid, then the softmax / min-p / top-p / draw of the n best on one CTA.  Temperature > 0
 // only (greedy takes the argmax path).  Scratch: 4 arrays of n_valid words and a digit histogram.

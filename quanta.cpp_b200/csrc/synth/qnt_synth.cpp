@@ -342,7 +342,9 @@ int qnt_synth_write(const char* path, const qnt_synth_cfg* c) {
         put_u32(head, 1);  // tied embeddings
         put_u32(head, 1);  // qkv bias
         put_u32(head, c->flags);
-        const std::vector<uint8_t> tok = tokenizer_section(c->n_tokens > 0 ? c->n_tokens : c->vocab_size);
+        const std::vector<uint8_t> tok = c->tok_blob && c->tok_len
+                                             ? std::vector<uint8_t>(c->tok_blob, c->tok_blob + c->tok_len)
+                                             : tokenizer_section(c->n_tokens > 0 ? c->n_tokens : c->vocab_size);
         put_u32(head, uint32_t(tok.size()));
         head.insert(head.end(), tok.begin(), tok.end());
 

@@ -17,6 +17,8 @@ typedef struct qnt_synth_cfg {
     uint64_t seed;
     int n_threads;   // 0 = all hardware threads
     unsigned flags;  // header flags (1 = FLAG_HADAMARD_DOWN: the reference transforms the SwiGLU output before down)
+    const unsigned char* tok_blob;  // a complete tokenizer section to write instead of the synthetic byte vocabulary
+    uint64_t tok_len;               // (its vocabulary size must equal n_tokens; 0 / null: the synthetic one)
 } qnt_synth_cfg;
 
 int qnt_synth_write(const char* path, const qnt_synth_cfg* cfg);  // 0 on success

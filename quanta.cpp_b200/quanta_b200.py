@@ -54,7 +54,8 @@ class GenStatsC(C.Structure):
 class SynthCfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in "vocab_size dim n_layers n_heads n_kv_heads head_dim ffn_dim max_seq".split()] + [
         ("rope_theta", C.c_float), ("norm_eps", C.c_float)] + [(n, C.c_int) for n in "mlp_q4 q4_group shortlist n_tokens".split()] + [
-        ("w_std", C.c_float), ("seed", C.c_uint64), ("n_threads", C.c_int), ("flags", C.c_uint32)]
+        ("w_std", C.c_float), ("seed", C.c_uint64), ("n_threads", C.c_int), ("flags", C.c_uint32),
+        ("tok_blob", C.c_char_p), ("tok_len", C.c_uint64)]
 
 
 @dataclass
@@ -125,6 +126,17 @@ def lib() -> C.CDLL:
         L.qnt_sampler_free.argtypes = [P]
         L.qnt_sampler_free.restype = None
         L.qnt_bench_mma_i8.argtypes = [I, C.POINTER(C.c_double)]
+        L.qnt_session_feed.argtypes = [P, P, I]
+        L.qnt_model_nll.argtypes = [P, P, I, C.POINTER(C.c_double)]
+        L.qnt_session_rewind.argtypes = [P, I]
+        L.qnt_session_last.argtypes = [P, C.POINTER(I), C.POINTER(I)]
+        L.qnt_tokenizer_open.argtypes = [C.c_char_p, C.POINTER(P)]
+        L.qnt_tokenizer_free.argtypes = [P]
+        L.qnt_tokenizer_free.restype = None
+        L.qnt_tokenizer_n_tokens.argtypes = [P]
+        L.qnt_tokenize.argtypes = [P, C.c_char_p, C.c_size_t, P, I]
+        L.qnt_token_piece.argtypes = [P, I, C.c_char_p, I]
+        L.qnt_token_id.argtypes = [P, C.c_char_p]
         L.qnt_sampler_sample_noalloc.argtypes = [C.POINTER(SamplerParamsC), C.POINTER(C.c_uint64), P, I, P, I,
                                                  C.POINTER(I), P]
         _lib = L
@@ -256,6 +268,44 @@ def bench_mma_i8(iters: int = 4096) -> float:
     _check(lib().qnt_bench_mma_i8(iters, C.byref(v)))
     return v.value
 
+class Tokenizer:
+    """Tokenizer (engine/src/tokenizer.h:15-39) of a .qnt file, on the host: encode(text) -> ids, decode(id) -> bytes,
+    token_id(literal) -> special id or -1."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        _check(lib().qnt_tokenizer_open(str(path).encode(), C.byref(h)))
+        self.h = h
+        self.n_tokens = lib().qnt_tokenizer_n_tokens(h)
+
+    def encode(self, text) -> np.ndarray:
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        n = _check(lib().qnt_tokenize(self.h, b, len(b), None, 0))
+        out = np.zeros(max(n, 1), np.int32)
+        _check(lib().qnt_tokenize(self.h, b, len(b), _ptr(out), n))
+        return out[:n]
+
+    def decode(self, ids) -> bytes:
+        if np.isscalar(ids):
+            ids = [ids]
+        parts = []
+        for i in ids:
+            n = _check(lib().qnt_token_piece(self.h, int(i), None, 0))
+            buf = C.create_string_buffer(max(n, 1))
+            lib().qnt_token_piece(self.h, int(i), buf, n)
+            parts.append(buf.raw[:n])
+        return b"".join(parts)
+
+    def token_id(self, literal: str) -> int:
+        return lib().qnt_token_id(self.h, literal.encode())
+
+    def close(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.qnt_tokenizer_free(self.h)
+        self.h = None
+
+    __del__ = close
+
 # ---------------------------------------------------------------- model level
 
 def head_query(top_k=0, n_valid=0, must=None):
@@ -322,6 +372,13 @@ class Model:
             return self._logits.copy(), coarse, upper
         return self._logits.copy()
 
+    def nll(self, ids) -> float:
+        """Sum over p of -log softmax(logits after ids[:p+1])[ids[p+1]] (the CLI's ppl); perplexity = exp(nll/(n-1))."""
+        t = np.ascontiguousarray(ids, np.int32)
+        v = C.c_double(0)
+        _check(lib().qnt_model_nll(self.h, _ptr(t), t.size, C.byref(v)))
+        return v.value
+
     @property
     def last_head_rows(self) -> int:
         return lib().qnt_model_last_head_rows(self.h)
@@ -378,6 +435,19 @@ class Model:
     def session_step(self, n: int) -> int:
         return _check(lib().qnt_session_step(self.h, n))
 
+    def session_feed(self, ids):
+        t = np.ascontiguousarray(ids, np.int32)
+        _check(lib().qnt_session_feed(self.h, _ptr(t), t.size))
+
+    def session_rewind(self, n_drop: int):
+        _check(lib().qnt_session_rewind(self.h, n_drop))
+
+    def session_last(self):
+        """(last sampled id, history length) after the queued steps."""
+        tok, n = C.c_int(-1), C.c_int(0)
+        _check(lib().qnt_session_last(self.h, C.byref(tok), C.byref(n)))
+        return tok.value, n.value
+
     def session_read(self, max_ids: int = 1 << 16):
         out = np.zeros(max(max_ids, 1), np.int32)
         st = GenStatsC()
@@ -398,9 +468,11 @@ TINY = dict(vocab_size=5000, dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_
 
 
 def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: bool = True, q4_group: int = 128,
-                seed: int = 1234, w_std: float = 0.02, threads: int = 0, overwrite: bool = False, flags: int = 0) -> Path:
+                seed: int = 1234, w_std: float = 0.02, threads: int = 0, overwrite: bool = False, flags: int = 0,
+                tokenizer: bytes | None = None) -> Path:
     """Writes a seeded random-init .qnt (q4mix = attention Q8_0 + MLP GPTQ-sym int4; or all Q8_0); flags = the header
-    flags (1: FLAG_HADAMARD_DOWN)."""
+    flags (1: FLAG_HADAMARD_DOWN); tokenizer = a complete tokenizer section (its token count must be shape's n_tokens)
+    instead of the synthetic byte vocabulary."""
     global _synth
     path = Path(path)
     if path.exists() and not overwrite:
@@ -415,7 +487,7 @@ def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: 
     cfg = SynthCfg(**{k: shape[k] for k in ("vocab_size", "dim", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn_dim",
                                              "max_seq", "rope_theta", "norm_eps", "n_tokens")},
                    mlp_q4=int(mlp_q4), q4_group=q4_group, shortlist=int(shortlist), w_std=w_std, seed=seed,
-                   n_threads=threads, flags=flags)
+                   n_threads=threads, flags=flags, tok_blob=tokenizer, tok_len=len(tokenizer) if tokenizer else 0)
     path.parent.mkdir(parents=True, exist_ok=True)
     tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
     if _synth.qnt_synth_write(str(tmp).encode(), C.byref(cfg)) != 0:

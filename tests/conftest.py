@@ -13,6 +13,7 @@ ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT / "quanta.cpp_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
 
 MODEL_DIR = Path(os.environ.get("QNT_MODEL_DIR", "/tmp/qnt_models"))
 
@@ -48,10 +49,15 @@ def models(qb):
             "tiny_q4sl": dict(shape=qb.TINY, mlp_q4=True, shortlist=True, seed=11),
             "tiny_long": dict(shape=dict(qb.TINY, max_seq=2048), mlp_q4=True, shortlist=True, seed=13),
             "tiny_had": dict(shape=qb.TINY, mlp_q4=True, shortlist=True, seed=17, flags=1),  # FLAG_HADAMARD_DOWN
+            "tiny_text": dict(shape=qb.TINY, mlp_q4=False, shortlist=False, seed=19),  # + a trained BPE vocabulary
             "q8_0": dict(shape=qb.QWEN05B, mlp_q4=False, shortlist=False, seed=1234),
             "q4mix_sl": dict(shape=qb.QWEN05B, mlp_q4=True, shortlist=True, seed=1234),
         }
-        p = qb.synth_model(MODEL_DIR / f"{name}.qnt", **specs[name])
+        spec = specs[name]
+        if name == "tiny_text":
+            import tokenizer_vocab
+            spec = dict(spec, tokenizer=tokenizer_vocab.tokenizer_section(qb.TINY["n_tokens"]))
+        p = qb.synth_model(MODEL_DIR / f"{name}.qnt", **spec)
         made[name] = p
         return p
 
