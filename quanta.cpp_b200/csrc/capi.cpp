@@ -146,7 +146,7 @@ int matmul_dev(const qnt_dtensor* W, const int8_t* qx, const float* dx, int n, i
             return set_err(QNT_ERR_INVALID, "tensor-core matmul needs 16-byte aligned activations");
         if (n == 0 || r1 == r0) return QNT_OK;
         // the kernel reads the activation scales block-major: a stream-ordered transposed copy
-        const int nb = W->m.cols / 32, ldt = (n + 31) & ~31;
+        const int nb = W->m.cols / 32, ldt = (n + 63) & ~63;  // a whole number of the kernel's 64-token tiles
         const bool own = dxt == nullptr;
         if (own) {
             e = cudaMallocAsync(reinterpret_cast<void**>(&dxt), size_t(nb) * ldt * 4, s);
@@ -298,7 +298,7 @@ static int host_mm(const qnt_dtensor* W, const int8_t* qx, const float* dx, int 
     if (!W || !qx || !dx || !out || r0 < 0 || r1 > W->m.rows || r0 > r1 || n <= 0)
         return set_err(QNT_ERR_INVALID, "bad arguments");
     if (r0 == r1) return QNT_OK;
-    const int cols = W->m.cols, nb = cols / 32, ldt = (n + 31) & ~31;
+    const int cols = W->m.cols, nb = cols / 32, ldt = (n + 63) & ~63;
     const size_t qbytes = size_t(n) * cols, dbytes = size_t(n) * nb * 4;
     const size_t doff = align256(qbytes), toff = doff + align256(dbytes), ooff = toff + align256(size_t(nb) * ldt * 4);
     const size_t obytes = size_t(n) * r1 * 4;

@@ -725,6 +725,7 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
     // sampled ids do not change (only the count of exact rows does).
     const bool sl = use_shortlist && has_shortlist() && !wide && K + 8 <= 32;
     const bool penal = sp.repeat_penalty != 1.0f;
+    const bool had_session = sess_.active;
     sess_ = Sess{};
     sess_.active = false;
     sess_.sp = sp;
@@ -737,7 +738,7 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
     // session state: history = prompt, rng = seed | 1 (engine/src/sampler.cpp:15-20)
     SamplerState st{};
     st.rng = (sp.seed ? sp.seed : 0x9E3779B97F4A7C15ULL) | 1ULL;
-    if (keep_rng && sess_.active) {  // Chat::reset keeps its Sampler: the xorshift state carries on
+    if (keep_rng && had_session) {  // Chat::reset keeps its Sampler: the xorshift state carries on
         if (int rr = sync_check()) return rr;
         cudaMemcpy(&st.rng, &ss_->rng, sizeof st.rng, cudaMemcpyDeviceToHost);
     }
