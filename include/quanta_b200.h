@@ -257,6 +257,12 @@ void* qnt_model_stream(const qnt_model* m);
  * *tops = int8 TOP/s over the slowest SM.  The roofline denominator of the tensor-core matmul. */
 int qnt_bench_mma_i8(int iters, double* tops);
 
+/* Diagnostics (no reference counterpart): runs the tensor-core matmul's bounded wait on an mbarrier that nothing
+ * completes, with `limit` tries (1..2^20; each try may sleep up to 20 us), on `stream`.  The wait runs out, the kernel
+ * records the timeout in the calling thread's status word and returns, and the call reports it as QNT_ERR_DEVICE --
+ * the path a real timeout takes, shown without a fault; the context stays usable. */
+int qnt_wait_probe(unsigned limit, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -520,8 +520,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
     }
     // ---- outputs in position order, dimensions (2 lane, 2 lane + 1) per lane as one f32x2 pair: the product
     // a_j * v_jd as fma(v, a, -0.0) (exactly fmul's rounding; a mul feeding the add would be contracted), then the add
-    unsigned long long o2 = 0ull;
-    const unsigned long long nz2 = f2_pack(a.neg_zero, a.neg_zero);
+    float2 o2 = make_float2(0.f, 0.f);
+    const float2 nz2 = make_float2(a.neg_zero, a.neg_zero);
     fetch(a.vcache, 0);
     for (int p = 0; p < n; p += kPfTile) {
         __syncthreads();
@@ -531,25 +531,25 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
         if (head) {
             const int rows = min(kPfTile, n - p);
             const float* e = Eh + p;
-            const unsigned long long* v2 = reinterpret_cast<const unsigned long long*>(tile) + lane;
+            const float2* v2 = reinterpret_cast<const float2*>(tile) + lane;
             int j = 0;
             for (; j + 8 <= rows; j += 8) {
                 float av[8];
-                unsigned long long vv[8];
+                float2 vv[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     av[k] = e[j + k];
                     vv[k] = v2[(j + k) * (kPfStrideV / 2)];
                 }
 #pragma unroll
-                for (int k = 0; k < 8; ++k) o2 = f2_add(o2, f2_fma(vv[k], f2_pack(av[k], av[k]), nz2));
+                for (int k = 0; k < 8; ++k) o2 = __fadd2_rn(o2, __ffma2_rn(vv[k], make_float2(av[k], av[k]), nz2));
             }
-            for (; j < rows; ++j) o2 = f2_add(o2, f2_fma(v2[j * (kPfStrideV / 2)], f2_pack(e[j], e[j]), nz2));
+            for (; j < rows; ++j) o2 = __fadd2_rn(o2, __ffma2_rn(v2[j * (kPfStrideV / 2)], make_float2(e[j], e[j]), nz2));
         }
     }
     if (head) {
         float2* o = reinterpret_cast<float2*>(out + (size_t(t) * a.n_heads + size_t(g) * group + warp) * kHd);
-        o[lane] = f2_unpack(o2);
+        o[lane] = o2;
     }
 }
 

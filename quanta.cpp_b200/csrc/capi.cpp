@@ -565,6 +565,14 @@ int qnt_model_debug_buffer(qnt_model* m, int what, float* out) {
 
 void* qnt_model_stream(const qnt_model* m) { return m ? static_cast<void*>(m->eng.stream()) : nullptr; }
 
+int qnt_wait_probe(unsigned limit, void* stream) {
+    if (limit == 0 || limit > (1u << 20)) return set_err(QNT_ERR_INVALID, "qnt_wait_probe: 0 < limit <= 2^20 tries");
+    cudaError_t e = t_ops.ready();
+    if (e == cudaSuccess) e = qb::launch_wait_probe(limit, t_ops.status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "qnt_wait_probe");
+    return qnt_ops_check(stream);
+}
+
 int qnt_bench_mma_i8(int iters, double* tops) {
     if (iters <= 0 || !tops) return set_err(QNT_ERR_INVALID, "qnt_bench_mma_i8: iters > 0 and an output needed");
     unsigned status = 0;

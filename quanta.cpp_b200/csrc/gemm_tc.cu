@@ -83,15 +83,29 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: false when it gave up or another role aborted (then the caller unwinds).
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, volatile int* abort_flag, unsigned* status) {
-    for (unsigned i = 0; i < kWaitLimit; ++i) {
+// Bounded wait: false when it gave up after `limit` tries or another role aborted (then the caller unwinds).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, volatile int* abort_flag, unsigned* status,
+                                          unsigned limit = kWaitLimit) {
+    for (unsigned i = 0; i < limit; ++i) {
         if (mbar_try(b, parity)) return true;
         if (*abort_flag) return false;
     }
     *abort_flag = 1;
     set_error(status, ERR_WAIT_TIMEOUT);
     return false;
+}
+
+// The timeout path of the waits above, on its own: one thread waits on an mbarrier that nothing arrives on, with the
+// given limit, so the wait runs out, sets ERR_WAIT_TIMEOUT and the kernel returns (no copies or MMAs in flight).
+__global__ void k_wait_probe(unsigned limit, unsigned* status) {
+    __shared__ uint64_t never;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&never, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_wait(&never, 0, &abort_flag, status, limit);
+    }
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -307,16 +321,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         __syncwarp();
         if (lane == 0)
             for (int j = 0; j < kSlots; ++j) mbar_arrive(&slot_free[j]);
-        const unsigned long long nz2 = f2_pack(__int_as_float(int(g.nzero)), __int_as_float(int(g.nzero)));
+        const float2 nz2 = make_float2(__int_as_float(int(g.nzero)), __int_as_float(int(g.nzero)));
         int step = 0, u = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
             const int row = m0 + q * 32 + lane;
             const bool row_ok = row < g.r1;
-            unsigned long long acc[kTpt / 2];  // tokens (2 j, 2 j + 1) of this thread's 8
+            float2 acc[kTpt / 2];  // tokens (2 j, 2 j + 1) of this thread's 8
 #pragma unroll
-            for (int j = 0; j < kTpt / 2; ++j) acc[j] = 0ull;
+            for (int j = 0; j < kTpt / 2; ++j) acc[j] = make_float2(0.f, 0.f);
             for (int j = 0; j < nst && ok; ++j, ++u) {
                 const int d = u % kEpiRing, dround = u / kEpiRing, kk = min(kKPS, nks - j * kKPS);
                 const unsigned char* e = epi_ring + d * kEpi;
@@ -343,17 +357,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                     const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {  // acc = acc + (float(s) * dw) * dx, each rounded as in the reference
-                        const unsigned long long dw2 = f2_pack(dw[b], dw[b]);
+                        const float2 dw2 = make_float2(dw[b], dw[b]);
                         const float nm = -fmul(kMagicF, dw[b]);
-                        const unsigned long long nm2 = f2_pack(nm, nm);
+                        const float2 nm2 = make_float2(nm, nm);
                         const float4* sdx = reinterpret_cast<const float4*>(e + ((h * kStageBlocks + b) * kTileTok + cg * kTpt) * 4);
                         const float4 x0 = sdx[0], x1 = sdx[1];
-                        const unsigned long long dx2[4] = {f2_pack(x0.x, x0.y), f2_pack(x0.z, x0.w), f2_pack(x1.x, x1.y),
-                                                           f2_pack(x1.z, x1.w)};
+                        const float2 dx2[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w), make_float2(x1.x, x1.y),
+                                               make_float2(x1.z, x1.w)};
 #pragma unroll
-                        for (int i = 0; i < kTpt / 2; ++i)
-                            acc[i] = f2_add(acc[i], f2_fma(f2_fma(f2_pack_bits(v[8 * b + 2 * i], v[8 * b + 2 * i + 1]), dw2, nm2),
-                                                           dx2[i], nz2));
+                        for (int i = 0; i < kTpt / 2; ++i) {
+                            const float2 f = make_float2(__int_as_float(v[8 * b + 2 * i]), __int_as_float(v[8 * b + 2 * i + 1]));
+                            acc[i] = __fadd2_rn(acc[i], __ffma2_rn(__ffma2_rn(f, dw2, nm2), dx2[i], nz2));
+                        }
                     }
                 }
                 __syncwarp();  // the ring entry is read before it is freed
@@ -363,7 +378,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             float res[kTpt];
 #pragma unroll
             for (int i = 0; i < kTpt / 2; ++i) {
-                const float2 p = f2_unpack(acc[i]);
+                const float2 p = acc[i];
                 res[2 * i] = p.x;
                 res[2 * i + 1] = p.y;
             }
@@ -691,6 +706,11 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
 }
 
 int argmax_parts(int rows) { return ((rows + kTileRows - 1) / kTileRows) * 4; }
+
+cudaError_t launch_wait_probe(unsigned limit, unsigned* status, cudaStream_t st) {
+    k_wait_probe<<<1, 32, 0, st>>>(limit, status);
+    return cudaGetLastError();
+}
 
 cudaError_t bench_mma_i8(int iters, double* tops, unsigned* status_host) {
     int dev = 0, sms = 0;

@@ -61,4 +61,8 @@ cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids,
 // M = 128, N = 256, K = 32 from shared memory; *tops = 2 M N K * MMAs / the slowest SM's time (synchronous).
 cudaError_t bench_mma_i8(int iters, double* tops, unsigned* status);
 
+// One bounded mbarrier wait that nothing completes, with `limit` tries (each may suspend up to 20 us): sets
+// ERR_WAIT_TIMEOUT in *status and returns -- the error path of the matmul's waits, exercised on its own.
+cudaError_t launch_wait_probe(unsigned limit, unsigned* status, cudaStream_t st);
+
 }  // namespace qb

@@ -126,6 +126,7 @@ def lib() -> C.CDLL:
         L.qnt_sampler_free.argtypes = [P]
         L.qnt_sampler_free.restype = None
         L.qnt_bench_mma_i8.argtypes = [I, C.POINTER(C.c_double)]
+        L.qnt_wait_probe.argtypes = [C.c_uint, P]
         L.qnt_session_feed.argtypes = [P, P, I]
         L.qnt_model_nll.argtypes = [P, P, I, C.POINTER(C.c_double)]
         L.qnt_session_rewind.argtypes = [P, I]

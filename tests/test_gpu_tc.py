@@ -44,3 +44,19 @@ def test_tc_matmul_ragged_rows_and_256_tokens(qb, dt):
     simt = W.matmul(Q, D, 37, 4801, impl=1)
     assert np.array_equal(tc, simt)
     assert not tc[:, :37].any() and not tc[:, 4801:].any()
+
+
+def test_bounded_wait_runs_out_and_reports(qb):
+    """A device wait that nothing completes, with a short limit, ends in QNT_ERR_DEVICE (the timeout bit the matmul's
+    waits set), not a hang or a fault; the thread's status is cleared and the device stays usable."""
+    L = qb.lib()
+    rc = L.qnt_wait_probe(200, None)
+    assert rc == -6, (rc, L.qnt_last_error())
+    assert b"status bits 1" in L.qnt_last_error()
+    assert L.qnt_ops_check(None) == 0  # the bit was cleared
+    rng = np.random.default_rng(0)
+    W = qb.DeviceTensor(2, 128, 256, np.concatenate([rng.integers(-127, 128, 128 * 256).astype(np.int8).view(np.uint8),
+                                                      np.full(128 * 8, 0x2000, np.uint16).view(np.uint8)]))
+    q, d = qb.quantize_q8(rng.standard_normal(256).astype(np.float32))
+    assert np.isfinite(W.matvec(q, d)).all()
+    W.close()
