@@ -435,7 +435,7 @@ constexpr int kPfTileBytes = kPfTile * kPfStrideV * 4;
 
 __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const float* __restrict__ Q,
                                                            const int* __restrict__ pos_dev, int n_cap,
-                                                           float* __restrict__ out, TokMap tm) {
+                                                           float* __restrict__ out, TokMap tm, QuantOut qo) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* sq = reinterpret_cast<float*>(smem);                    // [kGmax][kHd]
     float* tile = sq + kGmax * kHd;                                // [kPfTile][kPfStride] K, [kPfTile][kPfStrideV] V
@@ -548,8 +548,26 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
         }
     }
     if (head) {
-        float2* o = reinterpret_cast<float2*>(out + (size_t(t) * a.n_heads + size_t(g) * group + warp) * kHd);
-        o[lane] = o2;
+        const int hh = g * group + warp;
+        if (qo.xq) {  // quantize_q8 of the head's two 32-blocks: lanes 0-15 hold block 2 hh, lanes 16-31 block 2 hh + 1
+            float amax = fmaxf(fabsf(o2.x), fabsf(o2.y));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float d = div127(amax);
+            const float inv = d > 0.f ? __frcp_rn(d) : 0.0f;
+            const int dim = a.n_heads * kHd, b = 2 * hh + (lane >> 4);
+            char2 qv;
+            qv.x = (signed char)round_away(fmul(o2.x, inv));
+            qv.y = (signed char)round_away(fmul(o2.y, inv));
+            reinterpret_cast<char2*>(qo.xq + size_t(t) * dim + hh * kHd)[lane] = qv;
+            if ((lane & 15) == 0) {
+                qo.dx[size_t(t) * (dim / QK) + b] = d;
+                if (qo.dxt) qo.dxt[size_t(b) * qo.ldt + t] = d;
+            }
+        } else {
+            float2* o = reinterpret_cast<float2*>(out + (size_t(t) * a.n_heads + hh) * kHd);
+            o[lane] = o2;
+        }
     }
 }
 
@@ -560,16 +578,20 @@ inline size_t prefill_smem_bytes(int group, int n_cap) {
 }  // namespace
 
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
-                                cudaStream_t st, bool pdl, TokMap tm) {
+                                cudaStream_t st, bool pdl, TokMap tm, const QuantOut* qo) {
     const int group = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
     if (a.head_dim != kHd || group < 1 || group > kGmax || group * a.n_kv != a.n_heads || pos_bound < (tm.pos ? 1 : n_tok))
         return cudaErrorInvalidValue;
     const size_t smem = prefill_smem_bytes(group, pos_bound);
     if (smem > 227 * 1024) {  // very long contexts (single sequence only)
         if (tm.pos) return cudaErrorInvalidValue;
-        return launch_attn(a, Q, pos_dev, n_tok, out, st, pdl);
+        cudaError_t e = launch_attn(a, Q, pos_dev, n_tok, out, st, pdl);
+        if (e == cudaSuccess && qo)
+            e = launch_norm_quant_rows(out, nullptr, n_tok, a.n_heads * kHd, 0.f, qo->xq, qo->dx, qo->dxt, qo->ldt, st, pdl);
+        return e;
     }
-    return launch_pdl(k_attn_prefill, dim3(a.n_kv, n_tok), dim3(kThreads), smem, st, pdl, a, Q, pos_dev, pos_bound, out, tm);
+    return launch_pdl(k_attn_prefill, dim3(a.n_kv, n_tok), dim3(kThreads), smem, st, pdl, a, Q, pos_dev, pos_bound, out, tm,
+                      qo ? *qo : QuantOut{});
 }
 
 cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, float* out, cudaStream_t st, bool pdl) {

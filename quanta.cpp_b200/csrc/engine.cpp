@@ -155,6 +155,8 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
     if (const char* v = std::getenv("QNT_GRAPHS")) use_graphs_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_FUSE_QKV")) fuse_qkv_attn_ = std::atoi(v) != 0;
     if (const char* v = std::getenv("QNT_FUSE_O")) fuse_o_ = std::atoi(v) != 0;
+    if (const char* v = std::getenv("QNT_TC_SWIGLU")) tc_swiglu_ = std::atoi(v) != 0;
+    if (const char* v = std::getenv("QNT_TC_QKV")) tc_qkv_ = std::atoi(v) != 0;
     try {
         const HostTensor& emb = file_.require("model.embed_tokens.weight");
         embed_ = upload_matrix(emb);
@@ -437,13 +439,15 @@ int Engine::launch_layers_decode(const int* pos_dev) {
     return 0;
 }
 
-int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out) {
+int Engine::launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out, bool residual) {
     const int8_t* xq = ffn_in ? HQ_ : XQ_;
     const float* dx = ffn_in ? HD_ : DX_;
-    if (wmap && n >= kTcChunkMin) {
-        QB_TRY(launch_matmul_tc(W, *wmap, ffn_in ? tm_h_ : tm_x_, n, 0, W.rows, out, W.rows, status_, st_));
+    if (wmap && n >= kTcChunkMin) {  // residual: the add onto X_ happens in the matmul's store
+        QB_TRY(launch_matmul_tc(W, *wmap, ffn_in ? tm_h_ : tm_x_, n, 0, W.rows, residual ? X_ : out, W.rows, status_, st_,
+                                pdl_, residual));
     } else {
         QB_TRY(launch_matmul_simt(W, xq, dx, n, 0, W.rows, out, W.rows, st_));
+        if (residual) QB_TRY(launch_residual(X_, out, (long long)n * W.rows, st_, pdl_));
     }
     return 0;
 }
@@ -463,18 +467,28 @@ int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm) {
             aa.max_chunks = (bctx_ + 63) / 64;
         }
         QB_TRY(launch_norm_quant_rows(X_, L.attn_norm, n, dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, pdl_));
-        if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_qkv_epilogue(qa, R_, n, pos_dev, Q_, st_, pdl_, tm));
-        QB_TRY(launch_attn_prefill(aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_, tm));
-        QB_TRY(launch_norm_quant_rows(ATT_, nullptr, n, dim, 0.f, XQ_, DX_, DXT_, kChunk, st_, pdl_));
-        if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
+        if (tc_qkv_ && L.tc && n >= kTcChunkMin && L.qkv.rows % 128 == 0) {  // bias, RoPE and the K/V stores in the matmul's epilogue
+            QB_TRY(launch_matmul_tc_qkv(L.qkv, L.t_qkv, tm_x_, n, qa, pos_dev, tm, Q_, status_, st_, pdl_));
+        } else {
+            if (int r = launch_matmul(L.qkv, L.tc ? &L.t_qkv : nullptr, false, n, R_)) return r;
+            QB_TRY(launch_qkv_epilogue(qa, R_, n, pos_dev, Q_, st_, pdl_, tm));
+        }
+        QuantOut qo;  // the attention quantizes its outputs for o_proj
+        qo.xq = XQ_;
+        qo.dx = DX_;
+        qo.dxt = DXT_;
+        qo.ldt = kChunk;
+        QB_TRY(launch_attn_prefill(aa, Q_, pos_dev, n, pos_bound, ATT_, st_, pdl_, tm, &qo));
+        if (int r = launch_matmul(L.o, L.tc ? &L.t_o : nullptr, false, n, R_, true)) return r;
         QB_TRY(launch_norm_quant_rows(X_, L.ffn_norm, n, dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, pdl_));
-        if (int r = launch_matmul(L.gu, L.tc ? &L.t_gu : nullptr, false, n, R_)) return r;
-        QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, exptab_, st_, pdl_, HF_));
+        if (tc_swiglu_ && L.tc && n >= kTcChunkMin && !hadamard_) {  // SwiGLU + quantize in the matmul's epilogue
+            QB_TRY(launch_matmul_tc_swiglu(L.gu, L.t_gu, tm_x_, n, HQ_, HD_, HDT_, kChunk, exptab_, status_, st_, pdl_));
+        } else {
+            if (int r = launch_matmul(L.gu, L.tc ? &L.t_gu : nullptr, false, n, R_)) return r;
+            QB_TRY(launch_swiglu_quant(R_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, exptab_, st_, pdl_, HF_));
+        }
         if (hadamard_) QB_TRY(launch_fwht_quant(HF_, n, hp_.ffn_dim, HQ_, HD_, HDT_, kChunk, st_, pdl_));
-        if (int r = launch_matmul(L.down, L.tc ? &L.t_down : nullptr, true, n, R_)) return r;
-        QB_TRY(launch_residual(X_, R_, (long long)n * dim, st_, pdl_));
+        if (int r = launch_matmul(L.down, L.tc ? &L.t_down : nullptr, true, n, R_, true)) return r;
     }
     return 0;
 }
@@ -1006,7 +1020,7 @@ int Engine::batch_reset(int seq) {
 
 int Engine::batch_head(int n, int* host_ids) {
     QB_TRY(launch_norm_quant_rows(X_, final_norm_, n, hp_.dim, hp_.norm_eps, XQ_, DX_, DXT_, kChunk, st_, false));
-    QB_TRY(launch_matmul_tc_argmax(lm_head_, t_head_, tm_x_, n, n_valid_default(), bcand_, status_, st_));
+    QB_TRY(launch_matmul_tc_argmax(lm_head_, t_head_, tm_x_, n, n_valid_default(), bcand_, status_, st_, pdl_));
     QB_TRY(launch_argmax_reduce(bcand_, argmax_parts(lm_head_.rows), n, bids_, nullptr, st_));
     cudaMemcpyAsync(host_ids, bids_, size_t(n) * 4, cudaMemcpyDeviceToHost, st_);
     return sync_check();

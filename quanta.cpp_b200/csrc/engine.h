@@ -148,7 +148,7 @@ private:
     int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
                     int n_list, bool penal, float penalty);
     // Prefill / batched matmul into R_: the tensor cores when the layer has TMA sources and n is large enough.
-    int launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out);
+    int launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out, bool residual = false);
     // TMA source of W for the tensor-core matmul (a Q4_0 matrix gets its int8 copy here); false: CUDA cores only
     bool tc_weights(const DMat& W, TcMap* map);
     int run_graph(const std::string& key, const std::function<int()>& body);
@@ -163,6 +163,11 @@ private:
     bool pdl_ = true, use_graphs_ = true;
     bool fuse_qkv_attn_ = true;  // decode: q|k|v matvec fused into the attention kernel (QNT_FUSE_QKV=0: two kernels)
     bool fuse_o_ = true;         // decode: o_proj folded into the attention + gate|up kernels (QNT_FUSE_O=0: its own kernel)
+    // chunks: SwiGLU + quantize (QNT_TC_SWIGLU=1) or bias, RoPE and the K/V stores (QNT_TC_QKV=1) in the matmul's
+    // epilogue instead of their own kernels.  Off: the matmul is bound by its epilogue's issue rate, and the added
+    // epilogue work costs more than the launch and the f32 round trip it saves (measured at 256 sequences).
+    bool tc_swiglu_ = false;
+    bool tc_qkv_ = false;
     float *OT_ = nullptr, *X2_ = nullptr;  // o_proj block terms [dim][n_heads * 2] and the o_proj residual [dim]
     bool hadamard_ = false;                // FLAG_HADAMARD_DOWN file
     float* HF_ = nullptr;                  // (hadamard_) f32 SwiGLU outputs [kChunk][ffn] before the transform

@@ -34,6 +34,7 @@
 #include "gemm_tc.h"
 #include "head_kernels.h"
 #include "kernels.cuh"
+#include "qkv_pair.cuh"
 
 namespace qb {
 
@@ -58,6 +59,7 @@ constexpr int kEpiDX = kKPS * kStageBlocks * kTileTok * 4;  // activation scales
 constexpr int kEpiDW = 2176;                       // weight scales of a stage: [K-step][kDWRows] x 4 f16 (padded)
 constexpr int kEpi = kEpiDX + kEpiDW;              // epilogue ring entry (TMA destinations on 128-byte boundaries)
 constexpr int kEpiRing = 8;                        // >= stages + slots / kKPS: the scales never hold the producer back
+constexpr int kSwiBytes = 2 * 8 * 32 * kTpt * 4;   // EPI 3: silu(gate) of each gate warp, per tile parity
 constexpr unsigned kWaitLimit = 1u << 22;
 constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
 
@@ -89,6 +91,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, volatile
     for (unsigned i = 0; i < limit; ++i) {
         if (mbar_try(b, parity)) return true;
         if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    set_error(status, ERR_WAIT_TIMEOUT);
+    return false;
+}
+
+// The same bounded wait run by a whole warp: every lane polls and a vote makes the outcome warp-uniform (a lane that
+// saw the phase complete polls again until all have; a completed phase keeps reading as complete until the barrier
+// moves on, which needs this warp's own arrival).
+__device__ __forceinline__ bool warp_wait(uint64_t* b, unsigned parity, volatile int* abort_flag, unsigned* status) {
+    for (unsigned i = 0; i < kWaitLimit; ++i) {
+        if (__all_sync(0xffffffffu, mbar_try(b, parity))) return true;
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
     }
     *abort_flag = 1;
     set_error(status, ERR_WAIT_TIMEOUT);
@@ -192,15 +207,25 @@ __device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid
     return av > bv || (av == bv && aid < bid);
 }
 
-// EPI 0: store the rows; EPI 1: per 32-row group and token, the best (value, id) into g.cand.
+// EPI 0: store the rows; EPI 1: per 32-row group and token, the best (value, id) into g.cand; EPI 2: add the rows onto
+// out (the residual stream: out = out + row, the reference's separate residual add, one rounding); EPI 3: gate|up rows
+// interleaved per 32-row block (gate block j = rows 64 j .., up block j = rows 64 j + 32 ..): the SwiGLU
+// h = silu(gate) * up and its quantize_q8 per block go to g.hq / g.hd / g.hdt (the gate rows' quadrant passes
+// silu(gate) to the up rows' quadrant through shared memory; one warp then holds a whole 32-block of h per token);
+// EPI 4: fused q|k|v rows (pair-interleaved: rows 2 i, 2 i + 1 sit in adjacent lanes), the even lane of each pair
+// applies bias and RoPE and stores q (f32) or the f16 K / V cache entry of each token.
+// Programmatic dependent launch: the weight loads (and the set-up) need nothing from the previous kernel on the stream,
+// so only the threads that read its outputs (the activation producers) or write this kernel's (the epilogue) wait.
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDW,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned (the 128-byte swizzle's period), as an offset from smem_raw so that loads stay shared-window
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* epi_ring = smem + kStages * kStageBytes;
+    float* swi = reinterpret_cast<float*>(epi_ring + kEpiRing * kEpi);
     __shared__ uint64_t full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots];
     __shared__ uint64_t epi_full[kEpiRing], epi_empty[kEpiRing], fin;
     __shared__ uint32_t tmem_base;
@@ -212,6 +237,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     auto tile_m0 = [&](int tile) { return g.r0 + (tile / n_tt) * kTileRows; };
     auto tile_t0 = [&](int tile) { return (tile % n_tt) * kTileTok; };
     const int my_tiles = (n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+    pdl_launch_dependents();  // the next kernel waits for this grid's completion before it reads anything
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -245,6 +271,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     if (warp == 0) {
         if (lane < 8) {  // TMA producers: kind = lane / 2 (weights, activations, their scales), parity of the stage
             const int kind = lane >> 1, ph = lane & 1;
+            if (kind & 1) pdl_wait();  // the activations and their scales come from the previous kernel
             int u = 0;
             bool go = true;
             for (int tile = blockIdx.x; tile < n_tiles && go; tile += gridDim.x) {
@@ -314,6 +341,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             mma_commit(&fin);  // arrives once every MMA issued above has completed
         }
     } else if (warp >= 4) {  // epilogue
+        pdl_wait();
         const int q = warp & 3, cg = (warp - 4) >> 2;
         const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * kTpt);
         for (int j = 0; j < kSlots; ++j) tmem_st8x4_fill(my_cols + uint32_t(j * kCols), kMagic);
@@ -322,9 +350,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         if (lane == 0)
             for (int j = 0; j < kSlots; ++j) mbar_arrive(&slot_free[j]);
         const float2 nz2 = make_float2(__int_as_float(int(g.nzero)), __int_as_float(int(g.nzero)));
-        int step = 0, u = 0;
+        int step = 0, u = 0, par = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, par ^= 1) {
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
             const int row = m0 + q * 32 + lane;
             const bool row_ok = row < g.r1;
@@ -334,12 +362,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             for (int j = 0; j < nst && ok; ++j, ++u) {
                 const int d = u % kEpiRing, dround = u / kEpiRing, kk = min(kKPS, nks - j * kKPS);
                 const unsigned char* e = epi_ring + d * kEpi;
-                int got = 1;
-                if (lane == 0) got = mbar_wait(&epi_full[d], dround & 1, ab, g.status);
+                if (!warp_wait(&epi_full[d], dround & 1, ab, g.status)) {
+                    ok = false;
+                    break;
+                }
                 for (int h = 0; h < kk; ++h, ++step) {
                     const int slot = step % kSlots, use = step / kSlots;
-                    if (lane == 0 && got) got = mbar_wait(&mma_done[slot], use & 1, ab, g.status);
-                    if (!__shfl_sync(0xffffffffu, got, 0)) {  // warp-uniform before the .sync.aligned TMEM load
+                    if (!warp_wait(&mma_done[slot], use & 1, ab, g.status)) {  // warp-uniform before the .sync.aligned TMEM load
                         ok = false;
                         break;
                     }
@@ -388,6 +417,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                     for (int i = 0; i < kTpt; ++i) {
                         const int t = t0 + cg * kTpt + i;
                         if (t < g.n) g.out[size_t(t) * g.ldo + row] = res[i];
+                    }
+                }
+            } else if (EPI == 3) {
+                float* xg = swi + ((par * 8 + (q >> 1) * 4 + cg) * kTpt) * 32;  // [token i][lane]
+                if (!(q & 1)) {
+#pragma unroll
+                    for (int i = 0; i < kTpt; ++i) xg[i * 32 + lane] = fdiv(res[i], fadd(1.0f, exp_ref(-res[i], g.tab)));
+                }
+                asm volatile("bar.sync %0, 64;" ::"r"(1 + (q >> 1) * 4 + cg) : "memory");  // the gate/up warp pair
+                if (q & 1) {
+                    const int j = (m0 - g.r0 + 32 * (q - 1)) >> 6, ffn = (g.r1 - g.r0) >> 1, nbk = ffn / QK;
+#pragma unroll
+                    for (int i = 0; i < kTpt; ++i) {
+                        const int t = t0 + cg * kTpt + i;
+                        float d;
+                        const int8_t qv = quantize_lane(fmul(xg[i * 32 + lane], res[i]), &d);  // the whole warp
+                        if (t < g.n) {
+                            g.hq[size_t(t) * ffn + j * QK + lane] = qv;
+                            if (lane == 0) {
+                                g.hd[size_t(t) * nbk + j] = d;
+                                if (g.hdt) g.hdt[size_t(j) * g.ldt + t] = d;
+                            }
+                        }
+                    }
+                }
+            } else if (EPI == 4) {
+                PairIn p;
+                pair_bias(g.qa, row & ~1, p);
+                const int pos_base = g.tm.pos ? 0 : __ldcg(g.pos_dev);
+#pragma unroll
+                for (int i = 0; i < kTpt; ++i) {
+                    const float vb = __shfl_down_sync(0xffffffffu, res[i], 1);  // row + 1 of the pair
+                    const int t = t0 + cg * kTpt + i;
+                    if (!(lane & 1) && t < g.n) {
+                        QkvArgs a = g.qa;
+                        int pos = pos_base + t;
+                        if (g.tm.pos) {  // this token's sequence cache
+                            pos = __ldcg(g.tm.pos + t);
+                            const long long off = __ldcg(g.tm.off + t);
+                            a.kcache += off;
+                            a.vcache += off;
+                        }
+                        pair_rope(a, row, pos, p);
+                        qkv_pair_store(a, row, res[i], vb, pos, p, g.qout + size_t(t) * a.n_heads * a.head_dim);
+                    }
+                }
+            } else if (EPI == 2) {
+                if (row_ok) {
+#pragma unroll
+                    for (int i = 0; i < kTpt; ++i) {
+                        const int t = t0 + cg * kTpt + i;
+                        if (t < g.n) {
+                            float* o = g.out + size_t(t) * g.ldo + row;
+                            *o = fadd(__ldcg(o), res[i]);
+                        }
                     }
                 }
             } else {
@@ -557,12 +641,12 @@ cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, 
     return cudaGetLastError();
 }
 
-size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kEpiRing) * kEpi + 1024; }
+size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kEpiRing) * kEpi + kSwiBytes + 1024; }
 
 namespace {
 
 template <int EPI>
-cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, GemmTcArgs g, cudaStream_t st) {
+cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, GemmTcArgs g, cudaStream_t st, bool pdl) {
     g.nzero = 0x80000000u;
     static int sms = 0;
     if (sms == 0) {
@@ -575,10 +659,7 @@ cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, Ge
     const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
     const size_t smem = gemm_tc_smem();
     if (W.dtype != DT_Q8_0 && W.dtype != DT_Q4_0) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    k_gemm_tc<EPI><<<grid, kTcThreads, smem, st>>>(wmap.m, act.q.m, wmap.s, act.d.m, g);
-    return cudaGetLastError();
+    return launch_pdl(k_gemm_tc<EPI>, grid, dim3(kTcThreads), smem, st, pdl, wmap.m, act.q.m, wmap.s, act.d.m, g);
 }
 
 // Peak probe: back-to-back tcgen05.mma.kind::i8 (M = 128, N = 256, K = 32, the largest single-CTA shape) on operands
@@ -691,7 +772,7 @@ __global__ void __launch_bounds__(256) k_argmax_reduce(const Cand* __restrict__ 
 }  // namespace
 
 cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int r0, int r1, float* out, int ldo,
-                             unsigned* status, cudaStream_t st) {
+                             unsigned* status, cudaStream_t st, bool pdl, bool residual) {
     if (r1 <= r0 || n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
     GemmTcArgs g{};
@@ -702,7 +783,43 @@ cudaError_t launch_matmul_tc(const DMat& W, const TcMap& wmap, const TcAct& act,
     g.out = out;
     g.ldo = ldo;
     g.status = status;
-    return launch_tc_any<0>(W, wmap, act, g, st);
+    return residual ? launch_tc_any<2>(W, wmap, act, g, st, pdl) : launch_tc_any<0>(W, wmap, act, g, st, pdl);
+}
+
+cudaError_t launch_matmul_tc_swiglu(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int8_t* hq, float* hd,
+                                    float* hdt, int ldt, const ExpTab& tab, unsigned* status, cudaStream_t st, bool pdl) {
+    if (n <= 0) return cudaSuccess;
+    if (W.cols % (kStageBlocks * QK) != 0 || W.rows % kTileRows != 0 || !hq || !hd) return cudaErrorInvalidValue;
+    GemmTcArgs g{};
+    g.r0 = 0;
+    g.r1 = W.rows;
+    g.nb = W.cols / QK;
+    g.n = n;
+    g.status = status;
+    g.hq = hq;
+    g.hd = hd;
+    g.hdt = hdt;
+    g.ldt = ldt;
+    g.tab = tab;
+    return launch_tc_any<3>(W, wmap, act, g, st, pdl);
+}
+
+cudaError_t launch_matmul_tc_qkv(const DMat& W, const TcMap& wmap, const TcAct& act, int n, const QkvArgs& qa,
+                                 const int* pos_dev, TokMap tm, float* qout, unsigned* status, cudaStream_t st, bool pdl) {
+    if (n <= 0) return cudaSuccess;
+    if (W.cols % (kStageBlocks * QK) != 0 || W.rows % kTileRows != 0 || !qout || (!tm.pos && !pos_dev))
+        return cudaErrorInvalidValue;
+    GemmTcArgs g{};
+    g.r0 = 0;
+    g.r1 = W.rows;
+    g.nb = W.cols / QK;
+    g.n = n;
+    g.status = status;
+    g.qa = qa;
+    g.tm = tm;
+    g.pos_dev = pos_dev;
+    g.qout = qout;
+    return launch_tc_any<4>(W, wmap, act, g, st, pdl);
 }
 
 int argmax_parts(int rows) { return ((rows + kTileRows - 1) / kTileRows) * 4; }
@@ -743,7 +860,7 @@ cudaError_t bench_mma_i8(int iters, double* tops, unsigned* status_host) {
 }
 
 cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAct& act, int n, int n_valid, void* cand,
-                                    unsigned* status, cudaStream_t st) {
+                                    unsigned* status, cudaStream_t st, bool pdl) {
     if (n <= 0) return cudaSuccess;
     if (W.cols % (kStageBlocks * QK) != 0) return cudaErrorInvalidValue;
     GemmTcArgs g{};
@@ -754,7 +871,7 @@ cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAc
     g.status = status;
     g.n_valid = n_valid;
     g.cand = cand;
-    return launch_tc_any<1>(W, wmap, act, g, st);
+    return launch_tc_any<1>(W, wmap, act, g, st, pdl);
 }
 
 cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids, float* vals, cudaStream_t st) {

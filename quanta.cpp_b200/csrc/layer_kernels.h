@@ -73,8 +73,18 @@ cudaError_t launch_attn(const AttnArgs& a, const float* Q, const int* pos_dev, i
 bool qkv_attn_supported(const QkvArgs& qa, const AttnArgs& a, const DMat* o);
 cudaError_t launch_qkv_attn(const QkvArgs& qa, const AttnArgs& a, const float* X, const float* norm_w, float eps,
                             const int* pos_dev, float* Qout, float* out, cudaStream_t st, bool pdl, const OArgs* o = nullptr);
+// The attention output quantized for o_proj (quantize_q8 of each token's n_heads * 64 outputs): xq [t][dim], dx [t][dim / 32]
+// and, when dxt is set, dxt[b * ldt + t].
+struct QuantOut {
+    int8_t* xq = nullptr;
+    float* dx = nullptr;
+    float* dxt = nullptr;
+    int ldt = 0;
+};
+// With qo, the outputs go to qo (quantized in the kernel, the same bits as launch_norm_quant_rows without a norm) instead
+// of out; out is then scratch for the long-context fallback.
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
-                                cudaStream_t st, bool pdl, TokMap tm = TokMap{});
+                                cudaStream_t st, bool pdl, TokMap tm = TokMap{}, const QuantOut* qo = nullptr);
 // DXT (optional): the block scales also block-major, DXT[b * ldt + t] (the tensor-core matmul's layout).
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
                                    float* DXT, int ldt, cudaStream_t st, bool pdl);
