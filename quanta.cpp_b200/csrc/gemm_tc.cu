@@ -178,20 +178,18 @@ __device__ __forceinline__ void tmem_st8x4_fill(uint32_t taddr, unsigned x) {
 }
 
 // TMEM -> registers: this warp's 32 lanes, 8 consecutive 32-bit columns at each of taddr + 32 b (b = 0..3):
-// v[8 b + i] = column 32 b + i.
-__device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
+// v[8 b + i] = column 32 b + i.  One load and its wait per block.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int* v) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%32];\n\t"
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n\t"
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%34];\n\t"
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%24,%25,%26,%27,%28,%29,%30,%31}, [%35];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
         "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr), "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u)
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+        : "r"(taddr)
         : "memory");
+}
+__device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) tmem_ld8(taddr + 32u * b, v + 8 * b);
 }
 
 // The accumulators start at the bits of 2^23 + 2^22 (kMagic): the MMA then leaves 12582912 + s, whose float value

@@ -67,3 +67,28 @@ def test_batch_rejects_duplicates_and_overflow(qb, models):
             m.prefill_batch(1, list(range(9)))
     finally:
         m.close()
+
+
+def test_matmul_epilogue_fusions_give_the_same_ids(qb, models, monkeypatch):
+    """QNT_TC_SWIGLU=1 / QNT_TC_QKV=1 move the SwiGLU + quantize and the q|k|v bias / RoPE / K-V stores into the
+    tensor-core matmul's epilogue: the batched ids (64 sequences at Qwen2.5-0.5B shapes) equal the default kernels'."""
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 4000, 48) for _ in range(64)]
+
+    def run():
+        m = qb.Model(models("q4mix_sl"), ctx_len=1024)
+        try:
+            m.batch_init(64, 128)
+            got = [[m.prefill_batch(s, p)] for s, p in enumerate(prompts)]
+            for _ in range(6):
+                nxt = m.decode_batch(np.arange(64), [g[-1] for g in got])
+                for s in range(64):
+                    got[s].append(int(nxt[s]))
+            return got
+        finally:
+            m.close()
+
+    want = run()
+    monkeypatch.setenv("QNT_TC_SWIGLU", "1")
+    monkeypatch.setenv("QNT_TC_QKV", "1")
+    assert run() == want
