@@ -43,23 +43,31 @@ namespace {
 constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = 128 + 32 * kEpiWarps;
 constexpr int kTileRows = 128;
-constexpr int kTileTok = 32;                       // tokens per tile (MMA N)
 constexpr int kStageBlocks = 4;                    // quant blocks per K-step (128 bytes of K)
-constexpr int kCols = kTileTok * kStageBlocks;     // TMEM columns of a K-step: block b of token t in column 32 b + t
-constexpr int kTpt = kTileTok / 4;                 // tokens per epilogue thread
-constexpr int kSlots = 4;                          // TMEM accumulator slots of kCols columns
-constexpr int kTmemCols = kSlots * kCols;          // 512: the whole TMEM of the SM (one CTA per SM)
+constexpr int kSlots = 4;                          // TMEM accumulator slots (one K-step each)
 constexpr int kASw = kTileRows * 128;              // swizzled int8 weight tile of a K-step
-constexpr int kB = kTileTok * 128;                 // activation tile of a K-step
 constexpr int kKPS = 2;                            // K-steps per stage (per TMA instruction)
 constexpr int kStages = 4;
-constexpr int kStageBytes = kKPS * (kASw + kB);    // kKPS weight tiles, then kKPS activation tiles
 constexpr int kDWRows = kTileRows + 2;             // weight-scale rows per load (from an even row: 16-byte start)
-constexpr int kEpiDX = kKPS * kStageBlocks * kTileTok * 4;  // activation scales of a stage: [block][token] f32
 constexpr int kEpiDW = 2176;                       // weight scales of a stage: [K-step][kDWRows] x 4 f16 (padded)
-constexpr int kEpi = kEpiDX + kEpiDW;              // epilogue ring entry (TMA destinations on 128-byte boundaries)
 constexpr int kEpiRing = 8;                        // >= stages + slots / kKPS: the scales never hold the producer back
-constexpr int kSwiBytes = 2 * 8 * 32 * kTpt * 4;   // EPI 3: silu(gate) of each gate warp, per tile parity
+
+// Token tiles of TOK = 32 tokens, or 16 where a matrix has too few 32-token tiles to fill the SMs (twice the tiles,
+// each with half the epilogue work).
+template <int TOK>
+struct Tc {
+    static constexpr int cols = TOK * kStageBlocks;         // TMEM columns of a K-step: block b of token t in column TOK b + t
+    static constexpr int tpt = TOK / 4;                     // tokens per epilogue thread
+    static constexpr int tmem_cols = kSlots * cols;         // 512 / 256 (a power of two, as tcgen05.alloc requires)
+    static constexpr int b = TOK * 128;                     // activation tile of a K-step
+    static constexpr int stage_bytes = kKPS * (kASw + b);   // kKPS weight tiles, then kKPS activation tiles
+    static constexpr int epi_dx = kKPS * kStageBlocks * TOK * 4;  // activation scales of a stage: [block][token] f32
+    static constexpr int epi = epi_dx + kEpiDW;             // epilogue ring entry (TMA destinations 128-byte aligned)
+    static constexpr int swi_bytes = 2 * 8 * 32 * tpt * 4;  // EPI 3: silu(gate) of each gate warp, per tile parity
+    // instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = TOK
+    static constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(TOK >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
+    static_assert(epi % 128 == 0 && (tmem_cols & (tmem_cols - 1)) == 0, "ring entries and TMEM allocation");
+};
 constexpr unsigned kWaitLimit = 1u << 22;
 constexpr unsigned kSuspendHintNs = 20000;  // a waiting thread sleeps (up to this long) instead of spinning
 
@@ -147,15 +155,12 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
     return d;
 }
 
-// Instruction descriptor: int32 accumulator, signed int8 A and B, both K-major, M = 128, N = kTileTok.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileTok >> 3) << 17) | (uint32_t(kTileRows >> 4) << 24);
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, bool accumulate) {
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate ? 1 : 0), "r"(0), "r"(0), "r"(0), "r"(0)
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1 : 0), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -165,31 +170,55 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-// registers -> TMEM: the same 32 lanes x 4 x 8 columns, all set to x.
-__device__ __forceinline__ void tmem_st8x4_fill(uint32_t taddr, unsigned x) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%3], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
-        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-        "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u), "r"(x)
-        : "memory");
+// registers -> TMEM: this warp's 32 lanes, NC columns at each of taddr + 4 NC b (b = 0..3), all set to x.
+template <int NC>
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, unsigned x) {
+    if constexpr (NC == 8) {
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%3], {%4,%4,%4,%4,%4,%4,%4,%4};\n\t"
+            "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+            "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u), "r"(x)
+            : "memory");
+    } else {
+        static_assert(NC == 4, "4 or 8 columns per block");
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x4.b32 [%1], {%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x4.b32 [%2], {%4,%4,%4,%4};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x4.b32 [%3], {%4,%4,%4,%4};\n\t"
+            "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+            "r"(taddr + 16u), "r"(taddr + 32u), "r"(taddr + 48u), "r"(x)
+            : "memory");
+    }
 }
 
-// TMEM -> registers: this warp's 32 lanes, 8 consecutive 32-bit columns at each of taddr + 32 b (b = 0..3):
-// v[8 b + i] = column 32 b + i.  One load and its wait per block.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int* v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-        : "r"(taddr)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_ld8x4(uint32_t taddr, int (&v)[32]) {
+// TMEM -> registers: this warp's 32 lanes, NC consecutive 32-bit columns at each of taddr + 4 NC b (b = 0..3):
+// v[NC b + i] = column 4 NC b + i.  One load and its wait per block.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_blocks(uint32_t taddr, int* v) {
 #pragma unroll
-    for (int b = 0; b < 4; ++b) tmem_ld8(taddr + 32u * b, v + 8 * b);
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t ta = taddr + uint32_t(4 * NC * b);
+        int* w = v + NC * b;
+        if constexpr (NC == 8) {
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+                "tcgen05.wait::ld.sync.aligned;"
+                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                : "r"(ta)
+                : "memory");
+        } else {
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n\t"
+                "tcgen05.wait::ld.sync.aligned;"
+                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                : "r"(ta)
+                : "memory");
+        }
+    }
 }
 
 // The accumulators start at the bits of 2^23 + 2^22 (kMagic): the MMA then leaves 12582912 + s, whose float value
@@ -214,26 +243,27 @@ __device__ __forceinline__ bool cand_better(float av, int aid, float bv, int bid
 // applies bias and RoPE and stores q (f32) or the f16 K / V cache entry of each token.
 // Programmatic dependent launch: the weight loads (and the set-up) need nothing from the previous kernel on the stream,
 // so only the threads that read its outputs (the activation producers) or write this kernel's (the epilogue) wait.
-template <int EPI>
+template <int EPI, int TOK>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmDW,
                                                            const __grid_constant__ CUtensorMap tmDX, GemmTcArgs g) {
+    using C = Tc<TOK>;
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte aligned (the 128-byte swizzle's period), as an offset from smem_raw so that loads stay shared-window
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    unsigned char* epi_ring = smem + kStages * kStageBytes;
-    float* swi = reinterpret_cast<float*>(epi_ring + kEpiRing * kEpi);
+    unsigned char* epi_ring = smem + kStages * C::stage_bytes;
+    float* swi = reinterpret_cast<float*>(epi_ring + kEpiRing * C::epi);
     __shared__ uint64_t full[kStages], empty[kStages], mma_done[kSlots], slot_free[kSlots];
     __shared__ uint64_t epi_full[kEpiRing], epi_empty[kEpiRing], fin;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nks = g.nb / kStageBlocks, nst = (nks + kKPS - 1) / kKPS;  // K-steps and stages per tile
-    const int n_tt = (g.n + kTileTok - 1) / kTileTok, n_tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * n_tt;
+    const int n_tt = (g.n + TOK - 1) / TOK, n_tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * n_tt;
     // tile -> (first weight row, first token); tiles blockIdx.x, blockIdx.x + gridDim.x, ...
     auto tile_m0 = [&](int tile) { return g.r0 + (tile / n_tt) * kTileRows; };
-    auto tile_t0 = [&](int tile) { return (tile % n_tt) * kTileTok; };
+    auto tile_t0 = [&](int tile) { return (tile % n_tt) * TOK; };
     const int my_tiles = (n_tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
     pdl_launch_dependents();  // the next kernel waits for this grid's completion before it reads anything
 
@@ -256,7 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                     "r"(kTmemCols)
+                     "r"(C::tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -283,12 +313,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                             go = false;
                             break;
                         }
-                        unsigned char* st = smem + s * kStageBytes;
+                        unsigned char* st = smem + s * C::stage_bytes;
                         if (kind == 0) {
                             mbar_expect_tx(&full[s], kKPS * kASw);
                             tma_load_3d(st, &tmA, 0, m0, j * kKPS, &full[s]);
                         } else {
-                            mbar_expect_tx(&full[s], kKPS * kB);
+                            mbar_expect_tx(&full[s], kKPS * C::b);
                             tma_load_3d(st + kKPS * kASw, &tmB, 0, t0, j * kKPS, &full[s]);
                         }
                     } else {
@@ -297,12 +327,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                             go = false;
                             break;
                         }
-                        unsigned char* e = epi_ring + d * kEpi;
+                        unsigned char* e = epi_ring + d * C::epi;
                         if (kind == 2) {  // x even: a TMA start must be 16-byte aligned
                             mbar_expect_tx(&epi_full[d], kKPS * kDWRows * 8);
-                            tma_load_2d(e + kEpiDX, &tmDW, m0 & ~1, j * kKPS, &epi_full[d]);
+                            tma_load_2d(e + C::epi_dx, &tmDW, m0 & ~1, j * kKPS, &epi_full[d]);
                         } else {
-                            mbar_expect_tx(&epi_full[d], kEpiDX);
+                            mbar_expect_tx(&epi_full[d], C::epi_dx);
                             tma_load_2d(e, &tmDX, t0, j * kKPS * kStageBlocks, &epi_full[d]);
                         }
                     }
@@ -317,7 +347,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 const int s = u % kStages, round = u / kStages;
                 if (!mbar_wait(&full[s], round & 1, ab, g.status)) break;
                 const int j = u % nst, kk = min(kKPS, nks - j * kKPS);  // K-steps of this stage in its tile
-                unsigned char* st = smem + s * kStageBytes;
+                unsigned char* st = smem + s * C::stage_bytes;
                 for (int h = 0; h < kk; ++h, ++step) {
                     const int slot = step % kSlots, use = step / kSlots;
                     // phase `use` of slot_free: the epilogue refilled the slot with the magic (phase 0: the initial fill)
@@ -327,11 +357,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                     }
                     tc_fence_after();
                     const unsigned char* a = st + h * kASw;
-                    const unsigned char* b = st + kKPS * kASw + h * kB;
+                    const unsigned char* b = st + kKPS * kASw + h * C::b;
 #pragma unroll
                     for (int k = 0; k < kStageBlocks; ++k)  // accumulate onto the magic-filled columns
-                        mma_i8(tmem + uint32_t(slot * kCols + k * kTileTok), sw128_desc(a + 32 * k), sw128_desc(b + 32 * k),
-                               true);
+                        mma_i8(tmem + uint32_t(slot * C::cols + k * TOK), sw128_desc(a + 32 * k), sw128_desc(b + 32 * k),
+                               C::idesc, true);
                     mma_commit(&mma_done[slot]);
                 }
                 if (go) mma_commit(&empty[s]);
@@ -341,8 +371,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     } else if (warp >= 4) {  // epilogue
         pdl_wait();
         const int q = warp & 3, cg = (warp - 4) >> 2;
-        const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * kTpt);
-        for (int j = 0; j < kSlots; ++j) tmem_st8x4_fill(my_cols + uint32_t(j * kCols), kMagic);
+        const uint32_t my_cols = tmem + (uint32_t(q * 32) << 16) + uint32_t(cg * C::tpt);
+        for (int j = 0; j < kSlots; ++j) tmem_fill<C::tpt>(my_cols + uint32_t(j * C::cols), kMagic);
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
@@ -354,12 +384,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
             const int row = m0 + q * 32 + lane;
             const bool row_ok = row < g.r1;
-            float2 acc[kTpt / 2];  // tokens (2 j, 2 j + 1) of this thread's 8
+            float2 acc[C::tpt / 2];  // tokens (2 j, 2 j + 1) of this thread's tpt
 #pragma unroll
-            for (int j = 0; j < kTpt / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+            for (int j = 0; j < C::tpt / 2; ++j) acc[j] = make_float2(0.f, 0.f);
             for (int j = 0; j < nst && ok; ++j, ++u) {
                 const int d = u % kEpiRing, dround = u / kEpiRing, kk = min(kKPS, nks - j * kKPS);
-                const unsigned char* e = epi_ring + d * kEpi;
+                const unsigned char* e = epi_ring + d * C::epi;
                 if (!warp_wait(&epi_full[d], dround & 1, ab, g.status)) {
                     ok = false;
                     break;
@@ -371,14 +401,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                         break;
                     }
                     tc_fence_after();
-                    int v[32];  // v[8 b + i]: kMagic + block b's dot of token cg * kTpt + i
-                    tmem_ld8x4(my_cols + uint32_t(slot * kCols), v);
-                    tmem_st8x4_fill(my_cols + uint32_t(slot * kCols), kMagic);  // ready for the slot's next use
+                    int v[4 * C::tpt];  // v[tpt b + i]: kMagic + block b's dot of token cg * tpt + i
+                    tmem_ld_blocks<C::tpt>(my_cols + uint32_t(slot * C::cols), v);
+                    tmem_fill<C::tpt>(my_cols + uint32_t(slot * C::cols), kMagic);  // ready for the slot's next use
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&slot_free[slot]);
                     const uint2 dq =
-                        *reinterpret_cast<const uint2*>(e + kEpiDX + (h * kDWRows + (m0 & 1) + q * 32 + lane) * 8);
+                        *reinterpret_cast<const uint2*>(e + C::epi_dx + (h * kDWRows + (m0 & 1) + q * 32 + lane) * 8);
                     const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&dq.x));
                     const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&dq.y));
                     const float dw[4] = {d01.x, d01.y, d23.x, d23.y};
@@ -387,13 +417,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                         const float2 dw2 = make_float2(dw[b], dw[b]);
                         const float nm = -fmul(kMagicF, dw[b]);
                         const float2 nm2 = make_float2(nm, nm);
-                        const float4* sdx = reinterpret_cast<const float4*>(e + ((h * kStageBlocks + b) * kTileTok + cg * kTpt) * 4);
-                        const float4 x0 = sdx[0], x1 = sdx[1];
-                        const float2 dx2[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w), make_float2(x1.x, x1.y),
-                                               make_float2(x1.z, x1.w)};
+                        const float4* sdx = reinterpret_cast<const float4*>(e + ((h * kStageBlocks + b) * TOK + cg * C::tpt) * 4);
+                        float2 dx2[C::tpt / 2];
 #pragma unroll
-                        for (int i = 0; i < kTpt / 2; ++i) {
-                            const float2 f = make_float2(__int_as_float(v[8 * b + 2 * i]), __int_as_float(v[8 * b + 2 * i + 1]));
+                        for (int k = 0; k < C::tpt / 4; ++k) {
+                            const float4 x = sdx[k];
+                            dx2[2 * k] = make_float2(x.x, x.y);
+                            dx2[2 * k + 1] = make_float2(x.z, x.w);
+                        }
+#pragma unroll
+                        for (int i = 0; i < C::tpt / 2; ++i) {
+                            const float2 f = make_float2(__int_as_float(v[C::tpt * b + 2 * i]), __int_as_float(v[C::tpt * b + 2 * i + 1]));
                             acc[i] = __fadd2_rn(acc[i], __ffma2_rn(__ffma2_rn(f, dw2, nm2), dx2[i], nz2));
                         }
                     }
@@ -402,9 +436,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 if (lane == 0 && ok) mbar_arrive(&epi_empty[d]);
             }
             if (!ok) break;
-            float res[kTpt];
+            float res[C::tpt];
 #pragma unroll
-            for (int i = 0; i < kTpt / 2; ++i) {
+            for (int i = 0; i < C::tpt / 2; ++i) {
                 const float2 p = acc[i];
                 res[2 * i] = p.x;
                 res[2 * i + 1] = p.y;
@@ -412,23 +446,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             if (EPI == 0) {
                 if (row_ok) {
 #pragma unroll
-                    for (int i = 0; i < kTpt; ++i) {
-                        const int t = t0 + cg * kTpt + i;
+                    for (int i = 0; i < C::tpt; ++i) {
+                        const int t = t0 + cg * C::tpt + i;
                         if (t < g.n) g.out[size_t(t) * g.ldo + row] = res[i];
                     }
                 }
             } else if (EPI == 3) {
-                float* xg = swi + ((par * 8 + (q >> 1) * 4 + cg) * kTpt) * 32;  // [token i][lane]
+                float* xg = swi + ((par * 8 + (q >> 1) * 4 + cg) * C::tpt) * 32;  // [token i][lane]
                 if (!(q & 1)) {
 #pragma unroll
-                    for (int i = 0; i < kTpt; ++i) xg[i * 32 + lane] = fdiv(res[i], fadd(1.0f, exp_ref(-res[i], g.tab)));
+                    for (int i = 0; i < C::tpt; ++i) xg[i * 32 + lane] = fdiv(res[i], fadd(1.0f, exp_ref(-res[i], g.tab)));
                 }
                 asm volatile("bar.sync %0, 64;" ::"r"(1 + (q >> 1) * 4 + cg) : "memory");  // the gate/up warp pair
                 if (q & 1) {
                     const int j = (m0 - g.r0 + 32 * (q - 1)) >> 6, ffn = (g.r1 - g.r0) >> 1, nbk = ffn / QK;
 #pragma unroll
-                    for (int i = 0; i < kTpt; ++i) {
-                        const int t = t0 + cg * kTpt + i;
+                    for (int i = 0; i < C::tpt; ++i) {
+                        const int t = t0 + cg * C::tpt + i;
                         float d;
                         const int8_t qv = quantize_lane(fmul(xg[i * 32 + lane], res[i]), &d);  // the whole warp
                         if (t < g.n) {
@@ -445,9 +479,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                 pair_bias(g.qa, row & ~1, p);
                 const int pos_base = g.tm.pos ? 0 : __ldcg(g.pos_dev);
 #pragma unroll
-                for (int i = 0; i < kTpt; ++i) {
+                for (int i = 0; i < C::tpt; ++i) {
                     const float vb = __shfl_down_sync(0xffffffffu, res[i], 1);  // row + 1 of the pair
-                    const int t = t0 + cg * kTpt + i;
+                    const int t = t0 + cg * C::tpt + i;
                     if (!(lane & 1) && t < g.n) {
                         QkvArgs a = g.qa;
                         int pos = pos_base + t;
@@ -464,8 +498,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             } else if (EPI == 2) {
                 if (row_ok) {
 #pragma unroll
-                    for (int i = 0; i < kTpt; ++i) {
-                        const int t = t0 + cg * kTpt + i;
+                    for (int i = 0; i < C::tpt; ++i) {
+                        const int t = t0 + cg * C::tpt + i;
                         if (t < g.n) {
                             float* o = g.out + size_t(t) * g.ldo + row;
                             *o = fadd(__ldcg(o), res[i]);
@@ -475,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             } else {
                 const int mt = tile / n_tt;
 #pragma unroll
-                for (int i = 0; i < kTpt; ++i) {
+                for (int i = 0; i < C::tpt; ++i) {
                     float v = row_ok && row < g.n_valid ? res[i] : -INFINITY;
                     int id = row_ok && row < g.n_valid ? row : INT_MAX;
 #pragma unroll
@@ -487,7 +521,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                             id = pid;
                         }
                     }
-                    const int t = t0 + cg * kTpt + i;
+                    const int t = t0 + cg * C::tpt + i;
                     if (lane == 0 && t < g.n) static_cast<Cand*>(g.cand)[(size_t(mt) * 4 + q) * g.n + t] = Cand{v, id};
                 }
             }
@@ -502,7 +536,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         }
         __syncwarp();
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::tmem_cols) : "memory");
     }
 }
 
@@ -624,13 +658,15 @@ cudaError_t tc_prepare_weights(const DMat& W, void* buf, TcMap* out, cudaStream_
 }
 
 bool make_act_maps(const int8_t* qx, const float* dxt, int rows, int ldt, int cols, TcAct* out) {
-    if (cols % (kStageBlocks * QK) != 0 || rows <= 0 || ldt % kTileTok != 0 || ldt < rows ||
-        reinterpret_cast<uintptr_t>(dxt) % 16 != 0)
+    if (cols % (kStageBlocks * QK) != 0 || rows <= 0 || ldt % 32 != 0 || ldt < rows || reinterpret_cast<uintptr_t>(dxt) % 16 != 0)
         return false;
     const int nb = cols / QK;
-    return encode_kchunks(&out->q.m, qx, uint64_t(rows), uint64_t(cols), kTileTok) &&
-           encode_2d(&out->d.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxt, uint64_t(rows), uint64_t(nb), uint64_t(ldt) * 4, kTileTok,
-                     kKPS * kStageBlocks, CU_TENSOR_MAP_SWIZZLE_NONE);
+    auto maps = [&](int tok, TcActMap* q, TcActMap* d) {  // boxes of one token tile
+        return encode_kchunks(&q->m, qx, uint64_t(rows), uint64_t(cols), uint32_t(tok)) &&
+               encode_2d(&d->m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxt, uint64_t(rows), uint64_t(nb), uint64_t(ldt) * 4,
+                         uint32_t(tok), kKPS * kStageBlocks, CU_TENSOR_MAP_SWIZZLE_NONE);
+    };
+    return maps(32, &out->q, &out->d) && maps(16, &out->q16, &out->d16);
 }
 
 cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, int ldt, cudaStream_t st) {
@@ -639,13 +675,15 @@ cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, 
     return cudaGetLastError();
 }
 
-size_t gemm_tc_smem() { return size_t(kStages) * kStageBytes + size_t(kEpiRing) * kEpi + kSwiBytes + 1024; }
-
 namespace {
 
-template <int EPI>
-cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, GemmTcArgs g, cudaStream_t st, bool pdl) {
-    g.nzero = 0x80000000u;
+template <int TOK>
+size_t gemm_tc_smem() {
+    using C = Tc<TOK>;
+    return size_t(kStages) * C::stage_bytes + size_t(kEpiRing) * C::epi + C::swi_bytes + 1024;
+}
+
+int sm_count() {
     static int sms = 0;
     if (sms == 0) {
         int dev = 0;
@@ -653,11 +691,27 @@ cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, Ge
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
-    const int tiles = ((g.r1 - g.r0 + kTileRows - 1) / kTileRows) * ((g.n + kTileTok - 1) / kTileTok);
-    const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
-    const size_t smem = gemm_tc_smem();
-    if (W.dtype != DT_Q8_0 && W.dtype != DT_Q4_0) return cudaErrorInvalidValue;
-    return launch_pdl(k_gemm_tc<EPI>, grid, dim3(kTcThreads), smem, st, pdl, wmap.m, act.q.m, wmap.s, act.d.m, g);
+    return sms;
+}
+
+// TOK: 32-token tiles, or 16 (TOK = 0: 16 when even the 16-token tiles fit on the SMs at once, i.e. the 32-token tiles
+// would leave half of them idle, and the tokens fill more than one 16-token tile).  Measured at 256 tokens (the
+// batched decode step) the small matrices gain from 16; at 512 they lose (weight tiles loaded twice as often).
+template <int EPI, int TOK = 0>
+cudaError_t launch_tc_any(const DMat& W, const TcMap& wmap, const TcAct& act, GemmTcArgs g, cudaStream_t st, bool pdl) {
+    g.nzero = 0x80000000u;
+    const int sms = sm_count(), row_tiles = (g.r1 - g.r0 + kTileRows - 1) / kTileRows;
+    if constexpr (TOK == 0) {
+        if (2 * row_tiles * ((g.n + 31) / 32) <= sms && g.n > 16) return launch_tc_any<EPI, 16>(W, wmap, act, g, st, pdl);
+        return launch_tc_any<EPI, 32>(W, wmap, act, g, st, pdl);
+    } else {
+        const int tiles = row_tiles * ((g.n + TOK - 1) / TOK);
+        const dim3 grid(unsigned(std::min(tiles, sms)));  // persistent: one CTA per SM at most
+        if (W.dtype != DT_Q8_0 && W.dtype != DT_Q4_0) return cudaErrorInvalidValue;
+        const TcActMap& q = TOK == 16 ? act.q16 : act.q;
+        const TcActMap& d = TOK == 16 ? act.d16 : act.d;
+        return launch_pdl(k_gemm_tc<EPI, TOK>, grid, dim3(kTcThreads), gemm_tc_smem<TOK>(), st, pdl, wmap.m, q.m, wmap.s, d.m, g);
+    }
 }
 
 // Peak probe: back-to-back tcgen05.mma.kind::i8 (M = 128, N = 256, K = 32, the largest single-CTA shape) on operands
@@ -799,7 +853,7 @@ cudaError_t launch_matmul_tc_swiglu(const DMat& W, const TcMap& wmap, const TcAc
     g.hdt = hdt;
     g.ldt = ldt;
     g.tab = tab;
-    return launch_tc_any<3>(W, wmap, act, g, st, pdl);
+    return launch_tc_any<3, 32>(W, wmap, act, g, st, pdl);
 }
 
 cudaError_t launch_matmul_tc_qkv(const DMat& W, const TcMap& wmap, const TcAct& act, int n, const QkvArgs& qa,
@@ -817,7 +871,7 @@ cudaError_t launch_matmul_tc_qkv(const DMat& W, const TcMap& wmap, const TcAct& 
     g.tm = tm;
     g.pos_dev = pos_dev;
     g.qout = qout;
-    return launch_tc_any<4>(W, wmap, act, g, st, pdl);
+    return launch_tc_any<4, 32>(W, wmap, act, g, st, pdl);
 }
 
 int argmax_parts(int rows) { return ((rows + kTileRows - 1) / kTileRows) * 4; }
@@ -869,7 +923,7 @@ cudaError_t launch_matmul_tc_argmax(const DMat& W, const TcMap& wmap, const TcAc
     g.status = status;
     g.n_valid = n_valid;
     g.cand = cand;
-    return launch_tc_any<1>(W, wmap, act, g, st, pdl);
+    return launch_tc_any<1, 32>(W, wmap, act, g, st, pdl);
 }
 
 cudaError_t launch_argmax_reduce(const void* cand, int n_parts, int n, int* ids, float* vals, cudaStream_t st) {

@@ -45,15 +45,15 @@ bool gemm_tc_supported(const DMat& W);
 size_t tc_weight_bytes(const DMat& W);
 // Writes those copies into buf (tc_weight_bytes(W) bytes, 256-byte aligned) on st and encodes the TMA sources.
 cudaError_t tc_prepare_weights(const DMat& W, void* buf, TcMap* out, cudaStream_t st);
-// Quantized activations as TMA sources: q [rows][cols] int8 (32-token boxes) and the block scales in block-major
-// order, dxt[b * ldt + t] = scale of block b of token t (ldt >= rows, a multiple of 32).
+// Quantized activations as TMA sources: q [rows][cols] int8 and the block scales in block-major order,
+// dxt[b * ldt + t] = scale of block b of token t (ldt >= rows, a multiple of 32); boxes of 32 tokens (q, d) and of 16
+// (q16, d16) for the two token-tile widths.
 struct TcActMap {
     CUtensorMap m;
 };
 struct TcAct {
-    TcActMap q, d;
+    TcActMap q, d, q16, d16;
 };
-size_t gemm_tc_smem();
 bool make_act_maps(const int8_t* qx, const float* dxt, int rows, int ldt, int cols, TcAct* out);
 // dxt[b * ldt + t] = dx[t * nb + b] for t < n (the block-major scales from the token-major ones).
 cudaError_t launch_transpose_scales(const float* dx, int n, int nb, float* dxt, int ldt, cudaStream_t st);
