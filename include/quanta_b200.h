@@ -99,7 +99,14 @@ typedef struct qnt_hparams {
 } qnt_hparams;
 
 /* Model::load (engine/src/model.h:35): mmaps the .qnt, uploads every tensor once to HBM in the device layout and
- * allocates one sequence's f16 KV cache for ctx_len positions (<= 0: the file's max_seq).  flags: reserved, 0. */
+ * allocates one sequence's f16 KV cache for ctx_len positions (<= 0: the file's max_seq).  flags: 0, or
+ * QNT_OPEN_NIBBLE_SCREEN: the Exact Shortlist Head screens with the high nibble plane of the Q8 output head (built at
+ * load: rows * cols / 2 bytes, plus an f16 norm per row and 32-block of the dropped low nibbles) instead of the
+ * file's quanta.head_q4 / quanta.head_err (not uploaded), and a file
+ * without those tensors gets a shortlist head too.  Exact rows, tau and the sampled ids are those of the full head
+ * either way; the coarse / upper scores and the count of exact rows differ.  No reference counterpart (the
+ * reference's research notes, docs/PROGRESS.md:121-130, describe the screen). */
+#define QNT_OPEN_NIBBLE_SCREEN 1
 int qnt_model_open(const char* path, int ctx_len, int flags, qnt_model** out);
 void qnt_model_close(qnt_model* m);
 int qnt_model_hparams(const qnt_model* m, qnt_hparams* out);

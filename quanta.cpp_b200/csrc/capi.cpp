@@ -351,11 +351,11 @@ int qnt_matmul_host(const qnt_dtensor* W, const int8_t* qx, const float* dx, int
 // ---------------------------------------------------------------- model level
 
 int qnt_model_open(const char* path, int ctx_len, int flags, qnt_model** out) {
-    (void)flags;
     if (!path || !out) return set_err(QNT_ERR_INVALID, "null argument");
+    if (flags & ~QNT_OPEN_NIBBLE_SCREEN) return set_err(QNT_ERR_INVALID, "unknown qnt_model_open flags");
     auto m = std::make_unique<qnt_model>();
     std::string err;
-    if (!m->eng.load(path, ctx_len, &err)) return set_err(m->eng.file_fault() ? QNT_ERR_IO : QNT_ERR_UNSUPPORTED, err);
+    if (!m->eng.load(path, ctx_len, &err, (flags & QNT_OPEN_NIBBLE_SCREEN) != 0)) return set_err(m->eng.file_fault() ? QNT_ERR_IO : QNT_ERR_UNSUPPORTED, err);
     *out = m.release();
     return QNT_OK;
 }

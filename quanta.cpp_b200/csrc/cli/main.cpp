@@ -30,7 +30,7 @@ struct Args {
     int n_gen = 256;
     int ctx = 4096;
     int threads = 0;  // accepted for the reference's flag set; the device does not use host threads
-    bool batch = true, full_head = false, kv_f32 = false;
+    bool batch = true, full_head = false, kv_f32 = false, nibble_head = false;
     qnt_sampler_params sp{0.7f, 20, 0.8f, 0.0f, 1.1f, 0, 0};
 };
 
@@ -52,6 +52,7 @@ struct Args {
                  "  quanta_b200 selftest                                        check + time kernels (no model needed)\n"
                  "common: --ctx 4096  -t THREADS (ignored: the GPU runs the model)  --no-batch (prefill token by token)\n"
                  "        --full-head (skip the shortlist head)  (--kv-f32 is not available: the device KV cache is f16)\n"
+                 "        --nibble-head (screen the shortlist head with the Q8 head's high nibble plane; no head_q4 needed)\n"
                  "        --ids 1,2,3 (token ids instead of -p / -f text, any command that takes text)\n"
                  "sampling: --temp 0.7 --top-k 20 --top-p 0.8 --min-p 0 --repeat-penalty 1.1 --seed N --greedy\n");
     std::exit(2);
@@ -92,6 +93,7 @@ Args parse(int argc, char** argv) {
         else if (k == "--kv-f32") a.kv_f32 = true;
         else if (k == "--no-batch") a.batch = false;
         else if (k == "--full-head") a.full_head = true;
+        else if (k == "--nibble-head") a.nibble_head = true;
         else if (k == "--temp") a.sp.temperature = float(std::atof(next().c_str()));
         else if (k == "--top-k") a.sp.top_k = std::atoi(next().c_str());
         else if (k == "--top-p") a.sp.top_p = float(std::atof(next().c_str()));
@@ -269,7 +271,8 @@ bool open_model(const Args& a, Model& md) {
         return false;
     }
     auto t0 = Clock::now();
-    if (!ok_or_report(qnt_model_open(a.model.c_str(), a.ctx, 0, &md.m), "load")) return false;
+    if (!ok_or_report(qnt_model_open(a.model.c_str(), a.ctx, a.nibble_head ? QNT_OPEN_NIBBLE_SCREEN : 0, &md.m), "load"))
+        return false;
     qnt_model_hparams(md.m, &md.hp);
     std::fprintf(stderr, "quanta_b200: loaded %s in %.2fs (dim=%d layers=%d heads=%d/%d vocab=%d ctx=%d)\n", a.model.c_str(),
                  seconds_since(t0), md.hp.dim, md.hp.n_layers, md.hp.n_heads, md.hp.n_kv_heads, md.hp.vocab_size,

@@ -122,7 +122,7 @@ DMat Engine::upload_fused(const std::vector<const HostTensor*>& parts, int mode)
     return m;
 }
 
-bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
+bool Engine::load(const std::string& path, int ctx_len, std::string* err, bool nibble_screen) {
     auto bad = [&](const std::string& m) {
         err_ = m;
         if (err) *err = m;
@@ -271,7 +271,20 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         // Exact Shortlist Head tensors (validated like engine/src/model.cpp:47-58).
         const HostTensor* q4 = file_.find("quanta.head_q4");
         const HostTensor* he = file_.find("quanta.head_err");
-        if (q4 || he) {
+        if (nibble_screen) {  // the screen comes from the Q8 head itself: no file tensors, a plane of rows * cols / 2 bytes
+            if (lm_head_.dtype != DT_Q8_0) return bad("the nibble-plane screen needs a Q8_0 output head");
+            const size_t pb = size_t(lm_head_.rows) * lm_head_.cols / 2, eb = size_t(lm_head_.rows) * (lm_head_.cols / QK) * 2;
+            uint8_t* plane = static_cast<uint8_t*>(dalloc(pb));
+            __half* perr = static_cast<__half*>(dalloc(eb));
+            if (launch_hi_plane(lm_head_, plane, perr, st_) != cudaSuccess) return bad("building the nibble plane failed");
+            weight_bytes_ += pb + eb;
+            head_err_ = perr;
+            head_q4_dm_ = lm_head_;
+            head_q4_dm_.dtype = DT_Q4_0;
+            head_q4_dm_.q = plane;  // the Q8 head's scales stay in d
+            head_q4_ = plane;
+            screen_ = kScreenHi4;
+        } else if (q4 || he) {
             const bool ok = q4 && he && q4->dtype == DT_Q4_0 && he->dtype == DT_F16 && lm_head_.dtype == DT_Q8_0 &&
                             q4->rows == lm_head_.rows && q4->cols == lm_head_.cols && he->rows == lm_head_.rows &&
                             he->cols == lm_head_.cols / QK;
@@ -314,6 +327,7 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err) {
         hin_.dx = static_cast<float*>(dalloc(size_t(nbd) * 4));
         hin_.xsum = static_cast<int*>(dalloc(size_t(nbd) * 4));
         hin_.xnorm = static_cast<float*>(dalloc(size_t(nbd) * 4));
+        hin_.xabs = static_cast<float*>(dalloc(size_t(nbd) * 4));
         n_lists_ = n_sm_;
         plan_full_ = plan_stream(lm_head_.dtype, V, hp_.dim, n_lists_, false, false);
         logits_ = static_cast<float*>(dalloc(size_t(V) * 4));
@@ -514,6 +528,7 @@ int Engine::launch_head(bool shortlist, int k, int n_valid, const int* must, con
     a.W8 = lm_head_;
     a.W4 = head_q4_dm_;
     a.err = head_err_;
+    a.screen = screen_;
     a.plan4 = plan_coarse_;
     a.plan8g = plan_gather_;
     a.k = k;

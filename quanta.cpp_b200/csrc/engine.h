@@ -51,7 +51,10 @@ public:
     Engine(const Engine&) = delete;
     Engine& operator=(const Engine&) = delete;
 
-    bool load(const std::string& path, int ctx_len, std::string* err);
+    // nibble_screen: screen the shortlist head with the high nibble plane of the Q8 head (kScreenHi4, plus a table of
+    // the low nibbles' norms) instead of the file's quanta.head_q4 / head_err, which are then not uploaded; works for
+    // files without them too.
+    bool load(const std::string& path, int ctx_len, std::string* err, bool nibble_screen = false);
 
     // Model::forward (model.h:39): token at `pos`, logits of the head query (copied to `out` if not null).
     int forward(int token, int pos, const HeadQueryC* hq, float* out);
@@ -182,6 +185,7 @@ private:
     DMat head_q4_dm_{};
     const void* head_q4_ = nullptr;
     const __half* head_err_ = nullptr;
+    int screen_ = kScreenQ4;  // the shortlist's screen (kScreenHi4: head_q4_dm_ is the Q8 head's high nibble plane)
     std::vector<Layer> layers_;
     float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
     __half *kcache_ = nullptr, *vcache_ = nullptr;

@@ -194,12 +194,16 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
     for (int b = warp; b < dim / QK; b += kWarps) {
         const float q = float(sx[b * QK + lane]);
         // exact: integers below 2^24, any order
-        float ss = fmul(q, q);
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        float ss = fmul(q, q), sa = fabsf(q);
+        for (int o = 16; o > 0; o >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            sa += __shfl_xor_sync(0xffffffffu, sa, o);
+        }
         if (lane == 0) {
             hin.dx[b] = sdx[b];
             hin.xsum[b] = ssum[b];
             hin.xnorm[b] = fmul(sdx[b], __fsqrt_rn(ss));
+            if (hin.xabs) hin.xabs[b] = sa;
         }
     }
 }
@@ -295,6 +299,62 @@ __device__ __forceinline__ void row_value_parts(const uint4* wq, const __half* w
     bnd = BOUND ? fadd(fmul(bd, 1.001f), 1e-5f) : 0.f;
 }
 
+// The nibble-plane screen of one row (kScreenHi4), with the same part layout as row_value_parts.  wq holds the high
+// nibbles hi = q >> 4 of the Q8 row as Q4_0 (hi + 8), wd the Q8 row's own scales.  With q = 16 hi + lo (0 <= lo <= 15)
+// the block dot s = 16 sum(hi x) + 8 sum(x) + sum((lo - 8) x), so the screen takes s' = 16 sum(hi x) + 8 sum(x) and
+// |s - s'| <= 8 sum|x|.  The row's exact logit E (block terms fl(fl(s dw) dx) chained in f32) and the screen value
+// (the same chain over s') each differ from their real sums by at most (nb + 2) 2^-24 of the sum of their terms'
+// magnitudes, so E <= value + (sum_b 8 |dw_b| dx_b sum|x_b| + (2 nb + 8) 2^-24 sum_b (|t'_b| + bound_b)) * 1.001 + 1e-6
+// (the factor covers the bound's own f32 rounding).  Per block the bound is the smaller of 8 |dw| dx sum|x| and
+// e_b |dw| dx ||x||_2, e_b = ||lo - 8||_2 of the row's block rounded up to f16 (k_hi_plane's table).
+template <int MAXB>
+__device__ __forceinline__ void row_screen_hi4(const uint4* wq, const __half* wd, const __half* we, const HeadAct& a,
+                                               const float* sxa, int nb, float& val, float& bnd) {
+    const int part = (threadIdx.x & 31) >> 3;
+    const int bpp = nb / kRowParts, b0 = part * bpp;
+    float t[MAXB];
+    float bd = 0.f, mag = 0.f;  // order-free sums (bounds)
+#pragma unroll
+    for (int k = 0; k < MAXB; ++k) {
+        if (k < bpp) {
+            const int b = b0 + k;
+            const int hx = chunk_dot<DT_Q4_0>(wq[b], a.sx, b) - 8 * a.ssum[b];  // sum(hi x)
+            const float dw = __half2float(wd[b]);
+            t[k] = block_term(16 * hx + 8 * a.ssum[b], dw, a.sdx[b]);
+            // the smaller of the L1 bound 8 |dw| dx sum|x| and the L2 bound ||lo - 8||_2 |dw| dx ||x||_2
+            const float u = fminf(fmul(fmul(8.0f * fabsf(dw), a.sdx[b]), sxa[b]),
+                                  fmul(fmul(__half2float(we[b]), fabsf(dw)), a.sxn[b]));
+            bd = fadd(bd, u);
+            mag = fadd(mag, fadd(fabsf(t[k]), u));
+        }
+    }
+    float acc = 0.f;
+    if (part == 0) {
+#pragma unroll
+        for (int k = 0; k < MAXB; ++k)
+            if (k < bpp) acc = fadd(acc, t[k]);
+    }
+#pragma unroll
+    for (int q = 1; q < kRowParts; ++q) {
+        const float pa = __shfl_up_sync(0xffffffffu, acc, 8);
+        if (part == q) {
+            acc = pa;
+#pragma unroll
+            for (int k = 0; k < MAXB; ++k)
+                if (k < bpp) acc = fadd(acc, t[k]);
+        }
+    }
+    // the parts' bound sums, gathered onto the last part's lanes
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+        bd += __shfl_xor_sync(0xffffffffu, bd, o);
+        mag += __shfl_xor_sync(0xffffffffu, mag, o);
+    }
+    const float gam = float(2 * nb + 8) * 5.9604644775390625e-8f;  // (2 nb + 8) 2^-24
+    val = acc;
+    bnd = fadd(fmul(fadd(bd, fmul(mag, gam)), 1.001f), 1e-6f);
+}
+
 __device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n groups are pending (n in 0..3)
     if (n <= 0) cp_wait<0>();
     else if (n == 1) cp_wait<1>();
@@ -311,6 +371,8 @@ __device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n g
 //   rows among [0, n_valid) after the repetition penalty of marked rows, and clears those marks.
 // mode 1 (coarse): W = quanta.head_q4; coarse / upper / logits = -inf, and each CTA's best n_list coarse scores among
 //   valid unmarked rows (the seeds).
+// mode 2 (coarse, nibble-plane screen): W = the Q8 head's high nibble plane with the Q8 scales (row_screen_hi4); the
+//   same outputs as mode 1, no bound table staged.
 template <int DT, int MODE, int MAXB>
 __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
                                                                      StreamPlan sp, int n_valid, int n_list, int penal,
@@ -321,7 +383,7 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ Cand slist[NT];
     const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16, S = sp.stages;
-    const HeadAct act = carve_act(smem, cols, MODE == 1);
+    const HeadAct act = carve_act(smem, cols, MODE != 0);
     unsigned char* ring = smem + sp.ring_off;
     const int ta = int((long long)blockIdx.x * sp.n_tiles / gridDim.x);
     const int tb = int((long long)(blockIdx.x + 1) * sp.n_tiles / gridDim.x);
@@ -338,7 +400,7 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
             const uint8_t* dsrc = reinterpret_cast<const uint8_t*>(W.d) + size_t(row0) * nb * 2;
             const int dch = (nrows * nb * 2 + 15) / 16;  // may read up to 15 bytes of the allocation's tail padding
             for (int c = threadIdx.x; c < dch; c += NT) cp_async16(st + sp.d_off + c * 16, dsrc + size_t(c) * 16);
-            if (MODE == 1) {
+            if (MODE != 0) {
                 const uint8_t* esrc = reinterpret_cast<const uint8_t*>(err) + size_t(row0) * nb * 2;
                 for (int c = threadIdx.x; c < dch; c += NT) cp_async16(st + sp.e_off + c * 16, esrc + size_t(c) * 16);
             }
@@ -350,6 +412,11 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
     pdl_wait();
     pdl_launch_dependents();
     load_head_act(hin, cols, act);
+    __shared__ float sxa[128];  // mode 2: sum|x| per block (nb <= 128)
+    if (MODE == 2) {
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) sxa[b] = __ldcg(hin.xabs + b);
+        __syncthreads();
+    }
 
     WarpTop32 L;
     L.init();
@@ -363,9 +430,15 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
         const unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
         const int row0 = t * TR, nrows = min(TR, W.rows - row0);
         float v, bound;
-        row_value_parts<DT, MODE == 1, MAXB>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
-                                       reinterpret_cast<const __half*>(st + sp.d_off + r * nb * 2),
-                                       reinterpret_cast<const __half*>(st + sp.e_off + r * nb * 2), act, nb, v, bound);
+        if constexpr (MODE == 2)
+            row_screen_hi4<MAXB>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
+                                 reinterpret_cast<const __half*>(st + sp.d_off + r * nb * 2),
+                                 reinterpret_cast<const __half*>(st + sp.e_off + r * nb * 2), act, sxa, nb, v, bound);
+        else
+            row_value_parts<DT, MODE == 1, MAXB>(reinterpret_cast<const uint4*>(st + r * sp.qstride),
+                                                 reinterpret_cast<const __half*>(st + sp.d_off + r * nb * 2),
+                                                 reinterpret_cast<const __half*>(st + sp.e_off + r * nb * 2), act, nb, v,
+                                                 bound);
         float cv = -INFINITY;
         int row = INT_MAX;
         bool ok = false;
@@ -728,6 +801,30 @@ __global__ void __launch_bounds__(kHeadThreads) k_sample_final(const Cand* __res
     }
 }
 
+// ---------------------------------------------------------------- the nibble plane of the Q8 head
+
+// One thread per output byte: block b of row r holds 16 bytes, byte j = (q[j] >> 4) + 8 | ((q[j + 16] >> 4) + 8) << 4
+// (q the block's int8 values; >> is the arithmetic shift, so hi in [-8, 7]).  The thread of byte 0 also writes
+// err[b] = ||lo - 8||_2 over the block's 32 low nibbles lo = q & 15, rounded up to f16 (the sum of squares is an exact
+// integer; the square root is rounded up, then the conversion).
+__global__ void k_hi_plane(const int8_t* __restrict__ q, long long n_blocks, uint8_t* __restrict__ plane,
+                           __half* __restrict__ err) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_blocks * 16; i += (long long)gridDim.x * blockDim.x) {
+        const long long b = i >> 4;
+        const int j = int(i & 15);
+        const int lo = (q[b * QK + j] >> 4) + 8, hi = (q[b * QK + j + 16] >> 4) + 8;
+        plane[i] = uint8_t(lo | (hi << 4));
+        if (j == 0) {
+            int ss = 0;
+            for (int k = 0; k < QK; ++k) {
+                const int e = (q[b * QK + k] & 15) - 8;
+                ss += e * e;
+            }
+            err[b] = __float2half_ru(__fsqrt_ru(float(ss)));
+        }
+    }
+}
+
 // ---------------------------------------------------------------- launchers
 
 namespace {
@@ -762,6 +859,14 @@ StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, boo
     return p;
 }
 
+cudaError_t launch_hi_plane(const DMat& W8, uint8_t* plane, __half* err, cudaStream_t st) {
+    if (W8.dtype != DT_Q8_0 || W8.cols % QK != 0) return cudaErrorInvalidValue;
+    const long long nbk = (long long)W8.rows * (W8.cols / QK);
+    k_hi_plane<<<unsigned(std::min<long long>((nbk * 16 + 255) / 256, 4096)), 256, 0, st>>>(
+        reinterpret_cast<const int8_t*>(W8.q), nbk, plane, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, float eps, const HeadIn& hin, HeadState* hs,
                               int full_rows, cudaStream_t st, bool pdl) {
     if (dim > 2048) return cudaErrorInvalidValue;
@@ -793,7 +898,9 @@ cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStre
                                a.n_valid, a.mark);
     if (e != cudaSuccess) return e;
     const bool small = a.W8.cols / QK / kRowParts <= 8;
-    e = launch_pdl(small ? k_head_rows<DT_Q4_0, 1, 8> : k_head_rows<DT_Q4_0, 1, kMaxBpp>, dim3(a.plan4.grid),
+    auto coarse_kernel = a.screen == kScreenHi4 ? (small ? k_head_rows<DT_Q4_0, 2, 8> : k_head_rows<DT_Q4_0, 2, kMaxBpp>)
+                                                : (small ? k_head_rows<DT_Q4_0, 1, 8> : k_head_rows<DT_Q4_0, 1, kMaxBpp>);
+    e = launch_pdl(coarse_kernel, dim3(a.plan4.grid),
                    dim3(a.plan4.threads), a.plan4.smem, st, pdl, a.W4, a.err, hin, a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark,
                    a.logits, a.coarse, a.upper, reinterpret_cast<Cand*>(a.seed_buf));
     if (e != cudaSuccess) return e;

@@ -20,6 +20,7 @@ struct HeadIn {
     float* dx;      // [dim/32] block scales
     int* xsum;      // [dim/32] sum of q per block (Q4 offset)
     float* xnorm;   // [dim/32] d_b * ||q_b||_2 (shortlist bound)
+    float* xabs;    // [dim/32] sum of |q| per block (the nibble-plane screen's bound; null: not computed)
 };
 
 struct HeadState {
@@ -43,6 +44,9 @@ struct StreamPlan {
 };
 // coarse: stage the bounds too; gather: room for the CTA's compacted row list.  stages == 0 when it cannot fit.
 StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather);
+// The high nibble plane of a Q8_0 matrix as Q4_0 nibbles: per 32-block, byte j = (q[j] >> 4) + 8 | ((q[j + 16] >> 4) + 8) << 4
+// (plane: rows * cols / 2 bytes), and err[row][block] = ||(q & 15) - 8||_2 rounded up to f16 (rows * cols / 32 halves).
+cudaError_t launch_hi_plane(const DMat& W8, uint8_t* plane, __half* err, cudaStream_t st);
 
 struct HeadFullArgs {
     DMat W;
@@ -56,10 +60,17 @@ struct HeadFullArgs {
     void* lists;        // plan.grid * n_list candidates
 };
 
+// The shortlist's screen.  kScreenQ4: the file's quanta.head_q4 with the bound of quanta.head_err (the reference's).
+// kScreenHi4: the high nibble plane of the Q8 head itself (W4 = the plane as Q4_0 nibbles q8 >> 4 offset by 8, with
+// the Q8 head's own scales; err = ||lo - 8||_2 per row and block, f16 rounded up): screen s' = 16 sum(hi q) + 8 sum(q)
+// per block, bound min(8 sum|q_b|, err_b ||q_b||_2) |d_b| dx_b plus the f32 rounding of both sums (head_kernels.cu).  Exact rows, tau and the sampled ids are the same either way.
+constexpr int kScreenQ4 = 0, kScreenHi4 = 1;
+
 struct ShortlistArgs {
     DMat W8;                // lm_head (Q8_0)
-    DMat W4;                // quanta.head_q4
-    const __half* err;      // quanta.head_err [V][dim/32]
+    DMat W4;                // quanta.head_q4, or the Q8 head's high nibble plane (kScreenHi4)
+    const __half* err;      // [V][dim/32]: quanta.head_err (kScreenQ4), or the low nibbles' norms (kScreenHi4)
+    int screen = kScreenQ4;
     StreamPlan plan4;       // streamed coarse pass over W4
     StreamPlan plan8g;      // candidate gather over W8
     int k, n_valid;

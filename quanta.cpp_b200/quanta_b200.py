@@ -319,9 +319,10 @@ def head_query(top_k=0, n_valid=0, must=None):
 class Model:
     """quanta::Model on the device (engine/src/model.h)."""
 
-    def __init__(self, path: str | os.PathLike, ctx_len: int = 0):
+    def __init__(self, path: str | os.PathLike, ctx_len: int = 0, nibble_screen: bool = False):
+        """nibble_screen: QNT_OPEN_NIBBLE_SCREEN (the shortlist head screens with the Q8 head's high nibble plane)."""
         h = C.c_void_p()
-        _check(lib().qnt_model_open(str(path).encode(), ctx_len, 0, C.byref(h)))
+        _check(lib().qnt_model_open(str(path).encode(), ctx_len, 1 if nibble_screen else 0, C.byref(h)))
         self.h = h
         hp = HParams()
         _check(lib().qnt_model_hparams(h, C.byref(hp)))
