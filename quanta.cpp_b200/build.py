@@ -1,6 +1,7 @@
 """Builds the native libraries of quanta.cpp_b200 in-tree (sm_100a only).
 
     python quanta.cpp_b200/build.py          # or __graft_entry__.build()
+    python quanta.cpp_b200/build.py --stamps # the phase-timed library (lib_stamps/, -DQNT_PHASE_STAMPS) for timeline.py
 
 Outputs (git-ignored, shipped with the repository snapshot):
     quanta.cpp_b200/lib/libquanta_b200.so   CUDA kernels + engine + the C ABI of include/quanta_b200.h
@@ -47,9 +48,11 @@ def _run(cmd):
     return r
 
 
-def build(verbose: bool = False, jobs: int = 0) -> None:
-    BUILD.mkdir(exist_ok=True)
-    LIB.mkdir(exist_ok=True)
+def build(verbose: bool = False, jobs: int = 0, stamps: bool = False) -> None:
+    build_dir, lib_dir = (PKG / "_build_stamps", PKG / "lib_stamps") if stamps else (BUILD, LIB)
+    build_dir.mkdir(exist_ok=True)
+    lib_dir.mkdir(exist_ok=True)
+    nvflags = NVFLAGS + (["-DQNT_PHASE_STAMPS"] if stamps else [])
     hdrs = _headers()
     todo = []
     objs = []
@@ -57,14 +60,14 @@ def build(verbose: bool = False, jobs: int = 0) -> None:
         s = CSRC / src
         if not s.exists():
             continue
-        o = BUILD / (src + ".o")
+        o = build_dir / (src + ".o")
         objs.append(o)
         if _newer(o, [s] + hdrs):
-            cmd = [NVCC] + NVFLAGS + (["-x", "cu"] if s.suffix == ".cpp" else []) + ["-c", str(s), "-o", str(o)]
+            cmd = [NVCC] + nvflags + (["-x", "cu"] if s.suffix == ".cpp" else []) + ["-c", str(s), "-o", str(o)]
             todo.append(cmd)
     for src in HOST_SOURCES:
         s = CSRC / src
-        o = BUILD / (src + ".o")
+        o = build_dir / (src + ".o")
         objs.append(o)
         if _newer(o, [s] + hdrs):
             todo.append(["g++", "-O3", "-std=c++17", "-fPIC", f"-I{CSRC}", "-c", str(s), "-o", str(o)])
@@ -72,9 +75,11 @@ def build(verbose: bool = False, jobs: int = 0) -> None:
         for r in ex.map(_run, todo):
             if verbose and (r.stdout or r.stderr):
                 print(r.stdout + r.stderr)
-    so = LIB / "libquanta_b200.so"
+    so = lib_dir / "libquanta_b200.so"
     if _newer(so, objs):
         _run([NVCC] + ARCH + ["-shared", "-o", str(so)] + [str(o) for o in objs] + ["-lpthread"])
+    if stamps:
+        return
     synth = LIB / "libqnt_synth.so"
     ssrc = CSRC / "synth" / "qnt_synth.cpp"
     if _newer(synth, [ssrc, CSRC / "synth" / "qnt_synth.h"]):
@@ -87,5 +92,6 @@ def build(verbose: bool = False, jobs: int = 0) -> None:
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
-    print("built", LIB)
+    st = "--stamps" in sys.argv
+    build(verbose="-v" in sys.argv, stamps=st)
+    print("built", PKG / "lib_stamps" if st else LIB)

@@ -32,6 +32,7 @@
 
 #include "kernels.cuh"
 #include "layer_kernels.h"
+#include "phase_stamps.cuh"
 
 namespace qb {
 
@@ -117,6 +118,8 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
     __shared__ float sred[kWarps];
     __shared__ float s_m, s_inv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    PhaseProbe probe;
+    probe.begin(1);
     // every CTA of the cluster has started before any remote shared-memory access (the wait comes before the first)
     asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
     // The launch's first position was written by an earlier launch (the host or the step's first kernel); K / V rows
@@ -226,6 +229,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
     load_v(0, min(pos0, n));
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();  // 1: the previous kernel is done
     float* kc = nullptr;  // (fused) the token's k and v, f32 of their f16 values
     float* vc = nullptr;
     if constexpr (UW == 0) {
@@ -241,6 +245,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
         kc = sterm + kQkvRows * qts;
         vc = kc + kHd;
         norm_quant(X, nw, qdim, eps, sx, sdx, nullptr, sredq);
+        probe.mark();  // 2: rmsnorm + quantize
 #pragma unroll
         for (int u = 0; u < UW; ++u) {  // block terms (Q8_0: a block's two chunks sit in adjacent lanes)
             if (u * kThreads >= qtotal) break;
@@ -286,6 +291,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
         }
         cluster_arrive();  // q, k and v of the token are in every CTA
         cluster_wait();
+        probe.mark();  // 3: q|k|v rows, bias, RoPE, exchange
         if (tid < dpc) vs[size_t(pos0) * dpc + tid] = __float2half_rn(vc[d0 + tid]);  // exact: vc holds f16 values
     }
 
@@ -327,6 +333,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
         cluster.map_shared_rank(smx, tid)[r] = m;
     }
     cluster.sync();
+    probe.mark();  // 4: scores and the maxima exchange
 
     // ---- 2. weights of [p0, p1) into every CTA's row
     if (warp == 0) {
@@ -342,10 +349,12 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
     cp_wait<0>();  // this thread's V copies (the barriers below publish them)
     cluster_arrive();
     cluster_wait();
+    probe.mark();  // 5: the exps and their exchange
 
     // ---- 3. every CTA: the ordered sum, then the products and chains of its dimensions
     if (tid == 0) s_inv = __frcp_rn(ordered_sum(E, n));  // = 1.0f / sum (IEEE round to nearest)
     __syncthreads();
+    probe.mark();  // 6: the softmax sum
     const float inv = s_inv;
     float o = 0.f;
     if (producer) {
@@ -384,6 +393,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
             }
         }
         if (tid < dpc) out[(size_t(t) * a.n_heads + h) * kHd + d0 + tid] = o;
+        probe.mark();  // 7: the output chains
     }
     if constexpr (UO > 0) {  // every CTA: the head's outputs, their quantization, this CTA's o_proj terms
         __shared__ __align__(16) int8_t sxo[kHd];
@@ -419,6 +429,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a, QkvArgs qa, OArgs
             if (lane == 0) a.dx[h * (kHd / QK) + warp] = d;
         }
     }
+    probe.end();  // 8: o_proj terms (or the output's quantization)
 }
 
 
@@ -576,6 +587,8 @@ inline size_t prefill_smem_bytes(int group, int n_cap) {
 }
 
 }  // namespace
+
+QNT_PHASE_READER(qnt_phase_read_attn)
 
 cudaError_t launch_attn_prefill(const AttnArgs& a, const float* Q, const int* pos_dev, int n_tok, int pos_bound, float* out,
                                 cudaStream_t st, bool pdl, TokMap tm, const QuantOut* qo) {

@@ -23,6 +23,7 @@
 #include "kernels.cuh"
 #include "layer_kernels.h"
 #include "qkv_pair.cuh"
+#include "phase_stamps.cuh"
 
 namespace qb {
 
@@ -132,15 +133,21 @@ __global__ void __launch_bounds__(kThreads) k_resid_dec(DMat W, const float* __r
     SliceSmem s = carve(smem, cols, rows_per_cta, term_stride(cols / QK));
     RowSlice S = make_slice(W, DT, row0, nrows, magic);
     float xres = 0.f;  // this thread's residual row (rows_per_cta <= blockDim)
+    PhaseProbe probe;
+    probe.begin(3);
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
         pdl_launch_dependents();
+        probe.mark();  // 1: the previous kernel is done
         if (int(threadIdx.x) < nrows) xres = __ldcg((Xres ? Xres : X) + row0 + threadIdx.x);
         if (MODE == 0) quant_only(xin, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
         else load_quant(qin, din, cols, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr);
+        probe.mark();  // 2: the input activation in shared memory
     });
     __syncthreads();
+    probe.mark();  // 3: the block terms of the matvec
     if (int(threadIdx.x) < nrows) X[row0 + threadIdx.x] = fadd(xres, row_sum(s.sterm + threadIdx.x * S.tstride, S.nb));
+    probe.end();  // 4: the row chains and the residual
 }
 
 // gate|up rows interleaved per 32-block: fused row 64j + i = gate row 32j + i, 64j + 32 + i = up row 32j + i.
@@ -166,9 +173,12 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
     RowSlice S = make_slice(W, DT, row0, nrows, magic);
     NormW nw;
     load_norm_w(norm_w, dim, nw);
+    PhaseProbe probe;
+    probe.begin(2);
     slice_terms<DT, U>(S, s.sx, s.sdx, s.ssum, s.sterm, [&] {
         pdl_wait();
         pdl_launch_dependents();
+        probe.mark();  // 1: the previous kernel is done
         if constexpr (RT) {
             cg::cluster_group cl = cg::this_cluster();
             const int cr = int(cl.block_rank()), rpc = (dim + 7) / 8, rr0 = cr * rpc, nr = min(rpc, dim - rr0);
@@ -203,17 +213,21 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
             }
             asm volatile("barrier.cluster.arrive.release;" ::: "memory");
             asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+            probe.mark();  // 2: the o_proj residual rows and their exchange
             float xv[kMaxRounds];
 #pragma unroll
             for (int k = 0; k < kMaxRounds; ++k) xv[k] = i + k * int(blockDim.x) < dim ? sxn[i + k * blockDim.x] : 0.f;
             norm_quant_v(xv, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
+            probe.mark();  // 3: rmsnorm + quantize
         } else {
             norm_quant(X, nw, dim, eps, s.sx, s.sdx, DT == DT_Q4_0 ? s.ssum : nullptr, s.sred);
         }
     });
     __syncthreads();
+    probe.mark();  // 4: the block terms of the gate|up matvec
     for (int r = threadIdx.x; r < nrows; r += blockDim.x) s.sval[r] = row_sum(s.sterm + r * S.tstride, S.nb);
     __syncthreads();
+    probe.mark();  // 5: the row chains
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int jb = warp; jb < nrows / 64; jb += kWarps) {
         const float h = swiglu1(s.sval[jb * 64 + lane], s.sval[jb * 64 + 32 + lane], tab);
@@ -227,6 +241,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup_dec(DMat W, const float* __
         HQ[j * QK + lane] = q;
         if (lane == 0) HD[j] = d;
     }
+    probe.end();  // 6: SwiGLU + quantize
 }
 
 // ---------------------------------------------------------------- batched (prefill) elementwise kernels
@@ -491,6 +506,8 @@ cudaError_t launch_gateup_dec(const DMat& W, const SlicePlan& p, const float* X,
     }
     return e;
 }
+
+QNT_PHASE_READER(qnt_phase_read_layers)
 
 cudaError_t launch_norm_quant_rows(const float* X, const float* norm_w, int n_tok, int dim, float eps, int8_t* XQ, float* DX,
                                    float* DXT, int ldt, cudaStream_t st, bool pdl) {

@@ -18,7 +18,7 @@ from pathlib import Path
 import numpy as np
 
 PKG = Path(__file__).resolve().parent
-LIB_DIR = PKG / "lib"
+LIB_DIR = Path(os.environ["QNT_LIB_DIR"]) if os.environ.get("QNT_LIB_DIR") else PKG / "lib"  # timeline.py: lib_stamps
 
 F32, F16, Q8_0, Q4_0 = 0, 1, 2, 3
 QK = 32
@@ -480,7 +480,7 @@ def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: 
     if path.exists() and not overwrite:
         return path
     if _synth is None:
-        p = LIB_DIR / "libqnt_synth.so"
+        p = PKG / "lib" / "libqnt_synth.so"  # the model writer is not part of the phase-timed build
         if not p.exists():
             raise RuntimeError(f"{p} is missing: run `python quanta.cpp_b200/build.py`")
         _synth = C.CDLL(str(p))
