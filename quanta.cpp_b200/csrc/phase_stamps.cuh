@@ -30,7 +30,7 @@ __device__ __forceinline__ unsigned long long phase_gtime() {
 }  // namespace
 
 struct PhaseProbe {
-    int slot = -1;
+    int slot = -1, n = 0;  // the mark count stays in a register: a mark only stores (no global read on the timed path)
     __device__ void begin(int kind) {
         if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
             const unsigned s = atomicAdd(&g_phase_n, 1u);
@@ -39,17 +39,15 @@ struct PhaseProbe {
                 g_phase[s].kind = kind;
                 g_phase[s].g0 = phase_gtime();
                 g_phase[s].c[0] = clock64();
+                n = 1;
                 g_phase[s].n = 1;
             }
         }
     }
     __device__ void mark() {
-        if (slot >= 0) {
-            const int k = g_phase[slot].n;
-            if (k < kPhaseMarks) {
-                g_phase[slot].c[k] = clock64();
-                g_phase[slot].n = k + 1;
-            }
+        if (slot >= 0 && n < kPhaseMarks) {
+            g_phase[slot].c[n] = clock64();
+            g_phase[slot].n = ++n;
         }
     }
     __device__ void end() {
