@@ -199,25 +199,29 @@ __device__ __forceinline__ void tmem_fill(uint32_t taddr, unsigned x) {
 // v[NC b + i] = column 4 NC b + i.  One load and its wait per block.
 template <int NC>
 __device__ __forceinline__ void tmem_ld_blocks(uint32_t taddr, int* v) {
+    if constexpr (NC == 4) {  // the four blocks' loads in flight together, one wait
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%16];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%4,%5,%6,%7}, [%17];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%8,%9,%10,%11}, [%18];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%12,%13,%14,%15}, [%19];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+              "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(taddr), "r"(taddr + 16u), "r"(taddr + 32u), "r"(taddr + 48u)
+            : "memory");
+        return;
+    }
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
         const uint32_t ta = taddr + uint32_t(4 * NC * b);
         int* w = v + NC * b;
-        if constexpr (NC == 8) {
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
-                "tcgen05.wait::ld.sync.aligned;"
-                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
-                : "r"(ta)
-                : "memory");
-        } else {
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n\t"
-                "tcgen05.wait::ld.sync.aligned;"
-                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
-                : "r"(ta)
-                : "memory");
-        }
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+            : "r"(ta)
+            : "memory");
     }
 }
 
@@ -384,6 +388,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             const int m0 = tile_m0(tile), t0 = tile_t0(tile);
             const int row = m0 + q * 32 + lane;
             const bool row_ok = row < g.r1;
+            float xo[EPI == 2 ? C::tpt : 1];  // EPI 2: the residual rows, loaded while the K loop runs
+            if constexpr (EPI == 2) {
+#pragma unroll
+                for (int i = 0; i < C::tpt; ++i) {
+                    const int t = t0 + cg * C::tpt + i;
+                    xo[i] = row_ok && t < g.n ? __ldcg(g.out + size_t(t) * g.ldo + row) : 0.f;
+                }
+            }
             float2 acc[C::tpt / 2];  // tokens (2 j, 2 j + 1) of this thread's tpt
 #pragma unroll
             for (int j = 0; j < C::tpt / 2; ++j) acc[j] = make_float2(0.f, 0.f);
@@ -500,10 +512,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
 #pragma unroll
                     for (int i = 0; i < C::tpt; ++i) {
                         const int t = t0 + cg * C::tpt + i;
-                        if (t < g.n) {
-                            float* o = g.out + size_t(t) * g.ldo + row;
-                            *o = fadd(__ldcg(o), res[i]);
-                        }
+                        if (t < g.n) g.out[size_t(t) * g.ldo + row] = fadd(xo[EPI == 2 ? i : 0], res[i]);
                     }
                 }
             } else {
