@@ -134,6 +134,18 @@ int qnt_model_has_shortlist(const qnt_model* m);
 size_t qnt_model_kv_cache_bytes(const qnt_model* m);
 size_t qnt_model_weight_bytes(const qnt_model* m);
 
+/* A copy of the .qnt at in_path, written to out_path, with the device's fused matrices stored pre-packed beside the
+ * original tensors (which stay byte for byte, so the reference's ModelFile reads the copy as it reads the original:
+ * engine/src/model_file.cpp:189-211 looks tensors up by name and ignores the rest).  Added, per layer l:
+ * b200.layers.<l>.qkv (q|k|v rows pair-interleaved per head), b200.layers.<l>.gate_up (gate|up interleaved per 32
+ * rows), b200.layers.<l>.qkv_bias (files with q|k|v biases), and the marker b200.layout (f32 [1], the layout
+ * version).  qnt_model_open uploads those tensors as they are instead of reordering rows on the host.  The writer of
+ * the format is scripts/export.py:290-315; this is its extension point (no reference counterpart).  QNT_ERR_IO if
+ * in_path does not open or out_path cannot be written. */
+int qnt_export_device_layout(const char* in_path, const char* out_path);
+/* How many fused tensors the last qnt_model_open took pre-packed from the file (0 for a plain .qnt). */
+int qnt_model_packed_tensors(const qnt_model* m);
+
 /* ---------------------------------------------------------------- session + sampling (engine/src/session.h, sampler.h) */
 
 /* SamplerParams (engine/src/sampler.h:9-18). */

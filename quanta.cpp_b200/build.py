@@ -27,7 +27,7 @@ NVFLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3", f
 
 # CUDA translation units (host files that include device headers are compiled as CUDA too)
 CU_SOURCES = ["ops.cu", "layer_kernels.cu", "attention.cu", "head_kernels.cu", "sampler_wide.cu", "nll.cu", "gemm_tc.cu", "engine.cpp", "capi.cpp", "sampler.cpp", "sampler_noalloc.cpp"]
-HOST_SOURCES = ["qnt_file.cpp", "exp_table.cpp", "tokenizer.cpp"]
+HOST_SOURCES = ["qnt_file.cpp", "exp_table.cpp", "tokenizer.cpp", "device_layout.cpp"]
 
 
 def _newer(target: Path, deps) -> bool:

@@ -418,6 +418,15 @@ int qnt_model_has_shortlist(const qnt_model* m) { return m && m->eng.has_shortli
 size_t qnt_model_kv_cache_bytes(const qnt_model* m) { return m ? m->eng.kv_cache_bytes() : 0; }
 size_t qnt_model_weight_bytes(const qnt_model* m) { return m ? m->eng.weight_bytes() : 0; }
 
+int qnt_export_device_layout(const char* in_path, const char* out_path) {
+    if (!in_path || !out_path) return set_err(QNT_ERR_INVALID, "null argument");
+    std::string err;
+    if (!qb::export_device_layout(in_path, out_path, &err)) return set_err(QNT_ERR_IO, err);
+    return QNT_OK;
+}
+
+int qnt_model_packed_tensors(const qnt_model* m) { return m ? m->eng.packed_tensors() : 0; }
+
 int qnt_generate(qnt_model* m, const int* prompt, int n_prompt, const qnt_sampler_params* sp, int flags, int n_gen,
                  int* out_ids, qnt_gen_stats* stats) {
     if (!m || !prompt || !sp || (n_gen > 0 && !out_ids)) return set_err(QNT_ERR_INVALID, "null argument");

@@ -50,6 +50,7 @@ struct Args {
                  "  quanta_b200 prompt                                          print the comparison prompt\n"
                  "  quanta_b200 bench     -m model.qnt                          full report (checks + speed)\n"
                  "  quanta_b200 selftest                                        check + time kernels (no model needed)\n"
+                 "  quanta_b200 export-layout IN.qnt OUT.qnt                    copy with the device's fused tensors pre-packed\n"
                  "common: --ctx 4096  -t THREADS (ignored: the GPU runs the model)  --no-batch (prefill token by token)\n"
                  "        --full-head (skip the shortlist head)  (--kv-f32 is not available: the device KV cache is f16)\n"
                  "        --nibble-head (screen the shortlist head with the Q8 head's high nibble plane; no head_q4 needed)\n"
@@ -712,6 +713,15 @@ int bench_report(Model& md, Text& tok, const Args& a) {  // engine/src/checks.cp
 
 int main(int argc, char** argv) {
     if (argc >= 2 && std::strcmp(argv[1], "selftest") == 0) return selftest();
+    if (argc >= 2 && std::strcmp(argv[1], "export-layout") == 0) {
+        if (argc != 4) usage();
+        if (qnt_export_device_layout(argv[2], argv[3]) != QNT_OK) {
+            std::fprintf(stderr, "export-layout: %s\n", qnt_last_error());
+            return 1;
+        }
+        std::printf("wrote %s\n", argv[3]);
+        return 0;
+    }
     if (argc >= 2 && std::strcmp(argv[1], "prompt") == 0) {
         std::fputs(compare_prompt().c_str(), stdout);
         return 0;

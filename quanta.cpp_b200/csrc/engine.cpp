@@ -72,54 +72,36 @@ DMat Engine::upload_matrix(const HostTensor& t) {
     return m;
 }
 
-// Fused matrices.  mode 0: q|k|v, rows pair-interleaved per head (row i and i + head_dim/2 adjacent);
-// mode 1: gate|up interleaved per 32 rows (64j..64j+31 gate block j, 64j+32..64j+63 up block j).
+// Fused matrices in the device's row order (fuse_rows, device_layout.h).  mode 0: q|k|v, rows pair-interleaved per
+// head (row i and i + head_dim/2 adjacent); mode 1: gate|up interleaved per 32 rows (64j..64j+31 gate block j,
+// 64j+32..64j+63 up block j).
 DMat Engine::upload_fused(const std::vector<const HostTensor*>& parts, int mode) {
-    const int dtype = parts[0]->dtype, cols = parts[0]->cols;
-    int rows = 0;
-    for (const HostTensor* p : parts) {
-        if (p->dtype != dtype || p->cols != cols) throw std::runtime_error("fused matrices need one dtype and width");
-        if (p->dtype != DT_Q8_0 && p->dtype != DT_Q4_0) throw std::runtime_error("weight matrices must be q8_0 or q4_0");
-        rows += p->rows;
-    }
-    const int rb = row_bytes_host(dtype, cols), nb = cols / QK;
-    std::vector<std::pair<const HostTensor*, int>> order;  // (source, source row) per fused row
-    order.reserve(size_t(rows));
-    if (mode == 0) {
-        const int hd = hp_.head_dim, half = hd / 2;
-        for (const HostTensor* p : parts)
-            for (int u = 0; u < p->rows / hd; ++u)
-                for (int i = 0; i < half; ++i) {
-                    order.emplace_back(p, u * hd + i);
-                    order.emplace_back(p, u * hd + i + half);
-                }
-    } else {
-        const HostTensor *g = parts[0], *up = parts[1];
-        for (int j = 0; j < g->rows / QK; ++j) {
-            for (int i = 0; i < QK; ++i) order.emplace_back(g, j * QK + i);
-            for (int i = 0; i < QK; ++i) order.emplace_back(up, j * QK + i);
-        }
-    }
-    std::vector<uint8_t> hq(size_t(rows) * rb);
-    std::vector<uint16_t> hd(size_t(rows) * nb);
-    for (int r = 0; r < rows; ++r) {
-        const HostTensor* src = order[size_t(r)].first;
-        const int sr = order[size_t(r)].second;
-        std::memcpy(hq.data() + size_t(r) * rb, src->data + size_t(sr) * rb, size_t(rb));
-        std::memcpy(hd.data() + size_t(r) * nb, src->scales() + size_t(sr) * nb, size_t(nb) * 2);
-    }
+    const FusedHost f = fuse_rows(parts, mode, hp_.head_dim);
     DMat m;
-    m.dtype = dtype;
-    m.rows = rows;
-    m.cols = cols;
-    void* q = dalloc(hq.size());
-    void* d = dalloc(hd.size() * 2);
-    cudaMemcpy(q, hq.data(), hq.size(), cudaMemcpyHostToDevice);
-    cudaMemcpy(d, hd.data(), hd.size() * 2, cudaMemcpyHostToDevice);
+    m.dtype = f.dtype;
+    m.rows = f.rows;
+    m.cols = f.cols;
+    void* q = dalloc(f.q.size());
+    void* d = dalloc(f.d.size() * 2);
+    if (cudaMemcpy(q, f.q.data(), f.q.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d, f.d.data(), f.d.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+        throw std::runtime_error("upload failed");
     m.q = static_cast<const uint8_t*>(q);
     m.d = static_cast<const __half*>(d);
-    weight_bytes_ += hq.size() + hd.size() * 2;
+    weight_bytes_ += f.q.size() + f.d.size() * 2;
     return m;
+}
+
+// A fused matrix stored pre-packed by export_device_layout: uploaded as it is when its dtype and shape are those the
+// parts fuse to, else fused here.
+DMat Engine::upload_packed(const HostTensor* packed, const std::vector<const HostTensor*>& parts, int mode) {
+    int rows = 0;
+    for (const HostTensor* p : parts) rows += p->rows;
+    if (packed && packed->dtype == parts[0]->dtype && packed->cols == parts[0]->cols && packed->rows == rows) {
+        ++packed_tensors_;
+        return upload_matrix(*packed);
+    }
+    return upload_fused(parts, mode);
 }
 
 bool Engine::load(const std::string& path, int ctx_len, std::string* err, bool nibble_screen) {
@@ -204,6 +186,11 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err, bool n
         }
         max_chunks_ = (ctx_ + 63) / 64;
 
+        // tensors pre-packed by export_device_layout, used when the file's layout version is this build's
+        const HostTensor* lay = file_.find("b200.layout");
+        const bool packed = lay && lay->dtype == DT_F32 && lay->rows * lay->cols == 1 &&
+                            *reinterpret_cast<const float*>(lay->data) == float(kDeviceLayoutVersion);
+        packed_tensors_ = 0;
         layers_.resize(size_t(hp_.n_layers));
         const size_t before_layers = weight_bytes_;
         for (int l = 0; l < hp_.n_layers; ++l) {
@@ -213,24 +200,24 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err, bool n
             L.ffn_norm = upload_f32(file_.require(p + "post_attention_layernorm.weight"));
             const HostTensor &wq = file_.require(p + "self_attn.q_proj.weight"), &wk = file_.require(p + "self_attn.k_proj.weight"),
                              &wv = file_.require(p + "self_attn.v_proj.weight");
-            L.qkv = upload_fused({&wq, &wk, &wv}, 0);
+            const std::string pk = "b200.layers." + std::to_string(l) + ".";
+            L.qkv = upload_packed(packed ? file_.find(pk + "qkv") : nullptr, {&wq, &wk, &wv}, 0);
             L.o = upload_matrix(file_.require(p + "self_attn.o_proj.weight"));
-            L.gu = upload_fused({&file_.require(p + "mlp.gate_proj.weight"), &file_.require(p + "mlp.up_proj.weight")}, 1);
+            L.gu = upload_packed(packed ? file_.find(pk + "gate_up") : nullptr,
+                                 {&file_.require(p + "mlp.gate_proj.weight"), &file_.require(p + "mlp.up_proj.weight")}, 1);
             L.down = upload_matrix(file_.require(p + "mlp.down_proj.weight"));
             // fused bias in the q|k|v pair-interleaved order
             std::vector<float> b(size_t(L.qkv.rows), 0.f);
             if (hp_.qkv_bias) {
-                const HostTensor* bs[3] = {&file_.require(p + "self_attn.q_proj.bias"), &file_.require(p + "self_attn.k_proj.bias"),
-                                           &file_.require(p + "self_attn.v_proj.bias")};
-                int fr = 0;
-                for (const HostTensor* t : bs) {
-                    if (t->dtype != DT_F32) throw std::runtime_error("qkv biases must be f32");
-                    const float* v = reinterpret_cast<const float*>(t->data);
-                    for (int u = 0; u < t->cols / hp_.head_dim; ++u)
-                        for (int i = 0; i < half; ++i) {
-                            b[size_t(fr++)] = v[u * hp_.head_dim + i];
-                            b[size_t(fr++)] = v[u * hp_.head_dim + i + half];
-                        }
+                const HostTensor* pb = packed ? file_.find(pk + "qkv_bias") : nullptr;
+                if (pb && pb->dtype == DT_F32 && pb->cols == L.qkv.rows) {
+                    std::memcpy(b.data(), pb->data, b.size() * 4);
+                    ++packed_tensors_;
+                } else {
+                    b = fuse_qkv_bias({&file_.require(p + "self_attn.q_proj.bias"), &file_.require(p + "self_attn.k_proj.bias"),
+                                       &file_.require(p + "self_attn.v_proj.bias")},
+                                      hp_.head_dim);
+                    if (b.size() != size_t(L.qkv.rows)) throw std::runtime_error("qkv bias lengths do not match the q|k|v rows");
                 }
             }
             float* db = static_cast<float*>(dalloc(b.size() * 4));

@@ -13,6 +13,7 @@
 #include <tuple>
 #include <vector>
 
+#include "device_layout.h"
 #include "gemm_tc.h"
 #include "head_kernels.h"
 #include "layer_kernels.h"
@@ -106,6 +107,8 @@ public:
     size_t kv_cache_bytes() const { return kv_bytes_; }
     // copies the tensor-core matmul reads beside the weights: stage-major block scales, int8 q - 8 of Q4_0 matrices
     size_t tc_copy_bytes() const { return tc_copy_bytes_; }
+    // fused tensors of the last load taken pre-packed from the file (export_device_layout), not fused at load
+    int packed_tensors() const { return packed_tensors_; }
     const std::string& error() const { return err_; }
     // the last load failed on the file itself (unreadable, malformed, or a tensor missing), not on the device
     bool file_fault() const { return file_fault_; }
@@ -142,6 +145,7 @@ private:
     void* dalloc(size_t bytes);
     DMat upload_matrix(const HostTensor& t);
     DMat upload_fused(const std::vector<const HostTensor*>& parts, int mode);
+    DMat upload_packed(const HostTensor* packed, const std::vector<const HostTensor*>& parts, int mode);
     int launch_layers_decode(const int* pos_dev);
     // positions of the chunk stay below pos_bound; with tm.pos set, tokens of the batch caches (their own positions)
     int launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm = TokMap{});
@@ -179,6 +183,7 @@ private:
 
     std::vector<void*> allocs_;
     size_t weight_bytes_ = 0, kv_bytes_ = 0, layer_bytes_ = 0, tc_copy_bytes_ = 0;
+    int packed_tensors_ = 0;
 
     DMat embed_{}, lm_head_{};
     const float* final_norm_ = nullptr;

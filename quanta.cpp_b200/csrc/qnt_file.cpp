@@ -225,6 +225,7 @@ bool decode_entry(Window& w, uint32_t index, const uint8_t* map, size_t file_siz
         return false;
     }
     t->dtype = int(dtype);
+    t->rank = int(rank);
     t->rows = int(dims[0]);
     t->cols = int(dims[1]);
     if ((dtype == 2 || dtype == 3) && t->cols % 32 != 0) {
@@ -308,6 +309,8 @@ bool QntFile::open(const std::string& path, std::string* err) {
     if (!decode_tokenizer(tok, &tok_, &f)) return fail();
 
     // region 3: the tensor directory
+    dir_offset_ = size_t(head.at() - map_);
+    order_.clear();
     Window dir(head.at(), map_ + size_, QntFault::Directory, "tensor directory");
     uint32_t n_tensors;
     if (!dir.scalar(&n_tensors, "tensor count", &f)) return fail();
@@ -320,6 +323,7 @@ bool QntFile::open(const std::string& path, std::string* err) {
             f = {QntFault::Directory, "tensor '" + name + "' appears twice in the directory"};
             return fail();
         }
+        order_.push_back(name);
     }
     fault_ = QntFault::None;
     return true;

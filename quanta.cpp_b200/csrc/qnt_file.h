@@ -42,6 +42,7 @@ const char* qnt_fault_name(QntFault f);
 
 struct HostTensor {
     int dtype = 0;  // 0 f32, 1 f16, 2 q8_0, 3 q4_0 (engine/src/model_file.h:16)
+    int rank = 2;   // as stored in the directory (rank 1: rows == 1)
     int rows = 0, cols = 0;
     const uint8_t* data = nullptr;  // quants, then fp16 scales for quantized types
     size_t quant_bytes() const;
@@ -88,6 +89,11 @@ public:
     size_t size_bytes() const { return size_; }
     size_t tensor_count() const { return tensors_.size(); }
     int special_id(const std::string& text) const;         // -1 if absent
+    // The raw file: its bytes, the offset of the tensor directory (everything before it is the header and the
+    // tokenizer section), and the tensor names in directory order.
+    const uint8_t* bytes() const { return map_; }
+    size_t directory_offset() const { return dir_offset_; }
+    const std::vector<std::string>& tensor_names() const { return order_; }
 
 private:
     void release();
@@ -96,6 +102,8 @@ private:
     std::unordered_map<std::string, HostTensor> tensors_;
     const uint8_t* map_ = nullptr;
     size_t size_ = 0;
+    size_t dir_offset_ = 0;
+    std::vector<std::string> order_;
     QntFault fault_ = QntFault::None;
 };
 

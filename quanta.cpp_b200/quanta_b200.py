@@ -110,6 +110,8 @@ def lib() -> C.CDLL:
         L.qnt_model_kv_cache_bytes.restype = C.c_size_t
         L.qnt_model_weight_bytes.argtypes = [P]
         L.qnt_model_weight_bytes.restype = C.c_size_t
+        L.qnt_export_device_layout.argtypes = [C.c_char_p, C.c_char_p]
+        L.qnt_model_packed_tensors.argtypes = [P]
         L.qnt_generate.argtypes = [P, P, I, C.POINTER(SamplerParamsC), I, I, P, C.POINTER(GenStatsC)]
         L.qnt_set_device.argtypes = [I]
         L.qnt_session_begin.argtypes = [P, P, I, C.POINTER(SamplerParamsC), I]
@@ -393,6 +395,11 @@ class Model:
     def weight_bytes(self) -> int:
         return int(lib().qnt_model_weight_bytes(self.h))
 
+    @property
+    def packed_tensors(self) -> int:
+        """Fused tensors this load took pre-packed from the file (export_device_layout); 0 for a plain .qnt."""
+        return int(lib().qnt_model_packed_tensors(self.h))
+
     def generate(self, prompt, sp: SamplerParams, n_gen: int, shortlist: bool = True, batch_prefill: bool = True):
         """Session::feed + generate with the device sampler; returns (ids, stats dict)."""
         p = np.ascontiguousarray(prompt, np.int32)
@@ -467,6 +474,14 @@ QWEN05B = dict(vocab_size=151936, dim=896, n_layers=24, n_heads=14, n_kv_heads=2
                rope_theta=1e6, norm_eps=1e-6, n_tokens=151665)
 TINY = dict(vocab_size=5000, dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, ffn_dim=512, max_seq=512,
             rope_theta=1e6, norm_eps=1e-6, n_tokens=4900)
+
+
+def export_device_layout(src, dst) -> Path:
+    """A copy of the .qnt at src, written to dst, with the device's fused q|k|v, gate|up and q|k|v-bias tensors stored
+    pre-packed beside the original ones (which stay byte for byte, so the reference reads the copy unchanged).  No
+    GPU needed."""
+    _check(lib().qnt_export_device_layout(str(src).encode(), str(dst).encode()))
+    return Path(dst)
 
 
 def synth_model(path, *, shape: dict = QWEN05B, mlp_q4: bool = True, shortlist: bool = True, q4_group: int = 128,
