@@ -495,9 +495,9 @@ int Engine::launch_chunk(int n, const int* pos_dev, int pos_bound, TokMap tm) {
 }
 
 int Engine::launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host,
-                        int window, int n_list, bool penal, float penalty) {
+                        int window, int n_list, bool penal, float penalty, bool marked) {
     if (!shortlist) {
-        if (penal) QB_TRY(launch_mark(must, n_must_dev, n_must_host, window, n_valid, mark_, st_, pdl_));
+        if (penal && !marked) QB_TRY(launch_mark(must, n_must_dev, n_must_host, window, n_valid, mark_, st_, pdl_));
         HeadFullArgs a;
         a.W = lm_head_;
         a.plan = plan_full_;
@@ -534,14 +534,15 @@ int Engine::launch_head(bool shortlist, int k, int n_valid, const int* must, con
     a.penal = penal ? 1 : 0;
     a.penalty = penalty;
     a.lists = part_buf_;
+    a.marked = marked;
     int extra = 0;
     QB_TRY(launch_shortlist(a, hin_, st_, pdl_, &extra));
     kernel_count_ += extra - 1;
     return 0;
 }
 
-int Engine::run_graph(const std::string& key, const std::function<int()>& body) {
-    if (!use_graphs_) return body();
+int Engine::run_graph(const std::string& key, const std::function<int()>& body, bool launch) {
+    if (!use_graphs_) return launch ? body() : 0;
     auto it = graphs_.find(key);
     if (it == graphs_.end()) {
         cudaGraph_t g;
@@ -556,6 +557,7 @@ int Engine::run_graph(const std::string& key, const std::function<int()>& body) 
         if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
         it = graphs_.emplace(key, ex).first;
     }
+    if (!launch) return 0;
     cudaError_t e = cudaGraphLaunch(it->second, st_);
     if (e != cudaSuccess) return cuda_fail(e, "graph launch");
     return 0;
@@ -801,6 +803,9 @@ int Engine::session_begin(const int* prompt, int n_prompt, const SamplerParamsC&
     return 0;
 }
 
+// decode steps per graph replay in session_step's runs
+constexpr int kStepsPerGraph = 8;
+
 int Engine::session_step(int n) {
     if (!sess_.active) {
         err_ = "no active session";
@@ -822,40 +827,61 @@ int Engine::session_step(int n) {
                             std::to_string(penal) + "|" + std::to_string(sp.repeat_window) + "|" +
                             std::to_string(sp.temperature) + "|" + std::to_string(sp.top_p) + "|" + std::to_string(sp.min_p) +
                             "|" + std::to_string(sp.repeat_penalty);
-    for (int s = 0; s < n; ++s) {
-        const int r = run_graph(key, [&]() -> int {
-            const int c0 = kernel_count_;
-            if (wide) {
-                // Sampler::sample over the whole logits: the penalty in place on the unique history ids, then the
-                // sorting sampler; the head below only writes logits
-                if (penal) {
-                    QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, pdl_));
-                    QB_TRY(launch_topk_partial(logits_, nv, 1, 1, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, pdl_,
-                                               logits_));
-                }
-                int extra = 0;
-                const cudaError_t e = launch_sample_wide(logits_, nv, K, sa, ss_, hist_, ctx_, wide_, st_, pdl_, &extra);
-                kernel_count_ += extra;
-                if (e != cudaSuccess) return cuda_fail(e, "launch_sample_wide");
-                QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
-                if (int rr = launch_layers_decode(&ss_->pos)) return rr;
-                QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, V, st_, pdl_));
-                const int rr = launch_head(false, 1, nv, nullptr, nullptr, 0, 0, 0, false, 1.0f);
-                kernels_per_step_ = kernel_count_ - c0;
-                return rr;
+    const auto step = [&]() -> int {
+        const int c0 = kernel_count_;
+        if (wide) {
+            // Sampler::sample over the whole logits: the penalty in place on the unique history ids, then the
+            // sorting sampler; the head below only writes logits
+            if (penal) {
+                QB_TRY(launch_mark(hist_, &ss_->n_hist, 0, sp.repeat_window, nv, mark_, st_, pdl_));
+                QB_TRY(launch_topk_partial(logits_, nv, 1, 1, sp.repeat_penalty, mark_, part_buf_, n_lists_, st_, pdl_,
+                                           logits_));
             }
-            QB_TRY(launch_sample_final(part_buf_, n_lists_, K, sa, ss_, hist_, ctx_, st_, pdl_));
+            int extra = 0;
+            const cudaError_t e = launch_sample_wide(logits_, nv, K, sa, ss_, hist_, ctx_, wide_, st_, pdl_, &extra);
+            kernel_count_ += extra;
+            if (e != cudaSuccess) return cuda_fail(e, "launch_sample_wide");
             QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
             if (int rr = launch_layers_decode(&ss_->pos)) return rr;
-            QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, sl ? 0 : V, st_, pdl_));
-            // must ids = the penalized history window (session.cpp:63-79); none without a penalty
-            const int rr = launch_head(sl, K, nv, penal ? hist_ : nullptr, penal ? &ss_->n_hist : nullptr, 0,
-                                       penal ? sp.repeat_window : 0, K, penal, sp.repeat_penalty);
+            QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, V, st_, pdl_));
+            const int rr = launch_head(false, 1, nv, nullptr, nullptr, 0, 0, 0, false, 1.0f);
             kernels_per_step_ = kernel_count_ - c0;
             return rr;
-        });
-        if (r) return r;
+        }
+        // must ids = the penalized history window (session.cpp:63-79), none without a penalty: the sampler marks
+        // them for this step's head once it has drawn, so the head needs no mark kernel
+        NextMarks nmk;
+        if (penal) {
+            nmk.mark = mark_;
+            nmk.window = sp.repeat_window;
+            nmk.n_valid = nv;
+        }
+        QB_TRY(launch_sample_final(part_buf_, n_lists_, K, sa, ss_, hist_, ctx_, st_, pdl_, &nmk));
+        QB_TRY(launch_embed(embed_, &ss_->token, 1, X_, status_, st_, pdl_));
+        if (int rr = launch_layers_decode(&ss_->pos)) return rr;
+        QB_TRY(launch_head_input(X_, final_norm_, hp_.dim, hp_.norm_eps, hin_, hs_, sl ? 0 : V, st_, pdl_));
+        const int rr = launch_head(sl, K, nv, penal ? hist_ : nullptr, penal ? &ss_->n_hist : nullptr, 0,
+                                   penal ? sp.repeat_window : 0, K, penal, sp.repeat_penalty, penal);
+        kernels_per_step_ = kernel_count_ - c0;
+        return rr;
+    };
+    // Runs of kStepsPerGraph steps replay one graph of that many steps: inside it each step's first kernel starts
+    // early behind the previous step's last (programmatic launch), which consecutive graph launches cannot do.  That
+    // graph is captured on the first call whatever n is, so a later call never spends time instantiating it.
+    const std::string key_run = key + "|x" + std::to_string(kStepsPerGraph);
+    const auto run = [&]() -> int {
+        for (int g = 0; g < kStepsPerGraph; ++g)
+            if (int rr = step()) return rr;
+        return 0;
+    };
+    int s = 0;
+    if (use_graphs_) {
+        if (int r = run_graph(key_run, run, false)) return r;
+        for (; s + kStepsPerGraph <= n; s += kStepsPerGraph)
+            if (int r = run_graph(key_run, run)) return r;
     }
+    for (; s < n; ++s)
+        if (int r = run_graph(key, step)) return r;
     sess_.steps += n;
     sess_.len += n;
     return n;

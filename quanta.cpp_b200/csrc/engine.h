@@ -152,13 +152,15 @@ private:
     int batch_head(int n, int* host_ids);  // greedy ids of the n rows of X_
     // Head pass: full or shortlist; n_list > 0 also produces the sampler's stage-1 lists (with the penalty of the
     // marked must ids when penal).
+    // marked: the must ids were marked already (by the step's sampler), so no mark kernel runs
     int launch_head(bool shortlist, int k, int n_valid, const int* must, const int* n_must_dev, int n_must_host, int window,
-                    int n_list, bool penal, float penalty);
+                    int n_list, bool penal, float penalty, bool marked = false);
     // Prefill / batched matmul into R_: the tensor cores when the layer has TMA sources and n is large enough.
     int launch_matmul(const DMat& W, const TcMap* wmap, bool ffn_in, int n, float* out, bool residual = false);
     // TMA source of W for the tensor-core matmul (a Q4_0 matrix gets its int8 copy here); false: CUDA cores only
     bool tc_weights(const DMat& W, TcMap* map);
-    int run_graph(const std::string& key, const std::function<int()>& body);
+    // launch = false: capture and instantiate the graph (once) without running it
+    int run_graph(const std::string& key, const std::function<int()>& body, bool launch = true);
     int sync_check();
 
     QntFile file_;

@@ -21,6 +21,7 @@
 // min-p -> top-p -> xorshift64*.
 #include <climits>
 
+#include "phase_stamps.cuh"
 #include "head_kernels.h"
 #include "kernels.cuh"
 
@@ -32,6 +33,9 @@ constexpr int kRowParts = 4;
 constexpr int kMaxBpp = 16;  // blocks per part: cols <= kRowParts * kMaxBpp * 32 (kernels instantiated for 8 and 16)
 __host__ __device__ constexpr int head_tile_rows(int dtype) { return dtype == DT_Q4_0 ? 128 : 64; }
 __host__ __device__ constexpr int head_threads(int dtype) { return head_tile_rows(dtype) * kRowParts; }
+// The coarse Q4 pass may take tiles of 176 rows (22 warps): for the 0.5B vocabulary over 148 CTAs that is at most 6 tiles
+// of 176 rows per CTA (1056 row slots) instead of 9 of 128 (1152), with more warps per SM to hide latency.
+constexpr int kWideTileRows = 176;
 constexpr int kHeadWarps = kHeadThreads / 32;
 constexpr int kStages = 4;
 
@@ -112,20 +116,22 @@ struct WarpTop32 {
     }
 };
 
-// Merges the CTA's warp lists into slist[0..32), best first, sentinels past K.  slist: (blockDim / 32) * 32 entries,
-// blockDim / 32 a power of two.
+// Merges the CTA's warp lists into slist[0..32), best first, sentinels past K.  slist: (blockDim / 32) * 32 entries.
+// Each level folds the upper half of the n live lists onto the lower (n odd: the middle list waits a level).
 __device__ void cta_merge_lists(WarpTop32& L, int K, Cand* slist) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     __syncthreads();
     slist[warp * 32 + lane] = Cand{L.v, L.id};
     __syncthreads();
-    for (int half = nw / 2; half >= 1; half >>= 1) {
-        if (warp < half) {
+    for (int n = int(blockDim.x >> 5); n > 1;) {
+        const int half = (n + 1) >> 1;
+        if (warp < n - half) {
             const Cand c = slist[(warp + half) * 32 + lane];
             warp_merge_top(L.v, L.id, c.v, c.id);
             slist[warp * 32 + lane] = Cand{L.v, L.id};
         }
         __syncthreads();
+        n = half;
     }
     if (warp == 0 && lane >= K) slist[lane] = Cand{-INFINITY, INT_MAX};
     __syncthreads();
@@ -135,10 +141,10 @@ __device__ void cta_merge_lists(WarpTop32& L, int K, Cand* slist) {
 // best first.  Each warp merges its share of the lists in registers, then a tree over the warps' results.
 // slist: (blockDim / 32) * 32 entries; blockDim / 32 a power of two.
 __device__ void cta_merge_sorted(const Cand* __restrict__ src, int n_lists, int K, Cand* slist) {
-    constexpr int kBatch = 8;
+    constexpr int kBatch = 10;  // 16 warps x 10 lists cover the 148 lists of one stream pass in one round of loads
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    float v = -INFINITY;
-    int id = INT_MAX;
+    float v = -INFINITY, v2 = -INFINITY;  // two independent merge chains (even / odd batch slots), merged at the end
+    int id = INT_MAX, id2 = INT_MAX;
     for (int l0 = warp; l0 < n_lists; l0 += kBatch * nw) {
         float bv[kBatch];
         int bid[kBatch];
@@ -150,9 +156,12 @@ __device__ void cta_merge_sorted(const Cand* __restrict__ src, int n_lists, int 
             bid[u] = ok ? __ldcg(&src[size_t(l) * K + lane].id) : INT_MAX;
         }
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u)
+        for (int u = 0; u < kBatch; u += 2) {
             if (l0 + u * nw < n_lists) warp_merge_top(v, id, bv[u], bid[u]);
+            if (l0 + (u + 1) * nw < n_lists) warp_merge_top(v2, id2, bv[u + 1], bid[u + 1]);
+        }
     }
+    warp_merge_top(v, id, v2, id2);  // the top 32 of a union do not depend on the order of the merges
     slist[warp * 32 + lane] = Cand{v, id};
     __syncthreads();
     for (int half = nw / 2; half >= 1; half >>= 1) {
@@ -179,11 +188,15 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
     __shared__ __align__(16) int8_t sx[2048];
     __shared__ float sdx[64];
     __shared__ int ssum[64];
+    PhaseProbe probe;
+    probe.begin(6);
     NormW nw;
     load_norm_w(norm_w, dim, nw);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     norm_quant(X, nw, dim, eps, sx, sdx, ssum, sred);
+    probe.mark();
     if (threadIdx.x == 0 && hs) {
         hs->rows_total += hs->calls ? hs->rows : 0;
         hs->calls += 1;
@@ -206,6 +219,7 @@ __global__ void __launch_bounds__(kThreads) k_head_input(const float* __restrict
             if (hin.xabs) hin.xabs[b] = sa;
         }
     }
+    probe.end();
 }
 
 // Activation of the head in shared memory: sx [cols] int8, then sdx, ssum, sxn [cols/32] (sxn: coarse pass only).
@@ -373,13 +387,13 @@ __device__ __forceinline__ void cp_wait_upto(int n) {  // wait until at most n g
 //   valid unmarked rows (the seeds).
 // mode 2 (coarse, nibble-plane screen): W = the Q8 head's high nibble plane with the Q8 scales (row_screen_hi4); the
 //   same outputs as mode 1, no bound table staged.
-template <int DT, int MODE, int MAXB>
-__global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
+template <int DT, int MODE, int MAXB, int TR = head_tile_rows(DT)>
+__global__ void __launch_bounds__(TR * kRowParts, 1) k_head_rows(DMat W, const __half* __restrict__ err, HeadIn hin,
                                                                      StreamPlan sp, int n_valid, int n_list, int penal,
                                                                      float penalty, unsigned char* __restrict__ mark,
                                                                      float* __restrict__ logits, float* __restrict__ coarse,
                                                                      float* __restrict__ upper, Cand* __restrict__ lists) {
-    constexpr int TR = head_tile_rows(DT), NT = head_threads(DT);
+    constexpr int NT = TR * kRowParts;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ Cand slist[NT];
     const int cols = W.cols, nb = cols / QK, rb = row_bytes(DT, cols), cpr = rb / 16, S = sp.stages;
@@ -408,9 +422,12 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
         cp_commit();
     };
 
+    PhaseProbe probe;
+    probe.begin(7);
     for (int s = 0; s < S - 1; ++s) issue(ta + s);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     load_head_act(hin, cols, act);
     __shared__ float sxa[128];  // mode 2: sum|x| per block (nb <= 128)
     if (MODE == 2) {
@@ -468,10 +485,12 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
         __syncthreads();  // this stage is refilled by the next iteration's issue()
     }
     cp_wait<0>();
+    probe.mark();
     if (n_list > 0) {
         cta_merge_lists(L, n_list, slist);
         if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
     }
+    probe.end();
 }
 
 // ---------------------------------------------------------------- shortlist head
@@ -479,8 +498,11 @@ __global__ void __launch_bounds__(head_threads(DT), 1) k_head_rows(DMat W, const
 // Marks the must ids: mark[id] = 1 for 0 <= id < n_valid (model.cpp:252-253).
 __global__ void k_sl_mark(const int* __restrict__ must, const int* __restrict__ n_must_dev, int n_must_host, int window,
                           int n_valid, unsigned char* __restrict__ mark) {
+    PhaseProbe probe;
+    probe.begin(5);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     int n = n_must_dev ? __ldcg(n_must_dev) : n_must_host;
     int from = 0;
     if (window > 0 && n > window) from = n - window;
@@ -488,6 +510,7 @@ __global__ void k_sl_mark(const int* __restrict__ must, const int* __restrict__ 
         const int id = __ldcg(must + i);
         if (id >= 0 && id < n_valid) mark[id] = 1;
     }
+    probe.end();
 }
 
 // Exact Q8 logit of one row by one warp, same terms and order as the streamed full head.  wterm: nb floats.
@@ -517,8 +540,49 @@ __device__ __forceinline__ float warp_exact_row(const DMat& W, int row, const in
     return __shfl_sync(0xffffffffu, acc, 0);
 }
 
+// Exact Q8 logits of rows ra and rb (< 0: none) by one warp for rows of at most 1024 columns: both rows' loads are in
+// flight together and lane 0 runs the two block-order chains interleaved.  wterm: 2 * nb floats.
+__device__ __forceinline__ void warp_exact_rows2(const DMat& W, int ra, int rb, const int8_t* sx, const float* sdx,
+                                                 float* wterm, float& va, float& vb) {
+    const int lane = threadIdx.x & 31, cols = W.cols, nb = cols / QK, cpr = cols / 16;
+    const int rows[2] = {ra, rb};
+    uint4 w[2][2];
+    __half dw[2][2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int c = k * 32 + lane;
+            const bool ok = rows[j] >= 0 && c < cpr;
+            w[j][k] = ok ? ld_stream(reinterpret_cast<const uint4*>(W.q + size_t(rows[j]) * cols) + c) : make_uint4(0, 0, 0, 0);
+            dw[j][k] = ok ? W.d[size_t(rows[j]) * nb + (c >> 1)] : __float2half(0.f);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int c = k * 32 + lane;
+            int s = c < cpr ? chunk_dot<DT_Q8_0>(w[j][k], sx, c) : 0;
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            if (c < cpr && !(c & 1)) wterm[j * nb + (c >> 1)] = block_term(s, __half2float(dw[j][k]), sdx[c >> 1]);
+        }
+    }
+    __syncwarp();
+    float a = 0.f, b = 0.f;
+    if (lane == 0) {
+        for (int i = 0; i < nb; ++i) {
+            a = fadd(a, wterm[i]);
+            b = fadd(b, wterm[nb + i]);
+        }
+    }
+    __syncwarp();
+    va = __shfl_sync(0xffffffffu, a, 0);
+    vb = __shfl_sync(0xffffffffu, b, 0);
+}
+
 // One CTA: global seeds (the n_seed best coarse scores), their exact logits, tau.
-__global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, const Cand* __restrict__ seed_lists,
+__global__ void __launch_bounds__(kHeadThreads, 1) k_sl_seeds(DMat W8, HeadIn hin, const Cand* __restrict__ seed_lists,
                                                            int n_lists, int n_seed, int k, unsigned char* __restrict__ mark,
                                                            float* __restrict__ logits, HeadState* __restrict__ hs) {
     __shared__ Cand slist[kHeadWarps * 32];
@@ -527,14 +591,18 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     __shared__ float wterm[kHeadWarps][128];
     __shared__ float exact[32];
     __shared__ int s_ns;
+    PhaseProbe probe;
+    probe.begin(8);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cols = W8.cols, nb = cols / QK;
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
         reinterpret_cast<int4*>(sx)[i] = __ldcg(reinterpret_cast<const int4*>(hin.xq) + i);
     for (int b = threadIdx.x; b < nb; b += blockDim.x) sdx[b] = __ldcg(hin.dx + b);
     cta_merge_sorted(seed_lists, n_lists, n_seed, slist);
+    probe.mark();
     if (threadIdx.x == 0) {
         int n = 0;
         while (n < n_seed && slist[n].id != INT_MAX) ++n;
@@ -542,16 +610,36 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
     }
     __syncthreads();
     const int ns = s_ns;
-    for (int s = warp; s < ns; s += kHeadWarps) {
-        const int id = slist[s].id;
-        const float v = warp_exact_row(W8, id, sx, sdx, wterm[warp]);
-        if (lane == 0) {
-            exact[s] = v;
-            logits[id] = v;
-            mark[id] = 2;
+    if (cols <= 1024) {  // two seeds per warp at once: every seed in one round of loads
+        for (int s = warp; s < ns; s += 2 * kHeadWarps) {
+            const int s2 = s + kHeadWarps;
+            const int id = slist[s].id, id2 = s2 < ns ? slist[s2].id : -1;
+            float v, v2;
+            warp_exact_rows2(W8, id, id2, sx, sdx, wterm[warp], v, v2);
+            if (lane == 0) {
+                exact[s] = v;
+                logits[id] = v;
+                mark[id] = 2;
+                if (id2 >= 0) {
+                    exact[s2] = v2;
+                    logits[id2] = v2;
+                    mark[id2] = 2;
+                }
+            }
+        }
+    } else {
+        for (int s = warp; s < ns; s += kHeadWarps) {
+            const int id = slist[s].id;
+            const float v = warp_exact_row(W8, id, sx, sdx, wterm[warp]);
+            if (lane == 0) {
+                exact[s] = v;
+                logits[id] = v;
+                mark[id] = 2;
+            }
         }
     }
     __syncthreads();
+    probe.mark();
     // tau = the k-th largest exact seed logit (model.cpp:308-313): the seed whose rank (ties by position) is k-1.
     if (threadIdx.x < 32) {
         const int i = threadIdx.x;
@@ -567,6 +655,7 @@ __global__ void __launch_bounds__(kHeadThreads) k_sl_seeds(DMat W8, HeadIn hin, 
             hs->rows = ns;
         }
     }
+    probe.end();
 }
 
 // Candidate pass over this CTA's contiguous rows.  One scan reads every mark / bound, clears the marks, and compacts
@@ -596,8 +685,11 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
         s_count = 0;
         s_seeds = 0;
     }
+    PhaseProbe probe;
+    probe.begin(9);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     load_head_act(hin, cols, act);
     const float tau = __ldcg(&hs->tau);
     const int lane = threadIdx.x & 31;
@@ -631,6 +723,7 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
         }
     }
     __syncthreads();
+    probe.mark();
     const int n = s_count, ns = s_seeds;
     const int n_tiles = (n + TR - 1) / TR;
     const int dpr = nb / 4;  // 8-byte scale groups per row (rows of scales are 8-byte aligned, not 16)
@@ -681,6 +774,7 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
         __syncthreads();
     }
     cp_wait<0>();
+    probe.mark();
     if (n_list > 0) {
         // the seeds: exact logits from the seed pass, never penalised (a must id carries mark 1, not 2)
         for (int i0 = 0; i0 < ns; i0 += NT) {
@@ -693,6 +787,7 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
         if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
     }
     if (threadIdx.x == 0 && n) atomicAdd(&hs->rows, n);
+    probe.end();
 }
 
 // ---------------------------------------------------------------- sampler
@@ -739,65 +834,101 @@ __device__ __forceinline__ uint64_t xorshift64s(uint64_t& s) {
 // history and advances the position.
 __global__ void __launch_bounds__(kHeadThreads) k_sample_final(const Cand* __restrict__ parts, int n_lists, int K, SamplerArgs sa,
                                                                SamplerState* __restrict__ ss, int* __restrict__ hist,
-                                                               int hist_cap) {
+                                                               int hist_cap, NextMarks nm) {
     __shared__ Cand slist[kHeadWarps * 32];
+    PhaseProbe probe;
+    probe.begin(10);
     pdl_wait();
     pdl_launch_dependents();
-    __shared__ float p[32];
+    probe.mark();
+    // the history length and the generator state, read ahead of the merge (warp 0 updates them after its barriers)
+    const int nh_before = __ldcg(&ss->n_hist);
+    const unsigned long long rng0 = __ldcg(&ss->rng);
     cta_merge_sorted(parts, n_lists, K, slist);
-    if (threadIdx.x >= 32) return;
+    probe.mark();
+    const bool appends = sa.append && nh_before < hist_cap;
+    if (threadIdx.x >= 32) {
+        // the next head's must ids already in the history (lane 0 marks the drawn id), while warp 0 draws
+        if (nm.mark) {
+            const int after = nh_before + (appends ? 1 : 0);
+            const int first = nm.window > 0 && after > nm.window ? after - nm.window : 0;
+            for (int i = first + int(threadIdx.x) - 32; i < nh_before; i += int(blockDim.x) - 32) {
+                const int id = __ldcg(hist + i);
+                if (id >= 0 && id < nm.n_valid) nm.mark[id] = 1;
+            }
+        }
+        return;
+    }
     const int lane = threadIdx.x;
     const int n = __popc(__ballot_sync(0xffffffffu, lane < K && slist[lane].id != INT_MAX));  // valid entries form a prefix
     const bool draw = sa.temperature > 0.f && n > 0;
-    if (draw) {  // the n exps in parallel, one per lane
-        const float mx = slist[0].v;
-        p[lane] = lane < n ? exp_ref(fdiv(fsub(slist[lane].v, mx), sa.temperature), sa.exptab) : 0.f;
-    }
-    __syncwarp();
-    if (lane != 0) return;
-    int pick = n > 0 ? slist[0].id : 0;
+    int pick_i = 0;
     if (draw) {
+        // the n exps in parallel, one per lane; then every lane holds all of them in registers and runs the
+        // reference's sequential sums and scans on them (the same operations in the same order on each lane)
+        const float mx = slist[0].v;
+        const float mine = lane < n ? exp_ref(fdiv(fsub(slist[lane].v, mx), sa.temperature), sa.exptab) : 0.f;
+        float p[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p[i] = __shfl_sync(0xffffffffu, mine, i);
         float sum = 0.f;
-        for (int i = 0; i < n; ++i) sum = fadd(sum, p[i]);
-        for (int i = 0; i < n; ++i) p[i] = fdiv(p[i], sum);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < n) sum = fadd(sum, p[i]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < n) p[i] = fdiv(p[i], sum);
         int keep = n;
-        if (sa.min_p > 0.f) {
+        if (sa.min_p > 0.f) {  // while (keep > 1 && p[keep - 1] < floor) --keep
             const float floor = fmul(p[0], sa.min_p);
-            while (keep > 1 && p[keep - 1] < floor) --keep;
+#pragma unroll
+            for (int i = 31; i >= 1; --i)
+                if (keep == i + 1 && p[i] < floor) keep = i;
         }
-        if (sa.top_p < 1.f) {
+        if (sa.top_p < 1.f) {  // the first prefix whose cumulative sum reaches top_p
             float cum = 0.f;
-            for (int i = 0; i < keep; ++i) {
-                cum = fadd(cum, p[i]);
-                if (cum >= sa.top_p) {
-                    keep = i + 1;
-                    break;
+            bool reached = false;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (!reached && i < keep) {
+                    cum = fadd(cum, p[i]);
+                    if (cum >= sa.top_p) {
+                        keep = i + 1;
+                        reached = true;
+                    }
                 }
             }
         }
         float total_p = 0.f;
-        for (int i = 0; i < keep; ++i) total_p = fadd(total_p, p[i]);
-        uint64_t st = __ldcg(&ss->rng);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < keep) total_p = fadd(total_p, p[i]);
+        uint64_t st = rng0;
         const float u = fmul(float(xorshift64s(st) >> 40), 1.0f / 16777216.0f);
-        ss->rng = st;
+        if (lane == 0) ss->rng = st;
         float r = fmul(u, total_p);
-        pick = slist[keep - 1].id;
-        for (int i = 0; i < keep; ++i) {
-            r = fsub(r, p[i]);
-            if (r <= 0.f) {
-                pick = slist[i].id;
-                break;
+        pick_i = keep - 1;
+        bool found = false;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (!found && i < keep) {
+                r = fsub(r, p[i]);
+                if (r <= 0.f) {
+                    pick_i = i;
+                    found = true;
+                }
             }
         }
     }
+    if (lane != 0) return;
+    const int pick = n > 0 ? slist[pick_i].id : 0;
+    probe.end();
+    if (nm.mark && appends && pick >= 0 && pick < nm.n_valid) nm.mark[pick] = 1;
     ss->token = pick;
-    if (sa.append) {
-        const int nh = __ldcg(&ss->n_hist);
-        if (nh < hist_cap) {
-            hist[nh] = pick;
-            ss->n_hist = nh + 1;
-            ss->pos = nh;  // the new token is fed at position len(history) - 1
-        }
+    if (appends) {
+        hist[nh_before] = pick;
+        ss->n_hist = nh_before + 1;
+        ss->pos = nh_before;  // the new token is fed at position len(history) - 1
     }
 }
 
@@ -825,6 +956,8 @@ __global__ void k_hi_plane(const int8_t* __restrict__ q, long long n_blocks, uin
     }
 }
 
+QNT_PHASE_READER(qnt_phase_read_head)
+
 // ---------------------------------------------------------------- launchers
 
 namespace {
@@ -833,12 +966,12 @@ size_t align16(size_t n) { return (n + 15) & ~size_t(15); }
 
 }  // namespace
 
-StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather) {
+namespace {
+StreamPlan plan_stream_tr(int dtype, int rows, int cols, int grid, bool coarse, bool gather, int tr) {
     StreamPlan p;
     const int rb = row_bytes_host(dtype, cols), cpr = rb / 16, nb = cols / QK;
-    const int tr = head_tile_rows(dtype);
     p.tile_rows = tr;
-    p.threads = head_threads(dtype);
+    p.threads = tr * kRowParts;
     p.n_tiles = (rows + tr - 1) / tr;
     p.cpr_magic = div_magic(unsigned(cpr));
     p.qstride = rb + 16;
@@ -850,12 +983,24 @@ StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, boo
     const size_t list_bytes = align16(size_t(p.list_cap) * 4);
     p.list_off = int(act_bytes);
     p.ring_off = int((act_bytes + list_bytes + 127) / 128 * 128);
-    const size_t budget = 227 * 1024 - size_t(p.threads) * sizeof(Cand) - 64;  // minus the kernels' static shared memory
+    // minus the kernels' static shared memory: the CTA list, sxa of the nibble screen, a few counters
+    const size_t budget = 227 * 1024 - size_t(p.threads) * sizeof(Cand) - 512 - 128;
     const size_t fit = budget > size_t(p.ring_off) ? (budget - p.ring_off) / size_t(p.stage_bytes) : 0;
     p.stages = int(std::min<size_t>(4, fit));
     if (p.stages < 2 || nb % 4 != 0 || nb % kRowParts != 0 || nb / kRowParts > kMaxBpp) p.stages = 0;
     p.smem = size_t(p.ring_off) + size_t(p.stages) * p.stage_bytes;
     p.grid = grid;
+    return p;
+}
+}  // namespace
+
+StreamPlan plan_stream(int dtype, int rows, int cols, int grid, bool coarse, bool gather) {
+    StreamPlan p = plan_stream_tr(dtype, rows, cols, grid, coarse, gather, head_tile_rows(dtype));
+    if (coarse && dtype == DT_Q4_0 && grid > 0) {  // the wide tile when it fits twice and leaves fewer padded rows per CTA
+        const StreamPlan w = plan_stream_tr(dtype, rows, cols, grid, coarse, gather, kWideTileRows);
+        const auto slots = [&](const StreamPlan& q) { return size_t((q.n_tiles + grid - 1) / grid) * size_t(q.tile_rows); };
+        if (w.stages >= 2 && (p.stages == 0 || slots(w) <= slots(p))) p = w;
+    }
     return p;
 }
 
@@ -894,12 +1039,21 @@ cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStre
     const int n_seed = a.k + 8;
     if (a.k < 1 || n_seed > 32 || a.W8.cols > 4096 || a.n_list > 32 || a.plan4.stages == 0 || a.plan8g.stages == 0)
         return cudaErrorInvalidValue;
-    cudaError_t e = launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, a.must, a.n_must_dev, a.n_must_host, a.window,
-                               a.n_valid, a.mark);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
+    if (!a.marked) {
+        e = launch_pdl(k_sl_mark, dim3(4), dim3(kThreads), 0, st, pdl, a.must, a.n_must_dev, a.n_must_host, a.window,
+                       a.n_valid, a.mark);
+        if (e != cudaSuccess) return e;
+    }
     const bool small = a.W8.cols / QK / kRowParts <= 8;
-    auto coarse_kernel = a.screen == kScreenHi4 ? (small ? k_head_rows<DT_Q4_0, 2, 8> : k_head_rows<DT_Q4_0, 2, kMaxBpp>)
-                                                : (small ? k_head_rows<DT_Q4_0, 1, 8> : k_head_rows<DT_Q4_0, 1, kMaxBpp>);
+    const bool wide = a.plan4.tile_rows == kWideTileRows;
+    constexpr int W = kWideTileRows;
+    auto coarse_kernel =
+        a.screen == kScreenHi4
+            ? (wide ? (small ? k_head_rows<DT_Q4_0, 2, 8, W> : k_head_rows<DT_Q4_0, 2, kMaxBpp, W>)
+                    : (small ? k_head_rows<DT_Q4_0, 2, 8> : k_head_rows<DT_Q4_0, 2, kMaxBpp>))
+            : (wide ? (small ? k_head_rows<DT_Q4_0, 1, 8, W> : k_head_rows<DT_Q4_0, 1, kMaxBpp, W>)
+                    : (small ? k_head_rows<DT_Q4_0, 1, 8> : k_head_rows<DT_Q4_0, 1, kMaxBpp>));
     e = launch_pdl(coarse_kernel, dim3(a.plan4.grid),
                    dim3(a.plan4.threads), a.plan4.smem, st, pdl, a.W4, a.err, hin, a.plan4, a.n_valid, n_seed, 0, 1.0f, a.mark,
                    a.logits, a.coarse, a.upper, reinterpret_cast<Cand*>(a.seed_buf));
@@ -910,7 +1064,7 @@ cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStre
     e = launch_pdl(small ? k_sl_cands<8> : k_sl_cands<kMaxBpp>, dim3(a.plan8g.grid), dim3(a.plan8g.threads), a.plan8g.smem, st, pdl, a.W8, hin, a.plan8g, a.n_valid,
                    a.n_list, a.penal, a.penalty, a.mark, (const float*)a.upper, a.logits, a.hs,
                    reinterpret_cast<Cand*>(a.lists));
-    if (kernels) *kernels += 4;
+    if (kernels) *kernels += a.marked ? 3 : 4;
     return e;
 }
 
@@ -927,10 +1081,11 @@ cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int pen
 }
 
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
-                                int hist_cap, cudaStream_t st, bool pdl) {
+                                int hist_cap, cudaStream_t st, bool pdl, const NextMarks* next) {
     if (K < 1 || K > 32) return cudaErrorInvalidValue;
+    if (next && next->mark && !hist) return cudaErrorInvalidValue;
     return launch_pdl(k_sample_final, dim3(1), dim3(kHeadThreads), 0, st, pdl, reinterpret_cast<const Cand*>(lists), n_lists,
-                      K, sa, ss, hist, hist_cap);
+                      K, sa, ss, hist, hist_cap, next ? *next : NextMarks{});
 }
 
 }  // namespace qb

@@ -88,6 +88,7 @@ struct ShortlistArgs {
     int penal;
     float penalty;
     void* lists;            // plan8g.grid * n_list candidates
+    bool marked = false;    // the must ids are marked already (k_sample_final's NextMarks): no mark kernel
 };
 
 struct SamplerArgs {
@@ -108,15 +109,22 @@ struct SamplerState {
 cudaError_t launch_head_input(const float* X, const float* norm_w, int dim, float eps, const HeadIn& hin, HeadState* hs,
                               int full_rows, cudaStream_t st, bool pdl);
 cudaError_t launch_head_full(const HeadFullArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl);
-// Launches 4 kernels (mark, coarse, seeds, candidates); adds 4 to *kernels.
+// Launches 4 kernels (mark, coarse, seeds, candidates; 3 without the mark kernel when a.marked); adds them to *kernels.
 cudaError_t launch_shortlist(const ShortlistArgs& a, const HeadIn& hin, cudaStream_t st, bool pdl, int* kernels);
 cudaError_t launch_mark(const int* must, const int* n_must_dev, int n_must_host, int window, int n_valid, unsigned char* mark,
                         cudaStream_t st, bool pdl);
 // write_back: where the penalised logits go (the logits array itself for an in-place edit), or null.
 cudaError_t launch_topk_partial(const float* logits, int n_valid, int K, int penal, float penalty, unsigned char* mark,
                                 void* lists, int n_lists, cudaStream_t st, bool pdl, float* write_back = nullptr);
+// The next head pass's must ids, marked by k_sample_final while it draws (a decode step's sampler, whose head follows
+// in the same step): mark[id] = 1 for the ids in [0, n_valid) among the last `window` ids of the history after this
+// draw's append (0: the whole history), the same marks the mark kernel would set before that head.
+struct NextMarks {
+    unsigned char* mark = nullptr;  // null: none
+    int window = 0, n_valid = 0;
+};
 cudaError_t launch_sample_final(const void* lists, int n_lists, int K, const SamplerArgs& sa, SamplerState* ss, int* hist,
-                                int hist_cap, cudaStream_t st, bool pdl);
+                                int hist_cap, cudaStream_t st, bool pdl, const NextMarks* next = nullptr);
 
 // nll.cu: *acc += -log softmax(logits[0..n_valid))[target] (the perplexity's term), f64 accumulation.
 cudaError_t launch_token_nll(const float* logits, int n_valid, int target, double* acc, cudaStream_t st, bool pdl);

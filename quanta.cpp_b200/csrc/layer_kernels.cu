@@ -33,8 +33,11 @@ constexpr int kRtMaxNb = 32;  // o_proj blocks per row that the gate|up residual
 // ---------------------------------------------------------------- embedding (engine/src/ops_ref.cpp:162-192 get_row)
 
 __global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float* __restrict__ X, unsigned* status) {
+    PhaseProbe probe;
+    probe.begin(4);
     pdl_wait();
     pdl_launch_dependents();
+    probe.mark();
     const int t = blockIdx.x;
     if (t >= n_tok) return;
     int tok = __ldcg(tokens + t);
@@ -47,6 +50,7 @@ __global__ void k_embed(DMat E, const int* __restrict__ tokens, int n_tok, float
     const __half* d = E.d + size_t(tok) * (dim / QK);
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
         X[size_t(t) * dim + i] = fmul(float(q[i]), __half2float(d[i / QK]));
+    probe.end();
 }
 
 // ---------------------------------------------------------------- shared epilogues

@@ -13,7 +13,8 @@ constexpr int kPhaseMarks = 12;
 struct PhaseRec {
     unsigned long long g0, g1;  // global timer (ns) at the start and the end of CTA 0
     long long c[kPhaseMarks];   // clock64 at each mark (c[0]: the start)
-    int kind, n;                // kernel kind (1 attention, 2 gate|up, 3 down / o_proj residual), marks recorded
+    int kind, n;                // kernel kind (1 attention, 2 gate|up, 3 down / o_proj residual, 4.. the rest), marks
+    unsigned long long g_last;  // global timer at the end of the launch's last CTA to finish
 };
 
 #ifdef QNT_PHASE_STAMPS
@@ -21,6 +22,7 @@ namespace {
 constexpr int kPhaseCap = 8192;
 __device__ PhaseRec g_phase[kPhaseCap];
 __device__ unsigned g_phase_n;
+__device__ int g_phase_cur[16];  // the record of the latest launch of each kind (read by the launch's other CTAs)
 
 __device__ __forceinline__ unsigned long long phase_gtime() {
     unsigned long long t;
@@ -30,17 +32,21 @@ __device__ __forceinline__ unsigned long long phase_gtime() {
 }  // namespace
 
 struct PhaseProbe {
-    int slot = -1, n = 0;  // the mark count stays in a register: a mark only stores (no global read on the timed path)
-    __device__ void begin(int kind) {
+    int slot = -1, n = 0, kind = 0;  // the mark count stays in a register: a mark only stores (no global read)
+    __device__ void begin(int k) {
+        kind = k & 15;
         if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
             const unsigned s = atomicAdd(&g_phase_n, 1u);
             if (s < unsigned(kPhaseCap)) {
                 slot = int(s);
-                g_phase[s].kind = kind;
+                g_phase[s].kind = k;
                 g_phase[s].g0 = phase_gtime();
+                g_phase[s].g_last = 0;
                 g_phase[s].c[0] = clock64();
                 n = 1;
                 g_phase[s].n = 1;
+                __threadfence();
+                *reinterpret_cast<volatile int*>(&g_phase_cur[kind]) = int(s);
             }
         }
     }
@@ -50,9 +56,16 @@ struct PhaseProbe {
             g_phase[slot].n = ++n;
         }
     }
+    // every CTA's thread 0 also raises the record's last end (the record is the latest of this kind: launches of one
+    // kind are far apart in time, so CTA 0 has written it long before the others end)
     __device__ void end() {
         mark();
-        if (slot >= 0) g_phase[slot].g1 = phase_gtime();
+        const unsigned long long t = phase_gtime();
+        if (slot >= 0) g_phase[slot].g1 = t;
+        if (threadIdx.x == 0) {
+            const int s = *reinterpret_cast<volatile int*>(&g_phase_cur[kind]);
+            if (s >= 0 && s < kPhaseCap) atomicMax(&g_phase[s].g_last, t);
+        }
     }
 };
 

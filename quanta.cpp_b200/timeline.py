@@ -26,7 +26,9 @@ import numpy as np  # noqa: E402
 import quanta_b200 as qb  # noqa: E402
 
 KINDS = {1: "k_attn (q|k|v + attention + o_proj terms)", 2: "k_gateup_dec (o_proj residual + norm + gate|up + SwiGLU)",
-         3: "k_resid_dec (down + residual)"}
+         3: "k_resid_dec (down + residual)", 4: "k_embed", 5: "k_sl_mark (must ids)",
+         6: "k_head_input (final norm + quantize)", 7: "k_head_rows (coarse pass)", 8: "k_sl_seeds (seeds, tau)",
+         9: "k_sl_cands (candidate rows + sampler lists)", 10: "k_sample_final (merge + draw)"}
 PHASES = {
     1: ["launch -> previous kernel done", "rmsnorm + quantize", "q|k|v rows, bias, RoPE, exchange",
         "scores + maxima exchange", "exps + exchange", "softmax sum (ordered)", "output chains (ordered)",
@@ -34,16 +36,24 @@ PHASES = {
     2: ["launch -> previous kernel done", "o_proj residual rows + exchange", "rmsnorm + quantize",
         "gate|up block terms", "row chains", "SwiGLU + quantize"],
     3: ["launch -> previous kernel done", "input activation", "down block terms", "row chains + residual"],
+    4: ["launch -> previous kernel done", "embedding row"],
+    5: ["launch -> previous kernel done", "marks"],
+    6: ["launch -> previous kernel done", "rmsnorm + quantize", "block sums and norms"],
+    7: ["launch -> previous kernel done", "tiles (coarse scores, bounds, lists)", "list merge"],
+    8: ["launch -> previous kernel done", "merge of the CTA lists", "exact seed rows", "tau"],
+    9: ["launch -> previous kernel done", "mark / upper scan", "exact candidate rows", "seed offers + list merge"],
+    10: ["launch -> previous kernel done", "merge of the lists", "softmax + draw"],
 }
 
 
 class PhaseRec(C.Structure):
-    _fields_ = [("g0", C.c_ulonglong), ("g1", C.c_ulonglong), ("c", C.c_longlong * 12), ("kind", C.c_int), ("n", C.c_int)]
+    _fields_ = [("g0", C.c_ulonglong), ("g1", C.c_ulonglong), ("c", C.c_longlong * 12), ("kind", C.c_int), ("n", C.c_int),
+                ("g_last", C.c_ulonglong)]
 
 
 def read(L, reset):
     out = []
-    for name in ("qnt_phase_read_attn", "qnt_phase_read_layers"):
+    for name in ("qnt_phase_read_attn", "qnt_phase_read_layers", "qnt_phase_read_head"):
         fn = getattr(L, name)
         fn.argtypes = [C.c_void_p, C.c_int, C.c_int]
         buf = (PhaseRec * 8192)()
@@ -64,8 +74,10 @@ def summarize(recs):
     for kind in sorted(by_kind):
         rs = by_kind[kind]
         names = PHASES.get(kind, [])
+        tails = [(int(r.g_last) - int(r.g1)) / 1e3 for r in rs if r.g_last]
+        tail = f", last CTA ends {statistics.median(tails):.2f} µs after CTA 0" if tails else ""
         lines.append(f"\n**{KINDS.get(kind, kind)}**: {len(rs)} launches, median span "
-                     f"{statistics.median((r.g1 - r.g0) / 1e3 for r in rs):.2f} µs (global timer)\n")
+                     f"{statistics.median((r.g1 - r.g0) / 1e3 for r in rs):.2f} µs (global timer){tail}\n")
         lines.append("| phase | median µs | share of the span |")
         lines.append("|---|---|---|")
         nmark = min(r.n for r in rs)
@@ -84,11 +96,29 @@ def summarize(recs):
     gaps = {}
     for a, b in zip(recs, recs[1:]):
         if a.g1 and b.g0:
-            gaps.setdefault((a.kind, b.kind), []).append((int(b.g0) - int(a.g1)) / 1e3)
-    lines.append("\n| from -> to | launches | median gap µs (next start - previous end) |")
-    lines.append("|---|---|---|")
+            last = int(a.g_last) if a.g_last else int(a.g1)
+            gaps.setdefault((a.kind, b.kind), []).append(((int(b.g0) - int(a.g1)) / 1e3, (int(b.g0) - last) / 1e3))
+    # the step outside the layers: each non-layer kernel's start and end after the last layer kernel's end
+    outside = {}
+    last_layer_end = None
+    for r in recs:
+        if r.kind in (1, 2, 3):
+            last_layer_end = int(r.g_last or r.g1) if r.kind == 3 else last_layer_end
+        elif last_layer_end is not None and r.g1:
+            outside.setdefault(r.kind, []).append(((int(r.g0) - last_layer_end) / 1e3, (int(r.g1) - last_layer_end) / 1e3,
+                                                   (int(r.g_last or r.g1) - last_layer_end) / 1e3))
+    if outside:
+        lines.append("\n| kernel after the last layer (its last CTA's end = 0) | launches | median start µs | "
+                     "median CTA 0 end µs | median last CTA end µs |")
+        lines.append("|---|---|---|---|---|")
+        for kind, v in sorted(outside.items(), key=lambda kv: statistics.median(x[0] for x in kv[1])):
+            lines.append(f"| {KINDS.get(kind, kind)} | {len(v)} | {statistics.median(x[0] for x in v):.2f} | "
+                         f"{statistics.median(x[1] for x in v):.2f} | {statistics.median(x[2] for x in v):.2f} |")
+    lines.append("\n| from -> to | launches | median gap µs (next start - previous CTA 0 end) | (next start - previous last end) |")
+    lines.append("|---|---|---|---|")
     for (ka, kb), v in sorted(gaps.items()):
-        lines.append(f"| {ka} -> {kb} | {len(v)} | {statistics.median(v):.2f} |")
+        lines.append(f"| {ka} -> {kb} | {len(v)} | {statistics.median(x[0] for x in v):.2f} | "
+                     f"{statistics.median(x[1] for x in v):.2f} |")
     return "\n".join(lines)
 
 
