@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(TR * kRowParts, 1) k_head_rows(DMat W, const _
         if (last_part && r < nrows) {
             row = row0 + r;
             cv = v;
-            if (MODE == 0) {
+            if constexpr (MODE == 0) {
                 logits[row] = v;
                 if (n_list > 0) {
                     ok = row < n_valid;
@@ -481,11 +481,26 @@ __global__ void __launch_bounds__(TR * kRowParts, 1) k_head_rows(DMat W, const _
                 ok = row < n_valid && __ldcg(mark + row) == 0;
             }
         }
-        if (n_list > 0) L.offer(cv, row, ok, n_list);
+        if constexpr (MODE == 0) {
+            if (n_list > 0) L.offer(cv, row, ok, n_list);
+        } else if (last_part) {  // the seeds are selected once after the tiles, from every row's score kept here
+            reinterpret_cast<Cand*>(smem + sp.cand_off)[(t - ta) * TR + r] = ok ? Cand{cv, row} : Cand{-INFINITY, INT_MAX};
+        }
         __syncthreads();  // this stage is refilled by the next iteration's issue()
     }
     cp_wait<0>();
     probe.mark();
+    if constexpr (MODE != 0) {
+        if (n_list > 0) {  // each warp offers 32 of the CTA's rows at a time
+            const Cand* cb = reinterpret_cast<const Cand*>(smem + sp.cand_off);
+            const int n_c = (tb - ta) * TR;
+            for (int i0 = 0; i0 < n_c; i0 += NT) {
+                const int i = i0 + int(threadIdx.x);
+                const Cand c = i < n_c ? cb[i] : Cand{-INFINITY, INT_MAX};
+                L.offer(c.v, c.id, c.id != INT_MAX, n_list);
+            }
+        }
+    }
     if (n_list > 0) {
         cta_merge_lists(L, n_list, slist);
         if (threadIdx.x < n_list) lists[size_t(blockIdx.x) * n_list + threadIdx.x] = slist[threadIdx.x];
@@ -985,10 +1000,13 @@ StreamPlan plan_stream_tr(int dtype, int rows, int cols, int grid, bool coarse, 
     p.ring_off = int((act_bytes + list_bytes + 127) / 128 * 128);
     // minus the kernels' static shared memory: the CTA list, sxa of the nibble screen, a few counters
     const size_t budget = 227 * 1024 - size_t(p.threads) * sizeof(Cand) - 512 - 128;
-    const size_t fit = budget > size_t(p.ring_off) ? (budget - p.ring_off) / size_t(p.stage_bytes) : 0;
+    p.cand_cap = coarse && grid > 0 ? (p.n_tiles + grid - 1) / grid * tr : 0;
+    const size_t cand_bytes = size_t(p.cand_cap) * sizeof(Cand), fixed = size_t(p.ring_off) + cand_bytes;
+    const size_t fit = budget > fixed ? (budget - fixed) / size_t(p.stage_bytes) : 0;
     p.stages = int(std::min<size_t>(4, fit));
     if (p.stages < 2 || nb % 4 != 0 || nb % kRowParts != 0 || nb / kRowParts > kMaxBpp) p.stages = 0;
-    p.smem = size_t(p.ring_off) + size_t(p.stages) * p.stage_bytes;
+    p.cand_off = int(size_t(p.ring_off) + size_t(p.stages) * p.stage_bytes);
+    p.smem = size_t(p.cand_off) + cand_bytes;
     p.grid = grid;
     return p;
 }

@@ -39,6 +39,7 @@ struct StreamPlan {
     unsigned cpr_magic = 0;
     int qstride = 0, d_off = 0, e_off = 0, stage_bytes = 0, stages = 0;
     int list_off = 0, list_cap = 0, ring_off = 0;
+    int cand_off = 0, cand_cap = 0;  // coarse pass: every row's (score, id) of the CTA, selected from after the tiles
     size_t smem = 0;
     int grid = 0;
 };
