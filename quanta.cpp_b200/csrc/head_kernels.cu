@@ -152,8 +152,10 @@ __device__ void cta_merge_sorted(const Cand* __restrict__ src, int n_lists, int 
         for (int u = 0; u < kBatch; ++u) {  // loads first: one list per batch slot
             const int l = l0 + u * nw;
             const bool ok = l < n_lists && lane < K;
-            bv[u] = ok ? __ldcg(&src[size_t(l) * K + lane].v) : -INFINITY;
-            bid[u] = ok ? __ldcg(&src[size_t(l) * K + lane].id) : INT_MAX;
+            const float2 c = ok ? __ldcg(reinterpret_cast<const float2*>(src + size_t(l) * K + lane))
+                                : make_float2(-INFINITY, __int_as_float(INT_MAX));  // (v, id) in one 8-byte load
+            bv[u] = c.x;
+            bid[u] = __float_as_int(c.y);
         }
 #pragma unroll
         for (int u = 0; u < kBatch; u += 2) {
@@ -441,9 +443,11 @@ __global__ void __launch_bounds__(TR * kRowParts, 1) k_head_rows(DMat W, const _
     const int r = (threadIdx.x >> 5) * 8 + (lane & 7);  // this lane's row in the tile
     const bool last_part = (lane >> 3) == kRowParts - 1;
     for (int t = ta; t < tb; ++t) {
-        issue(t + S - 1);
-        cp_wait_upto(S - 1);
+        // tile t landed (this thread's copies, then everyone's), and every thread is past tile t - 1, whose stage
+        // the next tile's copies refill: one barrier per tile
+        cp_wait_upto(S - 2);
         __syncthreads();
+        issue(t + S - 1);
         const unsigned char* st = ring + size_t((t - ta) % S) * sp.stage_bytes;
         const int row0 = t * TR, nrows = min(TR, W.rows - row0);
         float v, bound;
@@ -486,11 +490,11 @@ __global__ void __launch_bounds__(TR * kRowParts, 1) k_head_rows(DMat W, const _
         } else if (last_part) {  // the seeds are selected once after the tiles, from every row's score kept here
             reinterpret_cast<Cand*>(smem + sp.cand_off)[(t - ta) * TR + r] = ok ? Cand{cv, row} : Cand{-INFINITY, INT_MAX};
         }
-        __syncthreads();  // this stage is refilled by the next iteration's issue()
     }
     cp_wait<0>();
     probe.mark();
     if constexpr (MODE != 0) {
+        __syncthreads();  // every row's candidate is in shared memory
         if (n_list > 0) {  // each warp offers 32 of the CTA's rows at a time
             const Cand* cb = reinterpret_cast<const Cand*>(smem + sp.cand_off);
             const int n_c = (tb - ta) * TR;
@@ -766,9 +770,9 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
     WarpTop32 L;
     L.init();
     for (int t = 0; t < n_tiles; ++t) {
-        issue(t + S - 1);
-        cp_wait_upto(S - 1);
+        cp_wait_upto(S - 2);  // as in k_head_rows: one barrier per tile
         __syncthreads();
+        issue(t + S - 1);
         const unsigned char* st = ring + size_t(t % S) * sp.stage_bytes;
         const int nrows = min(TR, n - t * TR);
         float v, unused;
@@ -786,7 +790,6 @@ __global__ void __launch_bounds__(head_threads(DT_Q8_0), 1) k_sl_cands(DMat W8, 
             cv = (penal && (e >> 30)) ? penalize(v, penalty) : v;
         }
         if (n_list > 0) L.offer(cv, ok ? row : INT_MAX, ok, n_list);
-        __syncthreads();
     }
     cp_wait<0>();
     probe.mark();
