@@ -453,7 +453,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
     float* E = tile + kPfTile * kPfStrideV;                        // [group][ecap]
     pdl_wait();
     pdl_launch_dependents();
-    const int g = blockIdx.x, t = blockIdx.y;
+    // the last tokens attend to the most positions: they take the lowest block indices, so the longest CTAs start
+    // first and the short ones fill in behind them
+    const int g = blockIdx.x, t = int(gridDim.y) - 1 - int(blockIdx.y);
     const int group = a.n_heads / a.n_kv;
     const int n = (tm.pos ? __ldcg(tm.pos + t) : __ldcg(pos_dev) + t) + 1;
     if (tm.pos) {  // this token's sequence cache
