@@ -444,6 +444,18 @@ constexpr int kPfStride = kHd + 1;              // f32 K tile row stride (confli
 constexpr int kPfStrideV = kHd + 2;             // f32 V tile row stride (8-byte aligned dimension pairs)
 constexpr int kPfTileBytes = kPfTile * kPfStrideV * 4;
 
+// Scores of the first NG 32-position groups of a K tile for one query head (lane l: positions l, l + 32, ...): each
+// the dimension-order sum of the rounded products q_i * k_i.
+template <int NG>
+__device__ __forceinline__ void pf_scores(const float* qh, const float* tile, int lane, float (&sc)[4]) {
+#pragma unroll 8
+    for (int i = 0; i < kHd; ++i) {
+        const float qi = qh[i];
+#pragma unroll
+        for (int u = 0; u < NG; ++u) sc[u] = fadd(sc[u], fmul(qi, tile[(lane + 32 * u) * kPfStride + i]));
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const float* __restrict__ Q,
                                                            const int* __restrict__ pos_dev, int n_cap,
                                                            float* __restrict__ out, TokMap tm, QuantOut qo) {
@@ -503,12 +515,11 @@ __global__ void __launch_bounds__(kThreads) k_attn_prefill(AttnArgs a, const flo
         if (head) {
             const float* qh = sq + warp * kHd;
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-            for (int i = 0; i < kHd; ++i) {
-                const float qi = qh[i];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) sc[u] = fadd(sc[u], fmul(qi, tile[(lane + 32 * u) * kPfStride + i]));
-            }
+            const int groups = (min(kPfTile, n - p) + 31) >> 5;  // 32-position groups of the tile inside [0, n)
+            if (groups == 4) pf_scores<4>(qh, tile, lane, sc);
+            else if (groups == 3) pf_scores<3>(qh, tile, lane, sc);
+            else if (groups == 2) pf_scores<2>(qh, tile, lane, sc);
+            else pf_scores<1>(qh, tile, lane, sc);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int j = p + lane + 32 * u;
