@@ -143,7 +143,9 @@ size_t qnt_model_weight_bytes(const qnt_model* m);
  * the format is scripts/export.py:290-315; this is its extension point (no reference counterpart).  QNT_ERR_IO if
  * in_path does not open or out_path cannot be written. */
 int qnt_export_device_layout(const char* in_path, const char* out_path);
-/* How many fused tensors the last qnt_model_open took pre-packed from the file (0 for a plain .qnt). */
+/* How many fused tensors the last qnt_model_open took pre-packed from the file (0 for a plain .qnt).  A pre-packed
+ * tensor counts only when it holds the file's own rows in the fused order (shape and a sample of rows checked; the
+ * q|k|v bias in full); otherwise that layer's rows are fused at load. */
 int qnt_model_packed_tensors(const qnt_model* m);
 
 /* ---------------------------------------------------------------- session + sampling (engine/src/session.h, sampler.h) */

@@ -66,6 +66,30 @@ FusedHost fuse_rows(const std::vector<const HostTensor*>& parts, int mode, int h
     return f;
 }
 
+bool packed_rows_match(const HostTensor& packed, const std::vector<const HostTensor*>& parts, int mode, int head_dim) {
+    int rows = 0;
+    for (const HostTensor* p : parts) {
+        if (p->dtype != packed.dtype || p->cols != packed.cols) return false;
+        rows += p->rows;
+    }
+    if (packed.rows != rows || rows == 0 || (packed.dtype != 2 && packed.dtype != 3)) return false;
+    if (mode == 0 && head_dim <= 0) return false;
+    if (mode == 1 && (parts.size() != 2 || parts[0]->rows != parts[1]->rows || parts[0]->rows % kBlock != 0)) return false;
+    const auto order = fused_order(parts, mode, head_dim);
+    if (int(order.size()) != rows) return false;
+    const size_t rb = row_quant_bytes(packed), nb = size_t(packed.cols / kBlock);
+    constexpr int kSamples = 64;
+    for (int k = 0; k <= kSamples; ++k) {
+        const size_t r = size_t((long long)k * (rows - 1) / kSamples);
+        const HostTensor* src = order[r].first;
+        const size_t sr = size_t(order[r].second);
+        if (std::memcmp(packed.data + r * rb, src->data + sr * rb, rb) != 0 ||
+            std::memcmp(packed.scales() + r * nb, src->scales() + sr * nb, nb * 2) != 0)
+            return false;
+    }
+    return true;
+}
+
 std::vector<float> fuse_qkv_bias(const std::vector<const HostTensor*>& biases, int head_dim) {
     std::vector<float> b;
     const int half = head_dim / 2;

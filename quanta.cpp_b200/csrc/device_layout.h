@@ -33,6 +33,9 @@ struct FusedHost {
 FusedHost fuse_rows(const std::vector<const HostTensor*>& parts, int mode, int head_dim);
 // The q, k and v biases (f32) in fuse_rows' mode-0 row order.
 std::vector<float> fuse_qkv_bias(const std::vector<const HostTensor*>& biases, int head_dim);
+// True when `packed` has the fused matrix's dtype and shape and, on a sample of rows spread over it (the first and last
+// included), the parts' rows in fuse_rows' order: a stale or foreign pre-packed tensor is not uploaded.
+bool packed_rows_match(const HostTensor& packed, const std::vector<const HostTensor*>& parts, int mode, int head_dim);
 
 // Writes in_path's tensors plus the pre-packed ones to out_path.  Returns false with *err on failure.
 bool export_device_layout(const std::string& in_path, const std::string& out_path, std::string* err);

@@ -92,12 +92,10 @@ DMat Engine::upload_fused(const std::vector<const HostTensor*>& parts, int mode)
     return m;
 }
 
-// A fused matrix stored pre-packed by export_device_layout: uploaded as it is when its dtype and shape are those the
-// parts fuse to, else fused here.
+// A fused matrix stored pre-packed by export_device_layout: uploaded as it is when it holds the parts' rows in the
+// fused order (dtype, shape and a sample of rows checked), else fused here.
 DMat Engine::upload_packed(const HostTensor* packed, const std::vector<const HostTensor*>& parts, int mode) {
-    int rows = 0;
-    for (const HostTensor* p : parts) rows += p->rows;
-    if (packed && packed->dtype == parts[0]->dtype && packed->cols == parts[0]->cols && packed->rows == rows) {
+    if (packed && packed_rows_match(*packed, parts, mode, hp_.head_dim)) {
         ++packed_tensors_;
         return upload_matrix(*packed);
     }
@@ -209,16 +207,14 @@ bool Engine::load(const std::string& path, int ctx_len, std::string* err, bool n
             // fused bias in the q|k|v pair-interleaved order
             std::vector<float> b(size_t(L.qkv.rows), 0.f);
             if (hp_.qkv_bias) {
+                // the fused bias is small: it is built here and a pre-packed copy only counts when it is the same
+                b = fuse_qkv_bias({&file_.require(p + "self_attn.q_proj.bias"), &file_.require(p + "self_attn.k_proj.bias"),
+                                   &file_.require(p + "self_attn.v_proj.bias")},
+                                  hp_.head_dim);
+                if (b.size() != size_t(L.qkv.rows)) throw std::runtime_error("qkv bias lengths do not match the q|k|v rows");
                 const HostTensor* pb = packed ? file_.find(pk + "qkv_bias") : nullptr;
-                if (pb && pb->dtype == DT_F32 && pb->cols == L.qkv.rows) {
-                    std::memcpy(b.data(), pb->data, b.size() * 4);
+                if (pb && pb->dtype == DT_F32 && pb->cols == L.qkv.rows && std::memcmp(b.data(), pb->data, b.size() * 4) == 0)
                     ++packed_tensors_;
-                } else {
-                    b = fuse_qkv_bias({&file_.require(p + "self_attn.q_proj.bias"), &file_.require(p + "self_attn.k_proj.bias"),
-                                       &file_.require(p + "self_attn.v_proj.bias")},
-                                      hp_.head_dim);
-                    if (b.size() != size_t(L.qkv.rows)) throw std::runtime_error("qkv bias lengths do not match the q|k|v rows");
-                }
             }
             float* db = static_cast<float*>(dalloc(b.size() * 4));
             cudaMemcpy(db, b.data(), b.size() * 4, cudaMemcpyHostToDevice);

@@ -82,3 +82,24 @@ def test_exported_layout_with_nibble_screen(qb, models, exported):
     finally:
         a.close()
         b.close()
+
+
+def test_stale_packed_tensor_is_fused_at_load(qb, models, exported, tmp_path):
+    """A pre-packed matrix whose rows no longer match the file's own q|k|v (one byte changed in its first row) is not
+    uploaded: the engine fuses that layer's rows itself, and the logits stay the original file's."""
+    from test_device_layout import read_qnt
+    src = exported("tiny_q8")
+    tensors, _ = read_qnt(src)
+    off = tensors["b200.layers.0.qkv"][5]
+    data = bytearray(src.read_bytes())
+    data[off] ^= 0x5A
+    bad = tmp_path / "stale.qnt"
+    bad.write_bytes(bytes(data))
+    a, b = qb.Model(models("tiny_q8"), ctx_len=256), qb.Model(bad, ctx_len=256)
+    try:
+        assert b.packed_tensors == 3 * a.hp.n_layers - 1
+        prompt = np.random.default_rng(3).integers(0, a.hp.n_tokens, 32)
+        assert np.array_equal(a.forward_batch(prompt, 0), b.forward_batch(prompt, 0))
+    finally:
+        a.close()
+        b.close()
