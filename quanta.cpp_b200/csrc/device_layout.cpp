@@ -1,6 +1,8 @@
 // The device's fused row order on the host, and the pre-packed .qnt writer (device_layout.h).
 #include "device_layout.h"
 
+#include <sys/stat.h>
+
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -135,7 +137,11 @@ bool export_device_layout(const std::string& in_path, const std::string& out_pat
     QntFile in;
     std::string e;
     if (!in.open(in_path, &e)) return bad(e);
-    if (in_path == out_path) return bad("export_device_layout: the output must be another file");
+    // the input stays mapped while the output is written: the output must not be the same file under another name
+    struct stat si, so;
+    if (in_path == out_path ||
+        (::stat(in_path.c_str(), &si) == 0 && ::stat(out_path.c_str(), &so) == 0 && si.st_dev == so.st_dev && si.st_ino == so.st_ino))
+        return bad("export_device_layout: the output must be another file");
     const HParams& hp = in.hparams();
     std::vector<OutTensor> outs;
     for (const std::string& name : in.tensor_names()) {

@@ -114,6 +114,12 @@ def test_export_is_idempotent_and_rejects_bad_paths(qb, models, exported, tmp_pa
     assert e.value.code == -3
     with pytest.raises(qb.QntError):
         qb.export_device_layout(models("tiny_q8"), models("tiny_q8"))
+    before = models("tiny_q8").read_bytes()
+    alias = tmp_path / "alias.qnt"  # the same file under another name: refused, the input untouched
+    alias.symlink_to(models("tiny_q8"))
+    with pytest.raises(qb.QntError):
+        qb.export_device_layout(models("tiny_q8"), alias)
+    assert models("tiny_q8").read_bytes() == before
     with pytest.raises(qb.QntError):
         qb.export_device_layout(models("tiny_q8"), tmp_path / "no_such_dir" / "x.qnt")
 
