@@ -50,7 +50,7 @@ JOB_SEQS, JOB_WAVE, JOB_GEN = 2048, 256, 128
 
 # DRAM bytes of one decode step of this workload: dram__bytes_read.sum + dram__bytes_write.sum summed over the step's
 # launches in one ncu capture of this command
-STEP_TRAFFIC_BYTES = 339_400_192
+STEP_TRAFFIC_BYTES = 339_258_880
 
 
 def log(*a):
