@@ -210,18 +210,18 @@ __device__ __forceinline__ void tmem_ld_blocks(uint32_t taddr, int* v) {
               "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
             : "r"(taddr), "r"(taddr + 16u), "r"(taddr + 32u), "r"(taddr + 48u)
             : "memory");
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const uint32_t ta = taddr + uint32_t(4 * NC * b);
-        int* w = v + NC * b;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
-            "tcgen05.wait::ld.sync.aligned;"
-            : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
-            : "r"(ta)
-            : "memory");
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t ta = taddr + uint32_t(4 * NC * b);
+            int* w = v + NC * b;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+                "tcgen05.wait::ld.sync.aligned;"
+                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                : "r"(ta)
+                : "memory");
+        }
     }
 }
 
@@ -739,7 +739,7 @@ __global__ void __launch_bounds__(128, 1) k_mma_i8_peak(int iters, unsigned long
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t done;
     __shared__ uint32_t tmem_base;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < (kTileRows + kPeakN) * 128 / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(smem)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes visible to the MMA

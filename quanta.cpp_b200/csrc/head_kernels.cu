@@ -37,7 +37,6 @@ __host__ __device__ constexpr int head_threads(int dtype) { return head_tile_row
 // of 176 rows per CTA (1056 row slots) instead of 9 of 128 (1152), with more warps per SM to hide latency.
 constexpr int kWideTileRows = 176;
 constexpr int kHeadWarps = kHeadThreads / 32;
-constexpr int kStages = 4;
 
 // ---------------------------------------------------------------- candidate lists (K <= 32), kept with bitonic networks
 
