@@ -17,13 +17,6 @@ import sys
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-os.environ.setdefault("QNT_LIB_DIR", str(PKG / "lib_stamps"))
-sys.path.insert(0, str(PKG))
-sys.path.insert(0, str(PKG.parent))
-
-import numpy as np  # noqa: E402
-
-import quanta_b200 as qb  # noqa: E402
 
 KINDS = {1: "k_attn (q|k|v + attention + o_proj terms)", 2: "k_gateup_dec (o_proj residual + norm + gate|up + SwiGLU)",
          3: "k_resid_dec (down + residual)", 4: "k_embed", 5: "k_sl_mark (must ids)",
@@ -123,6 +116,12 @@ def summarize(recs):
 
 
 def main():
+    # the phase-timed library, chosen before the binding is first imported (importing this module has no such effect)
+    os.environ.setdefault("QNT_LIB_DIR", str(PKG / "lib_stamps"))
+    sys.path.insert(0, str(PKG))
+    sys.path.insert(0, str(PKG.parent))
+    import numpy as np
+    import quanta_b200 as qb
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     steps = int(sys.argv[sys.argv.index("--steps") + 1]) if "--steps" in sys.argv else 32
     if args and not args[0].isdigit():
