@@ -141,3 +141,16 @@ def test_reference_reads_exported_file_unchanged(models, exported, name):
         assert np.array_equal(a.forward(t, p), b.forward(t, p)), p
     nv = a.n_tokens
     assert np.array_equal(a.head(top_k=20, n_valid=nv), b.head(top_k=20, n_valid=nv))
+
+
+def test_cli_export_layout_writes_the_same_file(qb, models, exported, tmp_path):
+    """`quanta_b200 export-layout IN OUT` (host code only, no GPU) writes the same bytes as the C ABI entry."""
+    import subprocess
+    cli = Path(qb.__file__).resolve().parent / "lib" / "quanta_b200"
+    out = tmp_path / "cli.qnt"
+    r = subprocess.run([str(cli), "export-layout", str(models("tiny_q8")), str(out)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert out.read_bytes() == exported("tiny_q8").read_bytes()
+    r = subprocess.run([str(cli), "export-layout", str(tmp_path / "missing.qnt"), str(tmp_path / "y.qnt")],
+                       capture_output=True, text=True)
+    assert r.returncode == 1 and "export-layout:" in r.stderr
