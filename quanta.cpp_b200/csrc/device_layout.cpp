@@ -249,7 +249,12 @@ bool export_device_layout(const std::string& in_path, const std::string& out_pat
             at += piece.second;
         }
     }
-    if (!ok || std::fflush(f.get()) != 0) return bad("export_device_layout: writing '" + out_path + "' failed");
+    ok = ok && std::fflush(f.get()) == 0;
+    ok = std::fclose(f.release()) == 0 && ok;
+    if (!ok) {
+        std::remove(out_path.c_str());  // no partial file is left behind
+        return bad("export_device_layout: writing '" + out_path + "' failed");
+    }
     return true;
 }
 
